@@ -1,0 +1,195 @@
+"""PyTorch-on-CPU restatement of the reference's forward-Laplacian oracle (test only).
+
+Every function works on the packed 12,737-float parameter buffer (the ABI of
+``csrc/mlp_abi.cuh:8-17`` / ``src/fused_hoad/parameters.py:28-48``) so the same vectors
+drive the CUDA kernels and the oracle.
+
+Jet convention (``src/fused_hoad/backends/forward_laplacian.py:3-16``): each hidden state
+is ``[batch, dims + 2, width]`` = (value, d/dx_0, d/dx_1, Laplacian). A linear layer is one
+matmul with the bias added to the value row only (``:52-57``); tanh applies
+``h_v = a, h_J = s z_J, h_L = s z_L - 2 a s |z_J|^2`` with ``a = tanh(z_v), s = 1 - a^2``
+(``:28-31, :60-67``).
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+from torch import Tensor
+
+INPUTS = 2
+HIDDEN = 64
+HIDDEN_LAYERS = 4
+# (out_features, in_features) per linear layer: src/fused_hoad/parameters.py:29
+SHAPES = ((64, 2), (64, 64), (64, 64), (64, 64), (1, 64))
+PARAMETER_COUNT = sum(o * i + o for o, i in SHAPES)
+assert PARAMETER_COUNT == 12737
+
+
+def layer_offsets() -> list[tuple[int, int, int, int]]:
+    """(weight_offset, bias_offset, out, in) per layer; parameters.py:_make_layout."""
+    offsets, offset = [], 0
+    for out_features, in_features in SHAPES:
+        offsets.append((offset, offset + out_features * in_features, out_features, in_features))
+        offset += out_features * in_features + out_features
+    return offsets
+
+
+def unpack(params: Tensor) -> list[tuple[Tensor, Tensor]]:
+    """Views ``(W [out, in], b [out])`` into a packed buffer; parameters.py:87-99."""
+    if params.ndim != 1 or params.numel() != PARAMETER_COUNT:
+        raise ValueError(f"parameters must have shape [{PARAMETER_COUNT}]")
+    return [
+        (params[w : w + o * i].view(o, i), params[b : b + o])
+        for w, b, o, i in layer_offsets()
+    ]
+
+
+def init_parameters(seed: int = 0, scale: float = 1.0, dtype=torch.float32) -> Tensor:
+    """Packed parameters of ``torch.manual_seed(seed); build_mlp(DEFAULT_POISSON_MLP)``.
+
+    ``nn.Linear`` default init draws weight then bias per layer, in layer order
+    (``src/fused_hoad/models.py:15-26``); building the same modules reproduces the stream.
+    """
+    torch.manual_seed(seed)
+    layers = [torch.nn.Linear(i, o) for o, i in SHAPES]
+    with torch.no_grad():
+        flat = torch.cat([t.reshape(-1) for layer in layers for t in (layer.weight, layer.bias)])
+    return (flat * scale).to(dtype).contiguous()
+
+
+def uniform_points(n: int, seed: int = 1, dtype=torch.float32) -> Tensor:
+    """``torch.rand(n, 2, generator=CPU(seed)) * 2 - 1`` as in the benchmark configs."""
+    generator = torch.Generator().manual_seed(seed)
+    return (torch.rand(n, 2, generator=generator) * 2 - 1).to(dtype)
+
+
+def _tanh_jet(jet: Tensor) -> Tensor:
+    # forward_laplacian.py:28-31 (_tanh_jet) and :60-67 (_activation)
+    z_v, z_j = jet[:, :1], jet[:, 1:-1]
+    a = torch.tanh(z_v)
+    s = 1.0 - a * a
+    out = s * jet
+    out[:, -1:].add_(-2.0 * a * s * (z_j * z_j).sum(dim=1, keepdim=True))
+    out[:, :1].copy_(a)
+    return out
+
+
+def _linear(jet: Tensor, weight: Tensor, bias: Tensor) -> Tensor:
+    # forward_laplacian.py:52-57: bias on the value row only
+    out = jet @ weight.T
+    out[:, 0].add_(bias)
+    return out
+
+
+def forward_laplacian_from_linears(linears, coords: Tensor) -> tuple[Tensor, Tensor]:
+    """(u, lap) each ``[n, 1]``; forward_laplacian.py:84-92 with :116-132."""
+    n, dims = coords.shape
+    jet = coords.new_zeros(n, dims + 2, dims)
+    jet[:, 0] = coords
+    jet[:, 1:-1] = torch.eye(dims, dtype=coords.dtype, device=coords.device)
+    for index, (weight, bias) in enumerate(linears):
+        jet = _linear(jet, weight, bias)
+        if index < len(linears) - 1:
+            jet = _tanh_jet(jet)
+    return jet[:, 0], jet[:, -1]
+
+
+def forward_laplacian(params: Tensor, coords: Tensor) -> tuple[Tensor, Tensor]:
+    """Forward Laplacian of the packed MLP at ``coords [n, 2]`` in their dtype."""
+    return forward_laplacian_from_linears(unpack(params.to(coords.dtype)), coords)
+
+
+def eager_laplacian(params: Tensor, coords: Tensor) -> tuple[Tensor, Tensor]:
+    """Nested-autograd Laplacian; src/fused_hoad/autodiff.py:16-40, reference.py:9-20."""
+    linears = unpack(params.to(coords.dtype))
+    x = coords.detach().clone().requires_grad_(True)
+    with torch.enable_grad():
+        h = x
+        for index, (weight, bias) in enumerate(linears):
+            h = h @ weight.T + bias
+            if index < len(linears) - 1:
+                h = torch.tanh(h)
+        (first,) = torch.autograd.grad(h.sum(), x, create_graph=True)
+        lap = torch.zeros_like(h)
+        for d in range(x.shape[1]):
+            (second,) = torch.autograd.grad(first[:, d].sum(), x, create_graph=True)
+            lap = lap + second[:, d : d + 1]
+    return h.detach(), lap.detach()
+
+
+def recompute_backward(
+    params: Tensor, coords: Tensor, grad_u: Tensor, grad_lap: Tensor
+) -> tuple[Tensor, Tensor]:
+    """(grad_params [12737], grad_coords [n, 2]); backends/fused.py:76-101.
+
+    Rebuilds the jet from views of the flat buffer and differentiates it with autograd,
+    exactly as the reference's ``_recompute_backward`` does.
+    """
+    dtype = coords.dtype
+    with torch.enable_grad():
+        x = coords.detach().clone().requires_grad_(True)
+        flat = params.detach().to(dtype).clone().requires_grad_(True)
+        outputs = forward_laplacian_from_linears(unpack(flat), x)
+        grad_x, grad_p = torch.autograd.grad(
+            outputs,
+            [x, flat],
+            (grad_u.reshape(-1, 1).to(dtype), grad_lap.reshape(-1, 1).to(dtype)),
+            allow_unused=True,
+        )
+    if grad_x is None:  # empty batch
+        grad_x = torch.zeros_like(coords)
+    if grad_p is None:
+        grad_p = torch.zeros_like(flat)
+    return grad_p.detach(), grad_x.detach()
+
+
+def manufactured_source(coords: Tensor) -> Tensor:
+    """f = -2 pi^2 sin(pi x) sin(pi y); src/fused_hoad/problems/poisson.py:29-39."""
+    x, y = coords[:, 0:1], coords[:, 1:2]
+    return -2.0 * math.pi**2 * (torch.sin(math.pi * x) * torch.sin(math.pi * y))
+
+
+def poisson_step_gradients(
+    params: Tensor, coords: Tensor, total_points: int | None = None
+) -> tuple[Tensor, Tensor, Tensor]:
+    """Gradients of ``L = sum((lap - f)^2) / total_points`` (benchmark_training.py:46-48).
+
+    ``total_points`` defaults to ``len(coords)`` (the plain mean); a data-parallel shard
+    passes the global count so shard gradients sum to the global one. Returns
+    ``(loss_partial, grad_params, grad_coords)`` where ``loss_partial`` is this shard's
+    contribution to the loss.
+    """
+    n = coords.shape[0]
+    total = n if total_points is None else total_points
+    _, lap = forward_laplacian(params, coords)
+    residual = lap - manufactured_source(coords)
+    loss = (residual * residual).sum() / total
+    grad_lap = 2.0 * residual / total
+    grad_p, grad_x = recompute_backward(params, coords, torch.zeros_like(lap), grad_lap)
+    return loss, grad_p, grad_x
+
+
+def adam_update(
+    params: Tensor,
+    grad: Tensor,
+    exp_avg: Tensor,
+    exp_avg_sq: Tensor,
+    step: int,
+    lr: float = 1e-3,
+    beta1: float = 0.9,
+    beta2: float = 0.999,
+    eps: float = 1e-8,
+) -> None:
+    """In-place Adam step ``step`` (1-based) with torch.optim.Adam's defaults and formula.
+
+    Restates ``torch.optim.Adam`` (used at benchmarks/benchmark_training.py:41): moments by
+    lerp, ``denom = sqrt(v) / sqrt(1 - beta2^t) + eps``, ``p -= lr / (1 - beta1^t) * m / denom``.
+    """
+    exp_avg.mul_(beta1).add_(grad, alpha=1.0 - beta1)
+    exp_avg_sq.mul_(beta2).addcmul_(grad, grad, value=1.0 - beta2)
+    bias1 = 1.0 - beta1**step
+    bias2 = 1.0 - beta2**step
+    denom = exp_avg_sq.sqrt() / math.sqrt(bias2) + eps
+    params.addcdiv_(exp_avg, denom, value=-lr / bias1)

@@ -1,0 +1,127 @@
+"""Pin both CPU oracles to the golden vectors recorded from the unmodified reference."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+from conftest import assert_scaled_close
+
+from oracle import cjet, jet
+
+FORWARD_BATCHES = (1, 2, 15, 16, 17, 31, 32, 33, 63, 64, 65, 127, 128, 129, 1000, 1024)
+
+
+def test_parameter_init_matches_reference_pack(golden) -> None:
+    # build_mlp + pack_poisson_parameters (src/fused_hoad/parameters.py:55-84)
+    np.testing.assert_array_equal(jet.init_parameters(0).numpy(), golden["params_seed0"])
+    np.testing.assert_array_equal(
+        jet.init_parameters(1, scale=3.0).numpy(), golden["params_seed1_x3"]
+    )
+
+
+def test_points_match_reference_generator(golden) -> None:
+    for n in FORWARD_BATCHES:
+        np.testing.assert_array_equal(jet.uniform_points(n).numpy(), golden[f"fwd{n}_x"])
+
+
+@pytest.mark.parametrize("n", FORWARD_BATCHES)
+def test_torch_oracle_forward_fp32_matches_reference(golden, n: int) -> None:
+    params = torch.from_numpy(golden["params_seed0"])
+    x = torch.from_numpy(golden[f"fwd{n}_x"])
+    u, lap = jet.forward_laplacian(params, x)
+    # Same ops in the same order as the reference: agreement to FP32 rounding.
+    np.testing.assert_allclose(u.numpy(), golden[f"fwd{n}_u32"], rtol=1e-6, atol=1e-7)
+    np.testing.assert_allclose(lap.numpy(), golden[f"fwd{n}_lap32"], rtol=1e-6, atol=1e-7)
+
+
+@pytest.mark.parametrize("n", FORWARD_BATCHES)
+def test_torch_oracle_forward_fp64_matches_reference(golden, n: int) -> None:
+    params = torch.from_numpy(golden["params_seed0"]).double()
+    x = torch.from_numpy(golden[f"fwd{n}_x"]).double()
+    u, lap = jet.forward_laplacian(params, x)
+    np.testing.assert_allclose(u.numpy(), golden[f"fwd{n}_u64"], rtol=1e-12, atol=1e-14)
+    np.testing.assert_allclose(lap.numpy(), golden[f"fwd{n}_lap64"], rtol=1e-12, atol=1e-14)
+
+
+@pytest.mark.parametrize("n", (1, 33, 1000))
+def test_torch_oracle_eager_matches_reference(golden, n: int) -> None:
+    params = torch.from_numpy(golden["params_seed0"]).double()
+    x = torch.from_numpy(golden[f"fwd{n}_x"]).double()
+    _, lap = jet.eager_laplacian(params, x)
+    np.testing.assert_allclose(lap.numpy(), golden[f"fwd{n}_eager_lap64"], rtol=1e-10, atol=1e-12)
+
+
+@pytest.mark.parametrize("n", FORWARD_BATCHES)
+def test_c_oracle_forward_matches_reference_fp64(golden, n: int) -> None:
+    u, lap = cjet.forward(golden["params_seed0"], golden[f"fwd{n}_x"])
+    np.testing.assert_allclose(u, golden[f"fwd{n}_u64"][:, 0], rtol=1e-11, atol=1e-13)
+    np.testing.assert_allclose(lap, golden[f"fwd{n}_lap64"][:, 0], rtol=1e-11, atol=1e-13)
+
+
+def test_oracles_match_reference_on_saturated_weights(golden) -> None:
+    params = golden["params_seed1_x3"]
+    u, lap = cjet.forward(params, golden["sat_x"])
+    assert_scaled_close(lap, golden["sat_lap64"][:, 0], 1e-12, "c lap")
+    assert_scaled_close(u, golden["sat_u64"][:, 0], 1e-12, "c u")
+    tu, tl = jet.forward_laplacian(torch.from_numpy(params), torch.from_numpy(golden["sat_x"]))
+    np.testing.assert_allclose(tl.numpy(), golden["sat_lap32"], rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("n", (1, 15, 16, 17, 33, 1000))
+def test_torch_oracle_backward_fp32_matches_reference(golden, n: int) -> None:
+    params = torch.from_numpy(golden["params_seed0"])
+    gp, gx = jet.recompute_backward(
+        params,
+        torch.from_numpy(golden[f"bwd{n}_x"]),
+        torch.from_numpy(golden[f"bwd{n}_gu"]),
+        torch.from_numpy(golden[f"bwd{n}_gl"]),
+    )
+    assert_scaled_close(gp.numpy(), golden[f"bwd{n}_gp32"], 1e-6, "grad params")
+    assert_scaled_close(gx.numpy(), golden[f"bwd{n}_gx32"], 1e-6, "grad coords")
+
+
+@pytest.mark.parametrize("n", (33, 1000))
+def test_c_oracle_backward_matches_reference_fp64(golden, n: int) -> None:
+    gp, gx = cjet.backward(
+        golden["params_seed0"], golden[f"bwd{n}_x"], golden[f"bwd{n}_gu"], golden[f"bwd{n}_gl"]
+    )
+    assert_scaled_close(gp, golden[f"bwd{n}_gp64"], 1e-11, "grad params")
+    assert_scaled_close(gx, golden[f"bwd{n}_gx64"], 1e-11, "grad coords")
+    # every parameter block, not just the max (tests/test_fused.py:209-218)
+    for w, b, o, i in jet.layer_offsets():
+        assert_scaled_close(gp[w : w + o * i], golden[f"bwd{n}_gp64"][w : w + o * i], 1e-11)
+        assert_scaled_close(gp[b : b + o], golden[f"bwd{n}_gp64"][b : b + o], 1e-11)
+
+
+def test_c_oracle_backward_matches_reference_saturated(golden) -> None:
+    gp, gx = cjet.backward(
+        golden["params_seed1_x3"], golden["satbwd_x"], golden["satbwd_gu"], golden["satbwd_gl"]
+    )
+    assert_scaled_close(gp, golden["satbwd_gp64"], 1e-11, "grad params")
+    assert_scaled_close(gx, golden["satbwd_gx64"], 1e-11, "grad coords")
+
+
+def test_oracle_adam_trajectory_matches_reference(golden) -> None:
+    params = torch.from_numpy(golden["params_seed0"]).clone()
+    x = torch.from_numpy(golden["adam_x"])
+    m, v = torch.zeros_like(params), torch.zeros_like(params)
+    losses = []
+    for step in range(1, len(golden["adam_losses"]) + 1):
+        loss, grad, _ = jet.poisson_step_gradients(params, x)
+        losses.append(loss.item())
+        jet.adam_update(params, grad, m, v, step)
+    np.testing.assert_allclose(losses, golden["adam_losses"], rtol=1e-5)
+    np.testing.assert_allclose(params.numpy(), golden["adam_params_final"], rtol=1e-5, atol=1e-7)
+
+
+def test_known_answers() -> None:
+    # With every weight and bias zero except b_out the network is constant, so u = b_out
+    # and lap = 0 exactly (the analogue of tests/test_backends.py:104-108's linear case).
+    params = torch.zeros(jet.PARAMETER_COUNT, dtype=torch.float64)
+    params[-1] = 0.25
+    x = jet.uniform_points(17, dtype=torch.float64)
+    u, lap = jet.forward_laplacian(params, x)
+    assert torch.all(u == 0.25) and torch.all(lap == 0.0)
+    cu, cl = cjet.forward(params.numpy(), x.numpy())
+    assert np.all(cu == 0.25) and np.all(cl == 0.0)
