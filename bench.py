@@ -1,0 +1,404 @@
+"""Benchmark of the fused forward-Laplacian hot path (driver contract: one JSON line).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--points P] [--version V] [--train-steps T]
+
+Headline: residual evaluation ``(u, lap)`` of the
+2->64->64->64->64->1 tanh MLP (seed-0 nn.Linear init) at 65,536 uniform points in
+[-1,1]^2 per GPU, fp32. A step is one launch of the forward kernel over the rank's points.
+With N GPUs (torchrun, one process per GPU) every rank evaluates its own 65,536 points with
+no collective (weak scaling) and ``value`` is all ranks' points / the max-over-ranks device
+time. Inputs are smaller than L2, so L2 is flushed (a 192 MiB write) between timed steps,
+outside the timed events.
+
+Also reported in the same line:
+* ``e2e``: the same metric through the public op ``fused_hoad._C.fused_forward_laplacian``
+  with the points copied from pinned host memory and (u, lap) copied back every step;
+* ``train_step``: BASELINE.json config 2 (fused forward+loss+backward kernel, row
+  reduction, [all-reduce,] fused Adam) at 65,536 points per GPU;
+* ``roofline`` of the forward kernel against the measured peaks in MEASURED_PEAKS.json;
+* ``cpu_baseline``: the CPU oracle port of the reference's PyTorch forward Laplacian timed
+  on this host (rank 0, N=1 only), a reported baseline.
+
+``--impl reference`` times only that CPU port (the reference's own algorithm; the reference
+package itself does not exist on the GPU box) on the same metric and prints its line.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path[:0] = [str(ROOT), str(ROOT / "expanded-gpu-optimization_b200")]
+
+import torch  # noqa: E402
+
+METRIC = "collocation pts/sec for (u,Δu) eval and fwd+bwd step at 64K–16M pts, 1–8 GPU"
+UNIT = "pts/s"
+FLOP_FORWARD = 101_888  # per point: 3 hidden 64x64 jet GEMMs x 4 comps + layer 0/out + tanh jet
+FLOP_STEP = 98_304 * 3 + 256 * 2 + 6_000  # forward + input adjoint + weight gradient + small
+POINTS_PER_GPU = 65_536
+FLUSH_BYTES = 192 << 20
+PEAKS_FILE = ROOT / "MEASURED_PEAKS.json"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
+                  "sm_max_mhz": 1965.0}
+SM_COUNT = 148
+CLOCK_QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+
+def parse_args():
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawTextHelpFormatter)
+    p.add_argument("--gpus", type=int, default=int(os.environ.get("WORLD_SIZE", "1")))
+    p.add_argument("--steps", type=int, default=3000)
+    p.add_argument("--warmup", type=int, default=20)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--points", type=int, default=POINTS_PER_GPU, help="points per GPU")
+    p.add_argument("--version", type=int, default=None, help="forward kernel version")
+    p.add_argument("--train-steps", type=int, default=None)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def load_peaks() -> tuple[dict, str]:
+    if PEAKS_FILE.exists():
+        return json.loads(PEAKS_FILE.read_text()), "measured"
+    return FALLBACK_PEAKS, "fallback"
+
+
+# ------------------------------------------------------------------ clocks ----
+
+class ClockSampler:
+    """nvidia-smi sampling of this rank's GPU while the timed region runs."""
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={CLOCK_QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "50"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True,
+            )
+            time.sleep(0.3)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is None:
+            return False
+        time.sleep(0.1)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        self.lines = [line for line in out.splitlines() if line.strip()]
+        return False
+
+    def summary(self) -> dict:
+        sm, mx, reasons, power = [], 0.0, set(), []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = max(mx, float(f[2]))
+                power.append(float(f[3]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, f[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        return {
+            "sm_mhz": statistics.median(sm) if sm else None,
+            "sm_max_mhz": mx or None,
+            "reasons": sorted(reasons),
+            "samples": len(sm),
+            "power_w_max": max(power) if power else None,
+        }
+
+
+# ---------------------------------------------------------- CPU baseline ----
+
+def cpu_baseline(points: int, budget_s: float, steps: int | None = None) -> dict:
+    """The oracle port of the reference's PyTorch forward Laplacian on this host's cores."""
+    from oracle import jet
+
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    params = jet.init_parameters(0)
+    coords = jet.uniform_points(points)
+    jet.forward_laplacian(params, coords)  # warm-up
+    start = time.perf_counter()
+    jet.forward_laplacian(params, coords)
+    one = time.perf_counter() - start
+    sample = points
+    if steps is not None and steps * one > budget_s:
+        sample = max(1024, int(points * budget_s / (steps * one)))
+    coords = coords[:sample].contiguous()
+    times = []
+    deadline = time.perf_counter() + budget_s
+    runs = steps if steps is not None else 10_000
+    for _ in range(runs):
+        t0 = time.perf_counter()
+        jet.forward_laplacian(params, coords)
+        times.append(time.perf_counter() - t0)
+        if steps is None and time.perf_counter() > deadline and len(times) >= 5:
+            break
+    med = statistics.median(times)
+    return {
+        "value": sample / med,
+        "unit": UNIT,
+        "cores": cores,
+        "kind": "port",
+        "sample": (f"forward-Laplacian eval of {sample:,} of the config-1 points per call, "
+                   f"median of {len(times)} calls, torch {torch.__version__} on {cores} threads"),
+        "ms_per_call": med * 1e3,
+        "total_s": sum(times),
+    }
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle import jet
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    points = args.points
+    params = jet.init_parameters(0)
+    coords_full = jet.uniform_points(points)
+    jet.forward_laplacian(params, coords_full)
+    t0 = time.perf_counter()
+    jet.forward_laplacian(params, coords_full)
+    one = time.perf_counter() - t0
+    budget = 120.0
+    sample = points if args.steps * one <= budget else max(1024, int(points * budget / (args.steps * one)))
+    coords = coords_full[:sample].contiguous()
+    for _ in range(args.warmup):
+        jet.forward_laplacian(params, coords)
+    times = []
+    for _ in range(args.steps):
+        t = time.perf_counter()
+        jet.forward_laplacian(params, coords)
+        times.append(time.perf_counter() - t)
+    total = sum(times)
+    value = sample * args.steps / total
+    cores = os.cpu_count() or 1
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": total / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (uniform points in [-1,1]^2, CPU generator seed 1; seed-0 nn.Linear init)",
+        "config": {"workload": "config1: residual eval (u, lap), 2->64x4->1 tanh MLP",
+                   "points_per_step": sample, "parallelism": "rank 0 only (CPU)"},
+        "impl": "reference",
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": f"{sample:,} points per step of the 65,536-point config-1 "
+                                   f"workload; PyTorch forward Laplacian (oracle port of "
+                                   f"src/fused_hoad/backends/forward_laplacian.py) on {cores} threads"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------- our arm ----
+
+def run_ours(args) -> None:
+    import torch.distributed as dist
+
+    import fused_hoad
+    from fused_hoad.distributed import init_from_env
+
+    rank, world, local_rank = init_from_env("nccl")
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    C = fused_hoad.load_extension()
+    C.prepare_device(local_rank)
+    version = args.version if args.version is not None else 2
+    n = args.points
+    params = fused_hoad.pack_poisson_parameters(
+        (torch.manual_seed(0), fused_hoad.build_mlp())[1]
+    ).to(device)
+    # each rank's shard: points [rank*n, (rank+1)*n) of the global uniform set
+    host = fused_hoad.uniform_points(n * world, seed=1)[rank * n:(rank + 1) * n].contiguous()
+    coords = host.to(device)
+    flush = torch.empty(FLUSH_BYTES // 4, device=device)
+    stream = torch.cuda.current_stream()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- device-timed eval (headline) ----
+    for _ in range(args.warmup):
+        C.fused_forward_laplacian(coords, params, version)
+        flush.zero_()
+    events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(args.steps)]
+    barrier()
+    with ClockSampler(local_rank) as clocks:
+        for start, end in events:
+            flush.zero_()
+            start.record(stream)
+            C.fused_forward_laplacian(coords, params, version)
+            end.record(stream)
+        barrier()
+    eval_ms = [s.elapsed_time(e) for s, e in events]
+    total_ms = max_over_ranks(sum(eval_ms))
+    ms_per_step = total_ms / args.steps
+    value = n * world * args.steps / (total_ms / 1e3)
+
+    # ---- e2e through the public op with pinned host buffers ----
+    pinned_in = host.pin_memory()
+    pinned_u = torch.empty(n, 1).pin_memory()
+    pinned_lap = torch.empty(n, 1).pin_memory()
+    e2e_steps = max(1, min(args.steps, 1000))
+    dev_in = torch.empty_like(coords)
+
+    def e2e_step():
+        dev_in.copy_(pinned_in, non_blocking=True)
+        u, lap = C.fused_forward_laplacian(dev_in, params, version)
+        pinned_u.copy_(u, non_blocking=True)
+        pinned_lap.copy_(lap, non_blocking=True)
+
+    for _ in range(max(3, args.warmup)):
+        e2e_step()
+        flush.zero_()
+    ev2 = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(e2e_steps)]
+    barrier()
+    for start, end in ev2:
+        flush.zero_()
+        start.record(stream)
+        e2e_step()
+        end.record(stream)
+    barrier()
+    e2e_total = max_over_ranks(sum(s.elapsed_time(e) for s, e in ev2))
+    e2e_value = n * world * e2e_steps / (e2e_total / 1e3)
+    ok = torch.equal(pinned_lap, C.fused_forward_laplacian(coords, params, version)[1].cpu())
+
+    # ---- training step (config 2) ----
+    train_steps = args.train_steps if args.train_steps is not None else max(3, args.steps // 10)
+    trainer = fused_hoad.PoissonTrainer(params.clone())
+    for _ in range(max(3, args.warmup)):
+        trainer.step(coords, n * world)
+    ev3 = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(train_steps)]
+    barrier()
+    for start, end in ev3:
+        flush.zero_()
+        start.record(stream)
+        loss = trainer.step(coords, n * world)
+        end.record(stream)
+    barrier()
+    train_total = max_over_ranks(sum(s.elapsed_time(e) for s, e in ev3))
+    train_ms = train_total / train_steps
+    train_value = n * world * train_steps / (train_total / 1e3)
+    final_loss = float(loss.item())
+
+    peaks, peak_kind = load_peaks()
+    clk = clocks.summary()
+    if rank != 0:
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
+
+    per_launch_s = ms_per_step / 1e3
+    achieved_tflops = n * FLOP_FORWARD / per_launch_s / 1e12
+    fp32_peak = SM_COUNT * 128 * 2 * peaks.get("sm_max_mhz", 1965.0) * 1e6 / 1e12
+    if version <= 2:
+        roofline = {
+            "bound": "fp32", "achieved": achieved_tflops, "peak": fp32_peak, "unit": "TFLOP/s",
+            "frac": achieved_tflops / fp32_peak, "traffic": None,
+            "kernel": f"forward_fp32_kernel (version {version})",
+            "peak_note": ("FP32 CUDA-core peak 148 SMs x 128 lanes x 2 x sm_max_mhz "
+                          f"({peak_kind} sm_max_mhz); no measured FP32 peak exists"),
+            "flop_per_point": FLOP_FORWARD,
+        }
+    else:
+        bf16 = peaks["bf16_tflops"]
+        roofline = {
+            "bound": "tensor", "achieved": achieved_tflops, "peak": bf16, "unit": "TFLOP/s",
+            "frac": achieved_tflops / bf16, "traffic": None,
+            "kernel": f"forward_tc_kernel (version {version})",
+            "peak_note": (f"{peak_kind} bf16 burst peak; TF32 runs at half of it and 3xTF32 "
+                          "issues three MMAs per product, so the 3xTF32 ceiling is bf16/6"),
+            "frac_of_3xtf32_ceiling": achieved_tflops / (bf16 / 6.0),
+            "flop_per_point": FLOP_FORWARD,
+        }
+    if clk["sm_mhz"]:
+        roofline["fp32_peak_at_median_clock"] = SM_COUNT * 256 * clk["sm_mhz"] * 1e6 / 1e12
+
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (uniform points in [-1,1]^2, CPU generator seed 1; seed-0 nn.Linear init)",
+        "config": {
+            "workload": "config1: residual eval (u, lap) of the 2->64->64->64->64->1 tanh MLP",
+            "points_per_gpu": n, "global_points": n * world, "forward_version": version,
+            "l2": f"flushed between timed steps ({FLUSH_BYTES >> 20} MiB write, outside the events)",
+            "parallelism": f"dp{world}",
+        },
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": n * 8,
+                "d2h_bytes_per_step": n * 8, "steps": e2e_steps,
+                "api": "fused_hoad._C.fused_forward_laplacian", "result_checked": ok},
+        "gpu_launches": args.steps,
+        "roofline": roofline,
+        "clocks": clk,
+        "train_step": {
+            "workload": "config2: fused forward+loss+backward kernel, row reduction, "
+                        + ("all-reduce, " if world > 1 else "") + "fused Adam",
+            "value": train_value, "unit": UNIT, "ms_per_step": train_ms, "steps": train_steps,
+            "points_per_gpu": n, "launches_per_step": 3, "loss_after": final_loss,
+            "achieved_tflops": n * FLOP_STEP / (train_ms / 1e3) / 1e12,
+            "flop_per_point": FLOP_STEP,
+        },
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(n, budget_s=15.0)
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main() -> None:
+    args = parse_args()
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

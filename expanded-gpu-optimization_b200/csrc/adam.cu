@@ -1,0 +1,74 @@
+// Fused Adam over the flat 12,737-float parameter buffer, and the bounded-wait self-test.
+//
+// Adam follows torch.optim.Adam's single-tensor update (the optimizer of reference
+// benchmarks/benchmark_training.py:41), with no weight decay and no amsgrad:
+//   m = lerp(m, g, 1 - beta1); v = beta2 v + (1 - beta2) g^2
+//   p -= lr / (1 - beta1^t) * m / (sqrt(v) / sqrt(1 - beta2^t) + eps)
+// The step counter t lives in device memory so a captured CUDA graph can replay the step.
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace fhb {
+namespace {
+
+constexpr int kAdamThreads = 1024;
+
+// One CTA: every thread reads the counter before thread 0 stores the incremented value.
+__global__ void __launch_bounds__(kAdamThreads)
+    adam_kernel(float* __restrict__ params, const float* __restrict__ grad,
+                float* __restrict__ exp_avg, float* __restrict__ exp_avg_sq, int64_t count,
+                int64_t* __restrict__ step, float lr, float beta1, float beta2, float eps) {
+  const int64_t t = *step + 1;
+  const double bias1 = 1.0 - pow(static_cast<double>(beta1), static_cast<double>(t));
+  const double bias2 = 1.0 - pow(static_cast<double>(beta2), static_cast<double>(t));
+  const float step_size = static_cast<float>(static_cast<double>(lr) / bias1);
+  const float bias2_sqrt = static_cast<float>(sqrt(bias2));
+  for (int64_t i = threadIdx.x; i < count; i += kAdamThreads) {
+    const float g = grad[i];
+    float m = exp_avg[i];
+    m = fmaf(1.0f - beta1, g - m, m);
+    const float v = fmaf(beta2, exp_avg_sq[i], (1.0f - beta2) * g * g);
+    exp_avg[i] = m;
+    exp_avg_sq[i] = v;
+    const float denom = sqrtf(v) / bias2_sqrt + eps;
+    params[i] -= step_size * (m / denom);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) *step = t;
+}
+
+// Waits on an mbarrier that nothing arrives at; the bounded wait gives up after limit_ns,
+// records FHB_STATUS_SELFTEST and returns. Exercises the timeout path without a fault.
+__global__ void bounded_wait_selftest_kernel(uint64_t limit_ns, unsigned int* status) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  const uint64_t start = global_timer_ns();
+  bool done = false;
+  while (!done) {
+    done = mbar_try_wait(&bar, 0);
+    if (!done && global_timer_ns() - start > limit_ns) break;
+  }
+  if (!done && threadIdx.x == 0) report_status(status, FHB_STATUS_SELFTEST);
+}
+
+}  // namespace
+
+cudaError_t launch_adam(float* params, const float* grad, float* exp_avg, float* exp_avg_sq,
+                        int64_t count, int64_t* step, float lr, float beta1, float beta2,
+                        float eps, cudaStream_t stream) {
+  adam_kernel<<<1, kAdamThreads, 0, stream>>>(params, grad, exp_avg, exp_avg_sq, count, step,
+                                              lr, beta1, beta2, eps);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_bounded_wait_selftest(uint64_t limit_ns, unsigned int* status,
+                                         cudaStream_t stream) {
+  bounded_wait_selftest_kernel<<<1, 32, 0, stream>>>(limit_ns, status);
+  return cudaGetLastError();
+}
+
+}  // namespace fhb

@@ -1,0 +1,193 @@
+// torch.utils.cpp_extension binding: the module fused_hoad._C with the reference's op
+// contract (csrc/bindings.cpp:9-66 in the reference): same function names, argument names
+// and defaults, same validation order and messages. Every op calls the C ABI of
+// libfused_hoad_b200.so (include/fused_hoad_b200.h); outputs and workspaces come from the
+// ATen caching allocator on the current stream, so the ops stay asynchronous and
+// CUDA-graph capturable.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <cuda_runtime.h>
+#include <torch/extension.h>
+
+#include <vector>
+
+#include "../../include/fused_hoad_b200.h"
+
+namespace {
+
+constexpr int64_t kParameterCount = FHB_PARAMETER_COUNT;
+
+void check_inputs(const torch::Tensor& coordinates, const torch::Tensor& parameters) {
+  TORCH_CHECK(coordinates.is_cuda(), "coordinates must be a CUDA tensor");
+  TORCH_CHECK(parameters.is_cuda(), "parameters must be a CUDA tensor");
+  TORCH_CHECK(coordinates.is_contiguous(), "coordinates must be contiguous");
+  TORCH_CHECK(parameters.is_contiguous(), "parameters must be contiguous");
+  TORCH_CHECK(coordinates.scalar_type() == torch::kFloat32, "coordinates must use float32");
+  TORCH_CHECK(parameters.scalar_type() == torch::kFloat32, "parameters must use float32");
+  TORCH_CHECK(coordinates.dim() == 2 && coordinates.size(1) == 2,
+              "coordinates must have shape [batch, 2]");
+  TORCH_CHECK(parameters.dim() == 1 && parameters.numel() == kParameterCount,
+              "parameters must have shape [12737]");
+  TORCH_CHECK(coordinates.device() == parameters.device(),
+              "coordinates and parameters must be on the same device");
+}
+
+void check_vector(const torch::Tensor& t, const torch::Tensor& like, int64_t numel,
+                  const char* what) {
+  TORCH_CHECK(t.is_cuda() && t.is_contiguous() && t.scalar_type() == torch::kFloat32,
+              what, " must be a contiguous float32 CUDA tensor");
+  TORCH_CHECK(t.numel() == numel, what, " must have ", numel, " values");
+  TORCH_CHECK(t.device() == like.device(), what, " must be on the parameters' device");
+}
+
+void check_status(int code, const char* op) {
+  if (code == FHB_OK) return;
+  if (code == FHB_ERR_CUDA) {
+    const auto err = static_cast<cudaError_t>(fhb_last_cuda_error());
+    TORCH_CHECK(false, op, " failed: ", fhb_status_string(code), ": ", cudaGetErrorString(err));
+  }
+  TORCH_CHECK(false, op, " failed: ", fhb_status_string(code));
+}
+
+torch::Tensor workspace_for(int64_t batch, const torch::Tensor& like) {
+  const size_t bytes = fhb_backward_workspace_bytes(batch);
+  return torch::empty({static_cast<int64_t>((bytes + 15) / 16) * 4}, like.options());
+}
+
+}  // namespace
+
+std::vector<torch::Tensor> fused_forward_laplacian(torch::Tensor coordinates,
+                                                   torch::Tensor parameters, int64_t version) {
+  TORCH_CHECK(version >= 0 && version <= 5, "version must be 0 to 5");
+  check_inputs(coordinates, parameters);
+  const c10::cuda::CUDAGuard device_guard(coordinates.device());
+  const int64_t batch = coordinates.size(0);
+  auto output = torch::empty({batch, 1}, coordinates.options());
+  auto laplacian = torch::empty({batch, 1}, coordinates.options());
+  if (batch == 0) return {output, laplacian};
+  check_status(fhb_forward(coordinates.data_ptr<float>(), parameters.data_ptr<float>(),
+                           output.data_ptr<float>(), laplacian.data_ptr<float>(), batch,
+                           static_cast<int>(version), at::cuda::getCurrentCUDAStream()),
+               "fused_forward_laplacian");
+  return {output, laplacian};
+}
+
+std::vector<torch::Tensor> fused_forward_laplacian_backward(torch::Tensor coordinates,
+                                                            torch::Tensor parameters,
+                                                            torch::Tensor grad_output,
+                                                            torch::Tensor grad_laplacian,
+                                                            int64_t version) {
+  TORCH_CHECK(version >= 1 && version <= 6, "backward version must be 1 to 6");
+  check_inputs(coordinates, parameters);
+  for (const auto& grad : {grad_output, grad_laplacian}) {
+    TORCH_CHECK(grad.is_cuda() && grad.is_contiguous() && grad.scalar_type() == torch::kFloat32,
+                "upstream gradients must be contiguous float32 CUDA tensors");
+    TORCH_CHECK(grad.numel() == coordinates.size(0), "upstream gradients must have [batch] values");
+  }
+  const c10::cuda::CUDAGuard device_guard(coordinates.device());
+  const int64_t batch = coordinates.size(0);
+  auto grad_coordinates = torch::empty_like(coordinates);
+  if (batch == 0) return {torch::zeros_like(parameters), grad_coordinates};
+  auto grad_parameters = torch::empty_like(parameters);
+  auto workspace = workspace_for(batch, parameters);
+  check_status(
+      fhb_backward(coordinates.data_ptr<float>(), parameters.data_ptr<float>(),
+                   grad_output.data_ptr<float>(), grad_laplacian.data_ptr<float>(),
+                   grad_parameters.data_ptr<float>(), grad_coordinates.data_ptr<float>(), batch,
+                   static_cast<int>(version), workspace.data_ptr<float>(),
+                   static_cast<size_t>(workspace.numel()) * sizeof(float),
+                   at::cuda::getCurrentCUDAStream()),
+      "fused_forward_laplacian_backward");
+  return {grad_parameters, grad_coordinates};
+}
+
+// ---- B200-native training-step ops (no counterpart in the reference's _C) ----
+
+// Fused Poisson step gradients; see fhb_poisson_step_gradients. Returns
+// [grad_and_loss [12738] (gradient, then this shard's loss in the last slot),
+//  laplacian [N,1] or empty, grad_coordinates [N,2] or empty]. `total_points` is the
+// global batch (data-parallel shards pass the sum). One flat buffer lets a data-parallel
+// step all-reduce gradient and loss with a single collective.
+std::vector<torch::Tensor> poisson_step_gradients(torch::Tensor coordinates,
+                                                  torch::Tensor parameters,
+                                                  int64_t total_points, bool want_laplacian,
+                                                  bool want_grad_coordinates) {
+  check_inputs(coordinates, parameters);
+  const c10::cuda::CUDAGuard device_guard(coordinates.device());
+  const int64_t batch = coordinates.size(0);
+  TORCH_CHECK(total_points >= batch, "total_points must be >= the local batch");
+  auto grad_and_loss = torch::empty({kParameterCount + 1}, parameters.options());
+  auto laplacian = want_laplacian ? torch::empty({batch, 1}, coordinates.options())
+                                  : torch::empty({0}, coordinates.options());
+  auto grad_coordinates = want_grad_coordinates ? torch::empty_like(coordinates)
+                                                : torch::empty({0}, coordinates.options());
+  auto workspace = workspace_for(batch, parameters);
+  float* out = grad_and_loss.data_ptr<float>();
+  check_status(fhb_poisson_step_gradients(
+                   coordinates.data_ptr<float>(), parameters.data_ptr<float>(), batch,
+                   total_points, out,
+                   want_grad_coordinates ? grad_coordinates.data_ptr<float>() : nullptr,
+                   want_laplacian ? laplacian.data_ptr<float>() : nullptr,
+                   out + kParameterCount, batch ? workspace.data_ptr<float>() : nullptr,
+                   static_cast<size_t>(workspace.numel()) * sizeof(float),
+                   at::cuda::getCurrentCUDAStream()),
+               "poisson_step_gradients");
+  return {grad_and_loss, laplacian, grad_coordinates};
+}
+
+// In-place Adam on flat buffers; `step` is a CUDA int64 tensor of one element.
+void adam_step(torch::Tensor parameters, torch::Tensor grad, torch::Tensor exp_avg,
+               torch::Tensor exp_avg_sq, torch::Tensor step, double lr, double beta1,
+               double beta2, double eps) {
+  const int64_t count = parameters.numel();
+  check_vector(parameters, parameters, count, "parameters");
+  check_vector(grad, parameters, count, "grad");
+  check_vector(exp_avg, parameters, count, "exp_avg");
+  check_vector(exp_avg_sq, parameters, count, "exp_avg_sq");
+  TORCH_CHECK(step.is_cuda() && step.scalar_type() == torch::kInt64 && step.numel() == 1,
+              "step must be a CUDA int64 tensor with one element");
+  const c10::cuda::CUDAGuard device_guard(parameters.device());
+  check_status(fhb_adam_step(parameters.data_ptr<float>(), grad.data_ptr<float>(),
+                             exp_avg.data_ptr<float>(), exp_avg_sq.data_ptr<float>(), count,
+                             step.data_ptr<int64_t>(), static_cast<float>(lr),
+                             static_cast<float>(beta1), static_cast<float>(beta2),
+                             static_cast<float>(eps), at::cuda::getCurrentCUDAStream()),
+               "adam_step");
+}
+
+void prepare_device(int64_t device) {
+  check_status(fhb_prepare_device(static_cast<int>(device)), "prepare_device");
+}
+
+int64_t read_device_status(int64_t device) {
+  unsigned int status = 0;
+  check_status(fhb_read_device_status(static_cast<int>(device), &status), "read_device_status");
+  return static_cast<int64_t>(status);
+}
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, module) {
+  module.def("fused_forward_laplacian", &fused_forward_laplacian,
+             "Fixed MLP forward pass and input Laplacian (CUDA, sm_100a)",
+             pybind11::arg("coordinates"), pybind11::arg("parameters"),
+             pybind11::arg("version") = 2);
+  module.def("fused_forward_laplacian_backward", &fused_forward_laplacian_backward,
+             "Gradients of the fused forward Laplacian w.r.t. parameters and coordinates "
+             "(CUDA, sm_100a)",
+             pybind11::arg("coordinates"), pybind11::arg("parameters"),
+             pybind11::arg("grad_output"), pybind11::arg("grad_laplacian"),
+             pybind11::arg("version") = 6);
+  module.def("poisson_step_gradients", &poisson_step_gradients,
+             "Fused forward + interior Poisson loss + backward in one persistent kernel",
+             pybind11::arg("coordinates"), pybind11::arg("parameters"),
+             pybind11::arg("total_points"), pybind11::arg("want_laplacian") = false,
+             pybind11::arg("want_grad_coordinates") = false);
+  module.def("adam_step", &adam_step, "Fused Adam over a flat parameter buffer",
+             pybind11::arg("parameters"), pybind11::arg("grad"), pybind11::arg("exp_avg"),
+             pybind11::arg("exp_avg_sq"), pybind11::arg("step"), pybind11::arg("lr"),
+             pybind11::arg("beta1"), pybind11::arg("beta2"), pybind11::arg("eps"));
+  module.def("prepare_device", &prepare_device, "One-time per-device kernel set-up",
+             pybind11::arg("device"));
+  module.def("read_device_status", &read_device_status,
+             "Read and clear the device's bounded-wait status word (synchronises)",
+             pybind11::arg("device"));
+}

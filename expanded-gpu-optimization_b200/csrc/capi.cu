@@ -1,0 +1,215 @@
+// extern "C" entry points declared in include/fused_hoad_b200.h: argument validation,
+// one-time per-device set-up and dispatch onto the sm_100a kernels. No torch types, no
+// device allocation, no host synchronisation on the compute entry points.
+#include <mutex>
+
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+
+// One status word per device: a file-scope __device__ variable has a separate instance on
+// every device that loads this library. Kernels that give up on a bounded wait set bits.
+__device__ unsigned int g_status_word;
+
+thread_local int g_last_cuda_error = 0;
+fhb::DeviceInfo g_devices[kMaxDevices];
+int g_prepare_result[kMaxDevices];
+std::once_flag g_prepare_once[kMaxDevices];
+
+int record(cudaError_t e) {
+  if (e == cudaSuccess) return FHB_OK;
+  g_last_cuda_error = static_cast<int>(e);
+  return FHB_ERR_CUDA;
+}
+
+int prepare_locked(int device) {
+  int previous = 0;
+  cudaError_t e = cudaGetDevice(&previous);
+  if (e != cudaSuccess) return record(e);
+  if (previous != device && (e = cudaSetDevice(device)) != cudaSuccess) return record(e);
+  fhb::DeviceInfo info;
+  int code = FHB_OK;
+  do {
+    if ((e = cudaDeviceGetAttribute(&info.sms, cudaDevAttrMultiProcessorCount, device)) != cudaSuccess ||
+        (e = cudaDeviceGetAttribute(&info.cc_major, cudaDevAttrComputeCapabilityMajor, device)) != cudaSuccess ||
+        (e = cudaDeviceGetAttribute(&info.cc_minor, cudaDevAttrComputeCapabilityMinor, device)) != cudaSuccess) {
+      code = record(e);
+      break;
+    }
+    if (info.cc_major != 10 || info.cc_minor != 0) {
+      code = FHB_ERR_DEVICE;  // this library carries sm_100a code only
+      break;
+    }
+    if ((e = cudaGetSymbolAddress(reinterpret_cast<void**>(&info.status), g_status_word)) != cudaSuccess ||
+        (e = fhb::prepare_forward_fp32()) != cudaSuccess ||
+        (e = fhb::prepare_forward_tc()) != cudaSuccess ||
+        (e = fhb::prepare_backward_fp32()) != cudaSuccess) {
+      code = record(e);
+      break;
+    }
+    g_devices[device] = info;
+  } while (false);
+  if (previous != device) cudaSetDevice(previous);
+  return code;
+}
+
+int prepare(int device) {
+  if (device < 0 || device >= kMaxDevices) return FHB_ERR_INVALID_ARGUMENT;
+  std::call_once(g_prepare_once[device], [device] { g_prepare_result[device] = prepare_locked(device); });
+  return g_prepare_result[device];
+}
+
+int current_device(const fhb::DeviceInfo** info) {
+  int device = 0;
+  cudaError_t e = cudaGetDevice(&device);
+  if (e != cudaSuccess) return record(e);
+  const int code = prepare(device);
+  if (code != FHB_OK) return code;
+  *info = &g_devices[device];
+  return FHB_OK;
+}
+
+size_t backward_workspace_bytes(int64_t n, const fhb::DeviceInfo& dev) {
+  if (n <= 0) return 0;
+  return static_cast<size_t>(fhb::backward_grid(n, dev)) * fhb::kRowStride * sizeof(float);
+}
+
+bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+}  // namespace
+
+extern "C" {
+
+const char* fhb_status_string(int code) {
+  switch (code) {
+    case FHB_OK: return "ok";
+    case FHB_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case FHB_ERR_MISALIGNED: return "misaligned pointer";
+    case FHB_ERR_WORKSPACE: return "workspace missing or too small";
+    case FHB_ERR_DEVICE: return "current device is not sm_100 (B200); this library holds sm_100a code only";
+    case FHB_ERR_CUDA: return "CUDA runtime error";
+    case FHB_ERR_TOO_LARGE: return "size beyond the entry point's limit";
+    default: return "unknown status";
+  }
+}
+
+int fhb_last_cuda_error(void) { return g_last_cuda_error; }
+
+int fhb_parameter_count(void) { return fhb::kParamCount; }
+
+int fhb_prepare_device(int device) { return prepare(device); }
+
+int fhb_forward(const float* coords, const float* params, float* u, float* lap, int64_t n,
+                int version, fhb_stream_t stream) {
+  if (version < FHB_FORWARD_VERSION_MIN || version > FHB_FORWARD_VERSION_MAX || n < 0)
+    return FHB_ERR_INVALID_ARGUMENT;
+  if (n == 0) return FHB_OK;
+  if (!coords || !params || !u || !lap) return FHB_ERR_INVALID_ARGUMENT;
+  if (!aligned(coords, 4) || !aligned(params, 4) || !aligned(u, 4) || !aligned(lap, 4))
+    return FHB_ERR_MISALIGNED;
+  const fhb::DeviceInfo* dev = nullptr;
+  int code = current_device(&dev);
+  if (code != FHB_OK) return code;
+  cudaError_t e = version <= 2
+                      ? fhb::launch_forward_fp32(version, coords, params, u, lap, n, *dev, stream)
+                      : fhb::launch_forward_tc(coords, params, u, lap, n, *dev, stream);
+  return record(e);
+}
+
+size_t fhb_backward_workspace_bytes(int64_t n) {
+  const fhb::DeviceInfo* dev = nullptr;
+  if (current_device(&dev) != FHB_OK) return 0;
+  return backward_workspace_bytes(n, *dev);
+}
+
+static int backward_common(const float* coords, const float* params, const float* grad_u,
+                           const float* grad_lap, float* grad_params, float* grad_coords,
+                           float* lap_out, float* loss, int64_t n, int64_t n_total,
+                           bool poisson, void* workspace, size_t workspace_bytes,
+                           cudaStream_t stream) {
+  if (n < 0 || !params || !grad_params) return FHB_ERR_INVALID_ARGUMENT;
+  if (poisson && (!loss || n_total < n)) return FHB_ERR_INVALID_ARGUMENT;
+  const fhb::DeviceInfo* dev = nullptr;
+  int code = current_device(&dev);
+  if (code != FHB_OK) return code;
+  if (n == 0) {
+    cudaError_t e = cudaMemsetAsync(grad_params, 0, fhb::kParamCount * sizeof(float), stream);
+    if (e == cudaSuccess && poisson) e = cudaMemsetAsync(loss, 0, sizeof(float), stream);
+    return record(e);
+  }
+  if (!coords || (!poisson && !grad_lap)) return FHB_ERR_INVALID_ARGUMENT;
+  if (!aligned(coords, 4) || !aligned(params, 4)) return FHB_ERR_MISALIGNED;
+  const size_t need = backward_workspace_bytes(n, *dev);
+  if (workspace == nullptr || workspace_bytes < need) return FHB_ERR_WORKSPACE;
+  if (!aligned(workspace, 16)) return FHB_ERR_MISALIGNED;
+  float* partials = static_cast<float*>(workspace);
+  cudaError_t e = fhb::launch_backward_fp32(coords, params, grad_u, grad_lap, grad_coords,
+                                            lap_out, partials, n, n_total, poisson, *dev,
+                                            stream);
+  if (e == cudaSuccess)
+    e = fhb::launch_reduce_rows(partials, fhb::backward_grid(n, *dev), grad_params,
+                                poisson ? loss : nullptr, stream);
+  return record(e);
+}
+
+int fhb_backward(const float* coords, const float* params, const float* grad_u,
+                 const float* grad_lap, float* grad_params, float* grad_coords, int64_t n,
+                 int version, void* workspace, size_t workspace_bytes, fhb_stream_t stream) {
+  if (version < FHB_BACKWARD_VERSION_MIN || version > FHB_BACKWARD_VERSION_MAX)
+    return FHB_ERR_INVALID_ARGUMENT;
+  return backward_common(coords, params, grad_u, grad_lap, grad_params, grad_coords, nullptr,
+                         nullptr, n, n, false, workspace, workspace_bytes, stream);
+}
+
+int fhb_poisson_step_gradients(const float* coords, const float* params, int64_t n,
+                               int64_t n_total, float* grad_params, float* grad_coords,
+                               float* lap_out, float* loss, void* workspace,
+                               size_t workspace_bytes, fhb_stream_t stream) {
+  return backward_common(coords, params, nullptr, nullptr, grad_params, grad_coords, lap_out,
+                         loss, n, n_total, true, workspace, workspace_bytes, stream);
+}
+
+int fhb_adam_step(float* params, const float* grad, float* exp_avg, float* exp_avg_sq,
+                  int64_t count, int64_t* step, float lr, float beta1, float beta2, float eps,
+                  fhb_stream_t stream) {
+  if (!params || !grad || !exp_avg || !exp_avg_sq || !step || count < 0)
+    return FHB_ERR_INVALID_ARGUMENT;
+  if (!(lr >= 0.0f) || !(beta1 >= 0.0f && beta1 < 1.0f) || !(beta2 >= 0.0f && beta2 < 1.0f) ||
+      !(eps >= 0.0f))
+    return FHB_ERR_INVALID_ARGUMENT;
+  const fhb::DeviceInfo* dev = nullptr;
+  int code = current_device(&dev);
+  if (code != FHB_OK) return code;
+  if (count == 0) return FHB_OK;
+  return record(fhb::launch_adam(params, grad, exp_avg, exp_avg_sq, count, step, lr, beta1,
+                                 beta2, eps, stream));
+}
+
+int fhb_read_device_status(int device, unsigned int* status_out) {
+  if (!status_out) return FHB_ERR_INVALID_ARGUMENT;
+  int code = prepare(device);
+  if (code != FHB_OK) return code;
+  int previous = 0;
+  cudaError_t e = cudaGetDevice(&previous);
+  if (e != cudaSuccess) return record(e);
+  if (previous != device && (e = cudaSetDevice(device)) != cudaSuccess) return record(e);
+  const unsigned int zero = 0;
+  e = cudaDeviceSynchronize();
+  if (e == cudaSuccess) e = cudaMemcpyFromSymbol(status_out, g_status_word, sizeof(unsigned int));
+  if (e == cudaSuccess) e = cudaMemcpyToSymbol(g_status_word, &zero, sizeof(unsigned int));
+  if (previous != device) cudaSetDevice(previous);
+  return record(e);
+}
+
+int fhb_debug_bounded_wait_selftest(uint64_t limit_ns, fhb_stream_t stream) {
+  if (limit_ns == 0 || limit_ns > 10ull * 1000000000ull) return FHB_ERR_INVALID_ARGUMENT;
+  const fhb::DeviceInfo* dev = nullptr;
+  int code = current_device(&dev);
+  if (code != FHB_OK) return code;
+  return record(fhb::launch_bounded_wait_selftest(limit_ns, dev->status, stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,171 @@
+// Shared device helpers for the fused forward-Laplacian kernels (sm_100a).
+//
+// Parameter ABI: the packed 12,737-float buffer of the reference (csrc/mlp_abi.cuh:8-17,
+// src/fused_hoad/parameters.py:28-48): per linear layer W[out][in] row-major, then b[out],
+// for the layers 2->64, 64->64 (x3), 64->1. Kept bit-identical so buffers packed by the
+// reference's Python API drop straight in.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/fused_hoad_b200.h"
+
+namespace fhb {
+
+constexpr int kIn = 2;
+constexpr int kWidth = 64;
+constexpr int kHiddenGemms = 3;                                // layers 1..3 are 64x64
+constexpr int kB0 = kWidth * kIn;                              // 128
+constexpr int kHiddenBase = kB0 + kWidth;                      // 192
+constexpr int kHiddenStride = kWidth * kWidth + kWidth;        // 4160
+constexpr int kOutBase = kHiddenBase + kHiddenGemms * kHiddenStride;  // 12672
+constexpr int kParamCount = kOutBase + kWidth + 1;             // 12737
+static_assert(kParamCount == 12737, "parameter ABI drifted");
+// Parameters staged in shared memory: 12,736 floats by one bulk copy (50,944 B, a multiple
+// of 16) plus b_out by a plain load; padded to a 16-byte multiple.
+constexpr int kParamBulkFloats = 12736;
+constexpr int kParamSmemFloats = 12740;
+
+// Bounded waits: a wait that has not completed after this many nanoseconds gives up, sets
+// a bit in the caller's status word and lets the kernel return instead of hanging.
+constexpr uint64_t kWaitLimitNs = 1000000000ull;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t global_timer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void report_status(unsigned int* status, unsigned int bits) {
+  if (status != nullptr) atomicOr(status, bits);
+}
+
+// ---- mbarrier + bulk copy (non-multicast) ----
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+               : "memory");
+}
+
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t phase) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(phase)
+      : "memory");
+  return done != 0;
+}
+
+// Wait for `phase` of `bar` to complete, giving up after kWaitLimitNs. Returns false on
+// timeout (and records `bits` in *status).
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t phase,
+                                                  unsigned int* status, unsigned int bits) {
+  if (mbar_try_wait(bar, phase)) return true;
+  const uint64_t start = global_timer_ns();
+  while (true) {
+    if (mbar_try_wait(bar, phase)) return true;
+    if (global_timer_ns() - start > kWaitLimitNs) {
+      report_status(status, bits);
+      return false;
+    }
+  }
+}
+
+// One bulk (TMA, non-multicast) copy global -> this CTA's shared memory, completing on bar.
+// Both addresses 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32_t bytes,
+                                              uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+      ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Stage the whole packed parameter buffer into shared memory, once per CTA. When the
+// buffer is 16-byte aligned one thread issues a single bulk copy; otherwise the CTA copies
+// it with plain loads. Ends with __syncthreads(). Returns false if the copy timed out.
+__device__ __forceinline__ bool stage_parameters(float* sp, const float* __restrict__ params,
+                                                 uint64_t* bar, bool aligned,
+                                                 unsigned int* status) {
+  bool ok = true;
+  if (aligned) {
+    if (threadIdx.x == 0) {
+      mbar_init(bar, 1);
+      fence_barrier_init();
+      mbar_arrive_expect_tx(bar, kParamBulkFloats * 4);
+      bulk_copy_g2s(sp, params, kParamBulkFloats * 4, bar);
+    }
+    if (threadIdx.x == 32) {
+      for (int k = kParamBulkFloats; k < kParamCount; ++k) sp[k] = params[k];
+    }
+    __syncthreads();  // barrier initialised before anyone waits on it
+    ok = mbar_wait_bounded(bar, 0, status, FHB_STATUS_STAGE_TIMEOUT);
+  } else {
+    for (int k = threadIdx.x; k < kParamCount; k += blockDim.x) sp[k] = params[k];
+  }
+  __syncthreads();
+  return __syncthreads_and(ok ? 1 : 0) != 0;
+}
+
+// ---- the tanh jet and its adjoint ----
+//
+// Forward (reference csrc/fused_residual.cu:16-23): a = tanh(z_v), s = 1 - a^2,
+//   v = a, J_d = s z_Jd, L = s z_L - 2 a s (z_J0^2 + z_J1^2).
+__device__ __forceinline__ void tanh_jet(float zv, float zj0, float zj1, float zl, float& v,
+                                         float& j0, float& j1, float& l) {
+  const float a = tanhf(zv);
+  const float s = fmaf(-a, a, 1.0f);
+  const float q = fmaf(zj0, zj0, zj1 * zj1);
+  v = a;
+  j0 = s * zj0;
+  j1 = s * zj1;
+  l = fmaf(s, zl, -2.0f * a * s * q);
+}
+
+// Adjoint (reference csrc/fused_backward.cu:29-33): with s2 = -2 a s, s3 = -2 s^2 + 4 a^2 s,
+// q = z_J0^2 + z_J1^2, maps (vbar, J0bar, J1bar, Lbar) in place to
+//   zbar_v = vbar s + (Jbar . z_J) s2 + Lbar (z_L s2 + q s3)
+//   zbar_Jd = Jbar_d s + 2 Lbar s2 z_Jd,   zbar_L = Lbar s.
+__device__ __forceinline__ void tanh_jet_adjoint(float zv, float zj0, float zj1, float zl,
+                                                 float& av, float& aj0, float& aj1, float& al) {
+  const float a = tanhf(zv);
+  const float s = fmaf(-a, a, 1.0f);
+  const float s2 = -2.0f * a * s;
+  const float s3 = fmaf(-2.0f * s, s, 4.0f * a * a * s);
+  const float q = fmaf(zj0, zj0, zj1 * zj1);
+  const float gv = av * s + fmaf(aj0, zj0, aj1 * zj1) * s2 + al * fmaf(zl, s2, q * s3);
+  const float l2 = 2.0f * al * s2;
+  const float g0 = fmaf(aj0, s, l2 * zj0);
+  const float g1 = fmaf(aj1, s, l2 * zj1);
+  av = gv;
+  aj0 = g0;
+  aj1 = g1;
+  al = al * s;
+}
+
+// Warp-wide sum with a fixed butterfly order (deterministic).
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int m = 16; m >= 1; m >>= 1) v += __shfl_xor_sync(0xffffffffu, v, m);
+  return v;
+}
+
+}  // namespace fhb

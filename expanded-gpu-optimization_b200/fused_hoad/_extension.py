@@ -1,0 +1,73 @@
+"""Access to the compiled sm_100a extension (``fused_hoad._C``).
+
+Mirrors the reference's ``src/fused_hoad/_extension.py:8-65``: same function names,
+arguments, defaults and return shapes, so code written against the reference's Python API
+runs unchanged. There is no CPU or PyTorch fallback: if the extension is missing, every
+call raises.
+"""
+
+from __future__ import annotations
+
+from types import ModuleType
+
+from torch import Tensor
+
+BUILD_HINT = (
+    "The fused_hoad CUDA extension is not built. Build it in-tree with "
+    "`python expanded-gpu-optimization_b200/build.py` (nvcc for sm_100a); the kernels need "
+    "a B200 (sm_100) GPU to run."
+)
+
+
+def load_extension() -> ModuleType:
+    """Return the compiled extension or raise an actionable error."""
+    try:
+        from fused_hoad import _C
+    except ImportError as exc:
+        raise RuntimeError(BUILD_HINT) from exc
+    return _C
+
+
+def extension_available() -> bool:
+    """Return whether the compiled extension can be imported."""
+    try:
+        load_extension()
+    except RuntimeError:
+        return False
+    return True
+
+
+def fused_forward_laplacian(
+    coordinates: Tensor, parameters: Tensor, version: int = 2
+) -> tuple[Tensor, Tensor]:
+    """Evaluate the fixed MLP and its input Laplacian: ``(u [N,1], lap [N,1])``.
+
+    ``version`` 0, 1, 2: the FP32 CUDA-core kernel with 32-, 128- and 64-point tiles (2 is
+    the default, as in the reference). 3, 4, 5: the 3xTF32 tcgen05/TMEM tensor-core kernel,
+    which holds the same FP32 tolerance (the reference's single-TF32 v3-v5 did not).
+    """
+    output, laplacian = load_extension().fused_forward_laplacian(coordinates, parameters, version)
+    return output, laplacian
+
+
+def fused_forward_laplacian_backward(
+    coordinates: Tensor,
+    parameters: Tensor,
+    grad_output: Tensor,
+    grad_laplacian: Tensor,
+    version: int = 6,
+) -> tuple[Tensor, Tensor]:
+    """Return ``(grad_parameters [12737], grad_coordinates [N,2])``.
+
+    Every version 1..6 runs the same persistent adjoint-jet kernel, whose fixed-order
+    reduction makes the gradients bitwise reproducible; the argument is kept so callers of
+    the reference's versions keep working.
+    """
+    grad_parameters, grad_coordinates = load_extension().fused_forward_laplacian_backward(
+        coordinates,
+        parameters,
+        grad_output.reshape(-1).contiguous(),
+        grad_laplacian.reshape(-1).contiguous(),
+        version,
+    )
+    return grad_parameters, grad_coordinates

@@ -1,0 +1,170 @@
+"""Training on the fused kernels: the reference's whole-step CUDA-graph helper and the
+B200-native data-parallel Poisson trainer.
+
+``cuda_graph_step`` keeps the reference's signature and behaviour
+(``src/fused_hoad/training.py:9-40``) for autograd-based loops over ``fused_laplacian``.
+
+``PoissonTrainer`` is the native step (config: forward jet, backward w.r.t. all 12,737
+parameters, Adam at lr 1e-3, betas (0.9, 0.999) on the interior loss
+``mean((lap - f)^2)``):
+
+1. one persistent kernel per step recomputes the jet per tile, forms dL/dlap in registers
+   and runs the adjoint sweep (no separate forward launch), then a fixed-order row
+   reduction writes the gradient and the loss into one flat buffer;
+2. with more than one rank, one all-reduce (NCCL over NVLink) of that buffer;
+3. one fused Adam kernel updates the flat parameters in place.
+
+The parameters live in one flat buffer in the reference's ABI, so there is no per-step
+pack (``torch.cat``) or gradient split; an ``nn.Module`` handed to the trainer has its
+parameters rebound as views of that buffer. The whole step is CUDA-graph capturable.
+"""
+
+from __future__ import annotations
+
+from collections.abc import Callable
+
+import torch
+from torch import Tensor, nn
+
+from fused_hoad._extension import load_extension
+from fused_hoad.distributed import allreduce_sum_, world
+from fused_hoad.parameters import (
+    POISSON_PARAMETER_COUNT,
+    bind_model_to_flat,
+    pack_poisson_parameters,
+)
+
+
+def cuda_graph_step(
+    loss_fn: Callable[[], Tensor], optimizer: torch.optim.Optimizer, *, warmup: int = 3
+) -> Callable[[], Tensor]:
+    """Capture ``loss_fn() -> backward -> optimizer.step()`` as one CUDA graph.
+
+    Warm up on a side stream, drop grads so backward allocates them inside the graph's
+    pool, then capture. The optimizer must be built with ``capturable=True``. Returns a
+    function that replays the step and returns the static loss tensor.
+    """
+    side_stream = torch.cuda.Stream()
+    side_stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side_stream):
+        for _ in range(warmup):
+            optimizer.zero_grad(set_to_none=True)
+            loss_fn().backward()
+            optimizer.step()
+    torch.cuda.current_stream().wait_stream(side_stream)
+
+    graph = torch.cuda.CUDAGraph()
+    optimizer.zero_grad(set_to_none=True)
+    with torch.cuda.graph(graph):
+        static_loss = loss_fn()
+        static_loss.backward()
+        optimizer.step()
+
+    def replay() -> Tensor:
+        graph.replay()
+        return static_loss
+
+    return replay
+
+
+class PoissonTrainer:
+    """Data-parallel Poisson training step on the fused sm_100a kernels.
+
+    ``parameters`` is either the packed 12,737-float CUDA buffer (used in place) or the
+    Poisson ``nn.Module``, which is packed once and rebound to views of the buffer.
+    With an initialised process group every rank must call :meth:`step` with its own
+    shard and the same ``total_points``.
+    """
+
+    def __init__(
+        self,
+        parameters: Tensor | nn.Module,
+        *,
+        lr: float = 1e-3,
+        betas: tuple[float, float] = (0.9, 0.999),
+        eps: float = 1e-8,
+        group=None,
+    ) -> None:
+        self._C = load_extension()
+        if isinstance(parameters, nn.Module):
+            flat = pack_poisson_parameters(parameters).contiguous()
+            bind_model_to_flat(parameters, flat)
+        else:
+            flat = parameters
+        if not (flat.is_cuda and flat.dtype == torch.float32 and flat.is_contiguous()):
+            raise ValueError("parameters must be a contiguous float32 CUDA tensor")
+        if flat.numel() != POISSON_PARAMETER_COUNT:
+            raise ValueError(f"parameters must have {POISSON_PARAMETER_COUNT} values")
+        self.params = flat
+        self.exp_avg = torch.zeros_like(flat)
+        self.exp_avg_sq = torch.zeros_like(flat)
+        self.step_count = torch.zeros(1, dtype=torch.int64, device=flat.device)
+        self.lr, self.betas, self.eps = float(lr), (float(betas[0]), float(betas[1])), float(eps)
+        self.group = group
+        self._C.prepare_device(flat.device.index if flat.device.index is not None else 0)
+
+    def gradients(self, coordinates: Tensor, total_points: int) -> Tensor:
+        """Flat ``[12738]`` buffer: the gradient summed over ranks, then the loss."""
+        out, _, _ = self._C.poisson_step_gradients(coordinates, self.params, total_points)
+        return allreduce_sum_(out, self.group)
+
+    def step(self, coordinates: Tensor, total_points: int | None = None) -> Tensor:
+        """One training step on this rank's points; returns the (global) loss, a 1-element
+        device tensor of the loss before the update."""
+        if total_points is None:
+            total_points = coordinates.shape[0] * world()[1]
+        out = self.gradients(coordinates, total_points)
+        self._C.adam_step(
+            self.params,
+            out[:POISSON_PARAMETER_COUNT],
+            self.exp_avg,
+            self.exp_avg_sq,
+            self.step_count,
+            self.lr,
+            self.betas[0],
+            self.betas[1],
+            self.eps,
+        )
+        return out[POISSON_PARAMETER_COUNT:]
+
+    def capture(
+        self, coordinates: Tensor, total_points: int | None = None, *, warmup: int = 3
+    ) -> Callable[[], Tensor]:
+        """Capture :meth:`step` on ``coordinates`` as one CUDA graph; returns ``replay()``.
+
+        The warm-up steps are real steps (they update the parameters). Copy new points into
+        ``coordinates`` in place between replays.
+        """
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(warmup):
+                self.step(coordinates, total_points)
+        torch.cuda.current_stream().wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            static_loss = self.step(coordinates, total_points)
+
+        def replay() -> Tensor:
+            graph.replay()
+            return static_loss
+
+        replay.graph = graph  # keep alive; release before destroying a process group
+        return replay
+
+    def state_dict(self) -> dict[str, Tensor]:
+        """Checkpoint: parameters, Adam moments and the step counter."""
+        return {
+            "params": self.params.detach().clone(),
+            "exp_avg": self.exp_avg.clone(),
+            "exp_avg_sq": self.exp_avg_sq.clone(),
+            "step": self.step_count.clone(),
+        }
+
+    def load_state_dict(self, state: dict[str, Tensor]) -> None:
+        """Resume from :meth:`state_dict` (copies in place, so captured graphs stay valid)."""
+        with torch.no_grad():
+            self.params.copy_(state["params"])
+            self.exp_avg.copy_(state["exp_avg"])
+            self.exp_avg_sq.copy_(state["exp_avg_sq"])
+            self.step_count.copy_(state["step"])

@@ -1,0 +1,136 @@
+/*
+ * fused_hoad_b200 -- C ABI of the B200-native (sm_100a) forward-Laplacian kernels for the
+ * fixed 2 -> 64 -> 64 -> 64 -> 64 -> 1 tanh MLP.
+ *
+ * Plain pointers, sizes and a CUDA stream; no torch types. Every pointer is a device
+ * pointer on the current CUDA device unless stated. All calls are asynchronous on
+ * `stream`, never synchronise the host and never allocate device memory (callers pass the
+ * workspace a call needs), so they can be captured in a CUDA graph once the per-device
+ * set-up (fhb_prepare_device, or the first call on that device) has run outside capture.
+ *
+ * Parameter buffer: the reference's packed ABI (csrc/mlp_abi.cuh:8-17), 12,737 floats:
+ * W0[64][2] b0[64] | W1[64][64] b1[64] | W2 b2 | W3 b3 | w_out[64] b_out[1], W row-major
+ * [out][in] as nn.Linear stores it.
+ *
+ * Return value: FHB_OK or one of the FHB_ERR_* codes; fhb_status_string() names them.
+ */
+#ifndef FUSED_HOAD_B200_H_
+#define FUSED_HOAD_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same layout as cudaStream_t, so a cudaStream_t converts without a cast. */
+typedef struct CUstream_st* fhb_stream_t;
+
+#define FHB_PARAMETER_COUNT 12737
+
+#define FHB_OK 0
+#define FHB_ERR_INVALID_ARGUMENT 1 /* null pointer, negative size, bad version */
+#define FHB_ERR_MISALIGNED 2       /* a pointer breaks the alignment the call documents */
+#define FHB_ERR_WORKSPACE 3        /* workspace missing or smaller than required */
+#define FHB_ERR_DEVICE 4           /* current device is not sm_100 (B200) */
+#define FHB_ERR_CUDA 5             /* a CUDA runtime call failed; see fhb_last_cuda_error */
+#define FHB_ERR_TOO_LARGE 6        /* size beyond what the entry point supports */
+
+/* Bits of the per-device status word a kernel sets when a bounded wait gives up. */
+#define FHB_STATUS_STAGE_TIMEOUT 0x1u /* parameter staging copy never completed */
+#define FHB_STATUS_MMA_TIMEOUT 0x2u   /* tensor-core pipeline wait gave up */
+#define FHB_STATUS_SELFTEST 0x80u     /* set by fhb_debug_bounded_wait_selftest */
+
+/* Forward kernel families selected by `version` (reference csrc/bindings.cpp:33). */
+#define FHB_FORWARD_VERSION_MIN 0
+#define FHB_FORWARD_VERSION_MAX 5
+/* Backward versions accepted for drop-in compatibility (reference csrc/bindings.cpp:45). */
+#define FHB_BACKWARD_VERSION_MIN 1
+#define FHB_BACKWARD_VERSION_MAX 6
+
+const char* fhb_status_string(int code);
+/* Last CUDA runtime error seen by this library on the calling thread (cudaError_t). */
+int fhb_last_cuda_error(void);
+int fhb_parameter_count(void);
+
+/*
+ * One-time per-device set-up (kernel attributes, SM count, status word). Called
+ * implicitly by the first call of any entry point on a device; call it explicitly before
+ * capturing a CUDA graph on a device that has not run a kernel yet.
+ */
+int fhb_prepare_device(int device);
+
+/*
+ * Forward Laplacian: u[n], lap[n] for coords[n][2] (row-major, 8 bytes per point).
+ * Replaces fused_forward_laplacian_cuda (reference csrc/fused_residual.cu:587-643) behind
+ * fused_hoad._C.fused_forward_laplacian (csrc/bindings.cpp:31-36).
+ * version 0..2: FP32 CUDA-core kernel (0: 32-point tiles, 1: 128-point tiles,
+ *               2: 64-point tiles, the default);
+ * version 3..5: 3xTF32 tcgen05/TMEM tensor-core kernel (FP32-level accuracy).
+ * n == 0 is a no-op. The parameter buffer may have any 4-byte alignment.
+ */
+int fhb_forward(const float* coords, const float* params, float* u, float* lap, int64_t n,
+                int version, fhb_stream_t stream);
+
+/*
+ * Workspace the backward needs for n points on the current device, in bytes (0 for n==0).
+ * It holds one partial-gradient row per CTA of the persistent grid.
+ */
+size_t fhb_backward_workspace_bytes(int64_t n);
+
+/*
+ * Vector-Jacobian product of the forward Laplacian: given grad_u[n] and grad_lap[n]
+ * (dLoss/du, dLoss/dlap), writes grad_params[12737] and grad_coords[n][2].
+ * Replaces fused_forward_laplacian_backward_cuda (reference csrc/fused_backward.cu:859-934)
+ * behind fused_hoad._C.fused_forward_laplacian_backward (csrc/bindings.cpp:42-54).
+ * grad_u may be NULL (treated as zeros); grad_coords may be NULL (not written).
+ * The reduction over points has a fixed order: results are bitwise reproducible for a
+ * given n and device. n == 0 writes zeros to grad_params. All versions 1..6 run the same
+ * kernel. Workspace: fhb_backward_workspace_bytes(n) bytes, 16-byte aligned.
+ */
+int fhb_backward(const float* coords, const float* params, const float* grad_u,
+                 const float* grad_lap, float* grad_params, float* grad_coords, int64_t n,
+                 int version, void* workspace, size_t workspace_bytes, fhb_stream_t stream);
+
+/*
+ * Fused Poisson training-step gradients for the interior loss
+ *     L = sum_p (lap_p - f(x_p))^2 / n_total,  f = -2 pi^2 sin(pi x) sin(pi y)
+ * (reference benchmarks/benchmark_training.py:46-48, src/fused_hoad/problems/poisson.py:37-39):
+ * one persistent kernel recomputes the forward jet per tile, forms dL/dlap in registers and
+ * runs the adjoint sweep, so no separate forward launch is needed. Writes grad_params[12737]
+ * (this shard's contribution; n_total >= n lets data-parallel shards sum to the global
+ * gradient), *loss (this shard's contribution, device scalar), optionally lap_out[n] and
+ * grad_coords[n][2] (either may be NULL). Workspace as for fhb_backward.
+ */
+int fhb_poisson_step_gradients(const float* coords, const float* params, int64_t n,
+                               int64_t n_total, float* grad_params, float* grad_coords,
+                               float* lap_out, float* loss, void* workspace,
+                               size_t workspace_bytes, fhb_stream_t stream);
+
+/*
+ * One Adam step on a flat buffer, torch.optim.Adam semantics (no weight decay, no amsgrad),
+ * replacing the optimizer of reference benchmarks/benchmark_training.py:41, :54-56.
+ * `step` is a device int64 counter holding the number of steps taken so far; the kernel
+ * reads it, uses step+1 for the bias corrections and stores step+1, so the call can be
+ * replayed from a CUDA graph.
+ */
+int fhb_adam_step(float* params, const float* grad, float* exp_avg, float* exp_avg_sq,
+                  int64_t count, int64_t* step, float lr, float beta1, float beta2, float eps,
+                  fhb_stream_t stream);
+
+/* Reads and clears the status word of `device` (synchronises that device). */
+int fhb_read_device_status(int device, unsigned int* status_out);
+
+/*
+ * Test hook for the bounded-wait machinery: launches one CTA that waits on an mbarrier
+ * nothing arrives at, with a limit of `limit_ns` nanoseconds; the wait gives up, sets
+ * FHB_STATUS_SELFTEST in the device status word and the kernel returns normally.
+ */
+int fhb_debug_bounded_wait_selftest(uint64_t limit_ns, fhb_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FUSED_HOAD_B200_H_ */
