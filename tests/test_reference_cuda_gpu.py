@@ -57,3 +57,50 @@ def test_backward_matches_reference_bwd_v6(batch: int) -> None:
     gp, gx = fused_forward_laplacian_backward(coords, params, gu, gl)
     assert_scaled(gp, rp, 1e-4, "grad params")
     assert_scaled(gx, rx, 1e-4, "grad coords")
+
+
+def _median_ms(fn, flush, iterations: int = 50) -> float:
+    for _ in range(5):
+        fn()
+    times = []
+    for _ in range(iterations):
+        flush.zero_()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        fn()
+        end.record()
+        torch.cuda.synchronize()
+        times.append(start.elapsed_time(end))
+    times.sort()
+    return times[len(times) // 2]
+
+
+def test_speed_against_reference_kernels() -> None:
+    """The reference's own kernels on this GPU are the speed bar (per-call CUDA events,
+    median, L2 flushed between calls). Records the table in gpurun_out/ when present."""
+    import json
+    import os
+
+    ref = reference_module()
+    params = jet.init_parameters(0).cuda()
+    n = 65_536
+    coords = uniform_points(n, seed=1).cuda()
+    g = torch.Generator().manual_seed(5)
+    gu, gl = torch.randn(n, generator=g).cuda(), torch.randn(n, generator=g).cuda()
+    flush = torch.empty(48 << 20, device="cuda")
+    rows = {}
+    for v in (0, 1, 2, 3, 4, 5):
+        rows[f"reference fwd v{v}"] = _median_ms(lambda: ref.fused_forward_laplacian(coords, params, v), flush)
+    for v in (0, 1, 2):
+        rows[f"ours fwd v{v}"] = _median_ms(lambda: fused_forward_laplacian(coords, params, v), flush)
+    for v in (1, 6):
+        rows[f"reference bwd v{v}"] = _median_ms(
+            lambda: ref.fused_forward_laplacian_backward(coords, params, gu, gl, v), flush)
+    rows["ours bwd"] = _median_ms(lambda: fused_forward_laplacian_backward(coords, params, gu, gl), flush)
+    table = {k: {"ms": ms, "mpts_per_s": n / ms / 1e3} for k, ms in rows.items()}
+    print(json.dumps(table, indent=1))
+    if os.path.isdir("gpurun_out"):
+        with open("gpurun_out/reference_speed.json", "w") as fh:
+            json.dump({"points": n, "gpu": torch.cuda.get_device_name(), "rows": table}, fh, indent=1)
+    assert rows["ours fwd v2"] < 1.2 * rows["reference fwd v2"]
+    assert rows["ours bwd"] < 1.2 * rows["reference bwd v6"]
