@@ -232,7 +232,7 @@ def run_ours(args) -> None:
     device = torch.device("cuda", local_rank)
     C = fused_hoad.load_extension()
     C.prepare_device(local_rank)
-    version = args.version if args.version is not None else 2
+    version = args.version if args.version is not None else 3
     n = args.points
     params = fused_hoad.pack_poisson_parameters(
         (torch.manual_seed(0), fused_hoad.build_mlp())[1]

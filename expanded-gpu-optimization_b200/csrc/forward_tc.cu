@@ -1,15 +1,353 @@
-// 3xTF32 tcgen05/TMEM forward kernel (forward versions 3..5): not built yet. The launcher
-// reports cudaErrorNotSupported so a caller gets an error, never a different kernel.
+// 3xTF32 tcgen05/TMEM forward-Laplacian kernel (forward versions 3, 4, 5).
+//
+// Same math as the FP32 kernel and the reference (csrc/fused_residual.cu:16-23), with the
+// three hidden 64x64 jet GEMMs on the 5th-generation tensor cores. Each hidden layer is,
+// per tile of 128 points and per jet component c in {v, d/dx, d/dy, L},
+//     Z_c[128 x 64] = H_c[128 x 64] . W^T,
+// run as tcgen05.mma kind::tf32 with M = 128 points, N = 64 output neurons, K = 8 per
+// instruction. FP32 accuracy is kept by the 3xTF32 split (x = x_hi + x_lo, both rounded to
+// TF32): Z += H_hi W_hi + H_lo W_hi + H_hi W_lo, accumulated in FP32 in tensor memory.
+//
+// Where the data lives (per CTA, one CTA per SM, persistent over tiles):
+//   * weights: all three hidden layers, hi and lo, pre-split once per CTA into the K-major
+//     no-swizzle canonical layout in shared memory (96 KB) -- the MMA's B operand;
+//   * TMEM (512 columns x 128 lanes, lane = point):
+//       [0, 256)   accumulators D_c, component c at columns 64c..64c+63;
+//       [256, 448) a ring of 3 A-operand chunks; a chunk is one K step (8 input neurons)
+//                  of the next layer's activations: (component, hi/lo) blocks of 8 columns.
+//     The A operand lives in TMEM, not shared memory: with N = 64 an A tile read from
+//     shared memory would need ~1.5x the shared-memory bandwidth an SM has.
+//   * 16 warps: warp w serves TMEM lanes 32(w%4)..+31 (its quadrant) and neurons
+//     16(w/4)..+15. Per layer it loads its 4 x 16 accumulators (4 x tcgen05.ld.32x32b.x16),
+//     applies the tanh jet in registers and writes TF32 hi/lo activations chunk by chunk
+//     into the ring (tcgen05.st) for the next layer. The K order is permuted (chunk j holds
+//     neurons 16s+2j+{0,1} for s = 0..3) so all 16 warps contribute to every chunk; the
+//     weights' K order is permuted to match;
+//   * the warp that completes a chunk last (an acq_rel counter per ring slot) issues its
+//     MMAs from one lane: 4 components x 3 products, then tcgen05.commit to free the slot,
+//     and after a layer's 8th chunk a commit that marks D complete. A warp contributes to
+//     chunk 0 of layer l+1 only after it has read D of layer l, so when the last
+//     contribution arrives D may be overwritten -- no separate "D free" barrier.
+//   So the MMAs of layer l+1 consume chunk j while the epilogue of layer l produces chunk
+//   j+1. (No dedicated MMA warp: a 17th warp would put 5 warps on one SM sub-partition and
+//   cap registers at 96; with 16 warps each thread gets 128.)
+// Layer 0 (2 inputs) and the output layer (1 output) are elementwise/epilogue work.
+// Every mbarrier wait is bounded; a wait that gives up raises FHB_STATUS_MMA_TIMEOUT, sets
+// a CTA abort flag that stops the other warps, and the kernel frees TMEM and returns.
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.cuh"
+#include "tcgen05.cuh"
 
 namespace fhb {
+namespace {
 
-cudaError_t prepare_forward_tc() { return cudaSuccess; }
+constexpr int kTile = 128;            // points per tile = MMA M = TMEM lanes
+constexpr int kWarps = 16;            // 4 per TMEM lane quadrant
+constexpr int kThreads = kWarps * 32;
+constexpr int kChunks = 8;            // K steps of 8 per 64-wide layer
+constexpr int kChunksPerTile = kHiddenGemms * kChunks;
+constexpr int kRing = 3;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kRingCol = 256;
+constexpr uint32_t kIdesc = tc::idesc_tf32(128, 64);
 
-cudaError_t launch_forward_tc(const float*, const float*, float*, float*, int64_t,
-                              const DeviceInfo&, cudaStream_t) {
-  return cudaErrorNotSupported;
+// Shared memory layout (bytes).
+constexpr int kOperandBytes = kWidth * kWidth * 4;  // one [64 x 64] tf32 operand: 16 KB
+constexpr int kSmallOff = 6 * kOperandBytes;        // W0[128] b0[64] b1..b3[192] wout[64] bout
+constexpr int kSmW0 = 0, kSmB0 = 128, kSmB = 192, kSmWout = 384, kSmBout = 448;
+constexpr int kSmallFloats = 512;
+constexpr int kRedOff = kSmallOff + kSmallFloats * 4;  // [8][128] partial sums
+constexpr int kBarOff = kRedOff + 8 * kTile * 4;       // mbarriers: empty[3], dfull, red
+constexpr int kCountOff = kBarOff + 8 * 8;             // per-slot contribution counters
+constexpr int kMiscOff = kCountOff + 4 * 4;            // TMEM base, abort flag
+constexpr int kSmemUsed = kMiscOff + 16;
+// Padded so two CTAs never share an SM (each allocates all 512 TMEM columns).
+constexpr int kSmemBytes = 120 * 1024;
+static_assert(kSmemUsed <= kSmemBytes, "shared memory layout overflow");
+
+// Canonical K-major no-swizzle layout of a [64 rows x 64 K] tf32 operand: 8x4 core
+// matrices of 128 B; K chunks of 4 at LBO = 128 B, 8-row groups at SBO = 2048 B.
+constexpr uint32_t kLbo = 128, kSbo = 2048;
+__device__ __forceinline__ int operand_offset(int row, int k) {
+  return (row >> 3) * kSbo + (k >> 2) * kLbo + (row & 7) * 16 + (k & 3) * 4;
+}
+// K position k of a layer's input <-> input neuron: chunk j = k/8 holds neurons
+// 16s + 2j + t at position 2s + t (s = warp neuron block, t = 0, 1).
+__device__ __forceinline__ int k_to_neuron(int k) {
+  return 16 * ((k & 7) >> 1) + 2 * (k >> 3) + (k & 1);
+}
+
+struct Ctx {
+  uint8_t* smem;
+  uint64_t* empty;            // [kRing] ring slot consumed by its MMAs (tcgen05.commit)
+  uint64_t* dfull;            // accumulators complete (tcgen05.commit)
+  uint64_t* red;              // output-layer partial sums written (16 warps arrive)
+  uint32_t* count;            // [kRing] contributions to each slot, monotonic
+  volatile uint32_t* abort_flag;
+  unsigned int* status;
+  uint32_t tmem;
+};
+
+// Bounded wait that also gives up when another warp has aborted the CTA.
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, const Ctx& cx) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t start = global_timer_ns();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*cx.abort_flag) return false;
+    if (global_timer_ns() - start > kWaitLimitNs) {
+      *cx.abort_flag = 1u;
+      report_status(cx.status, FHB_STATUS_MMA_TIMEOUT);
+      return false;
+    }
+  }
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Release this warp's contribution to a slot and learn whether it was the last one.
+__device__ __forceinline__ uint32_t count_contribution(uint32_t* counter) {
+  uint32_t old;
+  asm volatile("atom.acq_rel.cta.shared::cta.add.u32 %0, [%1], 1;"
+               : "=r"(old)
+               : "r"(smem_u32(counter))
+               : "memory");
+  return old;
+}
+
+// The 12 MMAs of one chunk: K step j of hidden GEMM `layer`, A from ring slot `slot`.
+__device__ __forceinline__ void issue_chunk_mmas(const Ctx& cx, int layer, int j,
+                                                 uint32_t slot) {
+  const uint32_t w_hi = smem_u32(cx.smem + (2 * layer) * kOperandBytes + 256 * j);
+  const uint32_t w_lo = w_hi + kOperandBytes;
+  const uint64_t bhi = tc::smem_desc_kmajor(w_hi, kLbo, kSbo);
+  const uint64_t blo = tc::smem_desc_kmajor(w_lo, kLbo, kSbo);
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const uint32_t d = cx.tmem + 64u * c;
+    const uint32_t a_hi = cx.tmem + kRingCol + 64u * slot + 16u * c;
+    const uint32_t a_lo = a_hi + 8u;
+    tc::mma_tf32_ts(d, a_hi, bhi, kIdesc, j > 0 ? 1u : 0u);
+    tc::mma_tf32_ts(d, a_lo, bhi, kIdesc, 1u);
+    tc::mma_tf32_ts(d, a_hi, blo, kIdesc, 1u);
+  }
+  tc::commit(&cx.empty[slot]);
+  if (j == kChunks - 1) tc::commit(cx.dfull);
+}
+
+// Write chunk `n` (this warp's 2 neurons x 4 components, TF32 hi and lo) into ring slot
+// n % kRing; the warp completing the chunk last issues its MMAs. False if aborted.
+__device__ __forceinline__ bool produce_chunk(uint32_t n, const float (&h)[4][2],
+                                              uint32_t tmem_warp, int s, const Ctx& cx) {
+  const uint32_t slot = n % kRing;
+  if (!wait_or_abort(&cx.empty[slot], ((n / kRing) & 1u) ^ 1u, cx)) return false;
+  tc::fence_after_sync();
+  const uint32_t base = tmem_warp + kRingCol + 64u * slot + 2u * s;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const uint32_t hi0 = tc::to_tf32(h[c][0]), hi1 = tc::to_tf32(h[c][1]);
+    const uint32_t lo0 = tc::to_tf32(h[c][0] - __uint_as_float(hi0));
+    const uint32_t lo1 = tc::to_tf32(h[c][1] - __uint_as_float(hi1));
+    tc::st_x2(base + 16u * c, hi0, hi1);
+    tc::st_x2(base + 16u * c + 8u, lo0, lo1);
+  }
+  tc::wait_st();
+  tc::fence_before_sync();
+  __syncwarp();
+  uint32_t last = 0;
+  if ((threadIdx.x & 31) == 0) last = (count_contribution(&cx.count[slot]) % kWarps) == kWarps - 1;
+  last = __shfl_sync(0xffffffffu, last, 0);
+  if (last) {
+    if ((threadIdx.x & 31) == 0) {
+      tc::fence_after_sync();
+      const uint32_t in_tile = n % kChunksPerTile;
+      issue_chunk_mmas(cx, static_cast<int>(in_tile / kChunks), static_cast<int>(in_tile % kChunks),
+                       slot);
+    }
+    __syncwarp();
+  }
+  return true;
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    forward_tc_kernel(const float* __restrict__ coords, const float* __restrict__ params,
+                      float* __restrict__ u_out, float* __restrict__ lap_out, int64_t n,
+                      int64_t tiles, unsigned int* status) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  float* small = reinterpret_cast<float*>(smem + kSmallOff);
+  float* red = reinterpret_cast<float*>(smem + kRedOff);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kBarOff);
+  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(smem + kMiscOff);
+  Ctx cx;
+  cx.smem = smem;
+  cx.empty = bars;
+  cx.dfull = bars + kRing;
+  cx.red = bars + kRing + 1;
+  cx.count = reinterpret_cast<uint32_t*>(smem + kCountOff);
+  cx.abort_flag = reinterpret_cast<volatile uint32_t*>(smem + kMiscOff + 4);
+  cx.status = status;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  // ---- set-up: split weights to TF32 hi/lo in the canonical layout, small params ----
+  for (int idx = threadIdx.x; idx < kHiddenGemms * kWidth * kWidth; idx += kThreads) {
+    const int layer = idx >> 12, rem = idx & 4095, row = rem >> 6, k = rem & 63;
+    const float w = params[kHiddenBase + layer * kHiddenStride + row * kWidth + k_to_neuron(k)];
+    const uint32_t hi = tc::to_tf32(w);
+    const uint32_t lo = tc::to_tf32(w - __uint_as_float(hi));
+    const int off = operand_offset(row, k);
+    *reinterpret_cast<uint32_t*>(smem + (2 * layer) * kOperandBytes + off) = hi;
+    *reinterpret_cast<uint32_t*>(smem + (2 * layer + 1) * kOperandBytes + off) = lo;
+  }
+  for (int i = threadIdx.x; i < kSmallFloats; i += kThreads) {
+    float v = 0.0f;
+    if (i < kSmB0) v = params[i];                                       // W0
+    else if (i < kSmB) v = params[kB0 + (i - kSmB0)];                   // b0
+    else if (i < kSmWout) {                                             // b1..b3
+      const int l = (i - kSmB) >> 6, o = (i - kSmB) & 63;
+      v = params[kHiddenBase + l * kHiddenStride + kWidth * kWidth + o];
+    } else if (i < kSmBout) v = params[kOutBase + (i - kSmWout)];       // w_out
+    else if (i == kSmBout) v = params[kOutBase + kWidth];               // b_out
+    small[i] = v;
+  }
+  if (threadIdx.x == 0) {
+    for (int r = 0; r < kRing; ++r) {
+      mbar_init(&cx.empty[r], 1);
+      cx.count[r] = 0u;
+    }
+    mbar_init(cx.dfull, 1);
+    mbar_init(cx.red, kWarps);
+    *cx.abort_flag = 0u;
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tc::tmem_alloc(tmem_base_slot, kTmemCols);
+    tc::tmem_relinquish();
+  }
+  tc::fence_proxy_async_smem();  // weight operands visible to the tensor core
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  cx.tmem = *tmem_base_slot;
+
+  const int q = warp & 3;   // TMEM lane quadrant
+  const int s = warp >> 2;  // neuron block 16s..16s+15
+  const uint32_t tmem_warp = cx.tmem + (static_cast<uint32_t>(32 * q) << 16);
+  const int row = 32 * q + lane;
+  uint32_t chunk = 0, mlayer = 0, tile_count = 0;
+  bool ok = true;
+  for (int64_t tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x, ++tile_count) {
+    const int64_t p = tile * kTile + row;
+    const bool active = p < n;
+    const float x0 = active ? coords[2 * p] : 0.0f;
+    const float x1 = active ? coords[2 * p + 1] : 0.0f;
+
+    // layer 0: z = W0 x + b0, z_J = W0 columns, z_L = 0
+#pragma unroll
+    for (int j = 0; j < kChunks; ++j) {
+      float h[4][2];
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        const int o = 16 * s + 2 * j + t;
+        const float w0 = small[kSmW0 + 2 * o], w1 = small[kSmW0 + 2 * o + 1];
+        tanh_jet(fmaf(w0, x0, fmaf(w1, x1, small[kSmB0 + o])), w0, w1, 0.0f, h[0][t],
+                 h[1][t], h[2][t], h[3][t]);
+      }
+      if (!(ok = produce_chunk(chunk++, h, tmem_warp, s, cx))) break;
+    }
+
+    for (int l = 0; ok && l < kHiddenGemms; ++l, ++mlayer) {
+      if (!(ok = wait_or_abort(cx.dfull, mlayer & 1u, cx))) break;
+      tc::fence_after_sync();
+      float d[4][16];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tc::ld_x16(tmem_warp + 64u * c + 16u * s, d[c]);
+      tc::wait_ld();
+      const float* bias = small + kSmB + 64 * l;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) d[0][i] += bias[16 * s + i];
+
+      if (l + 1 < kHiddenGemms) {
+#pragma unroll
+        for (int j = 0; j < kChunks; ++j) {
+          float h[4][2];
+#pragma unroll
+          for (int t = 0; t < 2; ++t) {
+            const int i = 2 * j + t;
+            tanh_jet(d[0][i], d[1][i], d[2][i], d[3][i], h[0][t], h[1][t], h[2][t], h[3][t]);
+          }
+          if (!(ok = produce_chunk(chunk++, h, tmem_warp, s, cx))) break;
+        }
+      } else {
+        // output layer: u = w.v + b, lap = w.L, over this warp's 16 neurons
+        float pu = 0.0f, pl = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          float v, j0, j1, lv;
+          tanh_jet(d[0][i], d[1][i], d[2][i], d[3][i], v, j0, j1, lv);
+          const float w = small[kSmWout + 16 * s + i];
+          pu = fmaf(w, v, pu);
+          pl = fmaf(w, lv, pl);
+        }
+        red[s * kTile + row] = pu;
+        red[(4 + s) * kTile + row] = pl;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(cx.red);
+        // The s = 0 warps finish the tile. Nobody rewrites `red` before they are done:
+        // the next tile's output stage needs the next tile's chunks from them first.
+        if (s == 0) {
+          if (!(ok = wait_or_abort(cx.red, tile_count & 1u, cx))) break;
+          if (active) {
+            float uu = small[kSmBout], ll = 0.0f;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              uu += red[k * kTile + row];
+              ll += red[(4 + k) * kTile + row];
+            }
+            u_out[p] = uu;
+            lap_out[p] = ll;
+          }
+        }
+      }
+    }
+  }
+
+  // ---- teardown: every warp arrives here (all waits are bounded); free TMEM ----
+  // On the normal path each warp waited for the last dfull phase, so every MMA finished.
+  // After an abort, MMAs issued before it may still run: give them time to drain (they
+  // take microseconds) before the columns are released.
+  tc::fence_before_sync();
+  __syncthreads();
+  if (*cx.abort_flag) {
+    const uint64_t start = global_timer_ns();
+    while (global_timer_ns() - start < 2000000ull) {
+    }
+  }
+  if (warp == 0) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc(cx.tmem, kTmemCols);
+  }
+}
+
+}  // namespace
+
+cudaError_t prepare_forward_tc() {
+  return cudaFuncSetAttribute(forward_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              kSmemBytes);
+}
+
+cudaError_t launch_forward_tc(const float* coords, const float* params, float* u, float* lap,
+                              int64_t n, const DeviceInfo& dev, cudaStream_t stream) {
+  const int64_t tiles = (n + kTile - 1) / kTile;
+  const int grid = static_cast<int>(std::min<int64_t>(tiles, dev.sms));
+  forward_tc_kernel<<<grid, kThreads, kSmemBytes, stream>>>(coords, params, u, lap, n, tiles,
+                                                            dev.status);
+  return cudaGetLastError();
 }
 
 }  // namespace fhb

@@ -28,7 +28,8 @@ from oracle import jet
 pytestmark = pytest.mark.gpu
 
 FP32_VERSIONS = [0, 1, 2]
-ALL_VERSIONS = FP32_VERSIONS
+TC_VERSIONS = [3, 4, 5]
+ALL_VERSIONS = FP32_VERSIONS + TC_VERSIONS
 BATCHES = [1, 2, 31, 32, 33, 63, 64, 65, 127, 128, 129, 1_000, 65_536]
 ROUTES = ["capi", "torch"]
 
@@ -272,7 +273,7 @@ def _poisson_loss(u, lap, coords):
 
 
 @pytest.mark.parametrize("name", ["fused_cuda_v0", "fused_cuda_v1", "fused_cuda",
-                                  "fused_cuda_bwd_v1", "fused_cuda_bwd_v5"])
+                                  "fused_cuda_tf32", "fused_cuda_bwd_v1", "fused_cuda_bwd_v5"])
 def test_autograd_gradients_match_oracle(name: str) -> None:
     torch.manual_seed(0)
     model = build_mlp().cuda()
