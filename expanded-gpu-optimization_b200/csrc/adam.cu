@@ -55,7 +55,24 @@ __global__ void bounded_wait_selftest_kernel(uint64_t limit_ns, unsigned int* st
   if (!done && threadIdx.x == 0) report_status(status, FHB_STATUS_SELFTEST);
 }
 
+// out[i] = tanh_fast(x[i]) (fast != 0) or tanhf(x[i]): lets the tests bound tanh_fast
+// against CUDA's tanhf on the device.
+__global__ void debug_tanh_kernel(const float* __restrict__ x, float* __restrict__ out,
+                                  int64_t n, int fast) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    out[i] = fast ? tanh_fast(x[i]) : tanhf(x[i]);
+}
+
 }  // namespace
+
+cudaError_t launch_debug_tanh(const float* x, float* out, int64_t n, int fast,
+                              cudaStream_t stream) {
+  const int64_t blocks = (n + 255) / 256;
+  debug_tanh_kernel<<<static_cast<int>(blocks < 1024 ? blocks : 1024), 256, 0, stream>>>(x, out, n,
+                                                                                        fast);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_adam(float* params, const float* grad, float* exp_avg, float* exp_avg_sq,
                         int64_t count, int64_t* step, float lr, float beta1, float beta2,

@@ -212,4 +212,13 @@ int fhb_debug_bounded_wait_selftest(uint64_t limit_ns, fhb_stream_t stream) {
   return record(fhb::launch_bounded_wait_selftest(limit_ns, dev->status, stream));
 }
 
+int fhb_debug_tanh(const float* x, float* out, int64_t n, int fast, fhb_stream_t stream) {
+  if (n < 0 || (n > 0 && (!x || !out))) return FHB_ERR_INVALID_ARGUMENT;
+  const fhb::DeviceInfo* dev = nullptr;
+  int code = current_device(&dev);
+  if (code != FHB_OK) return code;
+  if (n == 0) return FHB_OK;
+  return record(fhb::launch_debug_tanh(x, out, n, fast, stream));
+}
+
 }  // extern "C"

@@ -161,6 +161,32 @@ __device__ __forceinline__ void tanh_jet_adjoint(float zv, float zj0, float zj1,
   al = al * s;
 }
 
+// tanh from the identity tanh(x) = 1 - 2 / (exp(2x) + 1), with exp(2x) = 2^(2 log2(e) x)
+// on the special-function unit (ex2.approx) and the reciprocal on the same unit
+// (rcp.approx): 5 instructions. Absolute error is a few 1e-7 for every x (relative error
+// grows as |x| -> 0, where tanh(x) ~ x, but the jet propagates absolute errors only); for
+// large |x| the formula saturates to exactly +-1, and NaN stays NaN. Used by the tensor-core
+// forward, whose 3xTF32 GEMMs carry errors of the same size; the GPU tests bound it against
+// CUDA's tanhf over a dense sweep.
+__device__ __forceinline__ float tanh_fast(float x) {
+  float e, r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(x * 2.8853900817779268f));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(e + 1.0f));
+  return fmaf(-2.0f, r, 1.0f);
+}
+
+// tanh_jet with tanh_fast.
+__device__ __forceinline__ void tanh_jet_fast(float zv, float zj0, float zj1, float zl, float& v,
+                                              float& j0, float& j1, float& l) {
+  const float a = tanh_fast(zv);
+  const float s = fmaf(-a, a, 1.0f);
+  const float q = fmaf(zj0, zj0, zj1 * zj1);
+  v = a;
+  j0 = s * zj0;
+  j1 = s * zj1;
+  l = fmaf(s, zl, -2.0f * a * s * q);
+}
+
 // Warp-wide sum with a fixed butterfly order (deterministic).
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll

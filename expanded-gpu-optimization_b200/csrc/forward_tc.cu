@@ -13,25 +13,29 @@
 //     no-swizzle canonical layout in shared memory (96 KB) -- the MMA's B operand;
 //   * TMEM (512 columns x 128 lanes, lane = point):
 //       [0, 256)   accumulators D_c, component c at columns 64c..64c+63;
-//       [256, 448) a ring of 3 A-operand chunks; a chunk is one K step (8 input neurons)
-//                  of the next layer's activations: (component, hi/lo) blocks of 8 columns.
+//       [256, 512) a ring of 2 A-operand chunks; a chunk is two K steps (16 input
+//                  neurons) of the next layer's activations: (component, hi/lo) blocks of
+//                  16 columns.
 //     The A operand lives in TMEM, not shared memory: with N = 64 an A tile read from
 //     shared memory would need ~1.5x the shared-memory bandwidth an SM has.
 //   * 16 warps: warp w serves TMEM lanes 32(w%4)..+31 (its quadrant) and neurons
 //     16(w/4)..+15. Per layer it loads its 4 x 16 accumulators (4 x tcgen05.ld.32x32b.x16),
 //     applies the tanh jet in registers and writes TF32 hi/lo activations chunk by chunk
 //     into the ring (tcgen05.st) for the next layer. The K order is permuted (chunk j holds
-//     neurons 16s+2j+{0,1} for s = 0..3) so all 16 warps contribute to every chunk; the
+//     neurons 16s+4j+{0..3} for s = 0..3) so all 16 warps contribute to every chunk; the
 //     weights' K order is permuted to match;
 //   * the warp that completes a chunk last (an acq_rel counter per ring slot) issues its
-//     MMAs from one lane: 4 components x 3 products, then tcgen05.commit to free the slot,
-//     and after a layer's 8th chunk a commit that marks D complete. A warp contributes to
+//     MMAs from one lane: 2 K steps x 4 components x 3 products, then tcgen05.commit to
+//     free the slot, and after a layer's 4th chunk a commit that marks D complete. A warp contributes to
 //     chunk 0 of layer l+1 only after it has read D of layer l, so when the last
 //     contribution arrives D may be overwritten -- no separate "D free" barrier.
 //   So the MMAs of layer l+1 consume chunk j while the epilogue of layer l produces chunk
 //   j+1. (No dedicated MMA warp: a 17th warp would put 5 warps on one SM sub-partition and
 //   cap registers at 96; with 16 warps each thread gets 128.)
-// Layer 0 (2 inputs) and the output layer (1 output) are elementwise/epilogue work.
+// Layer 0 (2 inputs) and the output layer (1 output) are elementwise/epilogue work. The
+// epilogue, not the tensor core, bounds this kernel, so it is kept lean: tanh_fast (SFU
+// exp2 + reciprocal), a 2-instruction TF32 split (hi = cvt.rna, lo = x - hi, which the
+// tensor core truncates to TF32) and 16-neuron chunks to halve the synchronisation.
 // Every mbarrier wait is bounded; a wait that gives up raises FHB_STATUS_MMA_TIMEOUT, sets
 // a CTA abort flag that stops the other warps, and the kernel frees TMEM and returns.
 #include <algorithm>
@@ -46,9 +50,10 @@ namespace {
 constexpr int kTile = 128;            // points per tile = MMA M = TMEM lanes
 constexpr int kWarps = 16;            // 4 per TMEM lane quadrant
 constexpr int kThreads = kWarps * 32;
-constexpr int kChunks = 8;            // K steps of 8 per 64-wide layer
+constexpr int kChunks = 4;            // chunks of 16 neurons (2 K steps) per 64-wide layer
 constexpr int kChunksPerTile = kHiddenGemms * kChunks;
-constexpr int kRing = 3;
+constexpr int kRing = 2;
+constexpr uint32_t kSlotCols = 128;   // 4 components x {hi, lo} x 16 K positions
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kRingCol = 256;
 constexpr uint32_t kIdesc = tc::idesc_tf32(128, 64);
@@ -59,7 +64,7 @@ constexpr int kSmallOff = 6 * kOperandBytes;        // W0[128] b0[64] b1..b3[192
 constexpr int kSmW0 = 0, kSmB0 = 128, kSmB = 192, kSmWout = 384, kSmBout = 448;
 constexpr int kSmallFloats = 512;
 constexpr int kRedOff = kSmallOff + kSmallFloats * 4;  // [8][128] partial sums
-constexpr int kBarOff = kRedOff + 8 * kTile * 4;       // mbarriers: empty[3], dfull, red
+constexpr int kBarOff = kRedOff + 8 * kTile * 4;       // mbarriers: empty[2], dfull, red
 constexpr int kCountOff = kBarOff + 8 * 8;             // per-slot contribution counters
 constexpr int kMiscOff = kCountOff + 4 * 4;            // TMEM base, abort flag
 constexpr int kSmemUsed = kMiscOff + 16;
@@ -70,13 +75,10 @@ static_assert(kSmemUsed <= kSmemBytes, "shared memory layout overflow");
 // Canonical K-major no-swizzle layout of a [64 rows x 64 K] tf32 operand: 8x4 core
 // matrices of 128 B; K chunks of 4 at LBO = 128 B, 8-row groups at SBO = 2048 B.
 constexpr uint32_t kLbo = 128, kSbo = 2048;
-__device__ __forceinline__ int operand_offset(int row, int k) {
-  return (row >> 3) * kSbo + (k >> 2) * kLbo + (row & 7) * 16 + (k & 3) * 4;
-}
-// K position k of a layer's input <-> input neuron: chunk j = k/8 holds neurons
-// 16s + 2j + t at position 2s + t (s = warp neuron block, t = 0, 1).
+// K position k of a layer's input <-> input neuron: chunk j = k/16 holds neurons
+// 16s + 4j + t at position 4s + t (s = warp neuron block, t = 0..3).
 __device__ __forceinline__ int k_to_neuron(int k) {
-  return 16 * ((k & 7) >> 1) + 2 * (k >> 3) + (k & 1);
+  return 16 * ((k & 15) >> 2) + 4 * (k >> 4) + (k & 3);
 }
 
 struct Ctx {
@@ -119,41 +121,51 @@ __device__ __forceinline__ uint32_t count_contribution(uint32_t* counter) {
   return old;
 }
 
-// The 12 MMAs of one chunk: K step j of hidden GEMM `layer`, A from ring slot `slot`.
+// The 24 MMAs of one chunk: K steps 2j, 2j+1 of hidden GEMM `layer`, A from ring slot
+// `slot` (component c, hi/lo sp, K step kk at columns 32c + 16sp + 8kk of the slot).
 __device__ __forceinline__ void issue_chunk_mmas(const Ctx& cx, int layer, int j,
                                                  uint32_t slot) {
-  const uint32_t w_hi = smem_u32(cx.smem + (2 * layer) * kOperandBytes + 256 * j);
-  const uint32_t w_lo = w_hi + kOperandBytes;
-  const uint64_t bhi = tc::smem_desc_kmajor(w_hi, kLbo, kSbo);
-  const uint64_t blo = tc::smem_desc_kmajor(w_lo, kLbo, kSbo);
 #pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    const uint32_t d = cx.tmem + 64u * c;
-    const uint32_t a_hi = cx.tmem + kRingCol + 64u * slot + 16u * c;
-    const uint32_t a_lo = a_hi + 8u;
-    tc::mma_tf32_ts(d, a_hi, bhi, kIdesc, j > 0 ? 1u : 0u);
-    tc::mma_tf32_ts(d, a_lo, bhi, kIdesc, 1u);
-    tc::mma_tf32_ts(d, a_hi, blo, kIdesc, 1u);
+  for (int kk = 0; kk < 2; ++kk) {
+    const uint32_t w_hi = smem_u32(cx.smem + (2 * layer) * kOperandBytes + 256 * (2 * j + kk));
+    const uint64_t bhi = tc::smem_desc_kmajor(w_hi, kLbo, kSbo);
+    const uint64_t blo = tc::smem_desc_kmajor(w_hi + kOperandBytes, kLbo, kSbo);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const uint32_t d = cx.tmem + 64u * c;
+      const uint32_t a_hi = cx.tmem + kRingCol + kSlotCols * slot + 32u * c + 8u * kk;
+      const uint32_t a_lo = a_hi + 16u;
+      tc::mma_tf32_ts(d, a_hi, bhi, kIdesc, (j > 0 || kk > 0) ? 1u : 0u);
+      tc::mma_tf32_ts(d, a_lo, bhi, kIdesc, 1u);
+      tc::mma_tf32_ts(d, a_hi, blo, kIdesc, 1u);
+    }
   }
   tc::commit(&cx.empty[slot]);
   if (j == kChunks - 1) tc::commit(cx.dfull);
 }
 
-// Write chunk `n` (this warp's 2 neurons x 4 components, TF32 hi and lo) into ring slot
+// TF32 split: hi = x rounded to TF32; lo = x - hi (exact in FP32), fed as is: the tensor
+// core reads only its TF32 bits, an error of at most 2^-21 |x|.
+__device__ __forceinline__ void split_tf32(float x, uint32_t& hi, uint32_t& lo) {
+  hi = tc::to_tf32(x);
+  lo = __float_as_uint(x - __uint_as_float(hi));
+}
+
+// Write chunk `n` (this warp's 4 neurons x 4 components, TF32 hi and lo) into ring slot
 // n % kRing; the warp completing the chunk last issues its MMAs. False if aborted.
-__device__ __forceinline__ bool produce_chunk(uint32_t n, const float (&h)[4][2],
+__device__ __forceinline__ bool produce_chunk(uint32_t n, const float (&h)[4][4],
                                               uint32_t tmem_warp, int s, const Ctx& cx) {
   const uint32_t slot = n % kRing;
   if (!wait_or_abort(&cx.empty[slot], ((n / kRing) & 1u) ^ 1u, cx)) return false;
   tc::fence_after_sync();
-  const uint32_t base = tmem_warp + kRingCol + 64u * slot + 2u * s;
+  const uint32_t base = tmem_warp + kRingCol + kSlotCols * slot + 4u * s;
 #pragma unroll
   for (int c = 0; c < 4; ++c) {
-    const uint32_t hi0 = tc::to_tf32(h[c][0]), hi1 = tc::to_tf32(h[c][1]);
-    const uint32_t lo0 = tc::to_tf32(h[c][0] - __uint_as_float(hi0));
-    const uint32_t lo1 = tc::to_tf32(h[c][1] - __uint_as_float(hi1));
-    tc::st_x2(base + 16u * c, hi0, hi1);
-    tc::st_x2(base + 16u * c + 8u, lo0, lo1);
+    uint32_t hi[4], lo[4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) split_tf32(h[c][t], hi[t], lo[t]);
+    tc::st_x4(base + 32u * c, hi[0], hi[1], hi[2], hi[3]);
+    tc::st_x4(base + 32u * c + 16u, lo[0], lo[1], lo[2], lo[3]);
   }
   tc::wait_st();
   tc::fence_before_sync();
@@ -195,14 +207,29 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int lane = threadIdx.x & 31;
 
   // ---- set-up: split weights to TF32 hi/lo in the canonical layout, small params ----
-  for (int idx = threadIdx.x; idx < kHiddenGemms * kWidth * kWidth; idx += kThreads) {
-    const int layer = idx >> 12, rem = idx & 4095, row = rem >> 6, k = rem & 63;
-    const float w = params[kHiddenBase + layer * kHiddenStride + row * kWidth + k_to_neuron(k)];
-    const uint32_t hi = tc::to_tf32(w);
-    const uint32_t lo = tc::to_tf32(w - __uint_as_float(hi));
-    const int off = operand_offset(row, k);
-    *reinterpret_cast<uint32_t*>(smem + (2 * layer) * kOperandBytes + off) = hi;
-    *reinterpret_cast<uint32_t*>(smem + (2 * layer + 1) * kOperandBytes + off) = lo;
+  // Element e of an operand, enumerated as (row group, K chunk, row in group, K in chunk),
+  // sits at byte 4e of the canonical layout: consecutive threads store consecutive words.
+  // All 24 loads of a thread are issued before any is used.
+  {
+    constexpr int kPerThread = kHiddenGemms * kWidth * kWidth / kThreads;  // 24
+    float w[kPerThread];
+#pragma unroll
+    for (int r = 0; r < kPerThread; ++r) {
+      const int idx = threadIdx.x + r * kThreads;
+      const int layer = idx >> 12, e = idx & 4095;
+      const int row = ((e >> 9) << 3) | ((e >> 2) & 7);
+      const int k = (((e >> 5) & 15) << 2) | (e & 3);
+      w[r] = params[kHiddenBase + layer * kHiddenStride + row * kWidth + k_to_neuron(k)];
+    }
+#pragma unroll
+    for (int r = 0; r < kPerThread; ++r) {
+      const int idx = threadIdx.x + r * kThreads;
+      const int layer = idx >> 12, e = idx & 4095;
+      const uint32_t hi = tc::to_tf32(w[r]);
+      const uint32_t lo = tc::to_tf32(w[r] - __uint_as_float(hi));
+      reinterpret_cast<uint32_t*>(smem + (2 * layer) * kOperandBytes)[e] = hi;
+      reinterpret_cast<uint32_t*>(smem + (2 * layer + 1) * kOperandBytes)[e] = lo;
+    }
   }
   for (int i = threadIdx.x; i < kSmallFloats; i += kThreads) {
     float v = 0.0f;
@@ -250,13 +277,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     // layer 0: z = W0 x + b0, z_J = W0 columns, z_L = 0
 #pragma unroll
     for (int j = 0; j < kChunks; ++j) {
-      float h[4][2];
+      float h[4][4];
 #pragma unroll
-      for (int t = 0; t < 2; ++t) {
-        const int o = 16 * s + 2 * j + t;
+      for (int t = 0; t < 4; ++t) {
+        const int o = 16 * s + 4 * j + t;
         const float w0 = small[kSmW0 + 2 * o], w1 = small[kSmW0 + 2 * o + 1];
-        tanh_jet(fmaf(w0, x0, fmaf(w1, x1, small[kSmB0 + o])), w0, w1, 0.0f, h[0][t],
-                 h[1][t], h[2][t], h[3][t]);
+        tanh_jet_fast(fmaf(w0, x0, fmaf(w1, x1, small[kSmB0 + o])), w0, w1, 0.0f, h[0][t],
+                      h[1][t], h[2][t], h[3][t]);
       }
       if (!(ok = produce_chunk(chunk++, h, tmem_warp, s, cx))) break;
     }
@@ -275,11 +302,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (l + 1 < kHiddenGemms) {
 #pragma unroll
         for (int j = 0; j < kChunks; ++j) {
-          float h[4][2];
+          float h[4][4];
 #pragma unroll
-          for (int t = 0; t < 2; ++t) {
-            const int i = 2 * j + t;
-            tanh_jet(d[0][i], d[1][i], d[2][i], d[3][i], h[0][t], h[1][t], h[2][t], h[3][t]);
+          for (int t = 0; t < 4; ++t) {
+            const int i = 4 * j + t;
+            tanh_jet_fast(d[0][i], d[1][i], d[2][i], d[3][i], h[0][t], h[1][t], h[2][t],
+                          h[3][t]);
           }
           if (!(ok = produce_chunk(chunk++, h, tmem_warp, s, cx))) break;
         }
@@ -289,7 +317,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           float v, j0, j1, lv;
-          tanh_jet(d[0][i], d[1][i], d[2][i], d[3][i], v, j0, j1, lv);
+          tanh_jet_fast(d[0][i], d[1][i], d[2][i], d[3][i], v, j0, j1, lv);
           const float w = small[kSmWout + 16 * s + i];
           pu = fmaf(w, v, pu);
           pl = fmaf(w, lv, pl);

@@ -46,6 +46,8 @@ cudaError_t launch_reduce_rows(const float* partials, int rows, float* grad_para
 cudaError_t launch_adam(float* params, const float* grad, float* exp_avg, float* exp_avg_sq,
                         int64_t count, int64_t* step, float lr, float beta1, float beta2,
                         float eps, cudaStream_t stream);
+cudaError_t launch_debug_tanh(const float* x, float* out, int64_t n, int fast,
+                              cudaStream_t stream);
 cudaError_t launch_bounded_wait_selftest(uint64_t limit_ns, unsigned int* status,
                                          cudaStream_t stream);
 

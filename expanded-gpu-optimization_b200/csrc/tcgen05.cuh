@@ -80,6 +80,12 @@ __device__ __forceinline__ void st_x2(uint32_t taddr, uint32_t a, uint32_t b) {
                "r"(b)
                : "memory");
 }
+__device__ __forceinline__ void st_x4(uint32_t taddr, uint32_t a, uint32_t b, uint32_t c,
+                                      uint32_t d) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};" ::"r"(taddr),
+               "r"(a), "r"(b), "r"(c), "r"(d)
+               : "memory");
+}
 __device__ __forceinline__ void wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }

@@ -37,6 +37,7 @@ _SIGNATURES: dict[str, tuple[object, list]] = {
     ),
     "fhb_read_device_status": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_uint)]),
     "fhb_debug_bounded_wait_selftest": (ctypes.c_int, [ctypes.c_uint64, _p]),
+    "fhb_debug_tanh": (ctypes.c_int, [_p, _p, _i64, ctypes.c_int, _p]),
 }
 
 

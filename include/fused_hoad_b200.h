@@ -129,6 +129,12 @@ int fhb_read_device_status(int device, unsigned int* status_out);
  */
 int fhb_debug_bounded_wait_selftest(uint64_t limit_ns, fhb_stream_t stream);
 
+/*
+ * Test hook for the tensor-core kernel's tanh: out[i] = tanh_fast(x[i]) when fast != 0
+ * (tanh from 1 - 2/(exp(2x)+1) on the special-function unit), else CUDA's tanhf(x[i]).
+ */
+int fhb_debug_tanh(const float* x, float* out, int64_t n, int fast, fhb_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

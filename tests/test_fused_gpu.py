@@ -466,3 +466,26 @@ def test_bounded_wait_gives_up_and_reports_without_a_fault() -> None:
     assert read_status() == 0x80  # FHB_STATUS_SELFTEST; the context stays usable
     u, _ = fused_forward_laplacian(uniform_points(64).cuda(), _params())
     assert torch.isfinite(u).all()
+
+
+def test_tanh_fast_error_bound_against_cuda_tanhf() -> None:
+    """The tensor-core kernel's tanh (1 - 2/(exp(2x)+1) on the SFU) stays within 5e-7 of
+    CUDA's tanhf in absolute terms over a dense sweep, and saturates to exactly +-1."""
+    from fused_hoad import _native
+
+    lib = _native.library()
+    x = torch.cat([
+        torch.linspace(-20.0, 20.0, 2_000_001, device="cuda"),
+        torch.tensor([0.0, -0.0, 1e-30, -1e-30, 1e-8, 88.0, -88.0, 1e4, -1e4], device="cuda"),
+    ])
+    out = {}
+    for fast in (0, 1):
+        y = torch.empty_like(x)
+        _native.check(lib.fhb_debug_tanh(x.data_ptr(), y.data_ptr(), x.numel(), fast,
+                                         torch.cuda.current_stream().cuda_stream), "tanh")
+        out[fast] = y
+    torch.cuda.synchronize()
+    err = (out[1].double() - out[0].double()).abs()
+    assert err.max().item() <= 5e-7, err.max().item()
+    assert torch.all(out[1][x >= 10] == 1.0) and torch.all(out[1][x <= -10] == -1.0)
+    assert torch.all(out[1].abs() <= 1.0)
