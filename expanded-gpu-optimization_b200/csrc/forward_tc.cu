@@ -25,8 +25,10 @@
 //     neurons 16s+4j+{0..3} for s = 0..3) so all 16 warps contribute to every chunk; the
 //     weights' K order is permuted to match;
 //   * the warp that completes a chunk last (an acq_rel counter per ring slot) issues its
-//     MMAs from one lane: 2 K steps x 4 components x 3 products, then tcgen05.commit to
-//     free the slot, and after a layer's 4th chunk a commit that marks D complete. A warp contributes to
+//     MMAs as a converged warp (elect.sync picks the issuing lane; issued from a divergent
+//     lane these small MMAs cost ~4x their execution time): 2 K steps x 4 components x 3
+//     products, then tcgen05.commit to free the slot, and after a layer's 4th chunk a
+//     commit that marks D complete. A warp contributes to
 //     chunk 0 of layer l+1 only after it has read D of layer l, so when the last
 //     contribution arrives D may be overwritten -- no separate "D free" barrier.
 //   So the MMAs of layer l+1 consume chunk j while the epilogue of layer l produces chunk
@@ -135,13 +137,13 @@ __device__ __forceinline__ void issue_chunk_mmas(const Ctx& cx, int layer, int j
       const uint32_t d = cx.tmem + 64u * c;
       const uint32_t a_hi = cx.tmem + kRingCol + kSlotCols * slot + 32u * c + 8u * kk;
       const uint32_t a_lo = a_hi + 16u;
-      tc::mma_tf32_ts(d, a_hi, bhi, kIdesc, (j > 0 || kk > 0) ? 1u : 0u);
-      tc::mma_tf32_ts(d, a_lo, bhi, kIdesc, 1u);
-      tc::mma_tf32_ts(d, a_hi, blo, kIdesc, 1u);
+      tc::mma_tf32_ts_warp(d, a_hi, bhi, kIdesc, (j > 0 || kk > 0) ? 1u : 0u);
+      tc::mma_tf32_ts_warp(d, a_lo, bhi, kIdesc, 1u);
+      tc::mma_tf32_ts_warp(d, a_hi, blo, kIdesc, 1u);
     }
   }
-  tc::commit(&cx.empty[slot]);
-  if (j == kChunks - 1) tc::commit(cx.dfull);
+  tc::commit_warp(&cx.empty[slot]);
+  if (j == kChunks - 1) tc::commit_warp(cx.dfull);
 }
 
 // TF32 split: hi = x rounded to TF32; lo = x - hi (exact in FP32), fed as is: the tensor
@@ -173,13 +175,11 @@ __device__ __forceinline__ bool produce_chunk(uint32_t n, const float (&h)[4][4]
   uint32_t last = 0;
   if ((threadIdx.x & 31) == 0) last = (count_contribution(&cx.count[slot]) % kWarps) == kWarps - 1;
   last = __shfl_sync(0xffffffffu, last, 0);
-  if (last) {
-    if ((threadIdx.x & 31) == 0) {
-      tc::fence_after_sync();
-      const uint32_t in_tile = n % kChunksPerTile;
-      issue_chunk_mmas(cx, static_cast<int>(in_tile / kChunks), static_cast<int>(in_tile % kChunks),
-                       slot);
-    }
+  if (last) {  // warp-uniform: the whole converged warp issues, elect.sync picks a lane
+    tc::fence_after_sync();
+    const uint32_t in_tile = n % kChunksPerTile;
+    issue_chunk_mmas(cx, static_cast<int>(in_tile / kChunks), static_cast<int>(in_tile % kChunks),
+                     slot);
     __syncwarp();
   }
   return true;

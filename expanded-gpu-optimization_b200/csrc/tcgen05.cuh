@@ -53,6 +53,30 @@ __device__ __forceinline__ void mma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, ui
       : "memory");
 }
 
+// The same MMA issued by a converged warp: every lane evaluates the operands (so they stay
+// warp-uniform) and elect.sync picks the one lane that issues. Issuing from a lane-divergent
+// branch instead costs ~4x the MMA's own execution time per instruction for these shapes.
+__device__ __forceinline__ void mma_tf32_ts_warp(uint32_t d_tmem, uint32_t a_tmem,
+                                                 uint64_t b_desc, uint32_t idesc,
+                                                 uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}"
+      ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u),
+      "r"(0u), "r"(0u)
+      : "memory");
+}
+// tcgen05.commit from one elected lane of a converged warp.
+__device__ __forceinline__ void commit_warp(uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}"
+      ::"r"(smem_u32(bar))
+      : "memory");
+}
+
 // Arrive once on `bar` when every tcgen05.mma issued so far by this thread has completed.
 __device__ __forceinline__ void commit(uint64_t* bar) {
   asm volatile(
