@@ -39,7 +39,9 @@ NVCC_FLAGS = [
     "-v",
     f"-I{INCLUDE}",
 ]
-CU_SOURCES = ["forward_fp32.cu", "forward_tc.cu", "backward_fp32.cu", "adam.cu", "capi.cu"]
+CU_SOURCES = [
+    "forward_fp32.cu", "forward_tc.cu", "backward_fp32.cu", "adam.cu", "capi.cu", "noalloc.cu",
+]
 
 
 def _headers() -> list[Path]:

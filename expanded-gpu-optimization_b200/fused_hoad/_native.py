@@ -26,6 +26,7 @@ _SIGNATURES: dict[str, tuple[object, list]] = {
         ctypes.c_int,
         [_p, _p, _p, _p, _p, _p, _i64, ctypes.c_int, _p, ctypes.c_size_t, _p],
     ),
+    "fhb_backward_noalloc": (ctypes.c_int, [_p, _p, _p, _p, _p, _p, _i64, _p]),
     "fhb_poisson_step_gradients": (
         ctypes.c_int,
         [_p, _p, _i64, _i64, _p, _p, _p, _p, _p, ctypes.c_size_t, _p],

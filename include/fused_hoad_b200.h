@@ -94,6 +94,24 @@ int fhb_backward(const float* coords, const float* params, const float* grad_u,
                  int version, void* workspace, size_t workspace_bytes, fhb_stream_t stream);
 
 /*
+ * fhb_backward without a workspace argument: no counterpart in the reference (its backward
+ * allocates partials and scratch with the ATen allocator on every call).
+ * For callers that cannot allocate device memory where they call the backward: inside a
+ * CUDA graph they are capturing (cudaMalloc synchronises and is not capturable), behind a
+ * thin FFI with no device allocator, or under a device-memory budget fixed at start-up.
+ * The scratch is a file-scope device array of 148 partial-gradient rows (7.5 MB, one row per
+ * SM of a B200) that every GPU loading this library holds until exit; the call returns
+ * FHB_ERR_TOO_LARGE when the persistent grid for n would need more rows (only on a GPU with
+ * more than 148 SMs). The first call on a device does the set-up (kernel attributes, the
+ * array's device address), so make it before any stream capture. All calls share the array:
+ * calls that overlap on the GPU race on it -- order them on one stream. Otherwise as
+ * fhb_backward (grad_u may be NULL, grad_coords may be NULL, n == 0 zeroes grad_params).
+ */
+int fhb_backward_noalloc(const float* coords, const float* params, const float* grad_u,
+                         const float* grad_lap, float* grad_params, float* grad_coords,
+                         int64_t n, fhb_stream_t stream);
+
+/*
  * Fused Poisson training-step gradients for the interior loss
  *     L = sum_p (lap_p - f(x_p))^2 / n_total,  f = -2 pi^2 sin(pi x) sin(pi y)
  * (reference benchmarks/benchmark_training.py:46-48, src/fused_hoad/problems/poisson.py:37-39):

@@ -1,0 +1,64 @@
+"""fhb_backward_noalloc: the backward for callers that cannot allocate device memory.
+
+Some callers cannot call cudaMalloc where they run the backward: inside a CUDA graph they
+are capturing, behind an FFI with no device allocator, or under a memory budget fixed at
+start-up. This entry point keeps its scratch in a static device array instead of a
+caller-supplied workspace. The test calls it through the C ABI twice in a row and checks
+each result against fhb_backward (which takes a workspace) at the parity tolerance used
+for gradients elsewhere (<= 1e-4 x max|expected|). The array keeps the previous call's
+contents, so the second call also shows that stale rows do not leak into the result.
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+from helpers import assert_scaled, capi_backward, ptr, stream_handle
+
+from fused_hoad import _native, uniform_points
+from oracle import jet
+
+pytestmark = pytest.mark.gpu
+
+
+def _noalloc(coords, params, grad_u, grad_lap):
+    n = coords.shape[0]
+    grad_p = torch.full((12737,), float("nan"), device="cuda")
+    grad_x = torch.full((n, 2), float("nan"), device="cuda")
+    code = _native.library().fhb_backward_noalloc(
+        ptr(coords), ptr(params), ptr(grad_u), ptr(grad_lap), ptr(grad_p), ptr(grad_x), n,
+        stream_handle(),
+    )
+    _native.check(code, "fhb_backward_noalloc")
+    return grad_p, grad_x
+
+
+@pytest.mark.parametrize("batch", [1_000, 65_536])
+def test_noalloc_backward_matches_workspace_backward_twice(batch: int) -> None:
+    if not torch.cuda.is_available():
+        pytest.fail("needs a CUDA device")
+    params = jet.init_parameters(0).cuda()
+    for call, seed in enumerate((31, 32)):  # two calls in a row, different inputs
+        coords = uniform_points(batch, seed=seed).cuda()
+        g = torch.Generator().manual_seed(seed)
+        gu = torch.randn(batch, generator=g).cuda()
+        gl = torch.randn(batch, generator=g).cuda()
+        want_p, want_x = capi_backward(coords, params, gu, gl)
+        got_p, got_x = _noalloc(coords, params, gu, gl)
+        torch.cuda.synchronize()
+        assert torch.isfinite(got_p).all() and torch.isfinite(got_x).all(), f"call {call}"
+        assert_scaled(got_p.cpu(), want_p.cpu(), 1e-4, f"grad params, call {call}")
+        assert_scaled(got_x.cpu(), want_x.cpu(), 1e-4, f"grad coords, call {call}")
+
+
+def test_noalloc_backward_empty_batch_zeroes_gradient() -> None:
+    params = jet.init_parameters(0).cuda()
+    grad_p = torch.full((12737,), 3.0, device="cuda")
+    empty = torch.empty(0, 2, device="cuda")
+    code = _native.library().fhb_backward_noalloc(
+        ptr(empty), ptr(params), None, ptr(torch.empty(0, device="cuda")), ptr(grad_p), None, 0,
+        stream_handle(),
+    )
+    _native.check(code, "fhb_backward_noalloc")
+    torch.cuda.synchronize()
+    assert torch.count_nonzero(grad_p) == 0
