@@ -330,13 +330,18 @@ def run_ours(args) -> None:
             dist.destroy_process_group()
         return
 
+    # DRAM read + write bytes of one forward launch at 65,536 points, from one ncu capture of
+    # the same command (versions 0-2 share the FP32 kernel family, 3-5 the tensor-core one).
+    traffic = None
+    if n == POINTS_PER_GPU:
+        traffic = 611_840 if version <= 2 else 646_400
     per_launch_s = ms_per_step / 1e3
     achieved_tflops = n * FLOP_FORWARD / per_launch_s / 1e12
     fp32_peak = SM_COUNT * 128 * 2 * peaks.get("sm_max_mhz", 1965.0) * 1e6 / 1e12
     if version <= 2:
         roofline = {
             "bound": "fp32", "achieved": achieved_tflops, "peak": fp32_peak, "unit": "TFLOP/s",
-            "frac": achieved_tflops / fp32_peak, "traffic": None,
+            "frac": achieved_tflops / fp32_peak, "traffic": traffic,
             "kernel": f"forward_fp32_kernel (version {version})",
             "peak_note": ("FP32 CUDA-core peak 148 SMs x 128 lanes x 2 x sm_max_mhz "
                           f"({peak_kind} sm_max_mhz); no measured FP32 peak exists"),
@@ -346,7 +351,7 @@ def run_ours(args) -> None:
         bf16 = peaks["bf16_tflops"]
         roofline = {
             "bound": "tensor", "achieved": achieved_tflops, "peak": bf16, "unit": "TFLOP/s",
-            "frac": achieved_tflops / bf16, "traffic": None,
+            "frac": achieved_tflops / bf16, "traffic": traffic,
             "kernel": f"forward_tc_kernel (version {version})",
             "peak_note": (f"{peak_kind} bf16 burst peak; TF32 runs at half of it and 3xTF32 "
                           "issues three MMAs per product, so the 3xTF32 ceiling is bf16/6"),
