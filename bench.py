@@ -81,7 +81,9 @@ class ClockSampler:
     """nvidia-smi sampling of this rank's GPU while the timed region runs."""
 
     def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
+        # nvidia-smi numbers GPUs physically; map through CUDA_VISIBLE_DEVICES when set
+        visible = [v.strip() for v in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if v.strip()]
+        self.gpu = visible[gpu_index] if gpu_index < len(visible) else gpu_index
         self.proc = None
         self.lines: list[str] = []
 

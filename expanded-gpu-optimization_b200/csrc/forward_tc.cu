@@ -109,6 +109,13 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, co
   }
 }
 
+// Every lane polls; the vote makes the outcome warp-uniform (it can differ between lanes only
+// when the time limit expires just as the phase completes), because the aligned tcgen05
+// ld/st and elect.sync that follow need the whole warp.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, const Ctx& cx) {
+  return __all_sync(0xffffffffu, wait_or_abort(bar, parity, cx) ? 1 : 0) != 0;
+}
+
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
@@ -158,7 +165,7 @@ __device__ __forceinline__ void split_tf32(float x, uint32_t& hi, uint32_t& lo) 
 __device__ __forceinline__ bool produce_chunk(uint32_t n, const float (&h)[4][4],
                                               uint32_t tmem_warp, int s, const Ctx& cx) {
   const uint32_t slot = n % kRing;
-  if (!wait_or_abort(&cx.empty[slot], ((n / kRing) & 1u) ^ 1u, cx)) return false;
+  if (!warp_wait(&cx.empty[slot], ((n / kRing) & 1u) ^ 1u, cx)) return false;
   tc::fence_after_sync();
   const uint32_t base = tmem_warp + kRingCol + kSlotCols * slot + 4u * s;
 #pragma unroll
@@ -289,7 +296,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 
     for (int l = 0; ok && l < kHiddenGemms; ++l, ++mlayer) {
-      if (!(ok = wait_or_abort(cx.dfull, mlayer & 1u, cx))) break;
+      if (!(ok = warp_wait(cx.dfull, mlayer & 1u, cx))) break;
       tc::fence_after_sync();
       float d[4][16];
 #pragma unroll
@@ -329,7 +336,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // The s = 0 warps finish the tile. Nobody rewrites `red` before they are done:
         // the next tile's output stage needs the next tile's chunks from them first.
         if (s == 0) {
-          if (!(ok = wait_or_abort(cx.red, tile_count & 1u, cx))) break;
+          if (!(ok = warp_wait(cx.red, tile_count & 1u, cx))) break;
           if (active) {
             float uu = small[kSmBout], ll = 0.0f;
 #pragma unroll
