@@ -101,7 +101,50 @@ std::vector<torch::Tensor> fused_forward_laplacian_backward(torch::Tensor coordi
   return {grad_parameters, grad_coordinates};
 }
 
-// ---- B200-native training-step ops (no counterpart in the reference's _C) ----
+// ---- B200-native additions (no counterpart in the reference's _C) ----
+
+// Zero-copy evaluation of points that live in pinned host memory: pinned allocations are
+// device-addressable, so the kernel reads the points and writes (u, lap) straight over the
+// host link while it computes -- no staging copies, the transfer overlaps the work. Outputs
+// are pinned host tensors ([N,1] each), valid once the current stream of the parameters'
+// device has completed; pass `output`/`laplacian` to reuse buffers.
+std::vector<torch::Tensor> fused_forward_laplacian_host(torch::Tensor coordinates,
+                                                        torch::Tensor parameters,
+                                                        int64_t version,
+                                                        c10::optional<torch::Tensor> output,
+                                                        c10::optional<torch::Tensor> laplacian) {
+  TORCH_CHECK(version >= 0 && version <= 5, "version must be 0 to 5");
+  TORCH_CHECK(!coordinates.is_cuda() && coordinates.is_pinned(),
+              "coordinates must be a pinned host tensor");
+  TORCH_CHECK(parameters.is_cuda(), "parameters must be a CUDA tensor");
+  TORCH_CHECK(coordinates.is_contiguous() && parameters.is_contiguous(),
+              "coordinates and parameters must be contiguous");
+  TORCH_CHECK(coordinates.scalar_type() == torch::kFloat32 &&
+                  parameters.scalar_type() == torch::kFloat32,
+              "coordinates and parameters must use float32");
+  TORCH_CHECK(coordinates.dim() == 2 && coordinates.size(1) == 2,
+              "coordinates must have shape [batch, 2]");
+  TORCH_CHECK(parameters.dim() == 1 && parameters.numel() == kParameterCount,
+              "parameters must have shape [12737]");
+  const int64_t batch = coordinates.size(0);
+  auto pinned = torch::TensorOptions().dtype(torch::kFloat32).pinned_memory(true);
+  auto u = output.has_value() ? *output : torch::empty({batch, 1}, pinned);
+  auto lap = laplacian.has_value() ? *laplacian : torch::empty({batch, 1}, pinned);
+  for (const auto& t : {u, lap}) {
+    TORCH_CHECK(!t.is_cuda() && t.is_pinned() && t.is_contiguous() &&
+                    t.scalar_type() == torch::kFloat32 && t.numel() == batch,
+                "outputs must be pinned contiguous float32 host tensors with [batch] values");
+  }
+  if (batch == 0) return {u, lap};
+  const c10::cuda::CUDAGuard device_guard(parameters.device());
+  check_status(fhb_forward(coordinates.data_ptr<float>(), parameters.data_ptr<float>(),
+                           u.data_ptr<float>(), lap.data_ptr<float>(), batch,
+                           static_cast<int>(version), at::cuda::getCurrentCUDAStream()),
+               "fused_forward_laplacian_host");
+  return {u, lap};
+}
+
+// ---- B200-native training-step ops ----
 
 // Fused Poisson step gradients; see fhb_poisson_step_gradients. Returns
 // [grad_and_loss [12738] (gradient, then this shard's loss in the last slot),
@@ -176,6 +219,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, module) {
              pybind11::arg("coordinates"), pybind11::arg("parameters"),
              pybind11::arg("grad_output"), pybind11::arg("grad_laplacian"),
              pybind11::arg("version") = 6);
+  module.def("fused_forward_laplacian_host", &fused_forward_laplacian_host,
+             "Forward Laplacian of points in pinned host memory, read and written by the "
+             "kernel over the host link (zero-copy)",
+             pybind11::arg("coordinates"), pybind11::arg("parameters"),
+             pybind11::arg("version") = 3, pybind11::arg("output") = pybind11::none(),
+             pybind11::arg("laplacian") = pybind11::none());
   module.def("poisson_step_gradients", &poisson_step_gradients,
              "Fused forward + interior Poisson loss + backward in one persistent kernel",
              pybind11::arg("coordinates"), pybind11::arg("parameters"),

@@ -275,11 +275,27 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int row = 32 * q + lane;
   uint32_t chunk = 0, mlayer = 0, tile_count = 0;
   bool ok = true;
+  // Points of the next tile are loaded one tile ahead, so the load latency (long when the
+  // points sit in pinned host memory read over the host link) overlaps a tile of work.
+  float nx0 = 0.0f, nx1 = 0.0f;
+  {
+    const int64_t p = static_cast<int64_t>(blockIdx.x) * kTile + row;
+    if (p < n) {
+      nx0 = coords[2 * p];
+      nx1 = coords[2 * p + 1];
+    }
+  }
   for (int64_t tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x, ++tile_count) {
     const int64_t p = tile * kTile + row;
     const bool active = p < n;
-    const float x0 = active ? coords[2 * p] : 0.0f;
-    const float x1 = active ? coords[2 * p + 1] : 0.0f;
+    const float x0 = nx0, x1 = nx1;
+    {
+      const int64_t pn = p + static_cast<int64_t>(gridDim.x) * kTile;
+      if (pn < n) {
+        nx0 = coords[2 * pn];
+        nx1 = coords[2 * pn + 1];
+      }
+    }
 
     // layer 0: z = W0 x + b0, z_J = W0 columns, z_L = 0
 #pragma unroll

@@ -11,6 +11,7 @@ from fused_hoad._extension import (
     extension_available,
     fused_forward_laplacian,
     fused_forward_laplacian_backward,
+    fused_forward_laplacian_host,
     load_extension,
 )
 from fused_hoad.backends import BACKENDS, FIXED_CONTRACT_BACKENDS, get_backend
@@ -48,6 +49,7 @@ __all__ = [
     "extension_available",
     "fused_forward_laplacian",
     "fused_forward_laplacian_backward",
+    "fused_forward_laplacian_host",
     "fused_laplacian",
     "get_backend",
     "load_extension",

@@ -71,3 +71,22 @@ def fused_forward_laplacian_backward(
         version,
     )
     return grad_parameters, grad_coordinates
+
+
+def fused_forward_laplacian_host(
+    coordinates: Tensor,
+    parameters: Tensor,
+    version: int = 3,
+    output: Tensor | None = None,
+    laplacian: Tensor | None = None,
+) -> tuple[Tensor, Tensor]:
+    """``(u, lap)`` for points in pinned host memory, without staging copies.
+
+    Pinned host memory is device-addressable, so the kernel reads the points and writes the
+    results over the host link while it computes. The results are pinned host tensors,
+    valid once the current CUDA stream of ``parameters``' device has completed.
+    """
+    u, lap = load_extension().fused_forward_laplacian_host(
+        coordinates, parameters, version, output, laplacian
+    )
+    return u, lap

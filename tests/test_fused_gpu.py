@@ -489,3 +489,23 @@ def test_tanh_fast_error_bound_against_cuda_tanhf() -> None:
     assert err.max().item() <= 5e-7, err.max().item()
     assert torch.all(out[1][x >= 10] == 1.0) and torch.all(out[1][x <= -10] == -1.0)
     assert torch.all(out[1].abs() <= 1.0)
+
+
+@pytest.mark.parametrize("version", [2, 3])
+@pytest.mark.parametrize("batch", [1, 1_000, 65_536, 1_048_577])
+def test_zero_copy_host_evaluation_matches_device_evaluation(batch: int, version: int) -> None:
+    """Points in pinned host memory, read and written by the kernel over the host link, give
+    bitwise the results of the same points in device memory."""
+    params = _params()
+    host = uniform_points(batch, seed=41).pin_memory()
+    u, lap = fused_hoad.fused_forward_laplacian_host(host, params, version)
+    du, dlap = fused_forward_laplacian(host.cuda(), params, version)
+    torch.cuda.synchronize()
+    assert u.is_pinned() and lap.is_pinned()
+    assert torch.equal(u, du.cpu()) and torch.equal(lap, dlap.cpu())
+    out_u, out_l = torch.empty(batch, 1).pin_memory(), torch.empty(batch, 1).pin_memory()
+    fused_hoad.fused_forward_laplacian_host(host, params, version, out_u, out_l)
+    torch.cuda.synchronize()
+    assert torch.equal(out_u, u) and torch.equal(out_l, lap)
+    with pytest.raises(RuntimeError, match="pinned"):
+        fused_hoad.fused_forward_laplacian_host(uniform_points(8), params, version)
