@@ -40,7 +40,8 @@ NVCC_FLAGS = [
     f"-I{INCLUDE}",
 ]
 CU_SOURCES = [
-    "forward_fp32.cu", "forward_tc.cu", "backward_fp32.cu", "adam.cu", "capi.cu", "noalloc.cu",
+    "forward_fp32.cu", "forward_tc.cu", "backward_fp32.cu", "backward_tc.cu", "adam.cu",
+    "capi.cu", "noalloc.cu",
 ]
 
 

@@ -154,11 +154,12 @@ std::vector<torch::Tensor> fused_forward_laplacian_host(torch::Tensor coordinate
 std::vector<torch::Tensor> poisson_step_gradients(torch::Tensor coordinates,
                                                   torch::Tensor parameters,
                                                   int64_t total_points, bool want_laplacian,
-                                                  bool want_grad_coordinates) {
+                                                  bool want_grad_coordinates, int64_t version) {
   check_inputs(coordinates, parameters);
   const c10::cuda::CUDAGuard device_guard(coordinates.device());
   const int64_t batch = coordinates.size(0);
   TORCH_CHECK(total_points >= batch, "total_points must be >= the local batch");
+  TORCH_CHECK(version >= 1 && version <= 6, "backward version must be 1 to 6");
   auto grad_and_loss = torch::empty({kParameterCount + 1}, parameters.options());
   auto laplacian = want_laplacian ? torch::empty({batch, 1}, coordinates.options())
                                   : torch::empty({0}, coordinates.options());
@@ -171,7 +172,8 @@ std::vector<torch::Tensor> poisson_step_gradients(torch::Tensor coordinates,
                    total_points, out,
                    want_grad_coordinates ? grad_coordinates.data_ptr<float>() : nullptr,
                    want_laplacian ? laplacian.data_ptr<float>() : nullptr,
-                   out + kParameterCount, batch ? workspace.data_ptr<float>() : nullptr,
+                   out + kParameterCount, static_cast<int>(version),
+                   batch ? workspace.data_ptr<float>() : nullptr,
                    static_cast<size_t>(workspace.numel()) * sizeof(float),
                    at::cuda::getCurrentCUDAStream()),
                "poisson_step_gradients");
@@ -229,7 +231,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, module) {
              "Fused forward + interior Poisson loss + backward in one persistent kernel",
              pybind11::arg("coordinates"), pybind11::arg("parameters"),
              pybind11::arg("total_points"), pybind11::arg("want_laplacian") = false,
-             pybind11::arg("want_grad_coordinates") = false);
+             pybind11::arg("want_grad_coordinates") = false, pybind11::arg("version") = 6);
   module.def("adam_step", &adam_step, "Fused Adam over a flat parameter buffer",
              pybind11::arg("parameters"), pybind11::arg("grad"), pybind11::arg("exp_avg"),
              pybind11::arg("exp_avg_sq"), pybind11::arg("step"), pybind11::arg("lr"),

@@ -1,6 +1,7 @@
 // extern "C" entry points declared in include/fused_hoad_b200.h: argument validation,
 // one-time per-device set-up and dispatch onto the sm_100a kernels. No torch types, no
 // device allocation, no host synchronisation on the compute entry points.
+#include <algorithm>
 #include <mutex>
 
 #include "common.cuh"
@@ -46,7 +47,8 @@ int prepare_locked(int device) {
     if ((e = cudaGetSymbolAddress(reinterpret_cast<void**>(&info.status), g_status_word)) != cudaSuccess ||
         (e = fhb::prepare_forward_fp32()) != cudaSuccess ||
         (e = fhb::prepare_forward_tc()) != cudaSuccess ||
-        (e = fhb::prepare_backward_fp32()) != cudaSuccess) {
+        (e = fhb::prepare_backward_fp32()) != cudaSuccess ||
+        (e = fhb::prepare_backward_tc()) != cudaSuccess) {
       code = record(e);
       break;
     }
@@ -72,9 +74,13 @@ int current_device(const fhb::DeviceInfo** info) {
   return FHB_OK;
 }
 
+// Enough for either backward kernel: the FP32 one needs one partial row per CTA, the
+// tensor-core one also its pre-split weights and per-CTA scratch.
 size_t backward_workspace_bytes(int64_t n, const fhb::DeviceInfo& dev) {
   if (n <= 0) return 0;
-  return static_cast<size_t>(fhb::backward_grid(n, dev)) * fhb::kRowStride * sizeof(float);
+  const size_t fp32 =
+      static_cast<size_t>(fhb::backward_grid(n, dev)) * fhb::kRowStride * sizeof(float);
+  return std::max(fp32, fhb::backward_tc_workspace_bytes(n, dev));
 }
 
 bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
@@ -128,8 +134,8 @@ size_t fhb_backward_workspace_bytes(int64_t n) {
 static int backward_common(const float* coords, const float* params, const float* grad_u,
                            const float* grad_lap, float* grad_params, float* grad_coords,
                            float* lap_out, float* loss, int64_t n, int64_t n_total,
-                           bool poisson, void* workspace, size_t workspace_bytes,
-                           cudaStream_t stream) {
+                           bool poisson, bool tensor_core, void* workspace,
+                           size_t workspace_bytes, cudaStream_t stream) {
   if (n < 0 || !params || !grad_params) return FHB_ERR_INVALID_ARGUMENT;
   if (poisson && (!loss || n_total < n)) return FHB_ERR_INVALID_ARGUMENT;
   const fhb::DeviceInfo* dev = nullptr;
@@ -145,13 +151,21 @@ static int backward_common(const float* coords, const float* params, const float
   const size_t need = backward_workspace_bytes(n, *dev);
   if (workspace == nullptr || workspace_bytes < need) return FHB_ERR_WORKSPACE;
   if (!aligned(workspace, 16)) return FHB_ERR_MISALIGNED;
-  float* partials = static_cast<float*>(workspace);
-  cudaError_t e = fhb::launch_backward_fp32(coords, params, grad_u, grad_lap, grad_coords,
-                                            lap_out, partials, n, n_total, poisson, *dev,
-                                            stream);
-  if (e == cudaSuccess)
-    e = fhb::launch_reduce_rows(partials, fhb::backward_grid(n, *dev), grad_params,
-                                poisson ? loss : nullptr, stream);
+  float* ws = static_cast<float*>(workspace);
+  cudaError_t e;
+  if (tensor_core) {
+    e = fhb::launch_backward_tc(coords, params, grad_u, grad_lap, grad_coords, lap_out, ws, n,
+                                n_total, poisson, *dev, stream);
+    if (e == cudaSuccess)
+      e = fhb::launch_reduce_rows(fhb::backward_tc_partials(ws), fhb::backward_tc_grid(n, *dev),
+                                  grad_params, poisson ? loss : nullptr, stream);
+  } else {
+    e = fhb::launch_backward_fp32(coords, params, grad_u, grad_lap, grad_coords, lap_out, ws, n,
+                                  n_total, poisson, *dev, stream);
+    if (e == cudaSuccess)
+      e = fhb::launch_reduce_rows(ws, fhb::backward_grid(n, *dev), grad_params,
+                                  poisson ? loss : nullptr, stream);
+  }
   return record(e);
 }
 
@@ -161,15 +175,19 @@ int fhb_backward(const float* coords, const float* params, const float* grad_u,
   if (version < FHB_BACKWARD_VERSION_MIN || version > FHB_BACKWARD_VERSION_MAX)
     return FHB_ERR_INVALID_ARGUMENT;
   return backward_common(coords, params, grad_u, grad_lap, grad_params, grad_coords, nullptr,
-                         nullptr, n, n, false, workspace, workspace_bytes, stream);
+                         nullptr, n, n, false, version == FHB_BACKWARD_VERSION_TENSOR_CORE,
+                         workspace, workspace_bytes, stream);
 }
 
 int fhb_poisson_step_gradients(const float* coords, const float* params, int64_t n,
                                int64_t n_total, float* grad_params, float* grad_coords,
-                               float* lap_out, float* loss, void* workspace,
+                               float* lap_out, float* loss, int version, void* workspace,
                                size_t workspace_bytes, fhb_stream_t stream) {
+  if (version < FHB_BACKWARD_VERSION_MIN || version > FHB_BACKWARD_VERSION_MAX)
+    return FHB_ERR_INVALID_ARGUMENT;
   return backward_common(coords, params, nullptr, nullptr, grad_params, grad_coords, lap_out,
-                         loss, n, n_total, true, workspace, workspace_bytes, stream);
+                         loss, n, n_total, true, version == FHB_BACKWARD_VERSION_TENSOR_CORE,
+                         workspace, workspace_bytes, stream);
 }
 
 int fhb_adam_step(float* params, const float* grad, float* exp_avg, float* exp_avg_sq,

@@ -18,12 +18,12 @@
 //                  16 columns.
 //     The A operand lives in TMEM, not shared memory: with N = 64 an A tile read from
 //     shared memory would need ~1.5x the shared-memory bandwidth an SM has.
-//   * 16 warps: warp w serves TMEM lanes 32(w%4)..+31 (its quadrant) and neurons
-//     16(w/4)..+15. Per layer it loads its 4 x 16 accumulators (4 x tcgen05.ld.32x32b.x16),
+//   * 16 warps: warp w serves TMEM lanes 32(w%4)..+31 (its quadrant) and, with s = w/4,
+//     neurons 16a+4s+t. Per layer it loads its 4 x 16 accumulators (16 x tcgen05.ld.x4),
 //     applies the tanh jet in registers and writes TF32 hi/lo activations chunk by chunk
-//     into the ring (tcgen05.st) for the next layer. The K order is permuted (chunk j holds
-//     neurons 16s+4j+{0..3} for s = 0..3) so all 16 warps contribute to every chunk; the
-//     weights' K order is permuted to match;
+//     into the ring (tcgen05.st) for the next layer. Warp s owns the strided neurons
+//     16a+4s+{0..3} (a = 0..3), so chunk j (neurons 16j..16j+15, natural K order) gets 4
+//     neurons from every warp and all 16 warps contribute to every chunk;
 //   * the warp that completes a chunk last (an acq_rel counter per ring slot) issues its
 //     MMAs as a converged warp (elect.sync picks the issuing lane; issued from a divergent
 //     lane these small MMAs cost ~4x their execution time): 2 K steps x 4 components x 3
@@ -77,11 +77,6 @@ static_assert(kSmemUsed <= kSmemBytes, "shared memory layout overflow");
 // Canonical K-major no-swizzle layout of a [64 rows x 64 K] tf32 operand: 8x4 core
 // matrices of 128 B; K chunks of 4 at LBO = 128 B, 8-row groups at SBO = 2048 B.
 constexpr uint32_t kLbo = 128, kSbo = 2048;
-// K position k of a layer's input <-> input neuron: chunk j = k/16 holds neurons
-// 16s + 4j + t at position 4s + t (s = warp neuron block, t = 0..3).
-__device__ __forceinline__ int k_to_neuron(int k) {
-  return 16 * ((k & 15) >> 2) + 4 * (k >> 4) + (k & 3);
-}
 
 struct Ctx {
   uint8_t* smem;
@@ -226,7 +221,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int layer = idx >> 12, e = idx & 4095;
       const int row = ((e >> 9) << 3) | ((e >> 2) & 7);
       const int k = (((e >> 5) & 15) << 2) | (e & 3);
-      w[r] = params[kHiddenBase + layer * kHiddenStride + row * kWidth + k_to_neuron(k)];
+      w[r] = params[kHiddenBase + layer * kHiddenStride + row * kWidth + k];
     }
 #pragma unroll
     for (int r = 0; r < kPerThread; ++r) {
@@ -303,7 +298,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       float h[4][4];
 #pragma unroll
       for (int t = 0; t < 4; ++t) {
-        const int o = 16 * s + 4 * j + t;
+        const int o = 16 * j + 4 * s + t;
         const float w0 = small[kSmW0 + 2 * o], w1 = small[kSmW0 + 2 * o + 1];
         tanh_jet_fast(fmaf(w0, x0, fmaf(w1, x1, small[kSmB0 + o])), w0, w1, 0.0f, h[0][t],
                       h[1][t], h[2][t], h[3][t]);
@@ -314,13 +309,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int l = 0; ok && l < kHiddenGemms; ++l, ++mlayer) {
       if (!(ok = warp_wait(cx.dfull, mlayer & 1u, cx))) break;
       tc::fence_after_sync();
+      // d[c][4a + t] = component c of neuron 16a + 4s + t
       float d[4][16];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) tc::ld_x16(tmem_warp + 64u * c + 16u * s, d[c]);
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int a = 0; a < 4; ++a)
+          tc::ld_x4(tmem_warp + 64u * c + 16u * a + 4u * s,
+                    *reinterpret_cast<float(*)[4]>(&d[c][4 * a]));
       tc::wait_ld();
       const float* bias = small + kSmB + 64 * l;
 #pragma unroll
-      for (int i = 0; i < 16; ++i) d[0][i] += bias[16 * s + i];
+      for (int i = 0; i < 16; ++i) d[0][i] += bias[16 * (i >> 2) + 4 * s + (i & 3)];
 
       if (l + 1 < kHiddenGemms) {
 #pragma unroll
@@ -341,7 +341,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int i = 0; i < 16; ++i) {
           float v, j0, j1, lv;
           tanh_jet_fast(d[0][i], d[1][i], d[2][i], d[3][i], v, j0, j1, lv);
-          const float w = small[kSmWout + 16 * s + i];
+          const float w = small[kSmWout + 16 * (i >> 2) + 4 * s + (i & 3)];
           pu = fmaf(w, v, pu);
           pl = fmaf(w, lv, pl);
         }

@@ -42,6 +42,17 @@ cudaError_t launch_backward_fp32(const float* coords, const float* params,
 cudaError_t launch_reduce_rows(const float* partials, int rows, float* grad_params,
                                float* loss, cudaStream_t stream);
 
+// ---- backward_tc.cu ----
+cudaError_t prepare_backward_tc();
+int backward_tc_grid(int64_t n, const DeviceInfo& dev);
+// Workspace: pre-split weights, one partial-gradient row per CTA, per-CTA L2 scratch.
+size_t backward_tc_workspace_bytes(int64_t n, const DeviceInfo& dev);
+float* backward_tc_partials(float* workspace);
+cudaError_t launch_backward_tc(const float* coords, const float* params, const float* grad_u,
+                               const float* grad_lap, float* grad_coords, float* lap_out,
+                               float* workspace, int64_t n, int64_t n_total, bool poisson,
+                               const DeviceInfo& dev, cudaStream_t stream);
+
 // ---- adam.cu ----
 cudaError_t launch_adam(float* params, const float* grad, float* exp_avg, float* exp_avg_sq,
                         int64_t count, int64_t* step, float lr, float beta1, float beta2,

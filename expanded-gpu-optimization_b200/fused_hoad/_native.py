@@ -29,7 +29,7 @@ _SIGNATURES: dict[str, tuple[object, list]] = {
     "fhb_backward_noalloc": (ctypes.c_int, [_p, _p, _p, _p, _p, _p, _i64, _p]),
     "fhb_poisson_step_gradients": (
         ctypes.c_int,
-        [_p, _p, _i64, _i64, _p, _p, _p, _p, _p, ctypes.c_size_t, _p],
+        [_p, _p, _i64, _i64, _p, _p, _p, _p, ctypes.c_int, _p, ctypes.c_size_t, _p],
     ),
     "fhb_adam_step": (
         ctypes.c_int,

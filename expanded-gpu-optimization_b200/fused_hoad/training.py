@@ -73,7 +73,8 @@ class PoissonTrainer:
     ``parameters`` is either the packed 12,737-float CUDA buffer (used in place) or the
     Poisson ``nn.Module``, which is packed once and rebound to views of the buffer.
     With an initialised process group every rank must call :meth:`step` with its own
-    shard and the same ``total_points``.
+    shard and the same ``total_points``. ``backward_version`` 6 (default) runs the
+    tensor-core step kernel, 1..5 the FP32 CUDA-core one.
     """
 
     def __init__(
@@ -84,6 +85,7 @@ class PoissonTrainer:
         betas: tuple[float, float] = (0.9, 0.999),
         eps: float = 1e-8,
         group=None,
+        backward_version: int = 6,
     ) -> None:
         self._C = load_extension()
         if isinstance(parameters, nn.Module):
@@ -101,11 +103,16 @@ class PoissonTrainer:
         self.step_count = torch.zeros(1, dtype=torch.int64, device=flat.device)
         self.lr, self.betas, self.eps = float(lr), (float(betas[0]), float(betas[1])), float(eps)
         self.group = group
+        if not 1 <= backward_version <= 6:
+            raise ValueError("backward_version must be 1 to 6")
+        self.backward_version = int(backward_version)
         self._C.prepare_device(flat.device.index if flat.device.index is not None else 0)
 
     def gradients(self, coordinates: Tensor, total_points: int) -> Tensor:
         """Flat ``[12738]`` buffer: the gradient summed over ranks, then the loss."""
-        out, _, _ = self._C.poisson_step_gradients(coordinates, self.params, total_points)
+        out, _, _ = self._C.poisson_step_gradients(
+            coordinates, self.params, total_points, version=self.backward_version
+        )
         return allreduce_sum_(out, self.group)
 
     def step(self, coordinates: Tensor, total_points: int | None = None) -> Tensor:

@@ -48,6 +48,10 @@ typedef struct CUstream_st* fhb_stream_t;
 /* Backward versions accepted for drop-in compatibility (reference csrc/bindings.cpp:45). */
 #define FHB_BACKWARD_VERSION_MIN 1
 #define FHB_BACKWARD_VERSION_MAX 6
+/* Backward versions 1..5 run the FP32 CUDA-core adjoint kernel; 6 (the reference's default)
+ * runs the tensor-core one (3xTF32 tcgen05 forward recompute and input adjoint, FP32 weight
+ * gradient). Both reduce in a fixed order. */
+#define FHB_BACKWARD_VERSION_TENSOR_CORE 6
 
 const char* fhb_status_string(int code);
 /* Last CUDA runtime error seen by this library on the calling thread (cudaError_t). */
@@ -74,8 +78,10 @@ int fhb_forward(const float* coords, const float* params, float* u, float* lap, 
                 int version, fhb_stream_t stream);
 
 /*
- * Workspace the backward needs for n points on the current device, in bytes (0 for n==0).
- * It holds one partial-gradient row per CTA of the persistent grid.
+ * Workspace the backward needs for n points on the current device, in bytes (0 for n==0),
+ * enough for every backward version: one partial-gradient row per CTA of the persistent
+ * grid, and for the tensor-core kernel also the pre-split weights (192 KB) and 512 KB of
+ * per-CTA scratch that stays in L2 (about 84 MB on a 148-SM B200 from 18,944 points up).
  */
 size_t fhb_backward_workspace_bytes(int64_t n);
 
@@ -86,8 +92,9 @@ size_t fhb_backward_workspace_bytes(int64_t n);
  * behind fused_hoad._C.fused_forward_laplacian_backward (csrc/bindings.cpp:42-54).
  * grad_u may be NULL (treated as zeros); grad_coords may be NULL (not written).
  * The reduction over points has a fixed order: results are bitwise reproducible for a
- * given n and device. n == 0 writes zeros to grad_params. All versions 1..6 run the same
- * kernel. Workspace: fhb_backward_workspace_bytes(n) bytes, 16-byte aligned.
+ * given n, version and device. n == 0 writes zeros to grad_params. Versions 1..5 run the
+ * FP32 CUDA-core kernel, 6 the tensor-core kernel (FHB_BACKWARD_VERSION_TENSOR_CORE).
+ * Workspace: fhb_backward_workspace_bytes(n) bytes, 16-byte aligned.
  */
 int fhb_backward(const float* coords, const float* params, const float* grad_u,
                  const float* grad_lap, float* grad_params, float* grad_coords, int64_t n,
@@ -119,11 +126,12 @@ int fhb_backward_noalloc(const float* coords, const float* params, const float* 
  * runs the adjoint sweep, so no separate forward launch is needed. Writes grad_params[12737]
  * (this shard's contribution; n_total >= n lets data-parallel shards sum to the global
  * gradient), *loss (this shard's contribution, device scalar), optionally lap_out[n] and
- * grad_coords[n][2] (either may be NULL). Workspace as for fhb_backward.
+ * grad_coords[n][2] (either may be NULL). `version` picks the kernel as for fhb_backward
+ * (6: tensor cores). Workspace as for fhb_backward.
  */
 int fhb_poisson_step_gradients(const float* coords, const float* params, int64_t n,
                                int64_t n_total, float* grad_params, float* grad_coords,
-                               float* lap_out, float* loss, void* workspace,
+                               float* lap_out, float* loss, int version, void* workspace,
                                size_t workspace_bytes, fhb_stream_t stream);
 
 /*

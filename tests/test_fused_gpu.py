@@ -183,7 +183,9 @@ def test_inference_path_stays_out_of_autograd() -> None:
 
 # ---------------------------------------------------------------- backward ----
 
-BACKWARD_BATCHES = [1, 15, 16, 17, 31, 32, 33, 1_000, 65_536]
+BACKWARD_BATCHES = [1, 15, 16, 17, 31, 32, 33, 127, 128, 129, 1_000, 65_536]
+# Backward kernels: 5 = FP32 CUDA-core kernel (versions 1..5), 6 = tensor-core kernel.
+BACKWARD_KERNELS = [pytest.param(5, id="fp32"), pytest.param(6, id="tc")]
 
 
 def _upstream(batch: int, seed: int = 2):
@@ -203,10 +205,11 @@ def _backward_pair(batch: int, route: str, scale: float = 1.0, seed: int = 0, ve
     return actual, expected
 
 
+@pytest.mark.parametrize("kernel", BACKWARD_KERNELS)
 @pytest.mark.parametrize("route", ROUTES)
 @pytest.mark.parametrize("batch", BACKWARD_BATCHES)
-def test_backward_matches_oracle(batch: int, route: str) -> None:
-    (gp, gx), (ep, ex) = _backward_pair(batch, route)
+def test_backward_matches_oracle(batch: int, route: str, kernel: int) -> None:
+    (gp, gx), (ep, ex) = _backward_pair(batch, route, version=kernel)
     assert_scaled(gp.cpu(), ep, 1e-4, "grad params")
     assert_scaled(gx.cpu(), ex, 1e-4, "grad coords")
 
@@ -217,45 +220,63 @@ def test_backward_every_version_number_is_accepted(version: int) -> None:
     assert_scaled(gp.cpu(), ep, 1e-4, "grad params")
 
 
-def test_backward_saturated_tanh() -> None:
-    (gp, gx), (ep, ex) = _backward_pair(4_096, "capi", scale=3.0, seed=1)
+@pytest.mark.parametrize("kernel", BACKWARD_KERNELS)
+def test_backward_saturated_tanh(kernel: int) -> None:
+    (gp, gx), (ep, ex) = _backward_pair(4_096, "capi", scale=3.0, seed=1, version=kernel)
     assert_scaled(gp.cpu(), ep, 1e-4, "grad params")
     assert_scaled(gx.cpu(), ex, 1e-4, "grad coords")
 
 
-def test_backward_per_parameter_block() -> None:
-    (gp, _), (ep, _) = _backward_pair(2_048, "torch")
+@pytest.mark.parametrize("kernel", BACKWARD_KERNELS)
+def test_backward_per_parameter_block(kernel: int) -> None:
+    (gp, _), (ep, _) = _backward_pair(2_048, "torch", version=kernel)
     actual = fused_hoad.unpack_poisson_parameters(gp.cpu())
     expected = fused_hoad.unpack_poisson_parameters(ep)
     for name, want in expected.items():
         assert_scaled(actual[name], want, 1e-4, name)
 
 
-def test_backward_against_reference_golden(golden) -> None:
+@pytest.mark.parametrize("kernel", BACKWARD_KERNELS)
+def test_backward_against_reference_golden(golden, kernel: int) -> None:
     params = torch.from_numpy(golden["params_seed0"]).cuda()
     for n in (1, 15, 16, 17, 33, 1000):
         coords = torch.from_numpy(golden[f"bwd{n}_x"]).cuda()
         gu = torch.from_numpy(golden[f"bwd{n}_gu"]).cuda()
         gl = torch.from_numpy(golden[f"bwd{n}_gl"]).cuda()
-        gp, gx = fused_forward_laplacian_backward(coords, params, gu, gl)
+        gp, gx = fused_forward_laplacian_backward(coords, params, gu, gl, kernel)
         assert_scaled(gp.cpu(), golden[f"bwd{n}_gp32"], 1e-4, f"grad params n={n}")
         assert_scaled(gx.cpu(), golden[f"bwd{n}_gx32"], 1e-4, f"grad coords n={n}")
     params = torch.from_numpy(golden["params_seed1_x3"]).cuda()
     gp, gx = fused_forward_laplacian_backward(
         torch.from_numpy(golden["satbwd_x"]).cuda(), params,
         torch.from_numpy(golden["satbwd_gu"]).cuda(), torch.from_numpy(golden["satbwd_gl"]).cuda(),
+        kernel,
     )
     assert_scaled(gp.cpu(), golden["satbwd_gp64"], 1e-4, "saturated grad params")
     assert_scaled(gx.cpu(), golden["satbwd_gx64"], 1e-4, "saturated grad coords")
 
 
-def test_backward_is_bitwise_reproducible() -> None:
+@pytest.mark.parametrize("kernel", BACKWARD_KERNELS)
+def test_backward_is_bitwise_reproducible(kernel: int) -> None:
     params = _params()
     coords = uniform_points(65_536, seed=9).cuda()
     gu, gl = (t.cuda() for t in _upstream(65_536))
-    a = fused_forward_laplacian_backward(coords, params, gu, gl)
-    b = fused_forward_laplacian_backward(coords, params, gu, gl)
+    a = fused_forward_laplacian_backward(coords, params, gu, gl, kernel)
+    b = fused_forward_laplacian_backward(coords, params, gu, gl, kernel)
     assert torch.equal(a[0], b[0]) and torch.equal(a[1], b[1])
+
+
+@pytest.mark.parametrize("batch", [129, 65_536, 300_000])
+def test_backward_kernels_agree(batch: int) -> None:
+    """The tensor-core and FP32 kernels agree far inside the oracle tolerance; 300,000
+    points give every CTA of the persistent grid several tiles and a ragged last tile."""
+    params = _params()
+    coords = uniform_points(batch, seed=14).cuda()
+    gu, gl = (t.cuda() for t in _upstream(batch, seed=5))
+    fp, fx = fused_forward_laplacian_backward(coords, params, gu, gl, 5)
+    tp, tx = fused_forward_laplacian_backward(coords, params, gu, gl, 6)
+    assert_scaled(tp.cpu(), fp.cpu(), 2e-5, "grad params")
+    assert_scaled(tx.cpu(), fx.cpu(), 2e-5, "grad coords")
 
 
 def test_backward_empty_batch() -> None:
@@ -355,12 +376,13 @@ def test_cuda_graph_training_step_matches_eager_step() -> None:
 
 # ------------------------------------------------------- fused Poisson step ----
 
-@pytest.mark.parametrize("batch", [1, 33, 1_000, 65_536])
-def test_poisson_step_gradients_match_oracle(batch: int) -> None:
+@pytest.mark.parametrize("kernel", BACKWARD_KERNELS)
+@pytest.mark.parametrize("batch", [1, 33, 129, 1_000, 65_536])
+def test_poisson_step_gradients_match_oracle(batch: int, kernel: int) -> None:
     params = _params()
     coords = uniform_points(batch, seed=12).cuda()
     out, lap, gx = fused_hoad.load_extension().poisson_step_gradients(
-        coords, params, batch, True, True
+        coords, params, batch, True, True, kernel
     )
     loss, gp, ex = jet.poisson_step_gradients(params.cpu(), coords.cpu())
     assert_scaled(out[:-1].cpu(), gp, 1e-4, "grad params")
@@ -370,26 +392,29 @@ def test_poisson_step_gradients_match_oracle(batch: int) -> None:
     torch.testing.assert_close(lap.cpu(), el, atol=1e-5, rtol=1e-4)
 
 
-def test_poisson_shard_gradients_sum_to_full_batch() -> None:
+@pytest.mark.parametrize("kernel", BACKWARD_KERNELS)
+def test_poisson_shard_gradients_sum_to_full_batch(kernel: int) -> None:
     """Data-parallel property on one GPU: shards with the global count sum to the full step."""
     params = _params()
     total = 100_000
     coords = uniform_points(total, seed=13).cuda()
     C = fused_hoad.load_extension()
-    full = C.poisson_step_gradients(coords, params, total)[0]
+    full = C.poisson_step_gradients(coords, params, total, version=kernel)[0]
     parts = torch.zeros_like(full)
     for r in range(4):
         a, b = fused_hoad.shard_range(total, r, 4)
-        parts += C.poisson_step_gradients(coords[a:b].contiguous(), params, total)[0]
+        parts += C.poisson_step_gradients(coords[a:b].contiguous(), params, total,
+                                          version=kernel)[0]
     assert_scaled(parts[:-1].cpu(), full[:-1].cpu(), 1e-5, "grad")
     torch.testing.assert_close(parts[-1].cpu(), full[-1].cpu(), rtol=1e-5, atol=0)
 
 
-def test_trainer_matches_reference_adam_trajectory(golden) -> None:
+@pytest.mark.parametrize("kernel", BACKWARD_KERNELS)
+def test_trainer_matches_reference_adam_trajectory(golden, kernel: int) -> None:
     """PoissonTrainer (fused step + fused Adam) vs the reference's torch.optim.Adam run."""
     params = torch.from_numpy(golden["params_seed0"]).cuda().clone()
     coords = torch.from_numpy(golden["adam_x"]).cuda()
-    trainer = fused_hoad.PoissonTrainer(params)
+    trainer = fused_hoad.PoissonTrainer(params, backward_version=kernel)
     losses = [trainer.step(coords).item() for _ in range(len(golden["adam_losses"]))]
     np.testing.assert_allclose(losses, golden["adam_losses"], rtol=1e-4)
     # Adam normalises each gradient element, so an element whose gradient is at rounding
