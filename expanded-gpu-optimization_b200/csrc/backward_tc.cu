@@ -2,40 +2,39 @@
 //
 // Math: the reverse pass of the reference backward (csrc/fused_backward.cu:15-33 adjoint
 // formulas, :208-233 output seed, :262-321 weight gradient and input adjoint, :324-359 layer
-// 0), on 128-point tiles with the two per-point contractions on the tensor cores:
-//   * forward recompute Z_l = H_{l-1} W_l^T (the forward kernel's 3xTF32 tcgen05 GEMMs);
-//   * input adjoint Hbar_{l-1} = Zbar_l W_l, also a 3xTF32 tcgen05 GEMM (M = 128 points,
-//     N = 64, K = 64) whose B operand is W_l^T;
-// and the third, dW_l = sum over points and jet components of zbar_l (x) h_{l-1}, on the
-// FP32 CUDA cores (a reduction over points: its operands would have to be transposed into
-// shared memory for the tensor core, and shared memory is full).
+// 0), on 128-point tiles with all three per-layer contractions on the tensor cores, each in
+// 3xTF32 split precision (x = hi + lo, error ~2^-21 |x|):
+//   * forward recompute  Z_l[128 x 64] = H_{l-1} W_l^T   (as the forward kernel: A = H in
+//     TMEM, B = W_l in shared memory, M = 128 points, N = 64, K = 64 per component);
+//   * input adjoint      Hbar_{l-1} = Zbar_l W_l           (A = Zbar in TMEM, B = W_l^T);
+//   * weight gradient    dW_l[64 x 64] = sum over points and components of zbar h^T, as
+//     M = 128 rows (zbar_hi rows 0..63, zbar_lo rows 64..127) x N = 64 x K = points, with
+//     B = h_hi then h_lo, so one pair of MMAs gives all four hi/lo products. A and B are
+//     written by the threads straight from registers into two shared-memory staging
+//     buffers (128-byte-swizzled K-major: a warp writes 32 consecutive points of one row,
+//     conflict-free), one per point half, one jet component at a time.
 //
 // Where the data lives (one CTA per SM, persistent over tiles):
-//   * TMEM exactly as in the forward kernel: accumulators D_c at columns 64c..64c+63, a ring
-//     of two A-operand chunks (16 K positions x 4 components x hi/lo) at [256, 512);
-//   * shared memory: three weight slots (hi + lo, 32 KB each). A slot holds W_l for the
-//     forward GEMM and W_l^T for the backward one: both are K-major B operands (the
-//     tensor core's MN-major tf32 operand form is not used). A one-thread bulk copy reloads
-//     a slot from a pre-split global copy of all six operands as soon as the GEMM that
-//     used it has completed, long before the next GEMM needs it;
-//   * per-CTA scratch in global memory, small enough to stay in L2 (512 KB per CTA): the
-//     activations h_0, h_1, h_2 written during the forward recompute and zbar_l of the
-//     current layer, as [component][point half][neuron][64 points] planes whose 16-byte
-//     point groups are XOR-swizzled by neuron (conflict-free shared-memory reads after a
-//     plain bulk copy). The adjoint reads its own h values back from there; the weight
-//     gradient stages (component, point-half) planes of zbar and h through two 32 KB
-//     shared-memory buffers filled by bulk copies one round ahead;
-//   * registers: per thread one point (TMEM lane) and 16 neurons 16a+4s+t, as in the
-//     forward kernel; 8 weight-gradient entries per layer, folded into a shared-memory
-//     accumulator at the end of every layer of every tile.
-// The adjoint is written in terms of the stored activation h = (a, a'z_J, L-part) rather
-// than the pre-activation: with s = 1 - a^2 it needs a, s, h_J and h_L only, the same
-// quantities the forward produced, so nothing else is stored.
-// Reductions over points are in a fixed order (warp butterflies, then quadrants in index
-// order, then tiles in loop order, then one partial row per CTA summed in row order), so
-// results are bitwise reproducible for a given grid. Every wait is bounded; a wait that
-// gives up sets the CTA abort flag, the warps leave together at the next block-wide
-// barrier, and TMEM is freed.
+//   * TMEM: accumulators D_c at columns 64c..64c+63 and a ring of two A-operand chunks at
+//     [256, 512), as in the forward kernel. The weight-gradient accumulator borrows ring
+//     columns [256, 320) while the ring is idle (after the input-adjoint GEMM of the layer
+//     has completed, before the next layer's chunks) and is emptied every layer;
+//   * shared memory: two weight slots (hi + lo, 32 KB each), the six operands of a tile's
+//     GEMMs (W1, W2, W3, then W3^T, W2^T, W1^T; all K-major) taking turns: a one-thread bulk
+//     copy reloads a slot from a pre-split global copy as soon as the GEMM that used it has
+//     completed, two GEMMs before the slot is needed again;
+//   * per-CTA scratch in global memory, 256 KB per CTA so it stays in L2: h_1 and h_2 of the
+//     tile, written during the forward recompute in a thread-private coalesced layout and
+//     read back by the same thread for the adjoint and the weight-gradient staging (h_0 is
+//     recomputed from the point);
+//   * registers: per thread one point (TMEM lane) and the 16 neurons 16a+4s+t.
+// The adjoint is written in terms of the stored activation h = (a, s z_J, s z_L - 2as|z_J|^2)
+// with s = 1 - a^2, the quantities the forward produced, so no pre-activation is stored.
+// Gradients are accumulated in a fixed order (warp butterflies, quadrants and tiles in
+// index order, the tensor core's own order for the weight gradient, one partial row per CTA
+// summed in row order), so results are bitwise reproducible for a given grid. Every wait
+// is bounded; a wait that gives up sets the CTA abort flag, the warps leave together at
+// the next block-wide barrier, and TMEM is freed.
 #include <algorithm>
 
 #include "common.cuh"
@@ -55,44 +54,51 @@ constexpr int kRing = 2;
 constexpr uint32_t kSlotCols = 128;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kRingCol = 256;
+constexpr uint32_t kDwCol = kRingCol;            // weight-gradient accumulator (borrowed)
 constexpr uint32_t kIdesc = tc::idesc_tf32(128, 64);
 constexpr uint32_t kLbo = 128, kSbo = 2048;      // K-major no-swizzle canonical operand
 
 constexpr int kOperandBytes = kWidth * kWidth * 4;   // 16 KB
 constexpr int kLayerBytes = 2 * kOperandBytes;       // hi + lo
 constexpr int kWeightBlocks = 6;                     // W1, W2, W3, W1^T, W2^T, W3^T
+constexpr int kWeightSlots = 2;
 
-// Scratch planes (floats): [component 4][half 2][neuron 64][point 64 + 1 pad]. The pad
-// makes rows 8 apart 8 banks apart, so the weight-gradient reads are conflict-free.
-constexpr int kRowFloats = 65;
-constexpr int kPlaneFloats = kWidth * kRowFloats;
-constexpr int kJetFloats = 4 * 2 * kPlaneFloats;     // one activation jet of a tile: 128 KB
-constexpr int kScratchJets = 4;                      // h0, h1, h2, zbar
+// Per-CTA scratch (floats): h_1 and h_2 as [jet 2][component 4][neuron slot 16][thread 512];
+// neuron slot 4a + t of thread (warp 4s + q, lane) is neuron 16a + 4s + t of its point.
+constexpr int kScratchFloats = 2 * 4 * 16 * kThreads;
+
+// Weight-gradient staging buffer (one per point half): A = [zbar_hi; zbar_lo] (128 rows x 64
+// points) and B_hi, B_lo = h_hi, h_lo (64 rows x 64 points), 128-byte-swizzled K-major: a K
+// atom is 32 points, rows in 8-row groups of 1024 bytes.
+constexpr int kStageA = 0, kStageBhi = 32768, kStageBlo = 49152;
+constexpr int kStageBytes = 65536;
+constexpr int kFlushStride = 65;                 // [128 rows][65] floats when emptying TMEM
 
 // Shared memory (bytes).
-constexpr int kWOff = 0;                                  // 3 weight slots
-constexpr int kStageOff = 3 * kLayerBytes;                // 2 x (zbar plane, h plane)
-constexpr int kStageBytes = 2 * kPlaneFloats * 4;         // 32.5 KB
-constexpr int kAccOff = kStageOff + 2 * kStageBytes;      // dW accumulators [3][8][512]
-constexpr int kSmallOff = kAccOff + 3 * 8 * kThreads * 4; // parameters for elementwise work
+constexpr int kWOff = 0;                                      // 2 weight slots
+constexpr int kStageOff = kWeightSlots * kLayerBytes;         // 2 staging buffers
+constexpr int kSmallOff = kStageOff + 2 * kStageBytes;        // parameters (elementwise)
 constexpr int kSmW0 = 0, kSmB0 = 128, kSmB = 192, kSmWout = 384, kSmBout = 448;
 constexpr int kSmallFloats = 512;
-constexpr int kGradOff = kSmallOff + kSmallFloats * 4;    // small-gradient accumulators
+constexpr int kGradOff = kSmallOff + kSmallFloats * 4;        // small-gradient accumulators
 constexpr int kGW0 = 0, kGBias = 128, kGWout = 384, kGBout = 448, kGLoss = 449;
 constexpr int kGradFloats = 512;
-constexpr int kRedOff = kGradOff + kGradFloats * 4;       // [8][128]: output sums, dx
-constexpr int kPartOff = kRedOff + 8 * kTile * 4;         // per-quadrant partials
-constexpr int kPWout = 0, kPB0 = 256, kPW0x = 512, kPW0y = 768, kPLoss = 1024, kPBout = 1028;
-constexpr int kPartFloats = 1032;
-constexpr int kXsOff = kPartOff + kPartFloats * 4;        // the tile's points: x[512], y[512]
-constexpr int kBarOff = kXsOff + 2 * kThreads * 4;        // empty[2] dfull red wfull[3] stage[2]
-constexpr int kNumBars = 9;
+constexpr int kRedOff = kGradOff + kGradFloats * 4;           // [8][128]: output sums, dx
+constexpr int kPartOff = kRedOff + 8 * kTile * 4;             // per-quadrant partials [q][64]
+// kinds: 0 w_out, 1 b0, 2 W0[:,0], 3 W0[:,1], 4..6 b1..b3
+constexpr int kPartKinds = 7;
+constexpr int kPLoss = kPartKinds * 256, kPBout = kPLoss + 4;
+constexpr int kPartFloats = kPBout + 4;
+constexpr int kXsOff = kPartOff + kPartFloats * 4;            // the tile's points x[512], y[512]
+constexpr int kBarOff = kXsOff + 2 * kThreads * 4;            // mbarriers
+constexpr int kNumBars = 7;    // empty[2] dfull red wfull[2] dwdone
 constexpr int kCountOff = kBarOff + kNumBars * 8;
-constexpr int kMiscOff = kCountOff + 4 * 4;               // TMEM base, abort flag
+constexpr int kMiscOff = kCountOff + 4 * 4;                   // TMEM base, abort flag, status
 constexpr int kSmemBytes = kMiscOff + 16;
 static_assert(kSmemBytes <= 227 * 1024, "shared memory layout overflow");
-static_assert(kStageOff % 1024 == 0 && kAccOff % 16 == 0 && kBarOff % 8 == 0, "alignment");
-static_assert((kPlaneFloats * 4) % 16 == 0, "bulk copies move whole 16-byte units");
+static_assert(kStageOff % 1024 == 0 && kBarOff % 8 == 0 && (kMiscOff + 8) % 8 == 0,
+              "alignment");
+static_assert(kTile * kFlushStride * 4 <= kStageBytes, "flush buffer fits a staging buffer");
 
 // Shared-memory objects are addressed as constant offsets of the dynamic shared-memory base
 // (no pointers kept in registers across the tile loop).
@@ -107,7 +113,7 @@ __device__ __forceinline__ uint64_t* bar_empty(uint32_t r) { return bar_at(stati
 __device__ __forceinline__ uint64_t* bar_dfull() { return bar_at(kRing); }
 __device__ __forceinline__ uint64_t* bar_red() { return bar_at(kRing + 1); }
 __device__ __forceinline__ uint64_t* bar_wfull(int k) { return bar_at(kRing + 2 + k); }
-__device__ __forceinline__ uint64_t* bar_stage(int b) { return bar_at(kRing + 5 + b); }
+__device__ __forceinline__ uint64_t* bar_dwdone() { return bar_at(kRing + 4); }
 __device__ __forceinline__ uint32_t* ring_count(uint32_t r) {
   return reinterpret_cast<uint32_t*>(dsmem() + kCountOff) + r;
 }
@@ -122,7 +128,7 @@ struct Ctx {
   uint32_t tmem;
 };
 
-__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, const Ctx& cx) {
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t start = global_timer_ns();
   while (true) {
@@ -137,8 +143,8 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, co
 }
 
 // Warp-uniform bounded wait (the tcgen05 ld/st and elect.sync after it need the whole warp).
-__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, const Ctx& cx) {
-  return __all_sync(0xffffffffu, wait_or_abort(bar, parity, cx) ? 1 : 0) != 0;
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
+  return __all_sync(0xffffffffu, wait_or_abort(bar, parity) ? 1 : 0) != 0;
 }
 
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
@@ -154,13 +160,8 @@ __device__ __forceinline__ uint32_t count_contribution(uint32_t* counter) {
   return old;
 }
 
-// Generic-proxy global writes of this thread -> visible to later bulk copies (async proxy).
-__device__ __forceinline__ void fence_proxy_async_global() {
-  asm volatile("fence.proxy.async.global;" ::: "memory");
-}
-
 // Block-wide barrier that also tells every warp whether any warp has aborted.
-__device__ __forceinline__ bool barrier_ok(const Ctx& cx) {
+__device__ __forceinline__ bool barrier_ok() {
   return __syncthreads_or(*abort_flag() != 0u ? 1 : 0) == 0;
 }
 
@@ -169,15 +170,26 @@ __device__ __forceinline__ void split_tf32(float x, uint32_t& hi, uint32_t& lo) 
   lo = __float_as_uint(x - __uint_as_float(hi));
 }
 
-// Weight slot used by GEMM g of a tile and the parity of the slot load it needs: slot l-1
-// holds W_l (forward GEMM g = l-1, even load) then W_l^T (backward GEMM g = 6-l, odd load).
-__device__ __forceinline__ int weight_slot(int g) { return g < 3 ? g : 5 - g; }
+// GEMM g of a tile (0..2: forward with W1..W3, 3..5: input adjoint with W3^T, W2^T, W1^T)
+// reads weight slot g % 2. A slot serves GEMMs g, g+2, g+4 of every tile, so GEMM g of the
+// tile with index t (counted per CTA) needs the slot's load number 3t + g/2.
+__device__ __forceinline__ int weight_block(int g) { return g < 3 ? g : 8 - g; }
+__device__ __forceinline__ uint32_t weight_parity(uint32_t tile_index, int g) {
+  return (3u * tile_index + static_cast<uint32_t>(g >> 1)) & 1u;
+}
+
+__device__ __forceinline__ void load_weight_slot(int slot, const float* wsplit, int block) {
+  mbar_arrive_expect_tx(bar_wfull(slot), kLayerBytes);
+  bulk_copy_g2s(dsmem() + kWOff + slot * kLayerBytes, wsplit + block * (kLayerBytes / 4),
+                kLayerBytes, bar_wfull(slot));
+}
 
 // The 24 MMAs of chunk j of GEMM g (A from ring slot `slot`); the first chunk of a GEMM
 // first waits for its weight slot. False if that wait gave up (nothing is issued).
-__device__ __forceinline__ bool issue_chunk_mmas(const Ctx& cx, int g, int j, uint32_t slot) {
-  const int ws = weight_slot(g);
-  if (j == 0 && !warp_wait(bar_wfull(ws), g >= 3 ? 1u : 0u, cx)) return false;
+__device__ __forceinline__ bool issue_chunk_mmas(const Ctx& cx, uint32_t tile_index, int g,
+                                                 int j, uint32_t slot) {
+  const int ws = g & 1;
+  if (j == 0 && !warp_wait(bar_wfull(ws), weight_parity(tile_index, g))) return false;
   tc::fence_after_sync();
 #pragma unroll
   for (int kk = 0; kk < 2; ++kk) {
@@ -204,7 +216,7 @@ __device__ __forceinline__ bool issue_chunk_mmas(const Ctx& cx, int g, int j, ui
 __device__ __forceinline__ bool produce_chunk(uint32_t n, const float (&h)[4][4],
                                               uint32_t tmem_warp, int s, const Ctx& cx) {
   const uint32_t slot = n % kRing;
-  if (!warp_wait(bar_empty(slot), ((n / kRing) & 1u) ^ 1u, cx)) return false;
+  if (!warp_wait(bar_empty(slot), ((n / kRing) & 1u) ^ 1u)) return false;
   tc::fence_after_sync();
   const uint32_t base = tmem_warp + kRingCol + kSlotCols * slot + 4u * s;
 #pragma unroll
@@ -225,7 +237,7 @@ __device__ __forceinline__ bool produce_chunk(uint32_t n, const float (&h)[4][4]
   if (last) {
     tc::fence_after_sync();
     const uint32_t in_tile = n % kChunksPerTile;
-    ok = issue_chunk_mmas(cx, static_cast<int>(in_tile / kChunks),
+    ok = issue_chunk_mmas(cx, n / kChunksPerTile, static_cast<int>(in_tile / kChunks),
                           static_cast<int>(in_tile % kChunks), slot);
     __syncwarp();
   }
@@ -234,7 +246,7 @@ __device__ __forceinline__ bool produce_chunk(uint32_t n, const float (&h)[4][4]
 
 // Adjoint of the tanh jet in terms of the activation it produced. With h = (a, h_J0, h_J1,
 // h_L), s = 1 - a^2 and the upstream adjoint (gv, g0, g1, gl) of h, the pre-activation
-// adjoint is (same formulas as tanh_jet_adjoint after substituting h_J = s z_J and
+// adjoint is (tanh_jet_adjoint's formulas after substituting h_J = s z_J and
 // h_L = s z_L - 2 a s |z_J|^2):
 //   zbar_v = gv s - 2 a (g . h_J) - 2 gl (a h_L + |h_J|^2)
 //   zbar_Jd = gd s - 4 a gl h_Jd,   zbar_L = gl s.
@@ -253,86 +265,28 @@ __device__ __forceinline__ void adjoint_h(float a, float hj0, float hj1, float h
   g1 = z1;
 }
 
-// One weight-gradient round over a staged (component, point-half) plane pair. Thread
-// (warp w, lane) owns the 8x8 block o = o0 + jj, i = i0 + kk (o0 = 8*(w>>1),
-// i0 = 8*(4*(w&1) + lane/8)) and the interleaved point slice p = sl + 8m (sl = lane%8,
-// m < 8) of the plane's 64 points: acc[jj][kk] += zbar[o][p] h[i][p]. Per point a warp
-// reads 8 consecutive words of one zbar row (broadcast to the 4 blocks) and of 4 h rows 8
-// apart, which the 65-float row stride puts 8 banks apart. kBias: also sum zbar into db.
-template <bool kBias>
-__device__ __forceinline__ void dw_round(const float* __restrict__ zs,
-                                         const float* __restrict__ hs, int o0, int i0,
-                                         int sl, float (&acc)[8][8], float (&db)[8]) {
-  const float* zrow = zs + o0 * kRowFloats + sl;
-  const float* hrow = hs + i0 * kRowFloats + sl;
-#pragma unroll 1
-  for (int m = 0; m < 8; ++m) {
-    float zv[8], hv[8];
+// The 32 weight-gradient MMAs of one jet component: both staging buffers (point halves), 8 K
+// steps of 8 points each, B = h_hi then h_lo. Issued by one converged warp, then committed.
+__device__ __forceinline__ void issue_dw_mmas(const Ctx& cx, bool first) {
+  constexpr uint32_t kIdescDw = tc::idesc_tf32(128, 64);
 #pragma unroll
-    for (int jj = 0; jj < 8; ++jj) zv[jj] = zrow[jj * kRowFloats + 8 * m];
+  for (int b = 0; b < 2; ++b) {
+    const uint32_t base = smem_u32(dsmem() + kStageOff + b * kStageBytes);
 #pragma unroll
-    for (int kk = 0; kk < 8; ++kk) hv[kk] = hrow[kk * kRowFloats + 8 * m];
-#pragma unroll
-    for (int jj = 0; jj < 8; ++jj)
-#pragma unroll
-      for (int kk = 0; kk < 8; ++kk) acc[jj][kk] = fmaf(zv[jj], hv[kk], acc[jj][kk]);
-    if (kBias) {
-#pragma unroll
-      for (int jj = 0; jj < 8; ++jj) db[jj] += zv[jj];
+    for (int ks = 0; ks < 8; ++ks) {
+      const uint32_t ka = static_cast<uint32_t>(ks >> 2), ko = static_cast<uint32_t>(ks & 3) * 32u;
+      const uint64_t a = tc::smem_desc_kmajor_sw128(base + kStageA + ka * 16384u + ko, 1024);
+      const uint64_t bh = tc::smem_desc_kmajor_sw128(base + kStageBhi + ka * 8192u + ko, 1024);
+      const uint64_t bl = tc::smem_desc_kmajor_sw128(base + kStageBlo + ka * 8192u + ko, 1024);
+      tc::mma_tf32_ss_warp(cx.tmem + kDwCol, a, bh, kIdescDw, (first && b == 0 && ks == 0) ? 0u : 1u);
+      tc::mma_tf32_ss_warp(cx.tmem + kDwCol, a, bl, kIdescDw, 1u);
     }
   }
+  tc::commit_warp(bar_dwdone());
 }
 
-// Sum acc[8][8] over the 8 lanes of a point slice group (lane bits 0..2) by a fixed
-// reduce-scatter: lane sl ends with out[v] = sum for jj = 4*b2 + 2*b0 + (v>>2),
-// kk = 4*b1 + (v&3), where b_k is bit k of sl.
-__device__ __forceinline__ void reduce_scatter_slices(float (&acc)[8][8], int sl,
-                                                      float (&out)[8]) {
-  const bool b2 = (sl & 4) != 0, b1 = (sl & 2) != 0, b0 = (sl & 1) != 0;
-  float r4[4][8];  // jj' = jj - 4*b2
-#pragma unroll
-  for (int j = 0; j < 4; ++j)
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const float keep = b2 ? acc[4 + j][k] : acc[j][k];
-      const float send = b2 ? acc[j][k] : acc[4 + j][k];
-      r4[j][k] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
-    }
-  float r2[4][4];  // kk' = kk - 4*b1
-#pragma unroll
-  for (int j = 0; j < 4; ++j)
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const float keep = b1 ? r4[j][4 + k] : r4[j][k];
-      const float send = b1 ? r4[j][k] : r4[j][4 + k];
-      r2[j][k] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
-    }
-#pragma unroll
-  for (int j = 0; j < 2; ++j)
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const float keep = b0 ? r2[2 + j][k] : r2[j][k];
-      const float send = b0 ? r2[j][k] : r2[2 + j][k];
-      out[4 * j + k] = keep + __shfl_xor_sync(0xffffffffu, send, 1);
-    }
-}
-
-__device__ __forceinline__ void load_weight_slot(const Ctx& cx, int slot, const float* src) {
-  mbar_arrive_expect_tx(bar_wfull(slot), kLayerBytes);
-  bulk_copy_g2s(dsmem() + kWOff + slot * kLayerBytes, src, kLayerBytes, bar_wfull(slot));
-}
-
-// Round r of a layer's weight gradient: plane (c = r/2, half = r%2) of zbar and of h into
-// staging buffer r % 2.
-__device__ __forceinline__ void issue_round(const Ctx& cx, int r, const float* zsrc,
-                                            const float* hsrc) {
-  const int b = r & 1;
-  uint8_t* dst = dsmem() + kStageOff + b * kStageBytes;
-  const int plane = (r >> 1) * 2 + (r & 1);
-  mbar_arrive_expect_tx(bar_stage(b), kStageBytes);
-  bulk_copy_g2s(dst, zsrc + plane * kPlaneFloats, kPlaneFloats * 4, bar_stage(b));
-  bulk_copy_g2s(dst + kPlaneFloats * 4, hsrc + plane * kPlaneFloats, kPlaneFloats * 4,
-                bar_stage(b));
+__device__ __forceinline__ void red_add(float* addr, float v) {
+  asm volatile("red.global.add.f32 [%0], %1;" ::"l"(addr), "f"(v) : "memory");
 }
 
 // Pre-split weights for the tensor-core backward: six K-major canonical tf32 operands, hi
@@ -363,21 +317,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                        float* __restrict__ lap_out, float* __restrict__ partials,
                        float* __restrict__ scratch, int64_t n, int64_t tiles, float inv_total,
                        unsigned int* status) {
-  extern __shared__ __align__(1024) uint8_t smem[];
+  uint8_t* const smem = dsmem();
   float* small = reinterpret_cast<float*>(smem + kSmallOff);
   float* grad = reinterpret_cast<float*>(smem + kGradOff);
   float* red = reinterpret_cast<float*>(smem + kRedOff);
   float* part = reinterpret_cast<float*>(smem + kPartOff);
-  float* dwacc = reinterpret_cast<float*>(smem + kAccOff);
+  float* xs = reinterpret_cast<float*>(smem + kXsOff);
   uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(smem + kMiscOff);
   Ctx cx;
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
+  float* const rowp = partials + static_cast<int64_t>(blockIdx.x) * kRowStride;
 
   // ---- set-up ----
-  for (int i = tid; i < 3 * 8 * kThreads; i += kThreads) dwacc[i] = 0.0f;
   for (int i = tid; i < kGradFloats; i += kThreads) grad[i] = 0.0f;
   for (int i = tid; i < kSmallFloats; i += kThreads) {
     float v = 0.0f;
@@ -390,6 +344,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     else if (i == kSmBout) v = params[kOutBase + kWidth];               // b_out
     small[i] = v;
   }
+  // The hidden-layer weight gradients are accumulated in place in this CTA's partial row
+  // (red.global.add by the thread that owns the entry, so the order is fixed).
+#pragma unroll
+  for (int l = 0; l < 3; ++l)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) rowp[kHiddenBase + l * kHiddenStride + tid + kThreads * j] = 0.0f;
   if (tid == 0) {
     for (uint32_t r = 0; r < kRing; ++r) {
       mbar_init(bar_empty(r), 1);
@@ -397,8 +357,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     mbar_init(bar_dfull(), 1);
     mbar_init(bar_red(), kWarps);
-    for (int k = 0; k < 3; ++k) mbar_init(bar_wfull(k), 1);
-    for (int k = 0; k < 2; ++k) mbar_init(bar_stage(k), 1);
+    for (int k = 0; k < kWeightSlots; ++k) mbar_init(bar_wfull(k), 1);
+    mbar_init(bar_dwdone(), 1);
     *abort_flag() = 0u;
     *status_slot() = status;
     fence_barrier_init();
@@ -412,36 +372,27 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc::fence_after_sync();
   cx.tmem = *tmem_base_slot;
   if (tid == 0)
-    for (int k = 0; k < 3; ++k) load_weight_slot(cx, k, wsplit + k * (kLayerBytes / 4));
+    for (int k = 0; k < kWeightSlots; ++k) load_weight_slot(k, wsplit, weight_block(k));
 
   const int q = warp & 3;   // TMEM lane quadrant
   const int s = warp >> 2;  // neurons 16a + 4s + t
   const uint32_t tmem_warp = cx.tmem + (static_cast<uint32_t>(32 * q) << 16);
   const int row = 32 * q + lane;
-  // Scratch addressing: element (component c, neuron 16a+4s+t) of this thread's point is at
-  // jet + c * 2 * kPlaneFloats + a * 16 * kRowFloats + toff[t].
-  int toff[4];
-  {
-    const int half = q >> 1, pl = 32 * (q & 1) + lane;
+  float* const hscratch = scratch + static_cast<int64_t>(blockIdx.x) * kScratchFloats + tid;
+  // Weight-gradient staging: this thread's point is K index `lane` of K atom q & 1 of
+  // staging buffer q >> 1; neuron row 16a + 4s + t sits at byte a * 2048 + soff[t] of an
+  // operand (plus 8192 for the zbar_lo rows 64.. of A).
+  uint8_t* const stage = smem + kStageOff + (q >> 1) * kStageBytes;
+  uint32_t soff[4];
 #pragma unroll
-    for (int t = 0; t < 4; ++t) {
-      const int nn = 4 * s + t;
-      toff[t] = half * kPlaneFloats + nn * kRowFloats + pl;
-    }
+  for (int t = 0; t < 4; ++t) {
+    const int r7 = 4 * (s & 1) + t;
+    soff[t] = static_cast<uint32_t>((s >> 1) * 1024 + r7 * 128 + (((lane >> 2) ^ r7) << 4) +
+                                    4 * (lane & 3));
   }
-  float* const jets = scratch + static_cast<int64_t>(blockIdx.x) * (kScratchJets * kJetFloats);
-  float* const zjet = jets + 3 * kJetFloats;
-  // Weight-gradient ownership (dw_round): block o0 + jj, i0 + kk over point slice sl; after
-  // the slice reduction this thread holds 8 entries (reduce_scatter_slices).
-  const int sl = lane & 7;
-  const int o0 = 8 * (warp >> 1);
-  const int i0 = 8 * (4 * (warp & 1) + (lane >> 3));
-  const bool bias_thread = i0 == 0;
-  const int own_o = o0 + 4 * ((sl >> 2) & 1) + 2 * (sl & 1);
-  const int own_i = i0 + 4 * ((sl >> 1) & 1);
+  const uint32_t ka = static_cast<uint32_t>(q & 1);
 
-  uint32_t chunk = 0, mlayer = 0, tile_count = 0;
-  uint32_t stage_fill[2] = {0u, 0u};
+  uint32_t chunk = 0, mlayer = 0, tile_count = 0, dw_issued = 0;
   bool alive = true;
   float nx0 = 0.0f, nx1 = 0.0f;
   {
@@ -456,11 +407,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int64_t p = tile * kTile + row;
     const bool active = p < n;
     // This tile's point, loaded during the previous tile, is kept in shared memory so that
-    // no register holds it through the weight-gradient rounds.
-    float* const xs = reinterpret_cast<float*>(smem + kXsOff);
+    // no register holds it through the backward sweep.
     xs[tid] = nx0;
     xs[kThreads + tid] = nx1;
-    const float x0 = nx0, x1 = nx1;
 
     // ---- forward recompute: layer 0, then the three hidden GEMMs ----
 #pragma unroll
@@ -470,21 +419,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int t = 0; t < 4; ++t) {
         const int o = 16 * a + 4 * s + t;
         const float w0 = small[kSmW0 + 2 * o], w1 = small[kSmW0 + 2 * o + 1];
-        tanh_jet_fast(fmaf(w0, x0, fmaf(w1, x1, small[kSmB0 + o])), w0, w1, 0.0f, h[0][t],
+        tanh_jet_fast(fmaf(w0, nx0, fmaf(w1, nx1, small[kSmB0 + o])), w0, w1, 0.0f, h[0][t],
                       h[1][t], h[2][t], h[3][t]);
-#pragma unroll
-        for (int c = 0; c < 4; ++c) jets[c * 2 * kPlaneFloats + a * 16 * kRowFloats + toff[t]] = h[c][t];
       }
       produce_chunk(chunk++, h, tmem_warp, s, cx);
     }
     float d[4][16];  // d[c][4a + t]: component c of neuron 16a + 4s + t
 #pragma unroll 1
     for (int g = 0; g < 3; ++g) {
-      warp_wait(bar_dfull(), mlayer & 1u, cx);
+      warp_wait(bar_dfull(), mlayer & 1u);
       ++mlayer;
       tc::fence_after_sync();
-      // GEMM g is complete: its weight slot now takes W_{g+1}^T for the backward.
-      if (tid == 0) load_weight_slot(cx, g, wsplit + (3 + g) * (kLayerBytes / 4));
+      // GEMM g is complete: its weight slot takes the operand of GEMM g + 2.
+      if (tid == 0) load_weight_slot(g & 1, wsplit, weight_block(g + 2));
 #pragma unroll
       for (int c = 0; c < 4; ++c)
 #pragma unroll
@@ -496,7 +443,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int i = 0; i < 16; ++i) d[0][i] += bias[16 * (i >> 2) + 4 * s + (i & 3)];
       if (g < 2) {
-        float* hjet = jets + (g + 1) * kJetFloats;
+        float* hj = hscratch + g * (4 * 16 * kThreads);  // h_{g+1}
 #pragma unroll
         for (int a = 0; a < kChunks; ++a) {
           float h[4][4];
@@ -506,7 +453,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tanh_jet_fast(d[0][i], d[1][i], d[2][i], d[3][i], h[0][t], h[1][t], h[2][t],
                           h[3][t]);
 #pragma unroll
-            for (int c = 0; c < 4; ++c) hjet[c * 2 * kPlaneFloats + a * 16 * kRowFloats + toff[t]] = h[c][t];
+            for (int c = 0; c < 4; ++c) hj[(c * 16 + i) * kThreads] = h[c][t];
           }
           produce_chunk(chunk++, h, tmem_warp, s, cx);
         }
@@ -527,7 +474,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       red[(4 + s) * kTile + row] = pl;
       __syncwarp();
       if (lane == 0) mbar_arrive(bar_red());
-      warp_wait(bar_red(), tile_count & 1u, cx);
+      warp_wait(bar_red(), tile_count & 1u);
       float lap = 0.0f;
 #pragma unroll
       for (int k = 0; k < 4; ++k) lap += red[(4 + k) * kTile + row];
@@ -557,9 +504,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int o = 16 * (i >> 2) + 4 * s + (i & 3);
         const float w = small[kSmWout + o];
         const float dwo = warp_sum(fmaf(gu, d[0][i], gl * d[3][i]));
-        if (lane == 0) part[kPWout + q * 64 + o] = dwo;
         float gv = gu * w, g0 = 0.0f, g1 = 0.0f, gL = gl * w;
         adjoint_h(d[0][i], d[1][i], d[2][i], d[3][i], gv, g0, g1, gL);
+        const float db = warp_sum(gv);
+        if (lane == 0) {
+          part[0 * 256 + q * 64 + o] = dwo;
+          part[6 * 256 + q * 64 + o] = db;  // b3
+        }
         d[0][i] = gv;
         d[1][i] = g0;
         d[2][i] = g1;
@@ -571,81 +522,90 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 1
     for (int l = 3; l >= 1; --l) {
       const int g = 6 - l;
-      const float* hsrc = jets + (l - 1) * kJetFloats;
-      // zbar_l -> scratch (weight gradient) and ring (input-adjoint GEMM g)
+      // zbar_l -> ring (input-adjoint GEMM g)
 #pragma unroll
       for (int a = 0; a < kChunks; ++a) {
         float z[4][4];
 #pragma unroll
         for (int t = 0; t < 4; ++t)
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            z[c][t] = d[c][4 * a + t];
-            zjet[c * 2 * kPlaneFloats + a * 16 * kRowFloats + toff[t]] = z[c][t];
-          }
+          for (int c = 0; c < 4; ++c) z[c][t] = d[c][4 * a + t];
         produce_chunk(chunk++, z, tmem_warp, s, cx);
       }
-      fence_proxy_async_global();
-      if (!(alive = barrier_ok(cx))) break;
 
-      // weight gradient dW_l over this tile, 8 rounds of (component, point half)
-      float acc[8][8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j)
-#pragma unroll
-        for (int k = 0; k < 8; ++k) acc[j][k] = 0.0f;
-      if (tid == 0) {
-        issue_round(cx, 0, zjet, hsrc);
-        issue_round(cx, 1, zjet, hsrc);
-      }
-      // Rounds 0 and 1 (value component) also sum zbar_v for the bias gradient.
-      {
-        float dbp[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) dbp[j] = 0.0f;
+      // weight gradient dW_l: per jet component, stage zbar_l and h_{l-1} (hi/lo) for the
+      // tile's 128 points and let one warp issue the MMAs
+      const float* hsrc = hscratch + (l == 3 ? 4 * 16 * kThreads : 0);  // h_{l-1} (l >= 2)
 #pragma unroll 1
-        for (int r = 0; r < 2; ++r) {
-          warp_wait(bar_stage(r), stage_fill[r] & 1u, cx);
-          ++stage_fill[r];
-          const float* zs = reinterpret_cast<const float*>(smem + kStageOff + r * kStageBytes);
-          if (bias_thread) dw_round<true>(zs, zs + kPlaneFloats, o0, i0, sl, acc, dbp);
-          else dw_round<false>(zs, zs + kPlaneFloats, o0, i0, sl, acc, dbp);
-          if (!(alive = barrier_ok(cx))) break;
-          if (tid == 0) issue_round(cx, r + 2, zjet, hsrc);
-        }
-        if (bias_thread) {  // lanes 0..7 of the even warps: sum the slices of db in lane 0
+      for (int c = 0; c < 4; ++c) {
+        float hv[16];
+        if (l > 1) {
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            float v = dbp[j];
-            v += __shfl_xor_sync(0x000000ffu, v, 4);
-            v += __shfl_xor_sync(0x000000ffu, v, 2);
-            v += __shfl_xor_sync(0x000000ffu, v, 1);
-            dbp[j] = v;
-          }
-          if (sl == 0) {
+          for (int i = 0; i < 16; ++i) hv[i] = hsrc[(c * 16 + i) * kThreads];
+        } else {
+          const float x0 = xs[tid], x1 = xs[kThreads + tid];
 #pragma unroll
-            for (int j = 0; j < 8; ++j) grad[kGBias + l * 64 + o0 + j] += dbp[j];
+          for (int i = 0; i < 16; ++i) {
+            const int o = 16 * (i >> 2) + 4 * s + (i & 3);
+            const float w0 = small[kSmW0 + 2 * o], w1 = small[kSmW0 + 2 * o + 1];
+            float v, j0, j1, lv;
+            tanh_jet_fast(fmaf(w0, x0, fmaf(w1, x1, small[kSmB0 + o])), w0, w1, 0.0f, v, j0,
+                          j1, lv);
+            hv[i] = c == 0 ? v : c == 1 ? j0 : c == 2 ? j1 : lv;
           }
         }
-      }
-      if (!alive) break;
-#pragma unroll 1
-      for (int r = 2; r < 8; ++r) {
-        const int b = r & 1;
-        warp_wait(bar_stage(b), stage_fill[b] & 1u, cx);
-        ++stage_fill[b];
-        const float* zs = reinterpret_cast<const float*>(smem + kStageOff + b * kStageBytes);
-        float unused[8];
-        dw_round<false>(zs, zs + kPlaneFloats, o0, i0, sl, acc, unused);
-        if (!(alive = barrier_ok(cx))) break;
-        if (tid == 0 && r + 2 < 8) issue_round(cx, r + 2, zjet, hsrc);
-      }
-      if (!alive) break;
-      {
-        float sums[8];
-        reduce_scatter_slices(acc, sl, sums);
+        if (c > 0) warp_wait(bar_dwdone(), (dw_issued - 1u) & 1u);  // staging free again
 #pragma unroll
-        for (int v = 0; v < 8; ++v) dwacc[((l - 1) * 8 + v) * kThreads + tid] += sums[v];
+        for (int i = 0; i < 16; ++i) {
+          const int a = i >> 2, t = i & 3;
+          const float z = c == 0 ? d[0][i] : c == 1 ? d[1][i] : c == 2 ? d[2][i] : d[3][i];
+          uint32_t zh, zl, hh, hl;
+          split_tf32(z, zh, zl);
+          split_tf32(hv[i], hh, hl);
+          const uint32_t o = a * 2048 + soff[t];
+          *reinterpret_cast<uint32_t*>(stage + kStageA + ka * 16384u + o) = zh;
+          *reinterpret_cast<uint32_t*>(stage + kStageA + ka * 16384u + 8192u + o) = zl;
+          *reinterpret_cast<uint32_t*>(stage + kStageBhi + ka * 8192u + o) = hh;
+          *reinterpret_cast<uint32_t*>(stage + kStageBlo + ka * 8192u + o) = hl;
+        }
+        tc::fence_proxy_async_smem();
+        if (!(alive = barrier_ok())) break;
+        if (warp == 0) {
+          if (c == 0) {
+            // the input-adjoint GEMM g has finished with the ring columns the weight-gradient
+            // accumulator borrows, and with its weight slot
+            warp_wait(bar_dfull(), mlayer & 1u);
+            tc::fence_after_sync();
+            if (lane == 0 && (g + 2 < kGemmsPerTile || has_next))
+              load_weight_slot(g & 1, wsplit, weight_block((g + 2) % kGemmsPerTile));
+          }
+          tc::fence_after_sync();
+          issue_dw_mmas(cx, c == 0);
+        }
+        ++dw_issued;
+      }
+      if (!alive) break;
+
+      // empty the accumulator into this CTA's partial row: hi and lo halves summed in shared
+      // memory (staging buffer 0), one owner thread per entry
+      warp_wait(bar_dwdone(), (dw_issued - 1u) & 1u);
+      tc::fence_after_sync();
+      {
+        float* fb = reinterpret_cast<float*>(smem + kStageOff);
+        float v[16];
+        tc::ld_x16(tmem_warp + kDwCol + 16u * s, v);
+        tc::wait_ld();
+#pragma unroll
+        for (int k = 0; k < 16; ++k) fb[row * kFlushStride + 16 * s + k] = v[k];
+        tc::fence_before_sync();
+        if (!(alive = barrier_ok())) break;
+        float* wrow = rowp + kHiddenBase + (l - 1) * kHiddenStride;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int e = tid + kThreads * j, o = e >> 6, i = e & 63;
+          red_add(wrow + e, fb[o * kFlushStride + i] + fb[(64 + o) * kFlushStride + i]);
+        }
+        if (!(alive = barrier_ok())) break;
       }
 
       // input adjoint hbar_{l-1} = zbar_l W_l (GEMM g), then zbar_{l-1}
@@ -654,14 +614,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int t = 0; t < 4; ++t)
 #pragma unroll
-          for (int c = 0; c < 4; ++c) hn[c][t] = hsrc[c * 2 * kPlaneFloats + toff[t]];
+          for (int c = 0; c < 4; ++c) hn[c][t] = hsrc[(c * 16 + t) * kThreads];
       }
-      warp_wait(bar_dfull(), mlayer & 1u, cx);
+      warp_wait(bar_dfull(), mlayer & 1u);
       ++mlayer;
       tc::fence_after_sync();
-      // GEMM g is complete: its slot takes W_l again for the next tile's forward.
-      if (tid == 0 && has_next)
-        load_weight_slot(cx, weight_slot(g), wsplit + (l - 1) * (kLayerBytes / 4));
 #pragma unroll
       for (int c = 0; c < 4; ++c)
 #pragma unroll
@@ -681,13 +638,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int t = 0; t < 4; ++t)
 #pragma unroll
-              for (int c = 0; c < 4; ++c)
-                hn[c][t] = hsrc[c * 2 * kPlaneFloats + (a + 1) * 16 * kRowFloats + toff[t]];
+              for (int c = 0; c < 4; ++c) hn[c][t] = hsrc[(c * 16 + 4 * (a + 1) + t) * kThreads];
           }
 #pragma unroll
           for (int t = 0; t < 4; ++t) {
             const int i = 4 * a + t;
             adjoint_h(h[0][t], h[1][t], h[2][t], h[3][t], d[0][i], d[1][i], d[2][i], d[3][i]);
+            const float db = warp_sum(d[0][i]);
+            if (lane == 0) part[(2 + l) * 256 + q * 64 + 16 * a + 4 * s + t] = db;  // b_{l-1}
           }
         }
       }
@@ -720,9 +678,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float d0 = warp_sum(fmaf(gv, x0, g0));
         const float d1 = warp_sum(fmaf(gv, x1, g1));
         if (lane == 0) {
-          part[kPB0 + q * 64 + o] = db;
-          part[kPW0x + q * 64 + o] = d0;
-          part[kPW0y + q * 64 + o] = d1;
+          part[1 * 256 + q * 64 + o] = db;
+          part[2 * 256 + q * 64 + o] = d0;
+          part[3 * 256 + q * 64 + o] = d1;
         }
         gx0 = fmaf(w0, gv, gx0);
         gx1 = fmaf(w1, gv, gx1);
@@ -730,7 +688,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       red[s * kTile + row] = gx0;
       red[(4 + s) * kTile + row] = gx1;
     }
-    if (!(alive = barrier_ok(cx))) break;
+    if (!(alive = barrier_ok())) break;
     if (s == 0 && active && grad_coords != nullptr) {
       float sx = 0.0f, sy = 0.0f;
 #pragma unroll
@@ -741,15 +699,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       grad_coords[2 * p] = sx;
       grad_coords[2 * p + 1] = sy;
     }
-    if (tid < 4 * kWidth) {
+    // per-quadrant partials -> accumulators, quadrants in index order
+    if (tid < kPartKinds * kWidth) {
       const int kind = tid >> 6, o = tid & 63;
-      const int base = kind == 0 ? kPWout : kind == 1 ? kPB0 : kind == 2 ? kPW0x : kPW0y;
-      const float v = ((part[base + o] + part[base + 64 + o]) + part[base + 128 + o]) +
-                      part[base + 192 + o];
+      const float* src = part + kind * 256 + o;
+      const float v = ((src[0] + src[64]) + src[128]) + src[192];
       if (kind == 0) grad[kGWout + o] += v;
       else if (kind == 1) grad[kGBias + o] += v;
-      else grad[kGW0 + 2 * o + (kind - 2)] += v;
-    } else if (tid == 4 * kWidth) {
+      else if (kind <= 3) grad[kGW0 + 2 * o + (kind - 2)] += v;
+      else grad[kGBias + (kind - 3) * kWidth + o] += v;
+    } else if (tid == kPartKinds * kWidth) {
       if (kPoisson) {
         grad[kGLoss] += (((part[kPLoss] + part[kPLoss + 1]) + part[kPLoss + 2]) + part[kPLoss + 3]) *
                         inv_total;
@@ -758,7 +717,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             ((part[kPBout] + part[kPBout + 1]) + part[kPBout + 2]) + part[kPBout + 3];
       }
     }
-    if (!(alive = barrier_ok(cx))) break;
+    if (!(alive = barrier_ok())) break;
   }
 
   // ---- teardown: free TMEM (after an abort, let issued MMAs and copies drain first) ----
@@ -776,14 +735,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   if (aborted) return;
 
-  // ---- this CTA's partial-gradient row, in the packed ABI layout ----
-  float* rowp = partials + static_cast<int64_t>(blockIdx.x) * kRowStride;
-#pragma unroll
-  for (int l = 0; l < 3; ++l)
-#pragma unroll
-    for (int v = 0; v < 8; ++v)
-      rowp[kHiddenBase + l * kHiddenStride + (own_o + (v >> 2)) * kWidth + own_i + (v & 3)] =
-          dwacc[(l * 8 + v) * kThreads + tid];
+  // ---- the rest of this CTA's partial-gradient row (hidden weights are already there) ----
   for (int k = tid; k < 2 * kWidth; k += kThreads) rowp[k] = grad[kGW0 + k];
   if (tid < kWidth) {
     rowp[kB0 + tid] = grad[kGBias + tid];
@@ -818,7 +770,7 @@ int backward_tc_grid(int64_t n, const DeviceInfo& dev) {
 size_t backward_tc_workspace_bytes(int64_t n, const DeviceInfo& dev) {
   const size_t grid = static_cast<size_t>(backward_tc_grid(n, dev));
   return (static_cast<size_t>(kWeightBlocks) * (kLayerBytes / 4) + grid * kRowStride +
-          grid * kScratchJets * kJetFloats) *
+          grid * kScratchFloats) *
          sizeof(float);
 }
 

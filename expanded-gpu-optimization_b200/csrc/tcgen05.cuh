@@ -68,6 +68,20 @@ __device__ __forceinline__ void mma_tf32_ts_warp(uint32_t d_tmem, uint32_t a_tme
       "r"(0u), "r"(0u)
       : "memory");
 }
+// D[tmem] (+)= A[smem] * B[smem]^T, kind::tf32, both operands from shared memory, issued by
+// a converged warp (elect.sync picks the lane).
+__device__ __forceinline__ void mma_tf32_ss_warp(uint32_t d_tmem, uint64_t a_desc,
+                                                 uint64_t b_desc, uint32_t idesc,
+                                                 uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
+      ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u),
+      "r"(0u), "r"(0u)
+      : "memory");
+}
 // tcgen05.commit from one elected lane of a converged warp.
 __device__ __forceinline__ void commit_warp(uint64_t* bar) {
   asm volatile(
@@ -146,6 +160,14 @@ __device__ __forceinline__ uint64_t smem_desc_kmajor(uint32_t smem_addr, uint32_
   d |= 1ull << 46;  // descriptor version for tcgen05
   // base_offset = 0, lbo mode = 0, layout type (bits 61..63) = 0: no swizzle
   return d;
+}
+
+// Shared-memory matrix descriptor, K-major, 128-byte swizzle: atoms of 8 rows x 128 bytes
+// (1024-byte aligned) whose 16-byte chunks are XOR-permuted by row % 8; `sbo` = byte distance
+// between consecutive 8-row atoms. Moving the start address by 32 bytes inside an atom
+// selects the next K step of 8 tf32 elements.
+__device__ __forceinline__ uint64_t smem_desc_kmajor_sw128(uint32_t smem_addr, uint32_t sbo) {
+  return smem_desc_kmajor(smem_addr, 16, sbo) | (2ull << 61);  // layout type 2: 128B swizzle
 }
 
 // Instruction descriptor for kind::tf32: D f32, A/B tf32, both K-major, shape M x N.
