@@ -185,8 +185,10 @@ __device__ __forceinline__ void load_weight_slot(int slot, const float* wsplit, 
 }
 
 // The 24 MMAs of chunk j of GEMM g (A from ring slot `slot`); the first chunk of a GEMM
-// first waits for its weight slot. False if that wait gave up (nothing is issued).
-__device__ __forceinline__ bool issue_chunk_mmas(const Ctx& cx, uint32_t tile_index, int g,
+// first waits for its weight slot. False if that wait gave up (nothing is issued). Not
+// inlined: one copy instead of twelve keeps the kernel small enough for the instruction
+// cache (measured faster than the inlined form here).
+__device__ __noinline__ bool issue_chunk_mmas(const Ctx& cx, uint32_t tile_index, int g,
                                                  int j, uint32_t slot) {
   const int ws = g & 1;
   if (j == 0 && !warp_wait(bar_wfull(ws), weight_parity(tile_index, g))) return false;
@@ -283,6 +285,44 @@ __device__ __forceinline__ void issue_dw_mmas(const Ctx& cx, bool first) {
     }
   }
   tc::commit_warp(bar_dwdone());
+}
+
+// Sums v[i] over the 32 lanes of the warp for every i < 16 with a fixed butterfly that
+// halves the values held per lane at each step (16 shuffles instead of 80); lane l returns
+// the total for i = l >> 1.
+__device__ __forceinline__ float warp_sum16(const float (&v)[16]) {
+  const int lane = threadIdx.x & 31;
+  float u8[8], u4[4], u2[2];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const bool hi = (lane & 16) != 0;
+    const float keep = hi ? v[8 + j] : v[j], send = hi ? v[j] : v[8 + j];
+    u8[j] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const bool hi = (lane & 8) != 0;
+    const float keep = hi ? u8[4 + j] : u8[j], send = hi ? u8[j] : u8[4 + j];
+    u4[j] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+  }
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const bool hi = (lane & 4) != 0;
+    const float keep = hi ? u4[2 + j] : u4[j], send = hi ? u4[j] : u4[2 + j];
+    u2[j] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+  }
+  const bool hi = (lane & 2) != 0;
+  float r = (hi ? u2[1] : u2[0]) + __shfl_xor_sync(0xffffffffu, hi ? u2[0] : u2[1], 2);
+  return r + __shfl_xor_sync(0xffffffffu, r, 1);
+}
+
+// Writes this warp's per-neuron sums (warp_sum16 output) to the per-quadrant partials.
+__device__ __forceinline__ void store_part16(float* part, int kind, int q, int s, float r) {
+  const int lane = threadIdx.x & 31;
+  if ((lane & 1) == 0) {
+    const int i = lane >> 1;
+    part[kind * 256 + q * 64 + 16 * (i >> 2) + 4 * s + (i & 3)] = r;
+  }
 }
 
 __device__ __forceinline__ void red_add(float* addr, float v) {
@@ -499,23 +539,21 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (lane == 0) part[kPBout + q] = sg;
         }
       }
+      float dwo[16];
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
         const int o = 16 * (i >> 2) + 4 * s + (i & 3);
         const float w = small[kSmWout + o];
-        const float dwo = warp_sum(fmaf(gu, d[0][i], gl * d[3][i]));
+        dwo[i] = fmaf(gu, d[0][i], gl * d[3][i]);
         float gv = gu * w, g0 = 0.0f, g1 = 0.0f, gL = gl * w;
         adjoint_h(d[0][i], d[1][i], d[2][i], d[3][i], gv, g0, g1, gL);
-        const float db = warp_sum(gv);
-        if (lane == 0) {
-          part[0 * 256 + q * 64 + o] = dwo;
-          part[6 * 256 + q * 64 + o] = db;  // b3
-        }
         d[0][i] = gv;
         d[1][i] = g0;
         d[2][i] = g1;
         d[3][i] = gL;
       }
+      store_part16(part, 0, q, s, warp_sum16(dwo));   // w_out
+      store_part16(part, 6, q, s, warp_sum16(d[0]));  // b3
     }
 
     // ---- backward through the hidden layers: d holds zbar_l on entry ----
@@ -534,9 +572,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
 
       // weight gradient dW_l: per jet component, stage zbar_l and h_{l-1} (hi/lo) for the
-      // tile's 128 points and let one warp issue the MMAs
+      // tile's 128 points and let one warp issue the MMAs. Unrolled, so that the registers
+      // of component c of zbar_l are free once its round is staged.
       const float* hsrc = hscratch + (l == 3 ? 4 * 16 * kThreads : 0);  // h_{l-1} (l >= 2)
-#pragma unroll 1
+#pragma unroll
       for (int c = 0; c < 4; ++c) {
         float hv[16];
         if (l > 1) {
@@ -644,10 +683,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int t = 0; t < 4; ++t) {
             const int i = 4 * a + t;
             adjoint_h(h[0][t], h[1][t], h[2][t], h[3][t], d[0][i], d[1][i], d[2][i], d[3][i]);
-            const float db = warp_sum(d[0][i]);
-            if (lane == 0) part[(2 + l) * 256 + q * 64 + 16 * a + 4 * s + t] = db;  // b_{l-1}
           }
         }
+        store_part16(part, 2 + l, q, s, warp_sum16(d[0]));  // b_{l-1}
       }
     }
     if (!alive) break;
@@ -674,17 +712,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                       hl);
         float gv = d[0][i], g0 = d[1][i], g1 = d[2][i], gL = d[3][i];
         adjoint_h(a, hj0, hj1, hl, gv, g0, g1, gL);
-        const float db = warp_sum(gv);
-        const float d0 = warp_sum(fmaf(gv, x0, g0));
-        const float d1 = warp_sum(fmaf(gv, x1, g1));
-        if (lane == 0) {
-          part[1 * 256 + q * 64 + o] = db;
-          part[2 * 256 + q * 64 + o] = d0;
-          part[3 * 256 + q * 64 + o] = d1;
-        }
+        d[0][i] = gv;                  // db0 terms
+        d[1][i] = fmaf(gv, x0, g0);    // dW0[:, 0] terms
+        d[2][i] = fmaf(gv, x1, g1);    // dW0[:, 1] terms
         gx0 = fmaf(w0, gv, gx0);
         gx1 = fmaf(w1, gv, gx1);
       }
+      store_part16(part, 1, q, s, warp_sum16(d[0]));
+      store_part16(part, 2, q, s, warp_sum16(d[1]));
+      store_part16(part, 3, q, s, warp_sum16(d[2]));
       red[s * kTile + row] = gx0;
       red[(4 + s) * kTile + row] = gx1;
     }
