@@ -14,6 +14,9 @@ namespace {
 constexpr int kAdamThreads = 1024;
 
 // One CTA: every thread reads the counter before thread 0 stores the incremented value.
+// The elements are processed in blocks of kAdamUnroll per thread with all loads of a block
+// issued before any is used, so a 12,737-element buffer takes two round trips to memory.
+constexpr int kAdamUnroll = 7;
 __global__ void __launch_bounds__(kAdamThreads)
     adam_kernel(float* __restrict__ params, const float* __restrict__ grad,
                 float* __restrict__ exp_avg, float* __restrict__ exp_avg_sq, int64_t count,
@@ -23,15 +26,28 @@ __global__ void __launch_bounds__(kAdamThreads)
   const double bias2 = 1.0 - pow(static_cast<double>(beta2), static_cast<double>(t));
   const float step_size = static_cast<float>(static_cast<double>(lr) / bias1);
   const float bias2_sqrt = static_cast<float>(sqrt(bias2));
-  for (int64_t i = threadIdx.x; i < count; i += kAdamThreads) {
-    const float g = grad[i];
-    float m = exp_avg[i];
-    m = fmaf(1.0f - beta1, g - m, m);
-    const float v = fmaf(beta2, exp_avg_sq[i], (1.0f - beta2) * g * g);
-    exp_avg[i] = m;
-    exp_avg_sq[i] = v;
-    const float denom = sqrtf(v) / bias2_sqrt + eps;
-    params[i] -= step_size * (m / denom);
+  for (int64_t base = 0; base < count; base += static_cast<int64_t>(kAdamThreads) * kAdamUnroll) {
+    float g[kAdamUnroll], m[kAdamUnroll], v[kAdamUnroll], p[kAdamUnroll];
+#pragma unroll
+    for (int k = 0; k < kAdamUnroll; ++k) {
+      const int64_t i = base + threadIdx.x + static_cast<int64_t>(k) * kAdamThreads;
+      const bool in = i < count;
+      g[k] = in ? grad[i] : 0.0f;
+      m[k] = in ? exp_avg[i] : 0.0f;
+      v[k] = in ? exp_avg_sq[i] : 0.0f;
+      p[k] = in ? params[i] : 0.0f;
+    }
+#pragma unroll
+    for (int k = 0; k < kAdamUnroll; ++k) {
+      const int64_t i = base + threadIdx.x + static_cast<int64_t>(k) * kAdamThreads;
+      if (i >= count) continue;
+      const float mk = fmaf(1.0f - beta1, g[k] - m[k], m[k]);
+      const float vk = fmaf(beta2, v[k], (1.0f - beta2) * g[k] * g[k]);
+      exp_avg[i] = mk;
+      exp_avg_sq[i] = vk;
+      const float denom = sqrtf(vk) / bias2_sqrt + eps;
+      params[i] = p[k] - step_size * (mk / denom);
+    }
   }
   __syncthreads();
   if (threadIdx.x == 0) *step = t;

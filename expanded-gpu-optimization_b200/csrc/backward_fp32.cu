@@ -388,20 +388,39 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// out[col] = sum over rows r = 0..rows-1 of partials[r][col], in row order.
-__global__ void __launch_bounds__(128)
+// out[col] = sum over the partial rows of partials[r][col] in a fixed order: a block takes 32
+// columns; its 8 row groups (rows g, g+8, g+16, ...) are summed in row order by 8 threads
+// of a column, each with its loads in flight together, then the 8 group sums are added in
+// group order.
+constexpr int kReduceCols = 32, kReduceGroups = 8;
+__global__ void __launch_bounds__(kReduceCols * kReduceGroups)
     reduce_rows_kernel(const float* __restrict__ partials, int rows,
                        float* __restrict__ grad_params, float* __restrict__ loss) {
-  const int col = blockIdx.x * blockDim.x + threadIdx.x;
-  if (col > kLossColumn) return;
-  if (col == kLossColumn && loss == nullptr) return;
+  __shared__ float sums[kReduceGroups][kReduceCols];
+  const int cx = threadIdx.x % kReduceCols, grp = threadIdx.x / kReduceCols;
+  const int col = blockIdx.x * kReduceCols + cx;
   float acc = 0.0f;
-#pragma unroll 8
-  for (int r = 0; r < rows; ++r) acc += partials[static_cast<int64_t>(r) * kRowStride + col];
+  if (col <= kLossColumn) {
+    int r = grp;
+    for (; r + 3 * kReduceGroups < rows; r += 4 * kReduceGroups) {
+      const float a = partials[static_cast<int64_t>(r) * kRowStride + col];
+      const float b = partials[static_cast<int64_t>(r + kReduceGroups) * kRowStride + col];
+      const float c = partials[static_cast<int64_t>(r + 2 * kReduceGroups) * kRowStride + col];
+      const float d = partials[static_cast<int64_t>(r + 3 * kReduceGroups) * kRowStride + col];
+      acc = (((acc + a) + b) + c) + d;
+    }
+    for (; r < rows; r += kReduceGroups) acc += partials[static_cast<int64_t>(r) * kRowStride + col];
+  }
+  sums[grp][cx] = acc;
+  __syncthreads();
+  if (grp != 0 || col > kLossColumn) return;
+  float total = sums[0][cx];
+#pragma unroll
+  for (int k = 1; k < kReduceGroups; ++k) total += sums[k][cx];
   if (col == kLossColumn) {
-    *loss = acc;
+    if (loss != nullptr) *loss = total;
   } else {
-    grad_params[col] = acc;
+    grad_params[col] = total;
   }
 }
 
@@ -447,7 +466,8 @@ cudaError_t launch_backward_fp32(const float* coords, const float* params,
 cudaError_t launch_reduce_rows(const float* partials, int rows, float* grad_params,
                                float* loss, cudaStream_t stream) {
   const int cols = kLossColumn + 1;
-  reduce_rows_kernel<<<(cols + 127) / 128, 128, 0, stream>>>(partials, rows, grad_params, loss);
+  reduce_rows_kernel<<<(cols + kReduceCols - 1) / kReduceCols, kReduceCols * kReduceGroups, 0,
+                       stream>>>(partials, rows, grad_params, loss);
   return cudaGetLastError();
 }
 
