@@ -8,8 +8,9 @@
 //     TMEM, B = W_l in shared memory, M = 128 points, N = 64, K = 64 per component);
 //   * input adjoint      Hbar_{l-1} = Zbar_l W_l           (A = Zbar in TMEM, B = W_l^T);
 //   * weight gradient    dW_l[64 x 64] = sum over points and components of zbar h^T, as
-//     M = 128 rows (zbar_hi rows 0..63, zbar_lo rows 64..127) x N = 64 x K = points, with
-//     B = h_hi then h_lo, so one pair of MMAs gives all four hi/lo products. A and B are
+//     M = 128 rows (zbar_hi rows 0..63, zbar_lo rows 64..127) x N = 128 columns (h_hi,
+//     h_lo) x K = points: one MMA per K step gives all four hi/lo products in four
+//     quadrants of the accumulator, summed when it is emptied. A and B are
 //     written by the threads straight from registers into two shared-memory staging
 //     buffers (128-byte-swizzled K-major: a warp writes 32 consecutive points of one row,
 //     conflict-free), one per point half, one jet component at a time.
@@ -17,7 +18,7 @@
 // Where the data lives (one CTA per SM, persistent over tiles):
 //   * TMEM: accumulators D_c at columns 64c..64c+63 and a ring of two A-operand chunks at
 //     [256, 512), as in the forward kernel. The weight-gradient accumulator borrows ring
-//     columns [256, 320) while the ring is idle (after the input-adjoint GEMM of the layer
+//     columns [256, 384) while the ring is idle (after the input-adjoint GEMM of the layer
 //     has completed, before the next layer's chunks) and is emptied every layer;
 //   * shared memory: two weight slots (hi + lo, 32 KB each), the six operands of a tile's
 //     GEMMs (W1, W2, W3, then W3^T, W2^T, W1^T; all K-major) taking turns: a one-thread bulk
@@ -67,10 +68,10 @@ constexpr int kWeightSlots = 2;
 // neuron slot 4a + t of thread (warp 4s + q, lane) is neuron 16a + 4s + t of its point.
 constexpr int kScratchFloats = 2 * 4 * 16 * kThreads;
 
-// Weight-gradient staging buffer (one per point half): A = [zbar_hi; zbar_lo] (128 rows x 64
-// points) and B_hi, B_lo = h_hi, h_lo (64 rows x 64 points), 128-byte-swizzled K-major: a K
-// atom is 32 points, rows in 8-row groups of 1024 bytes.
-constexpr int kStageA = 0, kStageBhi = 32768, kStageBlo = 49152;
+// Weight-gradient staging buffer (one per point half): A = [zbar_hi; zbar_lo] and
+// B = [h_hi; h_lo] (128 rows x 64 points each), 128-byte-swizzled K-major: a K atom is 32
+// points, rows in 8-row groups of 1024 bytes, the lo rows 8192 bytes after the hi rows.
+constexpr int kStageA = 0, kStageB = 32768;
 constexpr int kStageBytes = 65536;
 constexpr int kFlushStride = 65;                 // [128 rows][65] floats when emptying TMEM
 
@@ -267,10 +268,11 @@ __device__ __forceinline__ void adjoint_h(float a, float hj0, float hj1, float h
   g1 = z1;
 }
 
-// The 32 weight-gradient MMAs of one jet component: both staging buffers (point halves), 8 K
-// steps of 8 points each, B = h_hi then h_lo. Issued by one converged warp, then committed.
+// The 16 weight-gradient MMAs of one jet component (M = 128, N = 128, K = 8): both staging
+// buffers (point halves), 8 K steps of 8 points each. Issued by one converged warp, then
+// committed.
 __device__ __forceinline__ void issue_dw_mmas(const Ctx& cx, bool first) {
-  constexpr uint32_t kIdescDw = tc::idesc_tf32(128, 64);
+  constexpr uint32_t kIdescDw = tc::idesc_tf32(128, 128);
 #pragma unroll
   for (int b = 0; b < 2; ++b) {
     const uint32_t base = smem_u32(dsmem() + kStageOff + b * kStageBytes);
@@ -278,10 +280,8 @@ __device__ __forceinline__ void issue_dw_mmas(const Ctx& cx, bool first) {
     for (int ks = 0; ks < 8; ++ks) {
       const uint32_t ka = static_cast<uint32_t>(ks >> 2), ko = static_cast<uint32_t>(ks & 3) * 32u;
       const uint64_t a = tc::smem_desc_kmajor_sw128(base + kStageA + ka * 16384u + ko, 1024);
-      const uint64_t bh = tc::smem_desc_kmajor_sw128(base + kStageBhi + ka * 8192u + ko, 1024);
-      const uint64_t bl = tc::smem_desc_kmajor_sw128(base + kStageBlo + ka * 8192u + ko, 1024);
-      tc::mma_tf32_ss_warp(cx.tmem + kDwCol, a, bh, kIdescDw, (first && b == 0 && ks == 0) ? 0u : 1u);
-      tc::mma_tf32_ss_warp(cx.tmem + kDwCol, a, bl, kIdescDw, 1u);
+      const uint64_t bb = tc::smem_desc_kmajor_sw128(base + kStageB + ka * 16384u + ko, 1024);
+      tc::mma_tf32_ss_warp(cx.tmem + kDwCol, a, bb, kIdescDw, (first && b == 0 && ks == 0) ? 0u : 1u);
     }
   }
   tc::commit_warp(bar_dwdone());
@@ -604,8 +604,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t o = a * 2048 + soff[t];
           *reinterpret_cast<uint32_t*>(stage + kStageA + ka * 16384u + o) = zh;
           *reinterpret_cast<uint32_t*>(stage + kStageA + ka * 16384u + 8192u + o) = zl;
-          *reinterpret_cast<uint32_t*>(stage + kStageBhi + ka * 8192u + o) = hh;
-          *reinterpret_cast<uint32_t*>(stage + kStageBlo + ka * 8192u + o) = hl;
+          *reinterpret_cast<uint32_t*>(stage + kStageB + ka * 16384u + o) = hh;
+          *reinterpret_cast<uint32_t*>(stage + kStageB + ka * 16384u + 8192u + o) = hl;
         }
         tc::fence_proxy_async_smem();
         if (!(alive = barrier_ok())) break;
@@ -631,9 +631,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc::fence_after_sync();
       {
         float* fb = reinterpret_cast<float*>(smem + kStageOff);
-        float v[16];
+        float v[16], w[16];  // columns i (h_hi) and 64 + i (h_lo) of this warp's row
         tc::ld_x16(tmem_warp + kDwCol + 16u * s, v);
+        tc::ld_x16(tmem_warp + kDwCol + 64u + 16u * s, w);
         tc::wait_ld();
+#pragma unroll
+        for (int k = 0; k < 16; ++k) v[k] += w[k];
 #pragma unroll
         for (int k = 0; k < 16; ++k) fb[row * kFlushStride + 16 * s + k] = v[k];
         tc::fence_before_sync();
