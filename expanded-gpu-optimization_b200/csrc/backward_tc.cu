@@ -13,13 +13,15 @@
 //     quadrants of the accumulator, summed when it is emptied. A and B are
 //     written by the threads straight from registers into two shared-memory staging
 //     buffers (128-byte-swizzled K-major: a warp writes 32 consecutive points of one row,
-//     conflict-free), one per point half, one jet component at a time.
+//     conflict-free), one per point half, one jet component at a time. The halves run
+//     independently (named barriers, one commit barrier each), so one half stages its next
+//     component while the tensor core works through the other half's MMAs.
 //
 // Where the data lives (one CTA per SM, persistent over tiles):
 //   * TMEM: accumulators D_c at columns 64c..64c+63 and a ring of two A-operand chunks at
-//     [256, 512), as in the forward kernel. The weight-gradient accumulator borrows ring
-//     columns [256, 384) while the ring is idle (after the input-adjoint GEMM of the layer
-//     has completed, before the next layer's chunks) and is emptied every layer;
+//     [256, 512), as in the forward kernel. The two weight-gradient accumulators (one per
+//     point half) borrow the ring while it is idle (after the input-adjoint GEMM of the
+//     layer has completed, before the next layer's chunks) and are emptied every layer;
 //   * shared memory: two weight slots (hi + lo, 32 KB each), the six operands of a tile's
 //     GEMMs (W1, W2, W3, then W3^T, W2^T, W1^T; all K-major) taking turns: a one-thread bulk
 //     copy reloads a slot from a pre-split global copy as soon as the GEMM that used it has
@@ -55,7 +57,7 @@ constexpr int kRing = 2;
 constexpr uint32_t kSlotCols = 128;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kRingCol = 256;
-constexpr uint32_t kDwCol = kRingCol;            // weight-gradient accumulator (borrowed)
+constexpr uint32_t kDwCol = kRingCol;            // weight-gradient accumulators (borrowed)
 constexpr uint32_t kIdesc = tc::idesc_tf32(128, 64);
 constexpr uint32_t kLbo = 128, kSbo = 2048;      // K-major no-swizzle canonical operand
 
@@ -92,7 +94,7 @@ constexpr int kPLoss = kPartKinds * 256, kPBout = kPLoss + 4;
 constexpr int kPartFloats = kPBout + 4;
 constexpr int kXsOff = kPartOff + kPartFloats * 4;            // the tile's points x[512], y[512]
 constexpr int kBarOff = kXsOff + 2 * kThreads * 4;            // mbarriers
-constexpr int kNumBars = 7;    // empty[2] dfull red wfull[2] dwdone
+constexpr int kNumBars = 8;    // empty[2] dfull red wfull[2] dwdone[2]
 constexpr int kCountOff = kBarOff + kNumBars * 8;
 constexpr int kMiscOff = kCountOff + 4 * 4;                   // TMEM base, abort flag, status
 constexpr int kSmemBytes = kMiscOff + 16;
@@ -114,7 +116,7 @@ __device__ __forceinline__ uint64_t* bar_empty(uint32_t r) { return bar_at(stati
 __device__ __forceinline__ uint64_t* bar_dfull() { return bar_at(kRing); }
 __device__ __forceinline__ uint64_t* bar_red() { return bar_at(kRing + 1); }
 __device__ __forceinline__ uint64_t* bar_wfull(int k) { return bar_at(kRing + 2 + k); }
-__device__ __forceinline__ uint64_t* bar_dwdone() { return bar_at(kRing + 4); }
+__device__ __forceinline__ uint64_t* bar_dwdone(int half) { return bar_at(kRing + 4 + half); }
 __device__ __forceinline__ uint32_t* ring_count(uint32_t r) {
   return reinterpret_cast<uint32_t*>(dsmem() + kCountOff) + r;
 }
@@ -268,23 +270,26 @@ __device__ __forceinline__ void adjoint_h(float a, float hj0, float hj1, float h
   g1 = z1;
 }
 
-// The 16 weight-gradient MMAs of one jet component (M = 128, N = 128, K = 8): both staging
-// buffers (point halves), 8 K steps of 8 points each. Issued by one converged warp, then
-// committed.
-__device__ __forceinline__ void issue_dw_mmas(const Ctx& cx, bool first) {
+// The 8 weight-gradient MMAs of one jet component for one point half (M = 128, N = 128,
+// K = 8 points each) into that half's accumulator. Issued by one converged warp of the
+// half, then committed to the half's barrier.
+__device__ __forceinline__ void issue_dw_mmas(const Ctx& cx, int half, bool first) {
   constexpr uint32_t kIdescDw = tc::idesc_tf32(128, 128);
+  const uint32_t base = smem_u32(dsmem() + kStageOff + half * kStageBytes);
+  const uint32_t d = cx.tmem + kDwCol + 128u * static_cast<uint32_t>(half);
 #pragma unroll
-  for (int b = 0; b < 2; ++b) {
-    const uint32_t base = smem_u32(dsmem() + kStageOff + b * kStageBytes);
-#pragma unroll
-    for (int ks = 0; ks < 8; ++ks) {
-      const uint32_t ka = static_cast<uint32_t>(ks >> 2), ko = static_cast<uint32_t>(ks & 3) * 32u;
-      const uint64_t a = tc::smem_desc_kmajor_sw128(base + kStageA + ka * 16384u + ko, 1024);
-      const uint64_t bb = tc::smem_desc_kmajor_sw128(base + kStageB + ka * 16384u + ko, 1024);
-      tc::mma_tf32_ss_warp(cx.tmem + kDwCol, a, bb, kIdescDw, (first && b == 0 && ks == 0) ? 0u : 1u);
-    }
+  for (int ks = 0; ks < 8; ++ks) {
+    const uint32_t ka = static_cast<uint32_t>(ks >> 2), ko = static_cast<uint32_t>(ks & 3) * 32u;
+    const uint64_t a = tc::smem_desc_kmajor_sw128(base + kStageA + ka * 16384u + ko, 1024);
+    const uint64_t bb = tc::smem_desc_kmajor_sw128(base + kStageB + ka * 16384u + ko, 1024);
+    tc::mma_tf32_ss_warp(d, a, bb, kIdescDw, (first && ks == 0) ? 0u : 1u);
   }
-  tc::commit_warp(bar_dwdone());
+  tc::commit_warp(bar_dwdone(half));
+}
+
+// Barrier over the 8 warps (256 threads) of one point half; ids 1 and 2 (0 is __syncthreads).
+__device__ __forceinline__ void half_barrier(int half) {
+  asm volatile("bar.sync %0, 256;" ::"r"(1 + half) : "memory");
 }
 
 // Sums v[i] over the 32 lanes of the warp for every i < 16 with a fixed butterfly that
@@ -398,7 +403,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(bar_dfull(), 1);
     mbar_init(bar_red(), kWarps);
     for (int k = 0; k < kWeightSlots; ++k) mbar_init(bar_wfull(k), 1);
-    mbar_init(bar_dwdone(), 1);
+    mbar_init(bar_dwdone(0), 1);
+    mbar_init(bar_dwdone(1), 1);
     *abort_flag() = 0u;
     *status_slot() = status;
     fence_barrier_init();
@@ -431,6 +437,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                     4 * (lane & 3));
   }
   const uint32_t ka = static_cast<uint32_t>(q & 1);
+  const int half = q >> 1;
 
   uint32_t chunk = 0, mlayer = 0, tile_count = 0, dw_issued = 0;
   bool alive = true;
@@ -593,7 +600,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             hv[i] = c == 0 ? v : c == 1 ? j0 : c == 2 ? j1 : lv;
           }
         }
-        if (c > 0) warp_wait(bar_dwdone(), (dw_issued - 1u) & 1u);  // staging free again
+        if (c > 0) warp_wait(bar_dwdone(half), (dw_issued - 1u) & 1u);  // buffer free again
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           const int a = i >> 2, t = i & 3;
@@ -608,32 +615,45 @@ __global__ void __launch_bounds__(kThreads, 1)
           *reinterpret_cast<uint32_t*>(stage + kStageB + ka * 16384u + 8192u + o) = hl;
         }
         tc::fence_proxy_async_smem();
-        if (!(alive = barrier_ok())) break;
-        if (warp == 0) {
+        half_barrier(half);
+        if (s == 0 && (q & 1) == 0) {  // warp 2 * half issues for its half
           if (c == 0) {
             // the input-adjoint GEMM g has finished with the ring columns the weight-gradient
-            // accumulator borrows, and with its weight slot
+            // accumulators borrow, and with its weight slot
             warp_wait(bar_dfull(), mlayer & 1u);
             tc::fence_after_sync();
-            if (lane == 0 && (g + 2 < kGemmsPerTile || has_next))
+            if (half == 0 && lane == 0 && (g + 2 < kGemmsPerTile || has_next))
               load_weight_slot(g & 1, wsplit, weight_block((g + 2) % kGemmsPerTile));
           }
           tc::fence_after_sync();
-          issue_dw_mmas(cx, c == 0);
+          issue_dw_mmas(cx, half, c == 0);
         }
         ++dw_issued;
       }
-      if (!alive) break;
 
       // empty the accumulator into this CTA's partial row: hi and lo halves summed in shared
       // memory (staging buffer 0), one owner thread per entry
-      warp_wait(bar_dwdone(), (dw_issued - 1u) & 1u);
+      // Both halves first pass this barrier: each half has then waited for its round-2
+      // commit, so the parity wait below can only mean round 3 (without it, a half that is
+      // two rounds behind would satisfy the wait with its round-1 phase).
+      if (!(alive = barrier_ok())) break;
+      warp_wait(bar_dwdone(0), (dw_issued - 1u) & 1u);
+      warp_wait(bar_dwdone(1), (dw_issued - 1u) & 1u);
       tc::fence_after_sync();
       {
         float* fb = reinterpret_cast<float*>(smem + kStageOff);
-        float v[16], w[16];  // columns i (h_hi) and 64 + i (h_lo) of this warp's row
+        // columns i (h_hi) and 64 + i (h_lo) of this warp's row, in both halves' accumulators
+        float v[16], w[16];
         tc::ld_x16(tmem_warp + kDwCol + 16u * s, v);
         tc::ld_x16(tmem_warp + kDwCol + 64u + 16u * s, w);
+        tc::wait_ld();
+#pragma unroll
+        for (int k = 0; k < 16; ++k) v[k] += w[k];
+        tc::ld_x16(tmem_warp + kDwCol + 128u + 16u * s, w);
+        tc::wait_ld();
+#pragma unroll
+        for (int k = 0; k < 16; ++k) v[k] += w[k];
+        tc::ld_x16(tmem_warp + kDwCol + 192u + 16u * s, w);
         tc::wait_ld();
 #pragma unroll
         for (int k = 0; k < 16; ++k) v[k] += w[k];
