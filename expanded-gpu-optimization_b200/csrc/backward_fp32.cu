@@ -149,11 +149,11 @@ __device__ __forceinline__ void store_jet(float* buf, int o, int lane, float v, 
 
 template <bool kPoisson>
 __global__ void __launch_bounds__(kThreads, 1)
-    backward_fp32_kernel(const float* __restrict__ coords, const float* __restrict__ params,
+    backward_fp32_kernel(const PointSets ps, const float* __restrict__ params,
                          const float* __restrict__ grad_u, const float* __restrict__ grad_lap,
                          float* __restrict__ grad_coords, float* __restrict__ lap_out,
-                         float* __restrict__ partials, int64_t n, int64_t tiles,
-                         float inv_total, int params_aligned, unsigned int* status) {
+                         float* __restrict__ partials, int64_t tiles, int params_aligned,
+                         unsigned int* status) {
   extern __shared__ __align__(16) float smem[];
   float* sp = smem;
   float* hbuf = sp + kParamSmemFloats;  // forward jet h, [4][64][kStride]
@@ -186,11 +186,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int k = 0; k < 4; ++k) dw[l][j][k] = 0.0f;
 
   for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
-    const int64_t p = tile * kTile + lane;
-    const bool active = p < n;
+    const bool btile = tile >= ps.tiles;  // a tile of the boundary set (PINN step)
+    const int64_t p = (btile ? tile - ps.tiles : tile) * kTile + lane;
+    const bool active = p < (btile ? ps.nb : ps.n);
     if (tid < kTile) {
-      pts[tid] = active ? coords[2 * p] : 0.0f;
-      pts[kTile + tid] = active ? coords[2 * p + 1] : 0.0f;
+      load_point(ps, tile, kTile, tid, pts[tid], pts[kTile + tid]);
       if (!kPoisson) {
         pts[2 * kTile + tid] = (active && grad_u != nullptr) ? grad_u[p] : 0.0f;
         pts[3 * kTile + tid] = active ? grad_lap[p] : 0.0f;
@@ -243,24 +243,45 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       float gu, gl;
       if (kPoisson) {
-        float part = 0.0f;
+        float part = 0.0f, partu = 0.0f;
 #pragma unroll
-        for (int k = 0; k < 8; ++k) part = fmaf(wout[o0 + k], h3l[k], part);
+        for (int k = 0; k < 8; ++k) {
+          part = fmaf(wout[o0 + k], h3l[k], part);
+          partu = fmaf(wout[o0 + k], h3v[k], partu);
+        }
         red[warp * kTile + lane] = part;
+        red[(kWarps + warp) * kTile + lane] = partu;
         __syncthreads();
-        float lap = 0.0f;
+        float term;  // this point's loss term
+        if (!btile) {
+          float lap = 0.0f;
 #pragma unroll
-        for (int w = 0; w < kWarps; ++w) lap += red[w * kTile + lane];
-        // f = -2 pi^2 sin(pi x) sin(pi y)  (src/fused_hoad/problems/poisson.py:29-39)
-        const float pi = 3.14159265358979323846f;
-        const float f = -2.0f * pi * pi * (sinf(pi * x0) * sinf(pi * x1));
-        const float r = active ? lap - f : 0.0f;
-        gu = 0.0f;
-        gl = 2.0f * r * inv_total;
+          for (int w = 0; w < kWarps; ++w) lap += red[w * kTile + lane];
+          // f = -2 pi^2 sin(pi x) sin(pi y)  (src/fused_hoad/problems/poisson.py:29-39)
+          const float pi = 3.14159265358979323846f;
+          const float f = -2.0f * pi * pi * (sinf(pi * x0) * sinf(pi * x1));
+          const float r = active ? lap - f : 0.0f;
+          gu = 0.0f;
+          gl = 2.0f * r * ps.inv_total;
+          term = r * r * ps.inv_total;
+          if (warp == 0 && active && lap_out != nullptr) lap_out[p] = lap;
+        } else {
+          // boundary term weight * u^2 / boundary_total (src/fused_hoad/training.py:90-92)
+          float u = sp[kOutBase + kWidth];
+#pragma unroll
+          for (int w = 0; w < kWarps; ++w) u += red[(kWarps + w) * kTile + lane];
+          u = active ? u : 0.0f;
+          gu = 2.0f * ps.bweight * u * ps.inv_btotal;
+          gl = 0.0f;
+          term = ps.bweight * u * u * ps.inv_btotal;
+        }
         if (warp == 0) {
-          if (active && lap_out != nullptr) lap_out[p] = lap;
-          const float l2 = warp_sum(r * r);
-          if (lane == 0) small[kSmallLoss] += l2 * inv_total;
+          const float l2 = warp_sum(term);
+          const float sg = btile ? warp_sum(gu) : 0.0f;  // b_out gradient (boundary term)
+          if (lane == 0) {
+            small[kSmallLoss] += l2;
+            small[kSmallBout] += sg;
+          }
         }
       } else {
         gu = pts[2 * kTile + lane];
@@ -350,7 +371,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     red[warp * kTile + lane] = gx0;
     red[(kWarps + warp) * kTile + lane] = gx1;
     __syncthreads();  // also: every read of adj/hbuf for this tile is done
-    if (warp == 0 && active && grad_coords != nullptr) {
+    if (warp == 0 && active && !btile && grad_coords != nullptr) {
       float s0 = 0.0f, s1 = 0.0f;
 #pragma unroll
       for (int w = 0; w < kWarps; ++w) {
@@ -437,28 +458,28 @@ cudaError_t prepare_backward_fp32() {
   return e;
 }
 
-int backward_grid(int64_t n, const DeviceInfo& dev) {
-  const int64_t tiles = (n + kTile - 1) / kTile;
+int backward_grid(int64_t n, int64_t nb, const DeviceInfo& dev) {
+  const int64_t tiles = (n + kTile - 1) / kTile + (nb + kTile - 1) / kTile;
   return static_cast<int>(std::min<int64_t>(tiles, dev.sms));
 }
 
-cudaError_t launch_backward_fp32(const float* coords, const float* params,
+cudaError_t launch_backward_fp32(const PointSets& points, const float* params,
                                  const float* grad_u, const float* grad_lap,
                                  float* grad_coords, float* lap_out, float* partials,
-                                 int64_t n, int64_t n_total, bool poisson,
-                                 const DeviceInfo& dev, cudaStream_t stream) {
-  const int64_t tiles = (n + kTile - 1) / kTile;
-  const int grid = backward_grid(n, dev);
+                                 bool poisson, const DeviceInfo& dev, cudaStream_t stream) {
+  PointSets ps = points;
+  ps.tiles = (ps.n + kTile - 1) / kTile;
+  const int64_t tiles = ps.tiles + (ps.nb + kTile - 1) / kTile;
+  const int grid = backward_grid(ps.n, ps.nb, dev);
   const int aligned = (reinterpret_cast<uintptr_t>(params) % 16) == 0;
-  const float inv_total = n_total > 0 ? static_cast<float>(1.0 / static_cast<double>(n_total)) : 0.0f;
   if (poisson) {
     backward_fp32_kernel<true><<<grid, kThreads, kSmem, stream>>>(
-        coords, params, nullptr, nullptr, grad_coords, lap_out, partials, n, tiles, inv_total,
-        aligned, dev.status);
+        ps, params, nullptr, nullptr, grad_coords, lap_out, partials, tiles, aligned,
+        dev.status);
   } else {
     backward_fp32_kernel<false><<<grid, kThreads, kSmem, stream>>>(
-        coords, params, grad_u, grad_lap, grad_coords, nullptr, partials, n, tiles, 0.0f,
-        aligned, dev.status);
+        ps, params, grad_u, grad_lap, grad_coords, nullptr, partials, tiles, aligned,
+        dev.status);
   }
   return cudaGetLastError();
 }

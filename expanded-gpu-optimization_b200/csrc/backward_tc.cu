@@ -356,12 +356,11 @@ __global__ void __launch_bounds__(256) prep_weights_kernel(const float* __restri
 
 template <bool kPoisson>
 __global__ void __launch_bounds__(kThreads, 1)
-    backward_tc_kernel(const float* __restrict__ coords, const float* __restrict__ params,
+    backward_tc_kernel(const PointSets ps, const float* __restrict__ params,
                        const float* __restrict__ wsplit, const float* __restrict__ grad_u,
                        const float* __restrict__ grad_lap, float* __restrict__ grad_coords,
                        float* __restrict__ lap_out, float* __restrict__ partials,
-                       float* __restrict__ scratch, int64_t n, int64_t tiles, float inv_total,
-                       unsigned int* status) {
+                       float* __restrict__ scratch, int64_t tiles, unsigned int* status) {
   uint8_t* const smem = dsmem();
   float* small = reinterpret_cast<float*>(smem + kSmallOff);
   float* grad = reinterpret_cast<float*>(smem + kGradOff);
@@ -442,17 +441,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t chunk = 0, mlayer = 0, tile_count = 0, dw_issued = 0;
   bool alive = true;
   float nx0 = 0.0f, nx1 = 0.0f;
-  {
-    const int64_t p = static_cast<int64_t>(blockIdx.x) * kTile + row;
-    if (p < n) {
-      nx0 = coords[2 * p];
-      nx1 = coords[2 * p + 1];
-    }
-  }
+  load_point(ps, blockIdx.x, kTile, row, nx0, nx1);
   for (int64_t tile = blockIdx.x; alive && tile < tiles; tile += gridDim.x, ++tile_count) {
     const bool has_next = tile + gridDim.x < tiles;
-    const int64_t p = tile * kTile + row;
-    const bool active = p < n;
+    const bool btile = tile >= ps.tiles;  // a tile of the boundary set (PINN step)
+    const int64_t p = (btile ? tile - ps.tiles : tile) * kTile + row;
+    const bool active = p < (btile ? ps.nb : ps.n);
     // This tile's point, loaded during the previous tile, is kept in shared memory so that
     // no register holds it through the backward sweep.
     xs[tid] = nx0;
@@ -527,16 +521,34 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int k = 0; k < 4; ++k) lap += red[(4 + k) * kTile + row];
       float gu, gl;
       if (kPoisson) {
-        // f = -2 pi^2 sin(pi x) sin(pi y)  (src/fused_hoad/problems/poisson.py:29-39)
-        const float pi = 3.14159265358979323846f;
-        const float f = -2.0f * pi * pi * (sinf(pi * xs[tid]) * sinf(pi * xs[kThreads + tid]));
-        const float r = active ? lap - f : 0.0f;
-        gu = 0.0f;
-        gl = 2.0f * r * inv_total;
+        float term;  // this point's loss term
+        if (!btile) {
+          // f = -2 pi^2 sin(pi x) sin(pi y)  (src/fused_hoad/problems/poisson.py:29-39)
+          const float pi = 3.14159265358979323846f;
+          const float f =
+              -2.0f * pi * pi * (sinf(pi * xs[tid]) * sinf(pi * xs[kThreads + tid]));
+          const float r = active ? lap - f : 0.0f;
+          gu = 0.0f;
+          gl = 2.0f * r * ps.inv_total;
+          term = r * r * ps.inv_total;
+          if (s == 0 && active && lap_out != nullptr) lap_out[p] = lap;
+        } else {
+          // boundary term weight * u^2 / boundary_total (src/fused_hoad/training.py:90-92)
+          float u = small[kSmBout];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) u += red[k * kTile + row];
+          u = active ? u : 0.0f;
+          gu = 2.0f * ps.bweight * u * ps.inv_btotal;
+          gl = 0.0f;
+          term = ps.bweight * u * u * ps.inv_btotal;
+        }
         if (s == 0) {
-          if (active && lap_out != nullptr) lap_out[p] = lap;
-          const float l2 = warp_sum(r * r);
-          if (lane == 0) part[kPLoss + q] = l2;
+          const float l2 = warp_sum(term);
+          const float sg = btile ? warp_sum(gu) : 0.0f;  // b_out gradient (boundary term)
+          if (lane == 0) {
+            part[kPLoss + q] = l2;
+            part[kPBout + q] = sg;
+          }
         }
       } else {
         gu = (active && grad_u != nullptr) ? grad_u[p] : 0.0f;
@@ -714,13 +726,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (!alive) break;
 
     // The next tile's point: loaded now, used at the next tile's start.
-    {
-      const int64_t pn = p + static_cast<int64_t>(gridDim.x) * kTile;
-      if (pn < n) {
-        nx0 = coords[2 * pn];
-        nx1 = coords[2 * pn + 1];
-      }
-    }
+    load_point(ps, tile + gridDim.x, kTile, row, nx0, nx1);
 
     // ---- layer 0: z_v = W0 x + b0, z_J = W0, z_L = 0; d holds hbar_0 ----
     {
@@ -748,7 +754,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       red[(4 + s) * kTile + row] = gx1;
     }
     if (!(alive = barrier_ok())) break;
-    if (s == 0 && active && grad_coords != nullptr) {
+    if (s == 0 && active && !btile && grad_coords != nullptr) {
       float sx = 0.0f, sy = 0.0f;
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
@@ -768,13 +774,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       else if (kind <= 3) grad[kGW0 + 2 * o + (kind - 2)] += v;
       else grad[kGBias + (kind - 3) * kWidth + o] += v;
     } else if (tid == kPartKinds * kWidth) {
-      if (kPoisson) {
-        grad[kGLoss] += (((part[kPLoss] + part[kPLoss + 1]) + part[kPLoss + 2]) + part[kPLoss + 3]) *
-                        inv_total;
-      } else {
-        grad[kGBout] +=
-            ((part[kPBout] + part[kPBout + 1]) + part[kPBout + 2]) + part[kPBout + 3];
-      }
+      if (kPoisson)
+        grad[kGLoss] += ((part[kPLoss] + part[kPLoss + 1]) + part[kPLoss + 2]) + part[kPLoss + 3];
+      grad[kGBout] += ((part[kPBout] + part[kPBout + 1]) + part[kPBout + 2]) + part[kPBout + 3];
     }
     if (!(alive = barrier_ok())) break;
   }
@@ -821,38 +823,38 @@ cudaError_t prepare_backward_tc() {
   return e;
 }
 
-int backward_tc_grid(int64_t n, const DeviceInfo& dev) {
-  const int64_t tiles = (n + kTile - 1) / kTile;
+int backward_tc_grid(int64_t n, int64_t nb, const DeviceInfo& dev) {
+  const int64_t tiles = (n + kTile - 1) / kTile + (nb + kTile - 1) / kTile;
   return static_cast<int>(std::min<int64_t>(tiles, dev.sms));
 }
 
-size_t backward_tc_workspace_bytes(int64_t n, const DeviceInfo& dev) {
-  const size_t grid = static_cast<size_t>(backward_tc_grid(n, dev));
+size_t backward_tc_workspace_bytes(int64_t n, int64_t nb, const DeviceInfo& dev) {
+  const size_t grid = static_cast<size_t>(backward_tc_grid(n, nb, dev));
   return (static_cast<size_t>(kWeightBlocks) * (kLayerBytes / 4) + grid * kRowStride +
           grid * kScratchFloats) *
          sizeof(float);
 }
 
-cudaError_t launch_backward_tc(const float* coords, const float* params, const float* grad_u,
-                               const float* grad_lap, float* grad_coords, float* lap_out,
-                               float* workspace, int64_t n, int64_t n_total, bool poisson,
+cudaError_t launch_backward_tc(const PointSets& points, const float* params,
+                               const float* grad_u, const float* grad_lap, float* grad_coords,
+                               float* lap_out, float* workspace, bool poisson,
                                const DeviceInfo& dev, cudaStream_t stream) {
-  const int64_t tiles = (n + kTile - 1) / kTile;
-  const int grid = backward_tc_grid(n, dev);
+  PointSets ps = points;
+  ps.tiles = (ps.n + kTile - 1) / kTile;
+  const int64_t tiles = ps.tiles + (ps.nb + kTile - 1) / kTile;
+  const int grid = backward_tc_grid(ps.n, ps.nb, dev);
   float* wsplit = workspace;
   float* partials = wsplit + kWeightBlocks * (kLayerBytes / 4);
   float* scratch = partials + static_cast<size_t>(grid) * kRowStride;
   prep_weights_kernel<<<(kWeightBlocks * 4096 + 255) / 256, 256, 0, stream>>>(params, wsplit);
-  const float inv_total =
-      n_total > 0 ? static_cast<float>(1.0 / static_cast<double>(n_total)) : 0.0f;
   if (poisson) {
     backward_tc_kernel<true><<<grid, kThreads, kSmemBytes, stream>>>(
-        coords, params, wsplit, nullptr, nullptr, grad_coords, lap_out, partials, scratch, n,
-        tiles, inv_total, dev.status);
+        ps, params, wsplit, nullptr, nullptr, grad_coords, lap_out, partials, scratch, tiles,
+        dev.status);
   } else {
     backward_tc_kernel<false><<<grid, kThreads, kSmemBytes, stream>>>(
-        coords, params, wsplit, grad_u, grad_lap, grad_coords, nullptr, partials, scratch, n,
-        tiles, 0.0f, dev.status);
+        ps, params, wsplit, grad_u, grad_lap, grad_coords, nullptr, partials, scratch, tiles,
+        dev.status);
   }
   return cudaGetLastError();
 }

@@ -180,6 +180,38 @@ std::vector<torch::Tensor> poisson_step_gradients(torch::Tensor coordinates,
   return {grad_and_loss, laplacian, grad_coordinates};
 }
 
+// Fused gradients of the full PINN loss (residual on `coordinates` + boundary_weight *
+// mean(u^2) on `boundary`); see fhb_pinn_step_gradients. Returns grad_and_loss [12738]
+// (gradient, then this shard's loss). The totals are the global counts of each set.
+torch::Tensor pinn_step_gradients(torch::Tensor coordinates, torch::Tensor boundary,
+                                  torch::Tensor parameters, int64_t total_points,
+                                  int64_t boundary_total, double boundary_weight,
+                                  int64_t version) {
+  check_inputs(coordinates, parameters);
+  check_inputs(boundary, parameters);
+  const c10::cuda::CUDAGuard device_guard(coordinates.device());
+  const int64_t batch = coordinates.size(0), nb = boundary.size(0);
+  TORCH_CHECK(total_points >= batch, "total_points must be >= the local batch");
+  TORCH_CHECK(boundary_total >= nb, "boundary_total must be >= the local boundary batch");
+  TORCH_CHECK(version >= 1 && version <= 6, "backward version must be 1 to 6");
+  auto grad_and_loss = torch::empty({kParameterCount + 1}, parameters.options());
+  const size_t bytes = fhb_pinn_step_workspace_bytes(batch, nb);
+  auto workspace =
+      torch::empty({static_cast<int64_t>((bytes + sizeof(float) - 1) / sizeof(float))},
+                   parameters.options());
+  float* out = grad_and_loss.data_ptr<float>();
+  check_status(fhb_pinn_step_gradients(
+                   coordinates.data_ptr<float>(), batch, total_points,
+                   boundary.data_ptr<float>(), nb, boundary_total,
+                   static_cast<float>(boundary_weight), parameters.data_ptr<float>(), out,
+                   out + kParameterCount, static_cast<int>(version),
+                   bytes ? workspace.data_ptr<float>() : nullptr,
+                   static_cast<size_t>(workspace.numel()) * sizeof(float),
+                   at::cuda::getCurrentCUDAStream()),
+               "pinn_step_gradients");
+  return grad_and_loss;
+}
+
 // In-place Adam on flat buffers; `step` is a CUDA int64 tensor of one element.
 void adam_step(torch::Tensor parameters, torch::Tensor grad, torch::Tensor exp_avg,
                torch::Tensor exp_avg_sq, torch::Tensor step, double lr, double beta1,
@@ -227,6 +259,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, module) {
              pybind11::arg("coordinates"), pybind11::arg("parameters"),
              pybind11::arg("version") = 3, pybind11::arg("output") = pybind11::none(),
              pybind11::arg("laplacian") = pybind11::none());
+  module.def("pinn_step_gradients", &pinn_step_gradients,
+             "Fused gradients of the Poisson PINN loss (interior residual + boundary term)",
+             pybind11::arg("coordinates"), pybind11::arg("boundary"),
+             pybind11::arg("parameters"), pybind11::arg("total_points"),
+             pybind11::arg("boundary_total"), pybind11::arg("boundary_weight") = 100.0,
+             pybind11::arg("version") = 6);
   module.def("poisson_step_gradients", &poisson_step_gradients,
              "Fused forward + interior Poisson loss + backward in one persistent kernel",
              pybind11::arg("coordinates"), pybind11::arg("parameters"),

@@ -76,11 +76,11 @@ int current_device(const fhb::DeviceInfo** info) {
 
 // Enough for either backward kernel: the FP32 one needs one partial row per CTA, the
 // tensor-core one also its pre-split weights and per-CTA scratch.
-size_t backward_workspace_bytes(int64_t n, const fhb::DeviceInfo& dev) {
-  if (n <= 0) return 0;
+size_t backward_workspace_bytes(int64_t n, int64_t nb, const fhb::DeviceInfo& dev) {
+  if (n + nb <= 0) return 0;
   const size_t fp32 =
-      static_cast<size_t>(fhb::backward_grid(n, dev)) * fhb::kRowStride * sizeof(float);
-  return std::max(fp32, fhb::backward_tc_workspace_bytes(n, dev));
+      static_cast<size_t>(fhb::backward_grid(n, nb, dev)) * fhb::kRowStride * sizeof(float);
+  return std::max(fp32, fhb::backward_tc_workspace_bytes(n, nb, dev));
 }
 
 bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
@@ -128,45 +128,55 @@ int fhb_forward(const float* coords, const float* params, float* u, float* lap, 
 size_t fhb_backward_workspace_bytes(int64_t n) {
   const fhb::DeviceInfo* dev = nullptr;
   if (current_device(&dev) != FHB_OK) return 0;
-  return backward_workspace_bytes(n, *dev);
+  return backward_workspace_bytes(n, 0, *dev);
 }
 
-static int backward_common(const float* coords, const float* params, const float* grad_u,
+static int backward_common(const fhb::PointSets& ps, const float* params, const float* grad_u,
                            const float* grad_lap, float* grad_params, float* grad_coords,
-                           float* lap_out, float* loss, int64_t n, int64_t n_total,
-                           bool poisson, bool tensor_core, void* workspace,
-                           size_t workspace_bytes, cudaStream_t stream) {
-  if (n < 0 || !params || !grad_params) return FHB_ERR_INVALID_ARGUMENT;
-  if (poisson && (!loss || n_total < n)) return FHB_ERR_INVALID_ARGUMENT;
+                           float* lap_out, float* loss, bool poisson, bool tensor_core,
+                           void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  if (ps.n < 0 || ps.nb < 0 || !params || !grad_params) return FHB_ERR_INVALID_ARGUMENT;
+  if (poisson && !loss) return FHB_ERR_INVALID_ARGUMENT;
   const fhb::DeviceInfo* dev = nullptr;
   int code = current_device(&dev);
   if (code != FHB_OK) return code;
-  if (n == 0) {
+  if (ps.n + ps.nb == 0) {
     cudaError_t e = cudaMemsetAsync(grad_params, 0, fhb::kParamCount * sizeof(float), stream);
     if (e == cudaSuccess && poisson) e = cudaMemsetAsync(loss, 0, sizeof(float), stream);
     return record(e);
   }
-  if (!coords || (!poisson && !grad_lap)) return FHB_ERR_INVALID_ARGUMENT;
-  if (!aligned(coords, 4) || !aligned(params, 4)) return FHB_ERR_MISALIGNED;
-  const size_t need = backward_workspace_bytes(n, *dev);
+  if ((ps.n > 0 && !ps.interior) || (ps.nb > 0 && !ps.boundary) || (!poisson && !grad_lap))
+    return FHB_ERR_INVALID_ARGUMENT;
+  if (!aligned(ps.interior, 4) || !aligned(ps.boundary, 4) || !aligned(params, 4))
+    return FHB_ERR_MISALIGNED;
+  const size_t need = backward_workspace_bytes(ps.n, ps.nb, *dev);
   if (workspace == nullptr || workspace_bytes < need) return FHB_ERR_WORKSPACE;
   if (!aligned(workspace, 16)) return FHB_ERR_MISALIGNED;
   float* ws = static_cast<float*>(workspace);
   cudaError_t e;
   if (tensor_core) {
-    e = fhb::launch_backward_tc(coords, params, grad_u, grad_lap, grad_coords, lap_out, ws, n,
-                                n_total, poisson, *dev, stream);
+    e = fhb::launch_backward_tc(ps, params, grad_u, grad_lap, grad_coords, lap_out, ws, poisson,
+                                *dev, stream);
     if (e == cudaSuccess)
-      e = fhb::launch_reduce_rows(fhb::backward_tc_partials(ws), fhb::backward_tc_grid(n, *dev),
-                                  grad_params, poisson ? loss : nullptr, stream);
+      e = fhb::launch_reduce_rows(fhb::backward_tc_partials(ws),
+                                  fhb::backward_tc_grid(ps.n, ps.nb, *dev), grad_params,
+                                  poisson ? loss : nullptr, stream);
   } else {
-    e = fhb::launch_backward_fp32(coords, params, grad_u, grad_lap, grad_coords, lap_out, ws, n,
-                                  n_total, poisson, *dev, stream);
+    e = fhb::launch_backward_fp32(ps, params, grad_u, grad_lap, grad_coords, lap_out, ws,
+                                  poisson, *dev, stream);
     if (e == cudaSuccess)
-      e = fhb::launch_reduce_rows(ws, fhb::backward_grid(n, *dev), grad_params,
+      e = fhb::launch_reduce_rows(ws, fhb::backward_grid(ps.n, ps.nb, *dev), grad_params,
                                   poisson ? loss : nullptr, stream);
   }
   return record(e);
+}
+
+static fhb::PointSets interior_only(const float* coords, int64_t n, int64_t n_total) {
+  fhb::PointSets ps;
+  ps.interior = coords;
+  ps.n = n;
+  ps.inv_total = n_total > 0 ? static_cast<float>(1.0 / static_cast<double>(n_total)) : 0.0f;
+  return ps;
 }
 
 int fhb_backward(const float* coords, const float* params, const float* grad_u,
@@ -174,20 +184,50 @@ int fhb_backward(const float* coords, const float* params, const float* grad_u,
                  int version, void* workspace, size_t workspace_bytes, fhb_stream_t stream) {
   if (version < FHB_BACKWARD_VERSION_MIN || version > FHB_BACKWARD_VERSION_MAX)
     return FHB_ERR_INVALID_ARGUMENT;
-  return backward_common(coords, params, grad_u, grad_lap, grad_params, grad_coords, nullptr,
-                         nullptr, n, n, false, version == FHB_BACKWARD_VERSION_TENSOR_CORE,
-                         workspace, workspace_bytes, stream);
+  return backward_common(interior_only(coords, n, n), params, grad_u, grad_lap, grad_params,
+                         grad_coords, nullptr, nullptr, false,
+                         version == FHB_BACKWARD_VERSION_TENSOR_CORE, workspace,
+                         workspace_bytes, stream);
 }
 
 int fhb_poisson_step_gradients(const float* coords, const float* params, int64_t n,
                                int64_t n_total, float* grad_params, float* grad_coords,
                                float* lap_out, float* loss, int version, void* workspace,
                                size_t workspace_bytes, fhb_stream_t stream) {
-  if (version < FHB_BACKWARD_VERSION_MIN || version > FHB_BACKWARD_VERSION_MAX)
+  if (version < FHB_BACKWARD_VERSION_MIN || version > FHB_BACKWARD_VERSION_MAX ||
+      n_total < n)
     return FHB_ERR_INVALID_ARGUMENT;
-  return backward_common(coords, params, nullptr, nullptr, grad_params, grad_coords, lap_out,
-                         loss, n, n_total, true, version == FHB_BACKWARD_VERSION_TENSOR_CORE,
-                         workspace, workspace_bytes, stream);
+  return backward_common(interior_only(coords, n, n_total), params, nullptr, nullptr,
+                         grad_params, grad_coords, lap_out, loss, true,
+                         version == FHB_BACKWARD_VERSION_TENSOR_CORE, workspace,
+                         workspace_bytes, stream);
+}
+
+size_t fhb_pinn_step_workspace_bytes(int64_t n, int64_t n_boundary) {
+  const fhb::DeviceInfo* dev = nullptr;
+  if (n < 0 || n_boundary < 0 || current_device(&dev) != FHB_OK) return 0;
+  return backward_workspace_bytes(n, n_boundary, *dev);
+}
+
+int fhb_pinn_step_gradients(const float* coords, int64_t n, int64_t n_total,
+                            const float* boundary, int64_t n_boundary,
+                            int64_t n_boundary_total, float boundary_weight,
+                            const float* params, float* grad_params, float* loss, int version,
+                            void* workspace, size_t workspace_bytes, fhb_stream_t stream) {
+  if (version < FHB_BACKWARD_VERSION_MIN || version > FHB_BACKWARD_VERSION_MAX || n < 0 ||
+      n_boundary < 0 || n_total < n || n_boundary_total < n_boundary ||
+      !(boundary_weight >= 0.0f))
+    return FHB_ERR_INVALID_ARGUMENT;
+  fhb::PointSets ps = interior_only(coords, n, n_total);
+  ps.boundary = boundary;
+  ps.nb = n_boundary;
+  ps.inv_btotal = n_boundary_total > 0
+                      ? static_cast<float>(1.0 / static_cast<double>(n_boundary_total))
+                      : 0.0f;
+  ps.bweight = boundary_weight;
+  return backward_common(ps, params, nullptr, nullptr, grad_params, nullptr, nullptr, loss,
+                         true, version == FHB_BACKWARD_VERSION_TENSOR_CORE, workspace,
+                         workspace_bytes, stream);
 }
 
 int fhb_adam_step(float* params, const float* grad, float* exp_avg, float* exp_avg_sq,

@@ -11,6 +11,37 @@ namespace fhb {
 constexpr int kRowStride = 12740;
 constexpr int kLossColumn = 12737;
 
+// The points of one backward launch: the interior set (the VJP's points, or the collocation
+// points of the Poisson residual) and, for the PINN step, a boundary set whose loss term is
+// bweight * u^2 / nb_total. Tiles of the interior set come first, then the boundary's.
+struct PointSets {
+  const float* interior = nullptr;  // [n][2]
+  int64_t n = 0;
+  int64_t tiles = 0;                // tiles of the interior set (set by the launcher)
+  const float* boundary = nullptr;  // [nb][2]
+  int64_t nb = 0;
+  float inv_total = 0.0f;           // 1 / n_total: the residual term's normaliser
+  float inv_btotal = 0.0f;          // 1 / nb_total
+  float bweight = 0.0f;             // boundary term weight
+};
+
+#ifdef __CUDACC__
+// Coordinates of point `row` of tile `tile` (tiles of `tile_points` points), (0, 0) past the
+// end of its set.
+__device__ __forceinline__ void load_point(const PointSets& ps, int64_t tile, int tile_points,
+                                           int row, float& x0, float& x1) {
+  const bool b = tile >= ps.tiles;
+  const int64_t p = (b ? tile - ps.tiles : tile) * tile_points + row;
+  const float* src = b ? ps.boundary : ps.interior;
+  x0 = 0.0f;
+  x1 = 0.0f;
+  if (p < (b ? ps.nb : ps.n)) {
+    x0 = src[2 * p];
+    x1 = src[2 * p + 1];
+  }
+}
+#endif
+
 struct DeviceInfo {
   int sms = 0;
   int cc_major = 0;
@@ -32,25 +63,27 @@ cudaError_t launch_forward_tc(const float* coords, const float* params, float* u
 
 // ---- backward_fp32.cu ----
 cudaError_t prepare_backward_fp32();
-int backward_grid(int64_t n, const DeviceInfo& dev);
-// mode 0: plain VJP with caller-supplied grad_u/grad_lap; mode 1: fused Poisson step.
-cudaError_t launch_backward_fp32(const float* coords, const float* params,
+int backward_grid(int64_t n, int64_t nb, const DeviceInfo& dev);
+// poisson: fused Poisson / PINN step (loss gradient formed in the kernel); otherwise the
+// plain VJP of the interior set with caller-supplied grad_u / grad_lap.
+cudaError_t launch_backward_fp32(const PointSets& points, const float* params,
                                  const float* grad_u, const float* grad_lap,
                                  float* grad_coords, float* lap_out, float* partials,
-                                 int64_t n, int64_t n_total, bool poisson,
-                                 const DeviceInfo& dev, cudaStream_t stream);
+                                 bool poisson, const DeviceInfo& dev, cudaStream_t stream);
 cudaError_t launch_reduce_rows(const float* partials, int rows, float* grad_params,
                                float* loss, cudaStream_t stream);
 
 // ---- backward_tc.cu ----
 cudaError_t prepare_backward_tc();
-int backward_tc_grid(int64_t n, const DeviceInfo& dev);
+int backward_tc_grid(int64_t n, int64_t nb, const DeviceInfo& dev);
 // Workspace: pre-split weights, one partial-gradient row per CTA, per-CTA L2 scratch.
-size_t backward_tc_workspace_bytes(int64_t n, const DeviceInfo& dev);
+size_t backward_tc_workspace_bytes(int64_t n, int64_t nb, const DeviceInfo& dev);
 float* backward_tc_partials(float* workspace);
-cudaError_t launch_backward_tc(const float* coords, const float* params, const float* grad_u,
-                               const float* grad_lap, float* grad_coords, float* lap_out,
-                               float* workspace, int64_t n, int64_t n_total, bool poisson,
+// poisson: the loss gradient is formed in the kernel (residual term for the interior set,
+// boundary term for the boundary set); otherwise grad_u / grad_lap of the interior set.
+cudaError_t launch_backward_tc(const PointSets& points, const float* params,
+                               const float* grad_u, const float* grad_lap, float* grad_coords,
+                               float* lap_out, float* workspace, bool poisson,
                                const DeviceInfo& dev, cudaStream_t stream);
 
 // ---- adam.cu ----

@@ -72,10 +72,13 @@ extern "C" int fhb_backward_noalloc(const float* coords, const float* params,
     return e == cudaSuccess ? FHB_OK : FHB_ERR_CUDA;
   }
   if (!coords || !grad_lap) return FHB_ERR_INVALID_ARGUMENT;
-  const int rows = fhb::backward_grid(n, st.info);
+  const int rows = fhb::backward_grid(n, 0, st.info);
   if (rows > kNoAllocMaxRows) return FHB_ERR_TOO_LARGE;  // GPU with more SMs than rows
-  e = fhb::launch_backward_fp32(coords, params, grad_u, grad_lap, grad_coords, nullptr,
-                                st.rows, n, n, false, st.info, stream);
+  fhb::PointSets ps;
+  ps.interior = coords;
+  ps.n = n;
+  e = fhb::launch_backward_fp32(ps, params, grad_u, grad_lap, grad_coords, nullptr, st.rows,
+                                false, st.info, stream);
   if (e == cudaSuccess) e = fhb::launch_reduce_rows(st.rows, rows, grad_params, nullptr, stream);
   return e == cudaSuccess ? FHB_OK : FHB_ERR_CUDA;
 }

@@ -31,6 +31,12 @@ _SIGNATURES: dict[str, tuple[object, list]] = {
         ctypes.c_int,
         [_p, _p, _i64, _i64, _p, _p, _p, _p, ctypes.c_int, _p, ctypes.c_size_t, _p],
     ),
+    "fhb_pinn_step_workspace_bytes": (ctypes.c_size_t, [_i64, _i64]),
+    "fhb_pinn_step_gradients": (
+        ctypes.c_int,
+        [_p, _i64, _i64, _p, _i64, _i64, ctypes.c_float, _p, _p, _p, ctypes.c_int, _p,
+         ctypes.c_size_t, _p],
+    ),
     "fhb_adam_step": (
         ctypes.c_int,
         [_p, _p, _p, _p, _i64, _p, ctypes.c_float, ctypes.c_float, ctypes.c_float,

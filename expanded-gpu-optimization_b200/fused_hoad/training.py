@@ -75,6 +75,11 @@ class PoissonTrainer:
     With an initialised process group every rank must call :meth:`step` with its own
     shard and the same ``total_points``. ``backward_version`` 6 (default) runs the
     tensor-core step kernel, 1..5 the FP32 CUDA-core one.
+
+    The loss is the interior Poisson residual ``mean((lap - f)^2)`` (the benchmark's,
+    benchmarks/benchmark_training.py:46-48); passing ``boundary`` points to :meth:`step`
+    adds the PINN boundary term ``boundary_weight * mean(u^2)`` of the reference's training
+    driver (src/fused_hoad/training.py:68-94), in the same kernel launch.
     """
 
     def __init__(
@@ -86,6 +91,7 @@ class PoissonTrainer:
         eps: float = 1e-8,
         group=None,
         backward_version: int = 6,
+        boundary_weight: float = 100.0,
     ) -> None:
         self._C = load_extension()
         if isinstance(parameters, nn.Module):
@@ -106,21 +112,42 @@ class PoissonTrainer:
         if not 1 <= backward_version <= 6:
             raise ValueError("backward_version must be 1 to 6")
         self.backward_version = int(backward_version)
+        self.boundary_weight = float(boundary_weight)
         self._C.prepare_device(flat.device.index if flat.device.index is not None else 0)
 
-    def gradients(self, coordinates: Tensor, total_points: int) -> Tensor:
+    def gradients(
+        self,
+        coordinates: Tensor,
+        total_points: int,
+        boundary: Tensor | None = None,
+        boundary_total: int | None = None,
+    ) -> Tensor:
         """Flat ``[12738]`` buffer: the gradient summed over ranks, then the loss."""
-        out, _, _ = self._C.poisson_step_gradients(
-            coordinates, self.params, total_points, version=self.backward_version
-        )
+        if boundary is None:
+            out, _, _ = self._C.poisson_step_gradients(
+                coordinates, self.params, total_points, version=self.backward_version
+            )
+        else:
+            if boundary_total is None:
+                boundary_total = boundary.shape[0] * world()[1]
+            out = self._C.pinn_step_gradients(
+                coordinates, boundary, self.params, total_points, boundary_total,
+                self.boundary_weight, self.backward_version,
+            )
         return allreduce_sum_(out, self.group)
 
-    def step(self, coordinates: Tensor, total_points: int | None = None) -> Tensor:
-        """One training step on this rank's points; returns the (global) loss, a 1-element
-        device tensor of the loss before the update."""
+    def step(
+        self,
+        coordinates: Tensor,
+        total_points: int | None = None,
+        boundary: Tensor | None = None,
+        boundary_total: int | None = None,
+    ) -> Tensor:
+        """One training step on this rank's points (and boundary points, if given); returns
+        the (global) loss, a 1-element device tensor of the loss before the update."""
         if total_points is None:
             total_points = coordinates.shape[0] * world()[1]
-        out = self.gradients(coordinates, total_points)
+        out = self.gradients(coordinates, total_points, boundary, boundary_total)
         self._C.adam_step(
             self.params,
             out[:POISSON_PARAMETER_COUNT],
@@ -135,22 +162,29 @@ class PoissonTrainer:
         return out[POISSON_PARAMETER_COUNT:]
 
     def capture(
-        self, coordinates: Tensor, total_points: int | None = None, *, warmup: int = 3
+        self,
+        coordinates: Tensor,
+        total_points: int | None = None,
+        *,
+        boundary: Tensor | None = None,
+        boundary_total: int | None = None,
+        warmup: int = 3,
     ) -> Callable[[], Tensor]:
-        """Capture :meth:`step` on ``coordinates`` as one CUDA graph; returns ``replay()``.
+        """Capture :meth:`step` on ``coordinates`` (and ``boundary``) as one CUDA graph;
+        returns ``replay()``.
 
         The warm-up steps are real steps (they update the parameters). Copy new points into
-        ``coordinates`` in place between replays.
+        ``coordinates`` / ``boundary`` in place between replays.
         """
         side = torch.cuda.Stream()
         side.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(side):
             for _ in range(warmup):
-                self.step(coordinates, total_points)
+                self.step(coordinates, total_points, boundary, boundary_total)
         torch.cuda.current_stream().wait_stream(side)
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
-            static_loss = self.step(coordinates, total_points)
+            static_loss = self.step(coordinates, total_points, boundary, boundary_total)
 
         def replay() -> Tensor:
             graph.replay()

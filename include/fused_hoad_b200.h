@@ -135,6 +135,26 @@ int fhb_poisson_step_gradients(const float* coords, const float* params, int64_t
                                size_t workspace_bytes, fhb_stream_t stream);
 
 /*
+ * Fused gradients of the full Poisson PINN loss of the reference's training driver
+ * (src/fused_hoad/training.py:68-94, benchmarks/train_poisson.py):
+ *     L = sum_p (lap_p - f(x_p))^2 / n_total + w * sum_b u(x_b)^2 / n_boundary_total
+ * over interior points coords[n][2] and boundary points boundary[n_boundary][2] (w =
+ * boundary_weight, the reference's default is 100). One launch walks the interior tiles
+ * and then the boundary tiles (the boundary term is the VJP of u alone: grad_u = 2 w u /
+ * n_boundary_total, grad_lap = 0), so one reduction gives grad_params[12737] and *loss of
+ * both terms (this shard's contributions; the totals >= the local counts let data-parallel
+ * shards sum to the global values). No counterpart entry in the reference, whose boundary
+ * term is a separate eager forward and autograd backward. `version` as for fhb_backward.
+ * Workspace: fhb_pinn_step_workspace_bytes(n, n_boundary) bytes, 16-byte aligned.
+ */
+size_t fhb_pinn_step_workspace_bytes(int64_t n, int64_t n_boundary);
+int fhb_pinn_step_gradients(const float* coords, int64_t n, int64_t n_total,
+                            const float* boundary, int64_t n_boundary,
+                            int64_t n_boundary_total, float boundary_weight,
+                            const float* params, float* grad_params, float* loss, int version,
+                            void* workspace, size_t workspace_bytes, fhb_stream_t stream);
+
+/*
  * One Adam step on a flat buffer, torch.optim.Adam semantics (no weight decay, no amsgrad),
  * replacing the optimizer of reference benchmarks/benchmark_training.py:41, :54-56.
  * `step` is a device int64 counter holding the number of steps taken so far; the kernel

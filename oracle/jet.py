@@ -171,6 +171,46 @@ def poisson_step_gradients(
     return loss, grad_p, grad_x
 
 
+def boundary_points(count: int, seed: int = 2) -> Tensor:
+    """``count`` points uniform on the boundary of [-1, 1]^2 (CPU generator ``seed``): the
+    sampling of src/fused_hoad/training.py:45-53 (a side 0..3 for x=-1, x=1, y=-1, y=1,
+    a uniform coordinate along it)."""
+    g = torch.Generator().manual_seed(seed)
+    t = torch.rand(count, generator=g) * 2 - 1
+    side = torch.randint(0, 4, (count,), generator=g)
+    fixed = torch.where(side % 2 == 0, -1.0, 1.0)
+    x_is_fixed = side < 2
+    x = torch.where(x_is_fixed, fixed, t)
+    y = torch.where(x_is_fixed, t, fixed)
+    return torch.stack((x, y), dim=1)
+
+
+def pinn_step_gradients(
+    params: Tensor,
+    interior: Tensor,
+    boundary: Tensor,
+    interior_total: int | None = None,
+    boundary_total: int | None = None,
+    boundary_weight: float = 100.0,
+) -> tuple[Tensor, Tensor]:
+    """Gradient of the Poisson PINN loss of src/fused_hoad/training.py:68-94:
+    ``sum((lap - f)^2) / interior_total + boundary_weight * sum(u_b^2) / boundary_total``,
+    with the totals defaulting to the local counts (plain means). Returns
+    ``(loss_partial, grad_params)``; the interior part is ``poisson_step_gradients``, the
+    boundary part the VJP of ``u`` alone (grad_u = 2 w u_b / boundary_total, grad_lap = 0).
+    """
+    nb = boundary.shape[0]
+    btotal = nb if boundary_total is None else boundary_total
+    loss_i, grad_i, _ = poisson_step_gradients(params, interior, interior_total)
+    if nb == 0:
+        return loss_i, grad_i
+    u_b, _ = forward_laplacian(params, boundary)
+    loss_b = boundary_weight * (u_b * u_b).sum() / btotal
+    grad_u = 2.0 * boundary_weight * u_b / btotal
+    grad_b, _ = recompute_backward(params, boundary, grad_u, torch.zeros_like(u_b))
+    return loss_i + loss_b, grad_i + grad_b
+
+
 def adam_update(
     params: Tensor,
     grad: Tensor,

@@ -13,7 +13,10 @@ Imports ``fused_hoad`` from the reference checkout's ``src/`` (default: the path
 * ``_recompute_backward`` (``src/fused_hoad/backends/fused.py:76-101``) gradients for
   fixed upstream gradients;
 * a 5-step ``torch.optim.Adam(lr=1e-3)`` trajectory of the interior Poisson loss
-  ``mean((lap - f)^2)`` (``benchmarks/benchmark_training.py:39-57``).
+  ``mean((lap - f)^2)`` (``benchmarks/benchmark_training.py:39-57``);
+* the full PINN loss of ``poisson_loss_fn`` (``src/fused_hoad/training.py:68-94``: interior
+  residual + 100 * mean(u^2) on ``boundary_points``, ``:45-53``) through the FL backend, and
+  its parameter gradients.
 
 Inputs come from CPU generators (points: seed 1, ``rand*2-1``; upstream grads: seed 2).
 The result is ``tests/golden/golden.npz``; nothing at test time reads the reference.
@@ -36,6 +39,8 @@ SATURATED_BATCH = 4096
 SATURATED_BACKWARD_BATCH = 2048
 ADAM_BATCH = 512
 ADAM_STEPS = 5
+PINN_INTERIOR = 256
+PINN_BOUNDARY = 64
 
 
 def main() -> None:
@@ -142,6 +147,21 @@ def main() -> None:
     out["adam_x"] = x.numpy()
     out["adam_losses"] = np.array(losses, dtype=np.float64)
     out["adam_params_final"] = pack_poisson_parameters(train).detach().numpy()
+
+    # Full PINN loss (interior residual + weighted boundary term) and its gradients.
+    from fused_hoad import get_backend
+    from fused_hoad.training import boundary_points, poisson_loss_fn
+
+    pinn = model(0).requires_grad_(True)
+    xi = points(PINN_INTERIOR)
+    xb = boundary_points(PINN_BOUNDARY, device="cpu", generator=torch.Generator().manual_seed(2))
+    loss = poisson_loss_fn(get_backend("forward_laplacian"), pinn, xi, xb)()
+    loss.backward()
+    grads = [torch.cat([pinn[k].weight.grad.reshape(-1), pinn[k].bias.grad.reshape(-1)])
+             for k in range(0, len(pinn), 2)]
+    out["pinn_x"], out["pinn_xb"] = xi.numpy(), xb.numpy()
+    out["pinn_loss"] = np.array(loss.item(), dtype=np.float64)
+    out["pinn_grad"] = torch.cat(grads).detach().numpy()
 
     np.savez_compressed(OUT, **out)
     print(f"wrote {OUT} ({OUT.stat().st_size / 1024:.0f} KiB, {len(out)} arrays)")

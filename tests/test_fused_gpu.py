@@ -534,3 +534,79 @@ def test_zero_copy_host_evaluation_matches_device_evaluation(batch: int, version
     assert torch.equal(out_u, u) and torch.equal(out_l, lap)
     with pytest.raises(RuntimeError, match="pinned"):
         fused_hoad.fused_forward_laplacian_host(uniform_points(8), params, version)
+
+
+# ------------------------------------------------- PINN step (boundary term) ----
+
+@pytest.mark.parametrize("kernel", BACKWARD_KERNELS)
+@pytest.mark.parametrize("sizes", [(1, 1), (33, 17), (129, 128), (1_000, 300), (16_384, 1_024)])
+def test_pinn_step_gradients_match_oracle(sizes: tuple[int, int], kernel: int) -> None:
+    n, nb = sizes
+    params = _params()
+    x = uniform_points(n, seed=15).cuda()
+    xb = jet.boundary_points(nb, seed=3).cuda()
+    out = fused_hoad.load_extension().pinn_step_gradients(x, xb, params, n, nb, 100.0, kernel)
+    loss, grad = jet.pinn_step_gradients(params.cpu(), x.cpu(), xb.cpu())
+    assert_scaled(out[:-1].cpu(), grad, 1e-4, "grad params")
+    torch.testing.assert_close(out[-1].cpu(), loss.float(), rtol=1e-5, atol=0)
+
+
+@pytest.mark.parametrize("kernel", BACKWARD_KERNELS)
+def test_pinn_step_against_reference_golden(golden, kernel: int) -> None:
+    """The reference's own poisson_loss_fn (training.py:68-94) on its boundary_points."""
+    params = torch.from_numpy(golden["params_seed0"]).cuda()
+    x = torch.from_numpy(golden["pinn_x"]).cuda()
+    xb = torch.from_numpy(golden["pinn_xb"]).cuda()
+    out = fused_hoad.load_extension().pinn_step_gradients(
+        x, xb, params, len(x), len(xb), 100.0, kernel
+    )
+    assert_scaled(out[:-1].cpu(), golden["pinn_grad"], 1e-4, "grad params")
+    np.testing.assert_allclose(out[-1].item(), float(golden["pinn_loss"]), rtol=1e-5)
+
+
+@pytest.mark.parametrize("kernel", BACKWARD_KERNELS)
+def test_pinn_step_without_boundary_is_the_poisson_step(kernel: int) -> None:
+    params = _params()
+    x = uniform_points(5_000, seed=16).cuda()
+    C = fused_hoad.load_extension()
+    empty = torch.empty(0, 2, device="cuda")
+    a = C.pinn_step_gradients(x, empty, params, 5_000, 0, 100.0, kernel)
+    b = C.poisson_step_gradients(x, params, 5_000, version=kernel)[0]
+    assert_scaled(a.cpu(), b.cpu(), 1e-6, "grad and loss")
+
+
+@pytest.mark.parametrize("kernel", BACKWARD_KERNELS)
+def test_pinn_shard_gradients_sum_to_full_batch(kernel: int) -> None:
+    params = _params()
+    n, nb = 60_000, 4_000
+    x = uniform_points(n, seed=17).cuda()
+    xb = jet.boundary_points(nb, seed=4).cuda()
+    C = fused_hoad.load_extension()
+    full = C.pinn_step_gradients(x, xb, params, n, nb, 100.0, kernel)
+    parts = torch.zeros_like(full)
+    for r in range(4):
+        a, b = fused_hoad.shard_range(n, r, 4)
+        c, d = fused_hoad.shard_range(nb, r, 4)
+        parts += C.pinn_step_gradients(x[a:b].contiguous(), xb[c:d].contiguous(), params, n, nb,
+                                       100.0, kernel)
+    assert_scaled(parts[:-1].cpu(), full[:-1].cpu(), 1e-5, "grad")
+    torch.testing.assert_close(parts[-1].cpu(), full[-1].cpu(), rtol=1e-5, atol=0)
+
+
+def test_trainer_with_boundary_follows_oracle_adam() -> None:
+    """PoissonTrainer with boundary points vs the oracle's PINN gradient + Adam, 5 steps."""
+    params = _params()
+    x = uniform_points(2_048, seed=18)
+    xb = jet.boundary_points(256, seed=5)
+    trainer = fused_hoad.PoissonTrainer(params.clone())
+    losses = [trainer.step(x.cuda(), boundary=xb.cuda()).item() for _ in range(5)]
+    p = params.cpu().clone()
+    m, v = torch.zeros_like(p), torch.zeros_like(p)
+    want = []
+    for step in range(1, 6):
+        loss, grad = jet.pinn_step_gradients(p, x, xb)
+        want.append(loss.item())
+        jet.adam_update(p, grad, m, v, step)
+    np.testing.assert_allclose(losses, want, rtol=1e-4)
+    diff = (trainer.params.cpu() - p).abs()
+    assert float((diff > 1e-5).float().mean()) < 1e-3, float(diff.max())

@@ -115,6 +115,16 @@ def test_oracle_adam_trajectory_matches_reference(golden) -> None:
     np.testing.assert_allclose(params.numpy(), golden["adam_params_final"], rtol=1e-5, atol=1e-7)
 
 
+def test_oracle_pinn_loss_matches_reference(golden) -> None:
+    """Interior residual + 100 * mean(u^2) on the boundary (reference training.py:68-94)."""
+    params = torch.from_numpy(golden["params_seed0"])
+    xb = torch.from_numpy(golden["pinn_xb"])
+    np.testing.assert_array_equal(jet.boundary_points(len(xb), seed=2).numpy(), golden["pinn_xb"])
+    loss, grad = jet.pinn_step_gradients(params, torch.from_numpy(golden["pinn_x"]), xb)
+    np.testing.assert_allclose(loss.item(), float(golden["pinn_loss"]), rtol=1e-5)
+    assert_scaled_close(grad, golden["pinn_grad"], 1e-5, "PINN grad params")
+
+
 def test_known_answers() -> None:
     # With every weight and bias zero except b_out the network is constant, so u = b_out
     # and lap = 0 exactly (the analogue of tests/test_backends.py:104-108's linear case).
