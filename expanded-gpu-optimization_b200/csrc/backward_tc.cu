@@ -150,28 +150,13 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
   return __all_sync(0xffffffffu, wait_or_abort(bar, parity) ? 1 : 0) != 0;
 }
 
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
 
-__device__ __forceinline__ uint32_t count_contribution(uint32_t* counter) {
-  uint32_t old;
-  asm volatile("atom.acq_rel.cta.shared::cta.add.u32 %0, [%1], 1;"
-               : "=r"(old)
-               : "r"(smem_u32(counter))
-               : "memory");
-  return old;
-}
 
 // Block-wide barrier that also tells every warp whether any warp has aborted.
 __device__ __forceinline__ bool barrier_ok() {
   return __syncthreads_or(*abort_flag() != 0u ? 1 : 0) == 0;
 }
 
-__device__ __forceinline__ void split_tf32(float x, uint32_t& hi, uint32_t& lo) {
-  hi = tc::to_tf32(x);
-  lo = __float_as_uint(x - __uint_as_float(hi));
-}
 
 // GEMM g of a tile (0..2: forward with W1..W3, 3..5: input adjoint with W3^T, W2^T, W1^T)
 // reads weight slot g % 2. A slot serves GEMMs g, g+2, g+4 of every tile, so GEMM g of the
@@ -228,7 +213,7 @@ __device__ __forceinline__ bool produce_chunk(uint32_t n, const float (&h)[4][4]
   for (int c = 0; c < 4; ++c) {
     uint32_t hi[4], lo[4];
 #pragma unroll
-    for (int t = 0; t < 4; ++t) split_tf32(h[c][t], hi[t], lo[t]);
+    for (int t = 0; t < 4; ++t) tc::split_tf32(h[c][t], hi[t], lo[t]);
     tc::st_x4(base + 32u * c, hi[0], hi[1], hi[2], hi[3]);
     tc::st_x4(base + 32u * c + 16u, lo[0], lo[1], lo[2], lo[3]);
   }
@@ -618,8 +603,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int a = i >> 2, t = i & 3;
           const float z = c == 0 ? d[0][i] : c == 1 ? d[1][i] : c == 2 ? d[2][i] : d[3][i];
           uint32_t zh, zl, hh, hl;
-          split_tf32(z, zh, zl);
-          split_tf32(hv[i], hh, hl);
+          tc::split_tf32(z, zh, zl);
+          tc::split_tf32(hv[i], hh, hl);
           const uint32_t o = a * 2048 + soff[t];
           *reinterpret_cast<uint32_t*>(stage + kStageA + ka * 16384u + o) = zh;
           *reinterpret_cast<uint32_t*>(stage + kStageA + ka * 16384u + 8192u + o) = zl;

@@ -111,19 +111,7 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, const 
   return __all_sync(0xffffffffu, wait_or_abort(bar, parity, cx) ? 1 : 0) != 0;
 }
 
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
 
-// Release this warp's contribution to a slot and learn whether it was the last one.
-__device__ __forceinline__ uint32_t count_contribution(uint32_t* counter) {
-  uint32_t old;
-  asm volatile("atom.acq_rel.cta.shared::cta.add.u32 %0, [%1], 1;"
-               : "=r"(old)
-               : "r"(smem_u32(counter))
-               : "memory");
-  return old;
-}
 
 // The 24 MMAs of one chunk: K steps 2j, 2j+1 of hidden GEMM `layer`, A from ring slot
 // `slot` (component c, hi/lo sp, K step kk at columns 32c + 16sp + 8kk of the slot).
@@ -148,12 +136,6 @@ __device__ __forceinline__ void issue_chunk_mmas(const Ctx& cx, int layer, int j
   if (j == kChunks - 1) tc::commit_warp(cx.dfull);
 }
 
-// TF32 split: hi = x rounded to TF32; lo = x - hi (exact in FP32), fed as is: the tensor
-// core reads only its TF32 bits, an error of at most 2^-21 |x|.
-__device__ __forceinline__ void split_tf32(float x, uint32_t& hi, uint32_t& lo) {
-  hi = tc::to_tf32(x);
-  lo = __float_as_uint(x - __uint_as_float(hi));
-}
 
 // Write chunk `n` (this warp's 4 neurons x 4 components, TF32 hi and lo) into ring slot
 // n % kRing; the warp completing the chunk last issues its MMAs. False if aborted.
@@ -167,7 +149,7 @@ __device__ __forceinline__ bool produce_chunk(uint32_t n, const float (&h)[4][4]
   for (int c = 0; c < 4; ++c) {
     uint32_t hi[4], lo[4];
 #pragma unroll
-    for (int t = 0; t < 4; ++t) split_tf32(h[c][t], hi[t], lo[t]);
+    for (int t = 0; t < 4; ++t) tc::split_tf32(h[c][t], hi[t], lo[t]);
     tc::st_x4(base + 32u * c, hi[0], hi[1], hi[2], hi[3]);
     tc::st_x4(base + 32u * c + 16u, lo[0], lo[1], lo[2], lo[3]);
   }
@@ -208,11 +190,34 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
+  // The first tile's point, requested first: its latency overlaps the set-up below.
+  const int row0 = 32 * (warp & 3) + lane;
+  float nx0 = 0.0f, nx1 = 0.0f;
+  {
+    const int64_t p = static_cast<int64_t>(blockIdx.x) * kTile + row0;
+    if (p < n) {
+      nx0 = coords[2 * p];
+      nx1 = coords[2 * p + 1];
+    }
+  }
+
   // ---- set-up: split weights to TF32 hi/lo in the canonical layout, small params ----
   // Element e of an operand, enumerated as (row group, K chunk, row in group, K in chunk),
   // sits at byte 4e of the canonical layout: consecutive threads store consecutive words.
-  // All 24 loads of a thread are issued before any is used.
+  // All 25 loads of a thread (24 weights, one small parameter) are issued before any is used.
+  static_assert(kSmallFloats == kThreads, "one small parameter per thread");
   {
+    float sv = 0.0f;
+    {
+      const int i = threadIdx.x;
+      if (i < kSmB0) sv = params[i];                                       // W0
+      else if (i < kSmB) sv = params[kB0 + (i - kSmB0)];                   // b0
+      else if (i < kSmWout) {                                              // b1..b3
+        const int l = (i - kSmB) >> 6, o = (i - kSmB) & 63;
+        sv = params[kHiddenBase + l * kHiddenStride + kWidth * kWidth + o];
+      } else if (i < kSmBout) sv = params[kOutBase + (i - kSmWout)];       // w_out
+      else if (i == kSmBout) sv = params[kOutBase + kWidth];               // b_out
+    }
     constexpr int kPerThread = kHiddenGemms * kWidth * kWidth / kThreads;  // 24
     float w[kPerThread];
 #pragma unroll
@@ -232,17 +237,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       reinterpret_cast<uint32_t*>(smem + (2 * layer) * kOperandBytes)[e] = hi;
       reinterpret_cast<uint32_t*>(smem + (2 * layer + 1) * kOperandBytes)[e] = lo;
     }
-  }
-  for (int i = threadIdx.x; i < kSmallFloats; i += kThreads) {
-    float v = 0.0f;
-    if (i < kSmB0) v = params[i];                                       // W0
-    else if (i < kSmB) v = params[kB0 + (i - kSmB0)];                   // b0
-    else if (i < kSmWout) {                                             // b1..b3
-      const int l = (i - kSmB) >> 6, o = (i - kSmB) & 63;
-      v = params[kHiddenBase + l * kHiddenStride + kWidth * kWidth + o];
-    } else if (i < kSmBout) v = params[kOutBase + (i - kSmWout)];       // w_out
-    else if (i == kSmBout) v = params[kOutBase + kWidth];               // b_out
-    small[i] = v;
+    small[threadIdx.x] = sv;
   }
   if (threadIdx.x == 0) {
     for (int r = 0; r < kRing; ++r) {
@@ -272,14 +267,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   bool ok = true;
   // Points of the next tile are loaded one tile ahead, so the load latency (long when the
   // points sit in pinned host memory read over the host link) overlaps a tile of work.
-  float nx0 = 0.0f, nx1 = 0.0f;
-  {
-    const int64_t p = static_cast<int64_t>(blockIdx.x) * kTile + row;
-    if (p < n) {
-      nx0 = coords[2 * p];
-      nx1 = coords[2 * p + 1];
-    }
-  }
   for (int64_t tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x, ++tile_count) {
     const int64_t p = tile * kTile + row;
     const bool active = p < n;

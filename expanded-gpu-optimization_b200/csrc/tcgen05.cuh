@@ -147,6 +147,13 @@ __device__ __forceinline__ uint32_t to_tf32(float x) {
   return r;
 }
 
+// 3xTF32 split: hi = x rounded to TF32; lo = x - hi (exact in FP32), fed as is: the tensor
+// core reads only its TF32 bits of lo, an error of at most 2^-21 |x|.
+__device__ __forceinline__ void split_tf32(float x, uint32_t& hi, uint32_t& lo) {
+  hi = to_tf32(x);
+  lo = __float_as_uint(x - __uint_as_float(hi));
+}
+
 // Shared-memory matrix descriptor, K-major, no swizzle ("interleave" canonical layout):
 // core matrices of 8 rows x 16 bytes stored contiguously; `lbo` = byte distance between
 // the two 16-byte K halves of one 8-element (32-byte) K step, `sbo` = byte distance
