@@ -16,8 +16,10 @@ Also reported in the same line:
   in pinned host memory, read by the kernel over the host link, (u, lap) written back to
   pinned host memory (``fused_hoad.fused_forward_laplacian_host``); the explicit-copy route
   (H2D copy, ``_C.fused_forward_laplacian``, D2H copies) is reported beside it;
-* ``train_step``: BASELINE.json config 2 (fused forward+loss+backward kernel, row
-  reduction, [all-reduce,] fused Adam) at 65,536 points per GPU;
+* ``train_step``: BASELINE.json config 2 (fused forward+loss+backward kernel, then one
+  update kernel: row reduction, the sum over ranks through the in-kernel NVLink peer
+  exchange, Adam) at 65,536 points per GPU; ``--exchange nccl`` times the composition of
+  separate launches (row reduction, NCCL all-reduce, Adam) instead;
 * ``roofline`` of the forward kernel against the measured peaks in MEASURED_PEAKS.json;
 * ``cpu_baseline``: the CPU oracle port of the reference's PyTorch forward Laplacian timed
   on this host (rank 0, N=1 only), a reported baseline.
@@ -68,6 +70,8 @@ def parse_args():
     p.add_argument("--version", type=int, default=None, help="forward kernel version")
     p.add_argument("--train-steps", type=int, default=None)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
+                   help="how the training step sums gradients over ranks")
     return p.parse_args()
 
 
@@ -319,9 +323,10 @@ def run_ours(args) -> None:
     ok = torch.equal(pinned_lap, reference_lap) and staged_ok
 
     # ---- training step (config 2) ----
-    # One step = weight pre-split, fused forward+loss+backward kernel, row reduction,
-    # [all-reduce,] fused Adam. Timed as a CUDA-graph replay (the step's launches replayed
-    # without host round trips), and eagerly through PoissonTrainer.step beside it.
+    # One step = weight pre-split, fused forward+loss+backward kernel, update kernel (row
+    # reduction + sum over ranks through peer memory + Adam); with --exchange nccl the update
+    # is row reduction, [NCCL all-reduce,] Adam. Timed as a CUDA-graph replay (the step's
+    # launches replayed without host round trips), and eagerly through PoissonTrainer.step.
     train_steps = args.train_steps if args.train_steps is not None else max(3, args.steps // 10)
 
     def time_train(run) -> float:
@@ -336,7 +341,7 @@ def run_ours(args) -> None:
         barrier()
         return max_over_ranks(sum(s.elapsed_time(e) for s, e in events))
 
-    trainer = fused_hoad.PoissonTrainer(params.clone())
+    trainer = fused_hoad.PoissonTrainer(params.clone(), exchange=args.exchange)
     for _ in range(max(3, args.warmup)):
         trainer.step(coords, n * world)
     eager_total = time_train(lambda: trainer.step(coords, n * world))
@@ -353,6 +358,7 @@ def run_ours(args) -> None:
     if replay is not None:
         del replay.graph  # release the captured graph (and any collective in it)
         replay = None
+    trainer.close()  # collective over the ranks with the peer exchange
     train_ms = train_total / train_steps
     train_value = n * world * train_steps / (train_total / 1e3)
     eager_value = n * world * train_steps / (eager_total / 1e3)
@@ -418,12 +424,17 @@ def run_ours(args) -> None:
         "roofline": roofline,
         "clocks": clk,
         "train_step": {
-            "workload": "config2: fused forward+loss+backward kernel, row reduction, "
-                        + ("all-reduce, " if world > 1 else "") + "fused Adam",
+            "workload": "config2: fused forward+loss+backward kernel, " + (
+                "update kernel (row reduction, "
+                + ("sum over ranks through NVLink peer memory, " if world > 1 else "")
+                + "Adam)" if args.exchange == "peer" else
+                "row reduction, " + ("NCCL all-reduce, " if world > 1 else "") + "fused Adam"),
+            "exchange": args.exchange,
             "value": train_value, "unit": UNIT, "ms_per_step": train_ms, "steps": train_steps,
             "timing": train_mode, "eager_value": eager_value,
             "backward_kernel": "backward_tc_kernel (version 6)",
-            "points_per_gpu": n, "launches_per_step": 4 + (1 if world > 1 else 0),
+            "points_per_gpu": n,
+            "launches_per_step": 3 if args.exchange == "peer" else 4 + (1 if world > 1 else 0),
             "loss_after": final_loss,
             "achieved_tflops": n * FLOP_STEP / (train_ms / 1e3) / 1e12,
             "flop_per_point": FLOP_STEP,

@@ -1,9 +1,7 @@
 // Fused Adam over the flat 12,737-float parameter buffer, and the bounded-wait self-test.
 //
 // Adam follows torch.optim.Adam's single-tensor update (the optimizer of reference
-// benchmarks/benchmark_training.py:41), with no weight decay and no amsgrad:
-//   m = lerp(m, g, 1 - beta1); v = beta2 v + (1 - beta2) g^2
-//   p -= lr / (1 - beta1^t) * m / (sqrt(v) / sqrt(1 - beta2^t) + eps)
+// benchmarks/benchmark_training.py:41), with no weight decay and no amsgrad (adam_element).
 // The step counter t lives in device memory so a captured CUDA graph can replay the step.
 #include "common.cuh"
 #include "kernels.cuh"
@@ -22,10 +20,7 @@ __global__ void __launch_bounds__(kAdamThreads)
                 float* __restrict__ exp_avg, float* __restrict__ exp_avg_sq, int64_t count,
                 int64_t* __restrict__ step, float lr, float beta1, float beta2, float eps) {
   const int64_t t = *step + 1;
-  const double bias1 = 1.0 - pow(static_cast<double>(beta1), static_cast<double>(t));
-  const double bias2 = 1.0 - pow(static_cast<double>(beta2), static_cast<double>(t));
-  const float step_size = static_cast<float>(static_cast<double>(lr) / bias1);
-  const float bias2_sqrt = static_cast<float>(sqrt(bias2));
+  const AdamScalars s = adam_scalars(t, lr, beta1, beta2);
   for (int64_t base = 0; base < count; base += static_cast<int64_t>(kAdamThreads) * kAdamUnroll) {
     float g[kAdamUnroll], m[kAdamUnroll], v[kAdamUnroll], p[kAdamUnroll];
 #pragma unroll
@@ -41,12 +36,10 @@ __global__ void __launch_bounds__(kAdamThreads)
     for (int k = 0; k < kAdamUnroll; ++k) {
       const int64_t i = base + threadIdx.x + static_cast<int64_t>(k) * kAdamThreads;
       if (i >= count) continue;
-      const float mk = fmaf(1.0f - beta1, g[k] - m[k], m[k]);
-      const float vk = fmaf(beta2, v[k], (1.0f - beta2) * g[k] * g[k]);
-      exp_avg[i] = mk;
-      exp_avg_sq[i] = vk;
-      const float denom = sqrtf(vk) / bias2_sqrt + eps;
-      params[i] = p[k] - step_size * (mk / denom);
+      adam_element(g[k], p[k], m[k], v[k], s, beta1, beta2, eps);
+      exp_avg[i] = m[k];
+      exp_avg_sq[i] = v[k];
+      params[i] = p[k];
     }
   }
   __syncthreads();

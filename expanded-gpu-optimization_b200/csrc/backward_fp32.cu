@@ -411,27 +411,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // out[col] = sum over the partial rows of partials[r][col] in a fixed order: a block takes 32
 // columns; its 8 row groups (rows g, g+8, g+16, ...) are summed in row order by 8 threads
-// of a column, each with its loads in flight together, then the 8 group sums are added in
-// group order.
-constexpr int kReduceCols = 32, kReduceGroups = 8;
+// of a column (column_group_sum), then the 8 group sums are added in group order.
+constexpr int kReduceCols = kUpdateCols, kReduceGroups = kUpdateGroups;
 __global__ void __launch_bounds__(kReduceCols * kReduceGroups)
     reduce_rows_kernel(const float* __restrict__ partials, int rows,
                        float* __restrict__ grad_params, float* __restrict__ loss) {
   __shared__ float sums[kReduceGroups][kReduceCols];
   const int cx = threadIdx.x % kReduceCols, grp = threadIdx.x / kReduceCols;
   const int col = blockIdx.x * kReduceCols + cx;
-  float acc = 0.0f;
-  if (col <= kLossColumn) {
-    int r = grp;
-    for (; r + 3 * kReduceGroups < rows; r += 4 * kReduceGroups) {
-      const float a = partials[static_cast<int64_t>(r) * kRowStride + col];
-      const float b = partials[static_cast<int64_t>(r + kReduceGroups) * kRowStride + col];
-      const float c = partials[static_cast<int64_t>(r + 2 * kReduceGroups) * kRowStride + col];
-      const float d = partials[static_cast<int64_t>(r + 3 * kReduceGroups) * kRowStride + col];
-      acc = (((acc + a) + b) + c) + d;
-    }
-    for (; r < rows; r += kReduceGroups) acc += partials[static_cast<int64_t>(r) * kRowStride + col];
-  }
+  const float acc = col <= kLossColumn ? column_group_sum(partials, rows, col, grp) : 0.0f;
   sums[grp][cx] = acc;
   __syncthreads();
   if (grp != 0 || col > kLossColumn) return;

@@ -232,6 +232,98 @@ void adam_step(torch::Tensor parameters, torch::Tensor grad, torch::Tensor exp_a
                "adam_step");
 }
 
+// ---- data-parallel exchange and the fused training step ----
+// An exchange object crosses into Python as its address (an int).
+
+fhb_exchange* as_exchange(int64_t handle) {
+  TORCH_CHECK(handle != 0, "exchange is closed");
+  return reinterpret_cast<fhb_exchange*>(static_cast<intptr_t>(handle));
+}
+
+int64_t exchange_create(int64_t world, int64_t rank, double wait_limit_s, int64_t device) {
+  TORCH_CHECK(wait_limit_s > 0.0 && wait_limit_s <= 3600.0, "wait_limit_s must be in (0, 3600]");
+  const c10::cuda::CUDAGuard device_guard(static_cast<c10::DeviceIndex>(device));
+  fhb_exchange* ex = nullptr;
+  check_status(fhb_exchange_create(static_cast<int>(world), static_cast<int>(rank),
+                                   static_cast<uint64_t>(wait_limit_s * 1e9), &ex),
+               "exchange_create");
+  return static_cast<int64_t>(reinterpret_cast<intptr_t>(ex));
+}
+
+torch::Tensor exchange_handle(int64_t handle) {
+  auto out = torch::empty({FHB_EXCHANGE_HANDLE_BYTES}, torch::kUInt8);
+  check_status(fhb_exchange_handle(as_exchange(handle), out.data_ptr<uint8_t>()),
+               "exchange_handle");
+  return out;
+}
+
+void exchange_connect(int64_t handle, torch::Tensor handles) {
+  TORCH_CHECK(!handles.is_cuda() && handles.scalar_type() == torch::kUInt8 &&
+                  handles.is_contiguous() && handles.numel() % FHB_EXCHANGE_HANDLE_BYTES == 0,
+              "handles must be a contiguous CPU uint8 tensor of whole IPC handles");
+  check_status(fhb_exchange_connect(as_exchange(handle), handles.data_ptr<uint8_t>()),
+               "exchange_connect");
+}
+
+void exchange_connect_local(int64_t handle, std::vector<int64_t> peer_buffers) {
+  std::vector<void*> ptrs;
+  for (int64_t p : peer_buffers) ptrs.push_back(reinterpret_cast<void*>(static_cast<intptr_t>(p)));
+  check_status(fhb_debug_exchange_connect_local(as_exchange(handle), ptrs.data()),
+               "exchange_connect_local");
+}
+
+int64_t exchange_buffer(int64_t handle) {
+  void* buffer = nullptr;
+  check_status(fhb_exchange_buffer(as_exchange(handle), &buffer), "exchange_buffer");
+  return static_cast<int64_t>(reinterpret_cast<intptr_t>(buffer));
+}
+
+void exchange_destroy(int64_t handle) {
+  check_status(fhb_exchange_destroy(as_exchange(handle)), "exchange_destroy");
+}
+
+// One fused training step (fhb_train_step): gradient kernel, then sum over the exchange's
+// ranks + Adam in one update kernel. Returns the global loss [1]; grad_out, when given, gets
+// the global gradient and the loss (12,738 floats).
+torch::Tensor train_step(torch::Tensor coordinates, torch::Tensor boundary,
+                         torch::Tensor parameters, torch::Tensor exp_avg,
+                         torch::Tensor exp_avg_sq, torch::Tensor step, double lr, double beta1,
+                         double beta2, double eps, int64_t total_points, int64_t boundary_total,
+                         double boundary_weight, int64_t exchange, int64_t version,
+                         c10::optional<torch::Tensor> grad_out) {
+  check_inputs(coordinates, parameters);
+  check_inputs(boundary, parameters);
+  check_vector(exp_avg, parameters, kParameterCount, "exp_avg");
+  check_vector(exp_avg_sq, parameters, kParameterCount, "exp_avg_sq");
+  TORCH_CHECK(step.is_cuda() && step.scalar_type() == torch::kInt64 && step.numel() == 1 &&
+                  step.device() == parameters.device(),
+              "step must be a CUDA int64 tensor with one element on the parameters' device");
+  if (grad_out) check_vector(*grad_out, parameters, kParameterCount + 1, "grad_out");
+  const c10::cuda::CUDAGuard device_guard(coordinates.device());
+  const int64_t batch = coordinates.size(0), nb = boundary.size(0);
+  TORCH_CHECK(total_points >= batch, "total_points must be >= the local batch");
+  TORCH_CHECK(boundary_total >= nb, "boundary_total must be >= the local boundary batch");
+  TORCH_CHECK(version >= 1 && version <= 6, "backward version must be 1 to 6");
+  auto loss = torch::empty({1}, parameters.options());
+  const size_t bytes = fhb_pinn_step_workspace_bytes(batch, nb);
+  auto workspace =
+      torch::empty({static_cast<int64_t>((bytes + 15) / 16) * 4}, parameters.options());
+  check_status(
+      fhb_train_step(coordinates.data_ptr<float>(), batch, total_points,
+                     boundary.data_ptr<float>(), nb, boundary_total,
+                     static_cast<float>(boundary_weight), parameters.data_ptr<float>(),
+                     exp_avg.data_ptr<float>(), exp_avg_sq.data_ptr<float>(),
+                     step.data_ptr<int64_t>(), static_cast<float>(lr),
+                     static_cast<float>(beta1), static_cast<float>(beta2),
+                     static_cast<float>(eps), as_exchange(exchange),
+                     grad_out ? grad_out->data_ptr<float>() : nullptr, loss.data_ptr<float>(),
+                     static_cast<int>(version), bytes ? workspace.data_ptr<float>() : nullptr,
+                     static_cast<size_t>(workspace.numel()) * sizeof(float),
+                     at::cuda::getCurrentCUDAStream()),
+      "train_step");
+  return loss;
+}
+
 void prepare_device(int64_t device) {
   check_status(fhb_prepare_device(static_cast<int>(device)), "prepare_device");
 }
@@ -274,6 +366,33 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, module) {
              pybind11::arg("parameters"), pybind11::arg("grad"), pybind11::arg("exp_avg"),
              pybind11::arg("exp_avg_sq"), pybind11::arg("step"), pybind11::arg("lr"),
              pybind11::arg("beta1"), pybind11::arg("beta2"), pybind11::arg("eps"));
+  module.def("exchange_create", &exchange_create,
+             "New data-parallel exchange for rank `rank` of `world` on `device`",
+             pybind11::arg("world"), pybind11::arg("rank"), pybind11::arg("wait_limit_s"),
+             pybind11::arg("device"));
+  module.def("exchange_handle", &exchange_handle,
+             "CUDA IPC handle of this rank's exchange buffer (CPU uint8 [64])",
+             pybind11::arg("exchange"));
+  module.def("exchange_connect", &exchange_connect,
+             "Map the peers' exchange buffers from their IPC handles (rank order)",
+             pybind11::arg("exchange"), pybind11::arg("handles"));
+  module.def("exchange_connect_local", &exchange_connect_local,
+             "Test hook: connect to peer buffers given as device addresses",
+             pybind11::arg("exchange"), pybind11::arg("peer_buffers"));
+  module.def("exchange_buffer", &exchange_buffer, "Device address of this rank's buffer",
+             pybind11::arg("exchange"));
+  module.def("exchange_destroy", &exchange_destroy, "Unmap the peers and free the buffers",
+             pybind11::arg("exchange"));
+  module.def("train_step", &train_step,
+             "Fused training step: gradient kernel, then the sum over ranks and Adam in one "
+             "update kernel",
+             pybind11::arg("coordinates"), pybind11::arg("boundary"),
+             pybind11::arg("parameters"), pybind11::arg("exp_avg"),
+             pybind11::arg("exp_avg_sq"), pybind11::arg("step"), pybind11::arg("lr"),
+             pybind11::arg("beta1"), pybind11::arg("beta2"), pybind11::arg("eps"),
+             pybind11::arg("total_points"), pybind11::arg("boundary_total"),
+             pybind11::arg("boundary_weight"), pybind11::arg("exchange"),
+             pybind11::arg("version") = 6, pybind11::arg("grad_out") = pybind11::none());
   module.def("prepare_device", &prepare_device, "One-time per-device kernel set-up",
              pybind11::arg("device"));
   module.def("read_device_status", &read_device_status,

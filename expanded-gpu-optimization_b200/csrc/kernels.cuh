@@ -4,6 +4,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "../../include/fused_hoad_b200.h"
+
 namespace fhb {
 
 // Floats per partial-gradient row of the backward workspace: 12,737 gradients, one loss
@@ -25,7 +27,82 @@ struct PointSets {
   float bweight = 0.0f;             // boundary term weight
 };
 
+// The training step's update: the partial rows are summed per column block of kUpdateCols
+// columns (kUpdateGroups row groups each), one CTA per block.
+constexpr int kUpdateCols = 32;
+constexpr int kUpdateGroups = 8;
+constexpr int kUpdateBlocks = (kLossColumn + 1 + kUpdateCols - 1) / kUpdateCols;  // 399
+
+// Data-parallel exchange through peer memory (collective.cu). Each rank owns one buffer:
+//   float    slots[2][kMaxRanks][kRowStride]   slot = epoch % 2, row = source rank
+//   uint32_t flags[kUpdateBlocks][kMaxRanks]   last epoch the source rank published there
+// Every rank writes its column block into row `rank` of every rank's buffer and then raises
+// its flag there, so a rank reads only its own memory once the flags are up.
+constexpr int kMaxRanks = 8;
+constexpr size_t kExchangeFlagOffset = 2ull * kMaxRanks * kRowStride;  // in 4-byte words
+constexpr size_t kExchangeBytes =
+    (kExchangeFlagOffset + static_cast<size_t>(kUpdateBlocks) * kMaxRanks) * 4;
+static_assert(kMaxRanks == FHB_EXCHANGE_MAX_RANKS, "exchange ABI drifted");
+static_assert(kRowStride == FHB_EXCHANGE_ROW_FLOATS, "exchange ABI drifted");
+static_assert(kUpdateBlocks == FHB_EXCHANGE_BLOCKS, "exchange ABI drifted");
+
+// Device-resident state of one exchange (one per rank and trainer).
+struct ExchangeState {
+  float* peers[kMaxRanks];  // every rank's buffer as mapped in this process (own included)
+  uint32_t epoch;           // exchanges completed
+  uint32_t done;            // CTAs of the running update that have finished (0 between)
+};
+
+struct AdamArgs {
+  float* params;
+  float* exp_avg;
+  float* exp_avg_sq;
+  int64_t* step;
+  float lr, beta1, beta2, eps;
+};
+
 #ifdef __CUDACC__
+// Sum of column `col` over the partial rows grp, grp + kUpdateGroups, ... in row order, four
+// loads in flight. Adding the kUpdateGroups results in group order gives the column's total;
+// the order is fixed, so every kernel doing this gets the same bits.
+__device__ __forceinline__ float column_group_sum(const float* __restrict__ partials, int rows,
+                                                  int col, int grp) {
+  float acc = 0.0f;
+  int r = grp;
+  for (; r + 3 * kUpdateGroups < rows; r += 4 * kUpdateGroups) {
+    const float a = partials[static_cast<int64_t>(r) * kRowStride + col];
+    const float b = partials[static_cast<int64_t>(r + kUpdateGroups) * kRowStride + col];
+    const float c = partials[static_cast<int64_t>(r + 2 * kUpdateGroups) * kRowStride + col];
+    const float d = partials[static_cast<int64_t>(r + 3 * kUpdateGroups) * kRowStride + col];
+    acc = (((acc + a) + b) + c) + d;
+  }
+  for (; r < rows; r += kUpdateGroups) acc += partials[static_cast<int64_t>(r) * kRowStride + col];
+  return acc;
+}
+
+// torch.optim.Adam's single-tensor update (no weight decay, no amsgrad) for step t:
+//   m = lerp(m, g, 1 - beta1); v = beta2 v + (1 - beta2) g^2
+//   p -= lr / (1 - beta1^t) * m / (sqrt(v) / sqrt(1 - beta2^t) + eps)
+struct AdamScalars {
+  float step_size;
+  float bias2_sqrt;
+};
+__device__ __forceinline__ AdamScalars adam_scalars(int64_t t, float lr, float beta1,
+                                                    float beta2) {
+  const double bias1 = 1.0 - pow(static_cast<double>(beta1), static_cast<double>(t));
+  const double bias2 = 1.0 - pow(static_cast<double>(beta2), static_cast<double>(t));
+  return {static_cast<float>(static_cast<double>(lr) / bias1),
+          static_cast<float>(sqrt(bias2))};
+}
+__device__ __forceinline__ void adam_element(float g, float& p, float& m, float& v,
+                                             const AdamScalars& s, float beta1, float beta2,
+                                             float eps) {
+  m = fmaf(1.0f - beta1, g - m, m);
+  v = fmaf(beta2, v, (1.0f - beta2) * g * g);
+  const float denom = sqrtf(v) / s.bias2_sqrt + eps;
+  p = p - s.step_size * (m / denom);
+}
+
 // Coordinates of point `row` of tile `tile` (tiles of `tile_points` points), (0, 0) past the
 // end of its set.
 __device__ __forceinline__ void load_point(const PointSets& ps, int64_t tile, int tile_points,
@@ -90,6 +167,16 @@ cudaError_t launch_backward_tc(const PointSets& points, const float* params,
 cudaError_t launch_adam(float* params, const float* grad, float* exp_avg, float* exp_avg_sq,
                         int64_t count, int64_t* step, float lr, float beta1, float beta2,
                         float eps, cudaStream_t stream);
+// ---- collective.cu ----
+// The training step's tail in one launch: the column sums of the backward's partial rows,
+// with world > 1 the sum over ranks through the peer buffers of `state`, then Adam on the
+// parameters; grad_out (kLossColumn + 1 floats, may be null) receives the summed gradient and
+// loss, loss_out (may be null) the loss. A peer wait that exceeds wait_limit_ns sets
+// FHB_STATUS_PEER_TIMEOUT and leaves that CTA's parameters unchanged.
+cudaError_t launch_step_update(const float* partials, int rows, ExchangeState* state, int world,
+                               int rank, uint64_t wait_limit_ns, const AdamArgs& adam,
+                               float* grad_out, float* loss_out, unsigned int* status,
+                               cudaStream_t stream);
 cudaError_t launch_debug_tanh(const float* x, float* out, int64_t n, int fast,
                               cudaStream_t stream);
 cudaError_t launch_bounded_wait_selftest(uint64_t limit_ns, unsigned int* status,

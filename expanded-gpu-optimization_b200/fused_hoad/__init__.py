@@ -16,7 +16,7 @@ from fused_hoad._extension import (
 )
 from fused_hoad.backends import BACKENDS, FIXED_CONTRACT_BACKENDS, get_backend
 from fused_hoad.backends.fused import FusedForwardLaplacian, fused_laplacian
-from fused_hoad.distributed import shard_range
+from fused_hoad.distributed import PeerExchange, shard_range
 from fused_hoad.parameters import (
     POISSON_PARAMETER_COUNT,
     POISSON_PARAMETER_LAYOUT,
@@ -42,6 +42,7 @@ __all__ = [
     "MLPConfig",
     "POISSON_PARAMETER_COUNT",
     "POISSON_PARAMETER_LAYOUT",
+    "PeerExchange",
     "PoissonTrainer",
     "bind_model_to_flat",
     "build_mlp",

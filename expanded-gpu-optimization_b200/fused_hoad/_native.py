@@ -42,6 +42,21 @@ _SIGNATURES: dict[str, tuple[object, list]] = {
         [_p, _p, _p, _p, _i64, _p, ctypes.c_float, ctypes.c_float, ctypes.c_float,
          ctypes.c_float, _p],
     ),
+    "fhb_exchange_buffer_bytes": (ctypes.c_size_t, []),
+    "fhb_exchange_create": (
+        ctypes.c_int, [ctypes.c_int, ctypes.c_int, ctypes.c_uint64, ctypes.POINTER(_p)]
+    ),
+    "fhb_exchange_handle": (ctypes.c_int, [_p, _p]),
+    "fhb_exchange_connect": (ctypes.c_int, [_p, _p]),
+    "fhb_exchange_buffer": (ctypes.c_int, [_p, ctypes.POINTER(_p)]),
+    "fhb_debug_exchange_connect_local": (ctypes.c_int, [_p, ctypes.POINTER(_p)]),
+    "fhb_exchange_destroy": (ctypes.c_int, [_p]),
+    "fhb_train_step": (
+        ctypes.c_int,
+        [_p, _i64, _i64, _p, _i64, _i64, ctypes.c_float, _p, _p, _p, _p, ctypes.c_float,
+         ctypes.c_float, ctypes.c_float, ctypes.c_float, _p, _p, _p, ctypes.c_int, _p,
+         ctypes.c_size_t, _p],
+    ),
     "fhb_read_device_status": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_uint)]),
     "fhb_debug_bounded_wait_selftest": (ctypes.c_int, [ctypes.c_uint64, _p]),
     "fhb_debug_tanh": (ctypes.c_int, [_p, _p, _i64, ctypes.c_int, _p]),

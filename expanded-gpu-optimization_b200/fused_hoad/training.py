@@ -9,10 +9,15 @@ parameters, Adam at lr 1e-3, betas (0.9, 0.999) on the interior loss
 ``mean((lap - f)^2)``):
 
 1. one persistent kernel per step recomputes the jet per tile, forms dL/dlap in registers
-   and runs the adjoint sweep (no separate forward launch), then a fixed-order row
-   reduction writes the gradient and the loss into one flat buffer;
-2. with more than one rank, one all-reduce (NCCL over NVLink) of that buffer;
-3. one fused Adam kernel updates the flat parameters in place.
+   and runs the adjoint sweep (no separate forward launch), leaving one partial-gradient
+   row per CTA;
+2. one update kernel sums the rows in a fixed order, sums over the ranks through the peer
+   exchange (``exchange="peer"``, the default: in-kernel over NVLink, no collective launch)
+   and applies Adam to the flat parameters in place.
+
+``exchange="nccl"`` runs the same step as separate launches instead -- row reduction into a
+flat gradient + loss buffer, one NCCL all-reduce of it, the Adam kernel -- the composition
+a library all-reduce gives.
 
 The parameters live in one flat buffer in the reference's ABI, so there is no per-step
 pack (``torch.cat``) or gradient split; an ``nn.Module`` handed to the trainer has its
@@ -27,7 +32,7 @@ import torch
 from torch import Tensor, nn
 
 from fused_hoad._extension import load_extension
-from fused_hoad.distributed import allreduce_sum_, world
+from fused_hoad.distributed import PeerExchange, allreduce_sum_, world
 from fused_hoad.parameters import (
     POISSON_PARAMETER_COUNT,
     bind_model_to_flat,
@@ -74,7 +79,11 @@ class PoissonTrainer:
     Poisson ``nn.Module``, which is packed once and rebound to views of the buffer.
     With an initialised process group every rank must call :meth:`step` with its own
     shard and the same ``total_points``. ``backward_version`` 6 (default) runs the
-    tensor-core step kernel, 1..5 the FP32 CUDA-core one.
+    tensor-core step kernel, 1..5 the FP32 CUDA-core one. ``exchange`` picks how the
+    gradient is summed over ranks: ``"peer"`` (default) inside the update kernel through
+    :class:`PeerExchange` buffers, ``"nccl"`` by an NCCL all-reduce between separate reduction
+    and Adam launches. With ``"peer"`` and more than one rank, every rank must construct its
+    trainer in the same order and call :meth:`close` after its last step.
 
     The loss is the interior Poisson residual ``mean((lap - f)^2)`` (the benchmark's,
     benchmarks/benchmark_training.py:46-48); passing ``boundary`` points to :meth:`step`
@@ -92,6 +101,8 @@ class PoissonTrainer:
         group=None,
         backward_version: int = 6,
         boundary_weight: float = 100.0,
+        exchange: str = "peer",
+        wait_limit_s: float = 30.0,
     ) -> None:
         self._C = load_extension()
         if isinstance(parameters, nn.Module):
@@ -114,6 +125,19 @@ class PoissonTrainer:
         self.backward_version = int(backward_version)
         self.boundary_weight = float(boundary_weight)
         self._C.prepare_device(flat.device.index if flat.device.index is not None else 0)
+        if exchange not in ("peer", "nccl"):
+            raise ValueError('exchange must be "peer" or "nccl"')
+        self.exchange = exchange
+        self._peer = (
+            PeerExchange(flat.device, group, wait_limit_s) if exchange == "peer" else None
+        )
+        self._no_boundary = torch.empty((0, 2), dtype=torch.float32, device=flat.device)
+
+    def close(self) -> None:
+        """Release the peer exchange (collective over the group: call on every rank)."""
+        if self._peer is not None:
+            self._peer.close()
+            self._peer = None
 
     def gradients(
         self,
@@ -147,6 +171,19 @@ class PoissonTrainer:
         the (global) loss, a 1-element device tensor of the loss before the update."""
         if total_points is None:
             total_points = coordinates.shape[0] * world()[1]
+        if self.exchange == "peer":
+            if self._peer is None:
+                raise RuntimeError("trainer is closed")
+            if boundary is None:
+                boundary, boundary_total = self._no_boundary, 0
+            elif boundary_total is None:
+                boundary_total = boundary.shape[0] * world()[1]
+            return self._C.train_step(
+                coordinates, boundary, self.params, self.exp_avg, self.exp_avg_sq,
+                self.step_count, self.lr, self.betas[0], self.betas[1], self.eps,
+                total_points, boundary_total, self.boundary_weight, self._peer.handle,
+                self.backward_version,
+            )
         out = self.gradients(coordinates, total_points, boundary, boundary_total)
         self._C.adam_step(
             self.params,

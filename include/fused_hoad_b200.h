@@ -3,10 +3,12 @@
  * fixed 2 -> 64 -> 64 -> 64 -> 64 -> 1 tanh MLP.
  *
  * Plain pointers, sizes and a CUDA stream; no torch types. Every pointer is a device
- * pointer on the current CUDA device unless stated. All calls are asynchronous on
+ * pointer on the current CUDA device unless stated. All compute calls are asynchronous on
  * `stream`, never synchronise the host and never allocate device memory (callers pass the
  * workspace a call needs), so they can be captured in a CUDA graph once the per-device
  * set-up (fhb_prepare_device, or the first call on that device) has run outside capture.
+ * The set-up calls of the data-parallel exchange (fhb_exchange_*) are the exception: they
+ * allocate and synchronise, once per trainer.
  *
  * Parameter buffer: the reference's packed ABI (csrc/mlp_abi.cuh:8-17), 12,737 floats:
  * W0[64][2] b0[64] | W1[64][64] b1[64] | W2 b2 | W3 b3 | w_out[64] b_out[1], W row-major
@@ -40,6 +42,7 @@ typedef struct CUstream_st* fhb_stream_t;
 /* Bits of the per-device status word a kernel sets when a bounded wait gives up. */
 #define FHB_STATUS_STAGE_TIMEOUT 0x1u /* parameter staging copy never completed */
 #define FHB_STATUS_MMA_TIMEOUT 0x2u   /* tensor-core pipeline wait gave up */
+#define FHB_STATUS_PEER_TIMEOUT 0x4u  /* an exchange wait for a peer rank gave up */
 #define FHB_STATUS_SELFTEST 0x80u     /* set by fhb_debug_bounded_wait_selftest */
 
 /* Forward kernel families selected by `version` (reference csrc/bindings.cpp:33). */
@@ -164,6 +167,73 @@ int fhb_pinn_step_gradients(const float* coords, int64_t n, int64_t n_total,
 int fhb_adam_step(float* params, const float* grad, float* exp_avg, float* exp_avg_sq,
                   int64_t count, int64_t* step, float lr, float beta1, float beta2, float eps,
                   fhb_stream_t stream);
+
+/*
+ * ---- Training step: fused update and the data-parallel gradient exchange ----
+ * No counterpart in the reference (single GPU; its step is autograd + torch.optim.Adam,
+ * benchmarks/benchmark_training.py:51-56). The step's tail -- the fixed-order sum of the
+ * backward's partial rows, the sum over ranks and Adam -- is one kernel. With more than one
+ * rank, each rank writes its column sums straight into every peer's exchange buffer over
+ * NVLink (CUDA IPC mappings, plain stores), raises a flag there and waits, bounded, for the
+ * peers' flags in its own buffer; every rank then sums the ranks in rank order, so all
+ * replicas get bitwise the same gradient and update. No NCCL call on the step.
+ *
+ * An exchange object holds this rank's buffer, the mapped peer buffers and a device epoch
+ * counter. Set-up calls (create, handle, connect, destroy) allocate, synchronise and may not
+ * be captured; the step itself is asynchronous and capturable. Every rank of a group must run
+ * the same number of steps, in order; ranks one process per GPU (never two ranks of a group on
+ * one GPU: their kernels wait on one another).
+ * Exchange buffer layout (FHB_EXCHANGE_BUFFER_BYTES, 4-byte words):
+ *   float    slots[2][FHB_EXCHANGE_MAX_RANKS][FHB_EXCHANGE_ROW_FLOATS]  slot = epoch % 2
+ *   uint32_t flags[FHB_EXCHANGE_BLOCKS][FHB_EXCHANGE_MAX_RANKS]         last published epoch
+ */
+#define FHB_EXCHANGE_MAX_RANKS 8
+#define FHB_EXCHANGE_ROW_FLOATS 12740
+#define FHB_EXCHANGE_BLOCKS 399
+#define FHB_EXCHANGE_HANDLE_BYTES 64
+
+typedef struct fhb_exchange fhb_exchange;
+
+/* Bytes of one rank's exchange buffer. */
+size_t fhb_exchange_buffer_bytes(void);
+/*
+ * New exchange for rank `rank` of `world` (1..FHB_EXCHANGE_MAX_RANKS) on the current device;
+ * wait_limit_ns bounds every wait for a peer. world == 1 needs no connect (and no buffer).
+ */
+int fhb_exchange_create(int world, int rank, uint64_t wait_limit_ns, fhb_exchange** out);
+/* CUDA IPC handle of this rank's buffer (FHB_EXCHANGE_HANDLE_BYTES bytes) for the peers. */
+int fhb_exchange_handle(const fhb_exchange* exchange, void* handle_out);
+/* Maps the peers' buffers: handles = world handles in rank order (own entry ignored). */
+int fhb_exchange_connect(fhb_exchange* exchange, const void* handles);
+/* This rank's buffer (device pointer), for tests and inspection. */
+int fhb_exchange_buffer(const fhb_exchange* exchange, void** buffer_out);
+/*
+ * Test hook: connect with peer buffers given as device pointers of the current device
+ * (peer_buffers[world], own entry ignored) instead of IPC handles, so one process can stand
+ * in for the peers of a rank by filling their rows and flags itself.
+ */
+int fhb_debug_exchange_connect_local(fhb_exchange* exchange, void* const* peer_buffers);
+/* Unmaps the peers and frees the buffers (synchronises the device). Every rank must have
+ * finished its last step first (a host barrier after a device synchronise). */
+int fhb_exchange_destroy(fhb_exchange* exchange);
+
+/*
+ * One fused training step of the Poisson PINN on this rank's shard: the gradient kernel of
+ * fhb_pinn_step_gradients (boundary may be NULL with n_boundary 0: the interior loss of
+ * fhb_poisson_step_gradients), then one update kernel that sums the partial rows, sums over
+ * the exchange's ranks and applies Adam (as fhb_adam_step) to params / exp_avg / exp_avg_sq /
+ * step. grad_out (NULL or 12,738 floats) receives the global gradient and then the global
+ * loss; loss_out (NULL or 1 float) the global loss. The totals are the global counts. If a
+ * peer wait gives up, FHB_STATUS_PEER_TIMEOUT is set, the parameters of the CTAs that gave up
+ * are left unchanged and the replicas are no longer consistent: stop or reload a checkpoint.
+ * Workspace: fhb_pinn_step_workspace_bytes(n, n_boundary) bytes, 16-byte aligned.
+ */
+int fhb_train_step(const float* coords, int64_t n, int64_t n_total, const float* boundary,
+                   int64_t n_boundary, int64_t n_boundary_total, float boundary_weight,
+                   float* params, float* exp_avg, float* exp_avg_sq, int64_t* step, float lr,
+                   float beta1, float beta2, float eps, fhb_exchange* exchange,
+                   float* grad_out, float* loss_out, int version, void* workspace,
+                   size_t workspace_bytes, fhb_stream_t stream);
 
 /* Reads and clears the status word of `device` (synchronises that device). */
 int fhb_read_device_status(int device, unsigned int* status_out);
