@@ -106,6 +106,7 @@ int on_device(int device, Body body) {
 }  // namespace
 
 static_assert(sizeof(cudaIpcMemHandle_t) == FHB_EXCHANGE_HANDLE_BYTES, "IPC handle size");
+static_assert(fhb::kExchangeBytes == FHB_EXCHANGE_BUFFER_BYTES, "exchange ABI drifted");
 
 // One rank's side of the data-parallel exchange (opaque to callers).
 struct fhb_exchange {
@@ -113,9 +114,9 @@ struct fhb_exchange {
   int world = 1;
   int rank = 0;
   uint64_t wait_limit_ns = 0;
-  float* buffer = nullptr;               // this rank's exchange buffer (world > 1)
+  uint64_t* buffer = nullptr;            // this rank's exchange buffer (world > 1)
   fhb::ExchangeState* state = nullptr;   // device-resident epoch, done count, peer table
-  float* peers[fhb::kMaxRanks] = {};     // host copy of state->peers
+  uint64_t* peers[fhb::kMaxRanks] = {};  // host copy of state->peers
   bool mapped[fhb::kMaxRanks] = {};      // peers[q] is an IPC mapping this object opened
   bool connected = false;
 };
@@ -381,7 +382,7 @@ int fhb_exchange_connect(fhb_exchange* ex, const void* handles) {
         unmap_peers(ex);
         return record(e);
       }
-      ex->peers[q] = static_cast<float*>(peer);
+      ex->peers[q] = static_cast<uint64_t*>(peer);
       ex->mapped[q] = true;
     }
     const int code = publish_peers(ex);
@@ -397,7 +398,7 @@ int fhb_debug_exchange_connect_local(fhb_exchange* ex, void* const* peer_buffers
       return FHB_ERR_INVALID_ARGUMENT;
   return on_device(ex->device, [&] {
     for (int q = 0; q < ex->world; ++q)
-      if (q != ex->rank) ex->peers[q] = static_cast<float*>(peer_buffers[q]);
+      if (q != ex->rank) ex->peers[q] = static_cast<uint64_t*>(peer_buffers[q]);
     return publish_peers(ex);
   });
 }

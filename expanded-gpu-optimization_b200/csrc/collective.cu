@@ -4,25 +4,32 @@
 // The reference trains on one GPU (autograd + torch.optim.Adam, reference
 // benchmarks/benchmark_training.py:51-56), so this exchange is new. A data-parallel step
 // would otherwise be three launches after the gradient kernel -- row reduction, an NCCL
-// all-reduce of 12,738 floats, Adam -- each a full launch gap for ~51 KB of work. Here one CTA
-// owns one block of 32 columns (399 CTAs, all resident at once) and, for epoch e = epoch + 1:
-//   1. sums its columns over the partial rows in a fixed order (column_group_sum);
-//   2. world > 1: stores the 32 sums into row `rank` of slot e % 2 of EVERY rank's exchange
-//      buffer (plain stores over NVLink into CUDA IPC mappings), then, after a system-scope
-//      fence, raises flags[block][rank] = e in every rank's buffer;
-//   3. waits, bounded by wait_limit_ns, until flags[block][q] has reached e for every q in its
-//      own buffer, and sums the rows q = 0, 1, ... of its own slot in that order, so every rank
-//      gets bitwise the same totals;
-//   4. applies Adam to its columns and writes the loss;
-// and the last CTA to finish advances the step counter and the epoch.
-// Reuse of a slot needs no second barrier: rank r writes slot e % 2 of rank q again at epoch
-// e + 2, which it reaches only after seeing rank q's flag for e + 1, and rank q raises that
-// flag only after its epoch-e reads of the block are done. Flags are compared as
-// (int32)(flag - e) >= 0 because a fast peer may already have published e + 1.
-// Peer memory is touched only by plain stores (no loads, no multicast, no TMA, no library
-// kernel). A wait that gives up sets FHB_STATUS_PEER_TIMEOUT; that CTA leaves its parameters
-// unchanged and the step counters still advance, so the host sees the error on its next
-// status read rather than a hung GPU.
+// all-reduce of 12,738 floats, Adam -- for ~51 KB of work. Here one CTA owns a block of 32
+// columns (399 CTAs, all resident at once) and one thread of it owns one column. For epoch
+// e = epoch + 1 the column's thread:
+//   1. sums the column over the partial rows in a fixed order (column_group_sum + the
+//      groups in order);
+//   2. world > 1: stores the 64-bit word (e << 32 | bits of the sum) into row `rank` of slot
+//      e % 2 of EVERY rank's exchange buffer (plain stores over NVLink into the CUDA IPC
+//      mappings), then reads the words of rows 0, 1, ... of its own buffer, each until its
+//      high half is e (bounded by wait_limit_ns), and adds their low halves in rank order,
+//      so every rank gets bitwise the same sum;
+//   3. applies Adam to its parameter (or writes the loss).
+// The last CTA to finish advances the step counter and the epoch.
+//
+// Why the words carry the epoch: an aligned 64-bit access is single-copy atomic, so a word
+// whose epoch half reads e carries that epoch's value. No flag and no memory fence is needed
+// between the data and its signal; a system-scope fence costs microseconds whenever stores
+// to a peer are in flight, and a flag-per-block protocol needing one measured 15-30 us per
+// step on two GPUs against about 7 us for this one.
+// Why two slots suffice: rank r stores into slot e % 2 of rank q again at epoch e + 2, which
+// its kernel starts only after its epoch e + 1 read of rank q's word for the same column;
+// rank q stored that word in its epoch e + 1 kernel, which starts only after its epoch e
+// kernel -- and with it the epoch e read of the slot -- has finished.
+// Peer memory is touched only by plain 64-bit stores (no loads, no multicast, no TMA, no
+// library kernel). A wait that gives up sets FHB_STATUS_PEER_TIMEOUT; that column keeps
+// its parameter and moments and the counters still advance, so the host sees the error at
+// its next status read instead of a hung GPU.
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -31,16 +38,13 @@ namespace {
 
 constexpr int kUpdateThreads = kUpdateCols * kUpdateGroups;
 
-__device__ __forceinline__ void store_release_sys(uint32_t* addr, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
+__device__ __forceinline__ void store_word_sys(uint64_t* addr, uint64_t v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(addr), "l"(v) : "memory");
 }
-__device__ __forceinline__ uint32_t load_acquire_sys(const uint32_t* addr) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
+__device__ __forceinline__ uint64_t load_word_sys(const uint64_t* addr) {
+  uint64_t v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(addr) : "memory");
   return v;
-}
-__device__ __forceinline__ uint32_t* exchange_flag(float* buffer, int block, int source) {
-  return reinterpret_cast<uint32_t*>(buffer) + kExchangeFlagOffset + block * kMaxRanks + source;
 }
 
 __global__ void __launch_bounds__(kUpdateThreads)
@@ -49,65 +53,53 @@ __global__ void __launch_bounds__(kUpdateThreads)
                        float* __restrict__ grad_out, float* __restrict__ loss_out,
                        unsigned int* status) {
   __shared__ float sums[kUpdateGroups][kUpdateCols];
-  __shared__ int gave_up;
   const int cx = threadIdx.x % kUpdateCols, grp = threadIdx.x / kUpdateCols;
-  const int block = blockIdx.x;
-  const int col = block * kUpdateCols + cx;
+  const int col = blockIdx.x * kUpdateCols + cx;
   const bool live = col <= kLossColumn;
   // Read before this CTA counts itself done, so before the last CTA advances them.
   const int64_t t = *adam.step + 1;
   const uint32_t e = state->epoch + 1u;
 
   sums[grp][cx] = live ? column_group_sum(partials, rows, col, grp) : 0.0f;
-  if (threadIdx.x == 0) gave_up = 0;
   __syncthreads();
-  float total = 0.0f;
-  if (grp == 0) {
-    total = sums[0][cx];
+  if (grp == 0 && live) {
+    float total = sums[0][cx];
 #pragma unroll
     for (int k = 1; k < kUpdateGroups; ++k) total += sums[k][cx];
-  }
-
-  if (world > 1) {
-    const size_t slot = (e & 1u) * kMaxRanks;
-    if (grp == 0 && live) {
-      for (int q = 0; q < world; ++q) state->peers[q][(slot + rank) * kRowStride + col] = total;
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      __threadfence_system();
-      for (int q = 0; q < world; ++q) store_release_sys(exchange_flag(state->peers[q], block, rank), e);
-    }
-    if (threadIdx.x < world) {
-      const uint32_t* flag = exchange_flag(state->peers[rank], block, threadIdx.x);
+    bool ok = true;
+    if (world > 1) {
+      const size_t slot = (e & 1u) * kMaxRanks;
+      const uint64_t word = (static_cast<uint64_t>(e) << 32) | __float_as_uint(total);
+      for (int q = 0; q < world; ++q)
+        store_word_sys(state->peers[q] + (slot + rank) * kRowStride + col, word);
+      const uint64_t* own = state->peers[rank] + slot * kRowStride + col;
       const uint64_t start = global_timer_ns();
-      while (static_cast<int32_t>(load_acquire_sys(flag) - e) < 0) {
-        if (global_timer_ns() - start > wait_limit_ns) {
-          report_status(status, FHB_STATUS_PEER_TIMEOUT);
-          gave_up = 1;
-          break;
+      for (int q = 0; q < world && ok; ++q) {
+        uint64_t got = load_word_sys(own + static_cast<size_t>(q) * kRowStride);
+        while (static_cast<uint32_t>(got >> 32) != e) {
+          if (global_timer_ns() - start > wait_limit_ns) {
+            report_status(status, FHB_STATUS_PEER_TIMEOUT);
+            ok = false;
+            break;
+          }
+          got = load_word_sys(own + static_cast<size_t>(q) * kRowStride);
         }
+        const float value = __uint_as_float(static_cast<uint32_t>(got));
+        total = q == 0 ? value : total + value;
       }
     }
-    __syncthreads();
-    if (grp == 0 && live && !gave_up) {
-      const float* own = state->peers[rank] + slot * kRowStride + col;
-      total = __ldcg(own);
-      for (int q = 1; q < world; ++q) total += __ldcg(own + static_cast<size_t>(q) * kRowStride);
-    }
-  }
-
-  if (grp == 0 && live && !gave_up) {
-    if (grad_out != nullptr) grad_out[col] = total;
-    if (col == kLossColumn) {
-      if (loss_out != nullptr) *loss_out = total;
-    } else {
-      const AdamScalars s = adam_scalars(t, adam.lr, adam.beta1, adam.beta2);
-      float p = adam.params[col], m = adam.exp_avg[col], v = adam.exp_avg_sq[col];
-      adam_element(total, p, m, v, s, adam.beta1, adam.beta2, adam.eps);
-      adam.exp_avg[col] = m;
-      adam.exp_avg_sq[col] = v;
-      adam.params[col] = p;
+    if (ok) {
+      if (grad_out != nullptr) grad_out[col] = total;
+      if (col == kLossColumn) {
+        if (loss_out != nullptr) *loss_out = total;
+      } else {
+        const AdamScalars s = adam_scalars(t, adam.lr, adam.beta1, adam.beta2);
+        float p = adam.params[col], m = adam.exp_avg[col], v = adam.exp_avg_sq[col];
+        adam_element(total, p, m, v, s, adam.beta1, adam.beta2, adam.eps);
+        adam.exp_avg[col] = m;
+        adam.exp_avg_sq[col] = v;
+        adam.params[col] = p;
+      }
     }
   }
 

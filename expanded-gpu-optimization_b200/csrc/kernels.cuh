@@ -27,30 +27,27 @@ struct PointSets {
   float bweight = 0.0f;             // boundary term weight
 };
 
-// The training step's update: the partial rows are summed per column block of kUpdateCols
-// columns (kUpdateGroups row groups each), one CTA per block.
+// The training step's update: the partial rows are summed per block of kUpdateCols columns
+// (kUpdateGroups row groups each), one CTA per block.
 constexpr int kUpdateCols = 32;
 constexpr int kUpdateGroups = 8;
 constexpr int kUpdateBlocks = (kLossColumn + 1 + kUpdateCols - 1) / kUpdateCols;  // 399
 
-// Data-parallel exchange through peer memory (collective.cu). Each rank owns one buffer:
-//   float    slots[2][kMaxRanks][kRowStride]   slot = epoch % 2, row = source rank
-//   uint32_t flags[kUpdateBlocks][kMaxRanks]   last epoch the source rank published there
-// Every rank writes its column block into row `rank` of every rank's buffer and then raises
-// its flag there, so a rank reads only its own memory once the flags are up.
+// Data-parallel exchange through peer memory (collective.cu). Each rank owns one buffer of
+// 64-bit words, words[2][kMaxRanks][kRowStride]: slot = epoch % 2, row = source rank, word =
+// (epoch << 32) | bits of the source rank's column sum for that epoch. Every rank stores its
+// words into row `rank` of every rank's buffer, so a rank reads only its own memory.
 constexpr int kMaxRanks = 8;
-constexpr size_t kExchangeFlagOffset = 2ull * kMaxRanks * kRowStride;  // in 4-byte words
-constexpr size_t kExchangeBytes =
-    (kExchangeFlagOffset + static_cast<size_t>(kUpdateBlocks) * kMaxRanks) * 4;
+constexpr size_t kExchangeWords = 2ull * kMaxRanks * kRowStride;
+constexpr size_t kExchangeBytes = kExchangeWords * sizeof(uint64_t);
 static_assert(kMaxRanks == FHB_EXCHANGE_MAX_RANKS, "exchange ABI drifted");
-static_assert(kRowStride == FHB_EXCHANGE_ROW_FLOATS, "exchange ABI drifted");
-static_assert(kUpdateBlocks == FHB_EXCHANGE_BLOCKS, "exchange ABI drifted");
+static_assert(kRowStride == FHB_EXCHANGE_ROW_WORDS, "exchange ABI drifted");
 
 // Device-resident state of one exchange (one per rank and trainer).
 struct ExchangeState {
-  float* peers[kMaxRanks];  // every rank's buffer as mapped in this process (own included)
-  uint32_t epoch;           // exchanges completed
-  uint32_t done;            // CTAs of the running update that have finished (0 between)
+  uint64_t* peers[kMaxRanks];  // every rank's buffer as mapped in this process (own included)
+  uint32_t epoch;              // exchanges completed
+  uint32_t done;               // CTAs of the running update that have finished (0 between)
 };
 
 struct AdamArgs {
@@ -172,7 +169,7 @@ cudaError_t launch_adam(float* params, const float* grad, float* exp_avg, float*
 // with world > 1 the sum over ranks through the peer buffers of `state`, then Adam on the
 // parameters; grad_out (kLossColumn + 1 floats, may be null) receives the summed gradient and
 // loss, loss_out (may be null) the loss. A peer wait that exceeds wait_limit_ns sets
-// FHB_STATUS_PEER_TIMEOUT and leaves that CTA's parameters unchanged.
+// FHB_STATUS_PEER_TIMEOUT and leaves that column's parameter unchanged.
 cudaError_t launch_step_update(const float* partials, int rows, ExchangeState* state, int world,
                                int rank, uint64_t wait_limit_ns, const AdamArgs& adam,
                                float* grad_out, float* loss_out, unsigned int* status,

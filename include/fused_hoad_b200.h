@@ -52,8 +52,8 @@ typedef struct CUstream_st* fhb_stream_t;
 #define FHB_BACKWARD_VERSION_MIN 1
 #define FHB_BACKWARD_VERSION_MAX 6
 /* Backward versions 1..5 run the FP32 CUDA-core adjoint kernel; 6 (the reference's default)
- * runs the tensor-core one (3xTF32 tcgen05 forward recompute and input adjoint, FP32 weight
- * gradient). Both reduce in a fixed order. */
+ * runs the tensor-core one (forward recompute, input adjoint and weight gradient on tcgen05
+ * in 3xTF32). Both reduce in a fixed order. */
 #define FHB_BACKWARD_VERSION_TENSOR_CORE 6
 
 const char* fhb_status_string(int code);
@@ -173,29 +173,30 @@ int fhb_adam_step(float* params, const float* grad, float* exp_avg, float* exp_a
  * No counterpart in the reference (single GPU; its step is autograd + torch.optim.Adam,
  * benchmarks/benchmark_training.py:51-56). The step's tail -- the fixed-order sum of the
  * backward's partial rows, the sum over ranks and Adam -- is one kernel. With more than one
- * rank, each rank writes its column sums straight into every peer's exchange buffer over
- * NVLink (CUDA IPC mappings, plain stores), raises a flag there and waits, bounded, for the
- * peers' flags in its own buffer; every rank then sums the ranks in rank order, so all
- * replicas get bitwise the same gradient and update. No NCCL call on the step.
+ * rank, each rank stores its column sums straight into every peer's exchange buffer over
+ * NVLink (CUDA IPC mappings, plain 64-bit stores of value and epoch together) and reads the
+ * peers' words from its own buffer, each wait bounded; every rank then sums the ranks in rank
+ * order, so all replicas get bitwise the same gradient and update. No NCCL call on the step.
  *
  * An exchange object holds this rank's buffer, the mapped peer buffers and a device epoch
  * counter. Set-up calls (create, handle, connect, destroy) allocate, synchronise and may not
  * be captured; the step itself is asynchronous and capturable. Every rank of a group must run
- * the same number of steps, in order; ranks one process per GPU (never two ranks of a group on
- * one GPU: their kernels wait on one another).
- * Exchange buffer layout (FHB_EXCHANGE_BUFFER_BYTES, 4-byte words):
- *   float    slots[2][FHB_EXCHANGE_MAX_RANKS][FHB_EXCHANGE_ROW_FLOATS]  slot = epoch % 2
- *   uint32_t flags[FHB_EXCHANGE_BLOCKS][FHB_EXCHANGE_MAX_RANKS]         last published epoch
+ * the same number of steps, in order, one process per GPU (never two ranks of a group on one
+ * GPU: their kernels wait on one another).
+ * Exchange buffer layout (FHB_EXCHANGE_BUFFER_BYTES):
+ *   uint64_t words[2][FHB_EXCHANGE_MAX_RANKS][FHB_EXCHANGE_ROW_WORDS]
+ *   slot = epoch % 2, row = source rank; word = (epoch << 32) | bits of the float column sum
+ *   (columns 0..12736 the gradient, 12737 the loss).
  */
 #define FHB_EXCHANGE_MAX_RANKS 8
-#define FHB_EXCHANGE_ROW_FLOATS 12740
-#define FHB_EXCHANGE_BLOCKS 399
+#define FHB_EXCHANGE_ROW_WORDS 12740
 #define FHB_EXCHANGE_HANDLE_BYTES 64
+#define FHB_EXCHANGE_BUFFER_BYTES (2 * FHB_EXCHANGE_MAX_RANKS * FHB_EXCHANGE_ROW_WORDS * 8)
 
 typedef struct fhb_exchange fhb_exchange;
 
 /* Bytes of one rank's exchange buffer. */
-size_t fhb_exchange_buffer_bytes(void);
+size_t fhb_exchange_buffer_bytes(void); /* FHB_EXCHANGE_BUFFER_BYTES */
 /*
  * New exchange for rank `rank` of `world` (1..FHB_EXCHANGE_MAX_RANKS) on the current device;
  * wait_limit_ns bounds every wait for a peer. world == 1 needs no connect (and no buffer).
@@ -210,7 +211,7 @@ int fhb_exchange_buffer(const fhb_exchange* exchange, void** buffer_out);
 /*
  * Test hook: connect with peer buffers given as device pointers of the current device
  * (peer_buffers[world], own entry ignored) instead of IPC handles, so one process can stand
- * in for the peers of a rank by filling their rows and flags itself.
+ * in for the peers of a rank by writing their words itself.
  */
 int fhb_debug_exchange_connect_local(fhb_exchange* exchange, void* const* peer_buffers);
 /* Unmaps the peers and frees the buffers (synchronises the device). Every rank must have
@@ -224,8 +225,8 @@ int fhb_exchange_destroy(fhb_exchange* exchange);
  * the exchange's ranks and applies Adam (as fhb_adam_step) to params / exp_avg / exp_avg_sq /
  * step. grad_out (NULL or 12,738 floats) receives the global gradient and then the global
  * loss; loss_out (NULL or 1 float) the global loss. The totals are the global counts. If a
- * peer wait gives up, FHB_STATUS_PEER_TIMEOUT is set, the parameters of the CTAs that gave up
- * are left unchanged and the replicas are no longer consistent: stop or reload a checkpoint.
+ * peer wait gives up, FHB_STATUS_PEER_TIMEOUT is set, the parameters whose wait gave up are
+ * left unchanged and the replicas are no longer consistent: stop or reload a checkpoint.
  * Workspace: fhb_pinn_step_workspace_bytes(n, n_boundary) bytes, 16-byte aligned.
  */
 int fhb_train_step(const float* coords, int64_t n, int64_t n_total, const float* boundary,

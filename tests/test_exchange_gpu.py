@@ -3,8 +3,8 @@
 Checks, against the separate launches it replaces (row reduction, flat-buffer sum, the Adam
 kernel) and the oracle:
   * one rank: the fused update gives bitwise the parameters of reduction + Adam;
-  * two ranks emulated on one GPU: the test plays rank 1 by writing its column sums and
-    flags into rank 0's exchange buffer before rank 0's step (no second kernel waits on the
+  * two ranks emulated on one GPU: the test plays rank 1 by writing its epoch-tagged column
+    sums into rank 0's exchange buffer before rank 0's step (no second kernel waits on the
     first), and rank 0's own sums must land in rank 1's buffer;
   * a peer that never publishes: the bounded wait gives up, sets FHB_STATUS_PEER_TIMEOUT,
     and the parameters stay unchanged.
@@ -25,10 +25,8 @@ from oracle import jet
 
 pytestmark = pytest.mark.gpu
 
-ROW = 12740          # FHB_EXCHANGE_ROW_FLOATS
+ROW = 12740          # FHB_EXCHANGE_ROW_WORDS
 MAX_RANKS = 8        # FHB_EXCHANGE_MAX_RANKS
-BLOCKS = 399         # FHB_EXCHANGE_BLOCKS
-FLAG_OFFSET = 2 * MAX_RANKS * ROW
 PEER_TIMEOUT = 0x4   # FHB_STATUS_PEER_TIMEOUT
 
 
@@ -41,18 +39,22 @@ def _cuda():
 
 
 class _DeviceWords:
-    """A device address seen as a torch tensor of 32-bit words (``__cuda_array_interface__``)."""
+    """A device address seen as a torch int64 tensor (``__cuda_array_interface__``)."""
 
     def __init__(self, address: int, words: int) -> None:
         self.__cuda_array_interface__ = {
-            "shape": (words,), "typestr": "<f4", "data": (address, False), "strides": None,
+            "shape": (words,), "typestr": "<i8", "data": (address, False), "strides": None,
             "version": 3,
         }
 
 
+def _buffer_words() -> int:
+    return _native.library().fhb_exchange_buffer_bytes() // 8
+
+
 def _exchange_words(C, handle: int) -> torch.Tensor:
-    words = _native.library().fhb_exchange_buffer_bytes() // 4
-    return torch.as_tensor(_DeviceWords(C.exchange_buffer(handle), words), device="cuda")
+    return torch.as_tensor(_DeviceWords(C.exchange_buffer(handle), _buffer_words()),
+                           device="cuda")
 
 
 def _slot_row(buf: torch.Tensor, epoch: int, source: int) -> torch.Tensor:
@@ -60,8 +62,17 @@ def _slot_row(buf: torch.Tensor, epoch: int, source: int) -> torch.Tensor:
     return buf[start:start + PARAMETER_COUNT + 1]
 
 
-def _flags(buf: torch.Tensor) -> torch.Tensor:
-    return buf[FLAG_OFFSET:FLAG_OFFSET + BLOCKS * MAX_RANKS].view(torch.int32).view(BLOCKS, MAX_RANKS)
+def _pack(values: torch.Tensor, epoch: int) -> torch.Tensor:
+    """The words a rank stores: epoch in the high half, the float's bits in the low half."""
+    return (values.view(torch.int32).to(torch.int64) & 0xFFFFFFFF) | (epoch << 32)
+
+
+def _epochs(words: torch.Tensor) -> torch.Tensor:
+    return words >> 32
+
+
+def _values(words: torch.Tensor) -> torch.Tensor:
+    return (words & 0xFFFFFFFF).to(torch.int32).view(torch.float32)
 
 
 def _adam_state(params: torch.Tensor):
@@ -133,7 +144,7 @@ def test_train_step_through_the_c_abi_matches_the_oracle() -> None:
 
 @pytest.mark.parametrize("kernel", [5, 6])
 def test_two_rank_exchange_emulated_on_one_gpu(kernel: int) -> None:
-    """Rank 0 of 2; the test writes rank 1's column sums and flags, as rank 1's kernel would."""
+    """Rank 0 of 2; the test writes rank 1's words, as rank 1's kernel would."""
     C = fused_hoad.load_extension()
     params = jet.init_parameters(2).cuda()
     total = 30_001
@@ -141,7 +152,7 @@ def test_two_rank_exchange_emulated_on_one_gpu(kernel: int) -> None:
     a, b = fused_hoad.shard_range(total, 0, 2)
     x0, x1 = x[a:b].contiguous(), x[b:].contiguous()
     ex = C.exchange_create(2, 0, 5.0, 0)
-    peer = torch.zeros(_native.library().fhb_exchange_buffer_bytes() // 4, device="cuda")
+    peer = torch.zeros(_buffer_words(), dtype=torch.int64, device="cuda")
     try:
         C.exchange_connect_local(ex, [0, peer.data_ptr()])
         own = _exchange_words(C, ex)
@@ -150,8 +161,7 @@ def test_two_rank_exchange_emulated_on_one_gpu(kernel: int) -> None:
         empty = torch.empty(0, 2, device="cuda")
         for epoch in (1, 2, 3):
             g1 = C.poisson_step_gradients(x1, p, total, version=kernel)[0]
-            _slot_row(own, epoch, 1).copy_(g1)
-            _flags(own)[:, 1] = epoch
+            _slot_row(own, epoch, 1).copy_(_pack(g1, epoch))
             grad = torch.empty(PARAMETER_COUNT + 1, device="cuda")
             loss = C.train_step(x0, empty, p, m, v, s, *HYPER.values(), total, 0, 100.0, ex,
                                 kernel, grad)
@@ -161,11 +171,10 @@ def test_two_rank_exchange_emulated_on_one_gpu(kernel: int) -> None:
             assert torch.equal(loss, want[PARAMETER_COUNT:])
             C.adam_step(pw, want[:PARAMETER_COUNT], mw, vw, sw, *HYPER.values())
             assert torch.equal(p, pw), epoch
-            # rank 0's own sums went into row 0 of both buffers, with its flags raised
-            assert torch.equal(_slot_row(peer, epoch, 0), g0)
-            assert torch.equal(_slot_row(own, epoch, 0), g0)
-            assert bool((_flags(peer)[:, 0] == epoch).all())
-            assert bool((_flags(own)[:, 0] == epoch).all())
+            # rank 0's own sums went into row 0 of both buffers, tagged with the epoch
+            for buf in (peer, own):
+                assert torch.equal(_values(_slot_row(buf, epoch, 0)), g0)
+                assert bool((_epochs(_slot_row(buf, epoch, 0)) == epoch).all())
         # the exchange of two shards is the full-batch step (up to summation order)
         full = C.poisson_step_gradients(x, params, total, version=kernel)[0]
         first = C.poisson_step_gradients(x0, params, total, version=kernel)[0] + \
@@ -177,12 +186,12 @@ def test_two_rank_exchange_emulated_on_one_gpu(kernel: int) -> None:
 
 
 def test_peer_that_never_publishes_times_out_without_update() -> None:
-    """Rank 1's flags are never raised: the bounded wait gives up after 2 ms."""
+    """Rank 1's words never arrive: the bounded wait gives up after 2 ms."""
     C = fused_hoad.load_extension()
     params = jet.init_parameters(3).cuda()
     x = uniform_points(2_048, seed=34).cuda()
     ex = C.exchange_create(2, 0, 0.002, 0)
-    peer = torch.zeros(_native.library().fhb_exchange_buffer_bytes() // 4, device="cuda")
+    peer = torch.zeros(_buffer_words(), dtype=torch.int64, device="cuda")
     try:
         C.exchange_connect_local(ex, [0, peer.data_ptr()])
         p, m, v, s = _adam_state(params)
@@ -191,8 +200,8 @@ def test_peer_that_never_publishes_times_out_without_update() -> None:
         torch.cuda.synchronize()
         assert read_status() & PEER_TIMEOUT
         assert torch.equal(p, params) and not m.any() and not v.any()
-        # rank 0 still published, so a peer would not wait on it
-        assert bool((_flags(peer)[:, 0] == 1).all())
+        # rank 0 still published its words, so a peer would not wait on it
+        assert bool((_epochs(_slot_row(peer, 1, 0)) == 1).all())
     finally:
         C.exchange_destroy(ex)
     assert read_status() == 0
