@@ -50,6 +50,7 @@ UNIT = "pts/s"
 FLOP_FORWARD = 101_888  # per point: 3 hidden 64x64 jet GEMMs x 4 comps + layer 0/out + tanh jet
 FLOP_STEP = 98_304 * 3 + 256 * 2 + 6_000  # forward + input adjoint + weight gradient + small
 POINTS_PER_GPU = 65_536
+F16_TRAFFIC = 657_920  # DRAM bytes of one version-3 launch at 65,536 points (ncu)
 FLUSH_BYTES = 192 << 20
 PEAKS_FILE = ROOT / "MEASURED_PEAKS.json"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
@@ -372,10 +373,10 @@ def run_ours(args) -> None:
         return
 
     # DRAM read + write bytes of one forward launch at 65,536 points, from one ncu capture of
-    # the same command (versions 0-2 share the FP32 kernel family, 3-5 the tensor-core one).
+    # the same command per kernel family (0-2: FP32 kernel, 3: 3xFP16, 4-5: 3xTF32).
     traffic = None
     if n == POINTS_PER_GPU:
-        traffic = 611_840 if version <= 2 else 646_400
+        traffic = {0: 611_840, 1: 611_840, 2: 611_840, 3: F16_TRAFFIC, 4: 646_400, 5: 646_400}[version]
     per_launch_s = ms_per_step / 1e3
     achieved_tflops = n * FLOP_FORWARD / per_launch_s / 1e12
     fp32_peak = SM_COUNT * 128 * 2 * peaks.get("sm_max_mhz", 1965.0) * 1e6 / 1e12
@@ -390,13 +391,18 @@ def run_ours(args) -> None:
         }
     else:
         bf16 = peaks["bf16_tflops"]
+        f16 = version == 3
         roofline = {
             "bound": "tensor", "achieved": achieved_tflops, "peak": bf16, "unit": "TFLOP/s",
             "frac": achieved_tflops / bf16, "traffic": traffic,
-            "kernel": f"forward_tc_kernel (version {version})",
-            "peak_note": (f"{peak_kind} bf16 burst peak; TF32 runs at half of it and 3xTF32 "
-                          "issues three MMAs per product, so the 3xTF32 ceiling is bf16/6"),
-            "frac_of_3xtf32_ceiling": achieved_tflops / (bf16 / 6.0),
+            "kernel": ("forward_f16_kernel (version 3, 3xFP16)" if f16 else
+                       f"forward_tc_kernel (version {version}, 3xTF32)"),
+            "peak_note": (f"{peak_kind} bf16 burst peak. Each algorithmic product costs three "
+                          "MMAs (hi.hi, lo.hi, hi.lo); f16 runs at the bf16 rate and tf32 at "
+                          "half of it, so the split ceiling is bf16/3 for 3xFP16 and bf16/6 "
+                          "for 3xTF32"),
+            "split_ceiling": bf16 / (3.0 if f16 else 6.0),
+            "frac_of_split_ceiling": achieved_tflops / (bf16 / (3.0 if f16 else 6.0)),
             "flop_per_point": FLOP_FORWARD,
         }
     if clk["sm_mhz"]:

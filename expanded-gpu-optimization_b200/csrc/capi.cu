@@ -48,6 +48,7 @@ int prepare_locked(int device) {
     if ((e = cudaGetSymbolAddress(reinterpret_cast<void**>(&info.status), g_status_word)) != cudaSuccess ||
         (e = fhb::prepare_forward_fp32()) != cudaSuccess ||
         (e = fhb::prepare_forward_tc()) != cudaSuccess ||
+        (e = fhb::prepare_forward_f16()) != cudaSuccess ||
         (e = fhb::prepare_backward_fp32()) != cudaSuccess ||
         (e = fhb::prepare_backward_tc()) != cudaSuccess) {
       code = record(e);
@@ -176,9 +177,13 @@ int fhb_forward(const float* coords, const float* params, float* u, float* lap, 
   const fhb::DeviceInfo* dev = nullptr;
   int code = current_device(&dev);
   if (code != FHB_OK) return code;
-  cudaError_t e = version <= 2
-                      ? fhb::launch_forward_fp32(version, coords, params, u, lap, n, *dev, stream)
-                      : fhb::launch_forward_tc(coords, params, u, lap, n, *dev, stream);
+  cudaError_t e;
+  if (version <= 2)
+    e = fhb::launch_forward_fp32(version, coords, params, u, lap, n, *dev, stream);
+  else if (version == FHB_FORWARD_VERSION_F16)
+    e = fhb::launch_forward_f16(coords, params, u, lap, n, *dev, stream);
+  else
+    e = fhb::launch_forward_tc(coords, params, u, lap, n, *dev, stream);
   return record(e);
 }
 

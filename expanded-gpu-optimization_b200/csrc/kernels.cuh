@@ -130,6 +130,11 @@ cudaError_t launch_forward_fp32(int tile, const float* coords, const float* para
                                 float* lap, int64_t n, const DeviceInfo& dev,
                                 cudaStream_t stream);
 
+// ---- forward_f16.cu ----
+cudaError_t prepare_forward_f16();
+cudaError_t launch_forward_f16(const float* coords, const float* params, float* u, float* lap,
+                               int64_t n, const DeviceInfo& dev, cudaStream_t stream);
+
 // ---- forward_tc.cu ----
 cudaError_t prepare_forward_tc();
 cudaError_t launch_forward_tc(const float* coords, const float* params, float* u, float* lap,

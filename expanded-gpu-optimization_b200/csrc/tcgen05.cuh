@@ -68,6 +68,20 @@ __device__ __forceinline__ void mma_tf32_ts_warp(uint32_t d_tmem, uint32_t a_tme
       "r"(0u), "r"(0u)
       : "memory");
 }
+// D[tmem] (+)= A[tmem] * B[smem]^T, kind::f16 (A and B both f16, D f32), issued by a converged
+// warp (elect.sync picks the lane). A holds two f16 K elements per 32-bit TMEM column.
+__device__ __forceinline__ void mma_f16_ts_warp(uint32_t d_tmem, uint32_t a_tmem,
+                                                uint64_t b_desc, uint32_t idesc,
+                                                uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}"
+      ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u),
+      "r"(0u), "r"(0u)
+      : "memory");
+}
 // D[tmem] (+)= A[smem] * B[smem]^T, kind::tf32, both operands from shared memory, issued by
 // a converged warp (elect.sync picks the lane).
 __device__ __forceinline__ void mma_tf32_ss_warp(uint32_t d_tmem, uint64_t a_desc,
@@ -182,6 +196,16 @@ __host__ __device__ constexpr uint32_t idesc_tf32(int m, int n) {
   return (1u << 4)                                  // D format: f32
          | (2u << 7)                                // A format: tf32
          | (2u << 10)                               // B format: tf32
+         | (0u << 15) | (0u << 16)                  // A, B K-major
+         | (static_cast<uint32_t>(n >> 3) << 17)    // N / 8
+         | (static_cast<uint32_t>(m >> 4) << 24);   // M / 16
+}
+
+// Instruction descriptor for kind::f16 with f16 A and B (format 0), D f32, both K-major.
+__host__ __device__ constexpr uint32_t idesc_f16(int m, int n) {
+  return (1u << 4)                                  // D format: f32
+         | (0u << 7)                                // A format: f16
+         | (0u << 10)                               // B format: f16
          | (0u << 15) | (0u << 16)                  // A, B K-major
          | (static_cast<uint32_t>(n >> 3) << 17)    // N / 8
          | (static_cast<uint32_t>(m >> 4) << 24);   // M / 16

@@ -48,6 +48,9 @@ typedef struct CUstream_st* fhb_stream_t;
 /* Forward kernel families selected by `version` (reference csrc/bindings.cpp:33). */
 #define FHB_FORWARD_VERSION_MIN 0
 #define FHB_FORWARD_VERSION_MAX 5
+/* Version 3 runs the 3xFP16 tensor-core kernel (f16 operand pairs with power-of-2 range
+ * scaling), 4 and 5 the 3xTF32 one; both keep FP32-level accuracy. */
+#define FHB_FORWARD_VERSION_F16 3
 /* Backward versions accepted for drop-in compatibility (reference csrc/bindings.cpp:45). */
 #define FHB_BACKWARD_VERSION_MIN 1
 #define FHB_BACKWARD_VERSION_MAX 6
@@ -74,7 +77,11 @@ int fhb_prepare_device(int device);
  * fused_hoad._C.fused_forward_laplacian (csrc/bindings.cpp:31-36).
  * version 0..2: FP32 CUDA-core kernel (0: 32-point tiles, 1: 128-point tiles,
  *               2: 64-point tiles, the default);
- * version 3..5: 3xTF32 tcgen05/TMEM tensor-core kernel (FP32-level accuracy).
+ * version 3:    3xFP16 tcgen05/TMEM tensor-core kernel (kind::f16; hi/lo f16 operand pairs
+ *               with per-launch power-of-2 scales derived from the weights, so no operand
+ *               leaves the f16 range; FP32-level accuracy), the fastest;
+ * version 4, 5: 3xTF32 tcgen05/TMEM tensor-core kernel (FP32-level accuracy over the whole
+ *               FP32 range).
  * n == 0 is a no-op. The parameter buffer may have any 4-byte alignment.
  */
 int fhb_forward(const float* coords, const float* params, float* u, float* lap, int64_t n,

@@ -28,7 +28,7 @@ from oracle import jet
 pytestmark = pytest.mark.gpu
 
 FP32_VERSIONS = [0, 1, 2]
-TC_VERSIONS = [3, 4, 5]
+TC_VERSIONS = [3, 4, 5]  # 3: 3xFP16 kernel; 4, 5: 3xTF32 kernel
 ALL_VERSIONS = FP32_VERSIONS + TC_VERSIONS
 BATCHES = [1, 2, 31, 32, 33, 63, 64, 65, 127, 128, 129, 1_000, 65_536]
 ROUTES = ["capi", "torch"]
@@ -92,6 +92,28 @@ def test_forward_saturated_weights_against_fp64(golden, version: int) -> None:
     u, lap = fused_forward_laplacian(coords, params, version)
     assert_scaled(lap.cpu(), golden["sat_lap64"], 1e-4, "lap")
     assert_scaled(u.cpu(), golden["sat_u64"], 1e-4, "u")
+
+
+@pytest.mark.parametrize("scale", [0.05, 1.0, 3.0, 10.0, 30.0])
+def test_forward_f16_kernel_tracks_tf32_across_weight_scales(scale: float) -> None:
+    """Version 3 (3xFP16 operands with per-launch power-of-2 range scales) against the FP64
+    oracle beside the 3xTF32 kernel (version 4): finite everywhere and within 2x of the
+    3xTF32 error at every weight scale. From x10 up, unscaled f16 operands would overflow
+    (the Laplacian jet passes 65,504)."""
+    params = jet.init_parameters(0, scale)
+    coords = uniform_points(4_096, seed=51)
+    u64, lap64 = jet.forward_laplacian(params.double(), coords.double())
+    errors = {}
+    for version in (3, 4):
+        u, lap = fused_forward_laplacian(coords.cuda(), params.cuda(), version)
+        assert bool(torch.isfinite(u).all() and torch.isfinite(lap).all())
+        errors[version] = ((u.cpu().double() - u64).abs().max().item(),
+                           (lap.cpu().double() - lap64).abs().max().item())
+    for k, ref in enumerate((u64, lap64)):
+        size = ref.abs().max().item()
+        assert errors[3][k] <= 2.0 * errors[4][k] + 1e-7 * size, (k, errors)
+        if scale <= 10.0:  # at x30 FP32 arithmetic itself misses 1e-4 on the Laplacian
+            assert errors[3][k] <= 1e-4 * size, (k, errors)
 
 
 @pytest.mark.parametrize("version", ALL_VERSIONS)
