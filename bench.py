@@ -395,8 +395,8 @@ def run_ours(args) -> None:
         roofline = {
             "bound": "tensor", "achieved": achieved_tflops, "peak": bf16, "unit": "TFLOP/s",
             "frac": achieved_tflops / bf16, "traffic": traffic,
-            "kernel": ("forward_f16_kernel (version 3, 3xFP16)" if f16 else
-                       f"forward_tc_kernel (version {version}, 3xTF32)"),
+            "kernel": ("forward_tc_kernel<true> (version 3, 3xFP16)" if f16 else
+                       f"forward_tc_kernel<false> (version {version}, 3xTF32)"),
             "peak_note": (f"{peak_kind} bf16 burst peak. Each algorithmic product costs three "
                           "MMAs (hi.hi, lo.hi, hi.lo); f16 runs at the bf16 rate and tf32 at "
                           "half of it, so the split ceiling is bf16/3 for 3xFP16 and bf16/6 "

@@ -40,8 +40,8 @@ NVCC_FLAGS = [
     f"-I{INCLUDE}",
 ]
 CU_SOURCES = [
-    "forward_fp32.cu", "forward_tc.cu", "forward_f16.cu", "backward_fp32.cu", "backward_tc.cu",
-    "adam.cu", "collective.cu", "capi.cu", "noalloc.cu",
+    "forward_fp32.cu", "forward_tc.cu", "backward_fp32.cu", "backward_tc.cu", "adam.cu",
+    "collective.cu", "capi.cu", "noalloc.cu",
 ]
 
 

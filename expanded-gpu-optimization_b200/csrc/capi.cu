@@ -48,7 +48,6 @@ int prepare_locked(int device) {
     if ((e = cudaGetSymbolAddress(reinterpret_cast<void**>(&info.status), g_status_word)) != cudaSuccess ||
         (e = fhb::prepare_forward_fp32()) != cudaSuccess ||
         (e = fhb::prepare_forward_tc()) != cudaSuccess ||
-        (e = fhb::prepare_forward_f16()) != cudaSuccess ||
         (e = fhb::prepare_backward_fp32()) != cudaSuccess ||
         (e = fhb::prepare_backward_tc()) != cudaSuccess) {
       code = record(e);
@@ -180,10 +179,9 @@ int fhb_forward(const float* coords, const float* params, float* u, float* lap, 
   cudaError_t e;
   if (version <= 2)
     e = fhb::launch_forward_fp32(version, coords, params, u, lap, n, *dev, stream);
-  else if (version == FHB_FORWARD_VERSION_F16)
-    e = fhb::launch_forward_f16(coords, params, u, lap, n, *dev, stream);
   else
-    e = fhb::launch_forward_tc(coords, params, u, lap, n, *dev, stream);
+    e = fhb::launch_forward_tc(coords, params, u, lap, n, version == FHB_FORWARD_VERSION_F16,
+                               *dev, stream);
   return record(e);
 }
 

@@ -1,45 +1,64 @@
-// 3xTF32 tcgen05/TMEM forward-Laplacian kernel (forward versions 3, 4, 5).
+// Tensor-core forward-Laplacian kernel, one template over the operand format:
+// 3xFP16 (forward version 3, the default tensor-core path) and 3xTF32 (versions 4, 5).
 //
 // Same math as the FP32 kernel and the reference (csrc/fused_residual.cu:16-23), with the
 // three hidden 64x64 jet GEMMs on the 5th-generation tensor cores. Each hidden layer is,
 // per tile of 128 points and per jet component c in {v, d/dx, d/dy, L},
 //     Z_c[128 x 64] = H_c[128 x 64] . W^T,
-// run as tcgen05.mma kind::tf32 with M = 128 points, N = 64 output neurons, K = 8 per
-// instruction. FP32 accuracy is kept by the 3xTF32 split (x = x_hi + x_lo, both rounded to
-// TF32): Z += H_hi W_hi + H_lo W_hi + H_hi W_lo, accumulated in FP32 in tensor memory.
+// run as tcgen05.mma with M = 128 points and N = 64 output neurons, the A operand
+// (activations) in tensor memory and B (weights) in shared memory. FP32 accuracy comes from a
+// split x = hi + lo into two low-precision parts and three products per product:
+//   * 3xTF32 (kind::tf32, K = 8): hi = tf32(x), lo = x - hi;
+//     Z += H_hi W_hi + H_lo W_hi + H_hi W_lo; a 16-neuron chunk is 24 MMAs;
+//   * 3xFP16 (kind::f16, K = 16): hi = f16(x), lo' = f16(2^11 (x - hi)) -- 11 + 11 significant
+//     bits, the precision of the tf32 split --; D = H_hi (2^11 W_hi) + H_lo' W_hi + H_hi W_lo'
+//     = 2^11 H W; a chunk is 12 MMAs and writes half the bytes into TMEM. The tf32 form spends
+//     its layer time on the MMAs and on the TMEM traffic between the chunk stores and the MMAs
+//     (a chunk's 24 MMAs take 0.57-0.74 us instead of 0.39 us while 16 warps store the next
+//     chunk), which this halves.
+//     Range: f16 holds magnitudes below 65,504, and the Laplacian jet grows fast with the
+//     weight scale. Each launch derives power-of-2 scales from the weights: tau_l maps
+//     max|W_l| to <= 16 (so 2^11 W_hi stays finite); sigma_{l,c} maps an upper bound of
+//     component c of GEMM l's A operand to <= 2^14. They are applied before the split and
+//     removed exactly from the accumulators (times 1 / (2^11 sigma tau), a power of 2). The
+//     bounds: |v| <= 1; |dv/dx|, |dv/dy| grow by N_l = max row-abs-sum of W_l per layer; |Lv|
+//     becomes N_l |Lv| + (N_l Bx)^2 + (N_l By)^2 (tanh' <= 1 and 2 |tanh tanh'| <= 1). A value
+//     keeps full relative precision until it is 2^28 times below its bound. The scales depend
+//     on the weights only (fixed-order warp reductions), so every CTA and every shard of a
+//     batch uses the same ones.
 //
 // Where the data lives (per CTA, one CTA per SM, persistent over tiles):
-//   * weights: all three hidden layers, hi and lo, pre-split once per CTA into the K-major
-//     no-swizzle canonical layout in shared memory (96 KB) -- the MMA's B operand;
+//   * weights: all three hidden layers pre-split once per CTA into the K-major no-swizzle
+//     canonical layout in shared memory (tf32: hi, lo, 96 KB; f16: 2^11 hi, hi, lo', 72 KB);
 //   * TMEM (512 columns x 128 lanes, lane = point):
 //       [0, 256)   accumulators D_c, component c at columns 64c..64c+63;
-//       [256, 512) a ring of 2 A-operand chunks; a chunk is two K steps (16 input
-//                  neurons) of the next layer's activations: (component, hi/lo) blocks of
-//                  16 columns.
+//       [256, 512) a ring of A-operand chunks; a chunk is 16 input neurons of the next
+//                  layer's activations in (component, hi/lo) blocks: tf32 2 slots of 128
+//                  columns; f16 4 slots (a whole layer) of 64 columns, two K elements per
+//                  32-bit column (K 2j in the low half of column j).
 //     The A operand lives in TMEM, not shared memory: with N = 64 an A tile read from
 //     shared memory would need ~1.5x the shared-memory bandwidth an SM has.
 //   * 16 warps: warp w serves TMEM lanes 32(w%4)..+31 (its quadrant) and, with s = w/4,
 //     neurons 16a+4s+t. Per layer it loads its 4 x 16 accumulators (16 x tcgen05.ld.x4),
-//     applies the tanh jet in registers and writes TF32 hi/lo activations chunk by chunk
-//     into the ring (tcgen05.st) for the next layer. Warp s owns the strided neurons
-//     16a+4s+{0..3} (a = 0..3), so chunk j (neurons 16j..16j+15, natural K order) gets 4
-//     neurons from every warp and all 16 warps contribute to every chunk;
+//     applies the tanh jet in registers and writes hi/lo activations chunk by chunk into the
+//     ring (tcgen05.st) for the next layer. Warp s owns the strided neurons 16a+4s+{0..3}
+//     (a = 0..3), so chunk j (neurons 16j..16j+15, natural K order) gets 4 neurons from every
+//     warp and all 16 warps contribute to every chunk;
 //   * the warp that completes a chunk last (an acq_rel counter per ring slot) issues its
 //     MMAs as a converged warp (elect.sync picks the issuing lane; issued from a divergent
-//     lane these small MMAs cost ~4x their execution time): 2 K steps x 4 components x 3
-//     products, then tcgen05.commit to free the slot, and after a layer's 4th chunk a
-//     commit that marks D complete. A warp contributes to
-//     chunk 0 of layer l+1 only after it has read D of layer l, so when the last
+//     lane these small MMAs cost ~4x their execution time), then tcgen05.commit to free the
+//     slot, and after a layer's 4th chunk a commit that marks D complete. A warp contributes
+//     to chunk 0 of layer l+1 only after it has read D of layer l, so when the last
 //     contribution arrives D may be overwritten -- no separate "D free" barrier.
 //   So the MMAs of layer l+1 consume chunk j while the epilogue of layer l produces chunk
-//   j+1. (No dedicated MMA warp: a 17th warp would put 5 warps on one SM sub-partition and
-//   cap registers at 96; with 16 warps each thread gets 128.)
-// Layer 0 (2 inputs) and the output layer (1 output) are elementwise/epilogue work. The
-// epilogue, not the tensor core, bounds this kernel, so it is kept lean: tanh_fast (SFU
-// exp2 + reciprocal), a 2-instruction TF32 split (hi = cvt.rna, lo = x - hi, which the
-// tensor core truncates to TF32) and 16-neuron chunks to halve the synchronisation.
+//   j+1. (Measured alternatives, all slower or no faster: a dedicated MMA warp -- 17 warps
+//   cap registers at 96 --, 8 epilogue warps plus an issuer, one warp per whole chunk.)
+// Layer 0 (2 inputs) and the output layer (1 output) are elementwise/epilogue work: tanh_fast
+// (SFU exp2 + reciprocal), the split, and 16-neuron chunks to halve the synchronisation.
 // Every mbarrier wait is bounded; a wait that gives up raises FHB_STATUS_MMA_TIMEOUT, sets
 // a CTA abort flag that stops the other warps, and the kernel frees TMEM and returns.
+#include <cuda_fp16.h>
+
 #include <algorithm>
 
 #include "common.cuh"
@@ -52,31 +71,55 @@ namespace {
 constexpr int kTile = 128;            // points per tile = MMA M = TMEM lanes
 constexpr int kWarps = 16;            // 4 per TMEM lane quadrant
 constexpr int kThreads = kWarps * 32;
-constexpr int kChunks = 4;            // chunks of 16 neurons (2 K steps) per 64-wide layer
+constexpr int kChunks = 4;            // chunks of 16 neurons per 64-wide layer
 constexpr int kChunksPerTile = kHiddenGemms * kChunks;
-constexpr int kRing = 2;
-constexpr uint32_t kSlotCols = 128;   // 4 components x {hi, lo} x 16 K positions
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kRingCol = 256;
-constexpr uint32_t kIdesc = tc::idesc_tf32(128, 64);
+constexpr float kLoScale = 2048.0f;   // f16: lo' = 2^11 (x - hi)
+constexpr uint32_t kLbo = 128;        // K-adjacent core matrices of the canonical layout
 
-// Shared memory layout (bytes).
-constexpr int kOperandBytes = kWidth * kWidth * 4;  // one [64 x 64] tf32 operand: 16 KB
-constexpr int kSmallOff = 6 * kOperandBytes;        // W0[128] b0[64] b1..b3[192] wout[64] bout
+// Operand formats. One [64 x 64] weight operand is kOperandBytes in the K-major no-swizzle
+// canonical layout: core matrices of 8 rows x 16 bytes (4 tf32 or 8 f16 elements), K chunks at
+// LBO = 128 B, 8-row groups at kSbo. kOperands weight operands per hidden layer.
+template <bool F16>
+struct Format;
+template <>
+struct Format<false> {  // 3xTF32, kind::tf32, K = 8 per MMA
+  static constexpr int kRing = 2;
+  static constexpr uint32_t kSlotCols = 128;  // 4 components x {hi, lo} x 16 K positions
+  static constexpr uint32_t kIdesc = tc::idesc_tf32(128, 64);
+  static constexpr int kOperandBytes = kWidth * kWidth * 4;  // 16 KB
+  static constexpr int kOperands = 2;                        // W_hi, W_lo
+  static constexpr uint32_t kSbo = 2048;
+};
+template <>
+struct Format<true> {  // 3xFP16, kind::f16, K = 16 per MMA
+  static constexpr int kRing = 4;
+  static constexpr uint32_t kSlotCols = 64;   // 4 components x {hi, lo'} x 8 columns of pairs
+  static constexpr uint32_t kIdesc = tc::idesc_f16(128, 64);
+  static constexpr int kOperandBytes = kWidth * kWidth * 2;  // 8 KB
+  static constexpr int kOperands = 3;                        // 2^11 W_hi, W_hi, W_lo'
+  static constexpr uint32_t kSbo = 1024;
+};
+
+// Shared memory layout (bytes): the weight operands, then the rest.
+template <bool F16>
+struct Layout {
+  static constexpr int kSmallOff = kHiddenGemms * Format<F16>::kOperands * Format<F16>::kOperandBytes;
+  static constexpr int kRedOff = kSmallOff + 512 * 4;     // small params, then [8][128] sums
+  static constexpr int kBarOff = kRedOff + 8 * kTile * 4;  // mbarriers: empty[kRing], dfull, red
+  static constexpr int kCountOff = kBarOff + 8 * 8;        // per-slot contribution counters
+  static constexpr int kMiscOff = kCountOff + 4 * 4;       // TMEM base, abort flag
+  static constexpr int kScaleOff = kMiscOff + 16;          // f16: sigma[3][4], unscale[3][4], tau[3]
+  static constexpr int kSmemUsed = kScaleOff + 32 * 4;
+};
 constexpr int kSmW0 = 0, kSmB0 = 128, kSmB = 192, kSmWout = 384, kSmBout = 448;
 constexpr int kSmallFloats = 512;
-constexpr int kRedOff = kSmallOff + kSmallFloats * 4;  // [8][128] partial sums
-constexpr int kBarOff = kRedOff + 8 * kTile * 4;       // mbarriers: empty[2], dfull, red
-constexpr int kCountOff = kBarOff + 8 * 8;             // per-slot contribution counters
-constexpr int kMiscOff = kCountOff + 4 * 4;            // TMEM base, abort flag
-constexpr int kSmemUsed = kMiscOff + 16;
 // Padded so two CTAs never share an SM (each allocates all 512 TMEM columns).
 constexpr int kSmemBytes = 120 * 1024;
-static_assert(kSmemUsed <= kSmemBytes, "shared memory layout overflow");
-
-// Canonical K-major no-swizzle layout of a [64 rows x 64 K] tf32 operand: 8x4 core
-// matrices of 128 B; K chunks of 4 at LBO = 128 B, 8-row groups at SBO = 2048 B.
-constexpr uint32_t kLbo = 128, kSbo = 2048;
+static_assert(Layout<false>::kSmemUsed <= kSmemBytes && Layout<true>::kSmemUsed <= kSmemBytes,
+              "shared memory layout overflow");
+static_assert(Format<true>::kRing <= 4, "bar and counter space");
 
 struct Ctx {
   uint8_t* smem;
@@ -87,6 +130,8 @@ struct Ctx {
   volatile uint32_t* abort_flag;
   unsigned int* status;
   uint32_t tmem;
+  const float* sigma;         // f16: [3][4] A-operand scale of GEMM l, component c (power of 2)
+  const float* unscale;       // f16: [3][4] 1 / (2^11 sigma tau) for the accumulators of GEMM l
 };
 
 // Bounded wait that also gives up when another warp has aborted the CTA.
@@ -111,47 +156,106 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, const 
   return __all_sync(0xffffffffu, wait_or_abort(bar, parity, cx) ? 1 : 0) != 0;
 }
 
-
-
-// The 24 MMAs of one chunk: K steps 2j, 2j+1 of hidden GEMM `layer`, A from ring slot
-// `slot` (component c, hi/lo sp, K step kk at columns 32c + 16sp + 8kk of the slot).
-__device__ __forceinline__ void issue_chunk_mmas(const Ctx& cx, int layer, int j,
-                                                 uint32_t slot) {
+__device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
-  for (int kk = 0; kk < 2; ++kk) {
-    const uint32_t w_hi = smem_u32(cx.smem + (2 * layer) * kOperandBytes + 256 * (2 * j + kk));
-    const uint64_t bhi = tc::smem_desc_kmajor(w_hi, kLbo, kSbo);
-    const uint64_t blo = tc::smem_desc_kmajor(w_hi + kOperandBytes, kLbo, kSbo);
+  for (int m = 16; m >= 1; m >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, m));
+  return v;
+}
+
+// Largest power of 2 <= x for x in [2^-126, 2^127]; clamped to that range otherwise.
+__device__ __forceinline__ float pow2_floor(float x) {
+  x = fminf(fmaxf(x, 1.17549435e-38f), 1.7e38f);
+  return __uint_as_float(__float_as_uint(x) & 0x7F800000u);
+}
+
+// f16 pairs of the A operand: hi = f16(x) and lo' = f16(2^11 (x - hi)), element a (even K)
+// in the low half.
+__device__ __forceinline__ uint32_t pack_hi(float a, float b) {
+  const __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+__device__ __forceinline__ uint32_t pack_lo(float a, float b) {
+  const float ha = __half2float(__float2half_rn(a)), hb = __half2float(__float2half_rn(b));
+  const __half2 h = __floats2half2_rn((a - ha) * kLoScale, (b - hb) * kLoScale);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// The MMAs of chunk j (input neurons 16j..16j+15) of hidden GEMM `layer`, A from ring slot
+// `slot`, then a commit that frees the slot (and after the 4th chunk one that marks D
+// complete). tf32: 2 K steps x 4 components x (H_hi W_hi + H_lo W_hi + H_hi W_lo), A block
+// (component c, hi/lo sp, K step kk) at columns 32c + 16sp + 8kk of the slot. f16: 4
+// components x (H_hi 2^11 W_hi + H_lo' W_hi + H_hi W_lo'), A block (c, sp) at 16c + 8sp.
+template <bool F16>
+__device__ __forceinline__ void issue_chunk_mmas(const Ctx& cx, int layer, int j, uint32_t slot) {
+  using F = Format<F16>;
+  const uint32_t slot_col = cx.tmem + kRingCol + F::kSlotCols * slot;
+  if constexpr (F16) {
+    const uint32_t w0 = smem_u32(cx.smem + (3 * layer) * F::kOperandBytes + 256 * j);
+    const uint64_t b_hs = tc::smem_desc_kmajor(w0, kLbo, F::kSbo);
+    const uint64_t b_hi = tc::smem_desc_kmajor(w0 + F::kOperandBytes, kLbo, F::kSbo);
+    const uint64_t b_lo = tc::smem_desc_kmajor(w0 + 2 * F::kOperandBytes, kLbo, F::kSbo);
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
       const uint32_t d = cx.tmem + 64u * c;
-      const uint32_t a_hi = cx.tmem + kRingCol + kSlotCols * slot + 32u * c + 8u * kk;
-      const uint32_t a_lo = a_hi + 16u;
-      tc::mma_tf32_ts_warp(d, a_hi, bhi, kIdesc, (j > 0 || kk > 0) ? 1u : 0u);
-      tc::mma_tf32_ts_warp(d, a_lo, bhi, kIdesc, 1u);
-      tc::mma_tf32_ts_warp(d, a_hi, blo, kIdesc, 1u);
+      const uint32_t a_hi = slot_col + 16u * c;
+      const uint32_t a_lo = a_hi + 8u;
+      tc::mma_f16_ts_warp(d, a_hi, b_hs, F::kIdesc, j > 0 ? 1u : 0u);
+      tc::mma_f16_ts_warp(d, a_lo, b_hi, F::kIdesc, 1u);
+      tc::mma_f16_ts_warp(d, a_hi, b_lo, F::kIdesc, 1u);
+    }
+  } else {
+#pragma unroll
+    for (int kk = 0; kk < 2; ++kk) {
+      const uint32_t w_hi =
+          smem_u32(cx.smem + (2 * layer) * F::kOperandBytes + 256 * (2 * j + kk));
+      const uint64_t bhi = tc::smem_desc_kmajor(w_hi, kLbo, F::kSbo);
+      const uint64_t blo = tc::smem_desc_kmajor(w_hi + F::kOperandBytes, kLbo, F::kSbo);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const uint32_t d = cx.tmem + 64u * c;
+        const uint32_t a_hi = slot_col + 32u * c + 8u * kk;
+        const uint32_t a_lo = a_hi + 16u;
+        tc::mma_tf32_ts_warp(d, a_hi, bhi, F::kIdesc, (j > 0 || kk > 0) ? 1u : 0u);
+        tc::mma_tf32_ts_warp(d, a_lo, bhi, F::kIdesc, 1u);
+        tc::mma_tf32_ts_warp(d, a_hi, blo, F::kIdesc, 1u);
+      }
     }
   }
   tc::commit_warp(&cx.empty[slot]);
   if (j == kChunks - 1) tc::commit_warp(cx.dfull);
 }
 
-
-// Write chunk `n` (this warp's 4 neurons x 4 components, TF32 hi and lo) into ring slot
-// n % kRing; the warp completing the chunk last issues its MMAs. False if aborted.
+// Write chunk `n` (this warp's 4 neurons x 4 components as hi/lo parts; f16: scaled by sigma
+// of their GEMM first) into ring slot n % kRing; the warp completing the chunk last issues its
+// MMAs. False if aborted.
+template <bool F16>
 __device__ __forceinline__ bool produce_chunk(uint32_t n, const float (&h)[4][4],
                                               uint32_t tmem_warp, int s, const Ctx& cx) {
-  const uint32_t slot = n % kRing;
-  if (!warp_wait(&cx.empty[slot], ((n / kRing) & 1u) ^ 1u, cx)) return false;
+  using F = Format<F16>;
+  const uint32_t slot = n % F::kRing;
+  if (!warp_wait(&cx.empty[slot], ((n / F::kRing) & 1u) ^ 1u, cx)) return false;
   tc::fence_after_sync();
-  const uint32_t base = tmem_warp + kRingCol + kSlotCols * slot + 4u * s;
+  const uint32_t slot_col = tmem_warp + kRingCol + F::kSlotCols * slot;
+  if constexpr (F16) {
+    const uint32_t base = slot_col + 2u * s;
+    const float* sig = cx.sigma + 4 * ((n % kChunksPerTile) / kChunks);
 #pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    uint32_t hi[4], lo[4];
+    for (int c = 0; c < 4; ++c) {
+      const float g = sig[c];
+      const float a0 = h[c][0] * g, a1 = h[c][1] * g, a2 = h[c][2] * g, a3 = h[c][3] * g;
+      tc::st_x2(base + 16u * c, pack_hi(a0, a1), pack_hi(a2, a3));
+      tc::st_x2(base + 16u * c + 8u, pack_lo(a0, a1), pack_lo(a2, a3));
+    }
+  } else {
+    const uint32_t base = slot_col + 4u * s;
 #pragma unroll
-    for (int t = 0; t < 4; ++t) tc::split_tf32(h[c][t], hi[t], lo[t]);
-    tc::st_x4(base + 32u * c, hi[0], hi[1], hi[2], hi[3]);
-    tc::st_x4(base + 32u * c + 16u, lo[0], lo[1], lo[2], lo[3]);
+    for (int c = 0; c < 4; ++c) {
+      uint32_t hi[4], lo[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) tc::split_tf32(h[c][t], hi[t], lo[t]);
+      tc::st_x4(base + 32u * c, hi[0], hi[1], hi[2], hi[3]);
+      tc::st_x4(base + 32u * c + 16u, lo[0], lo[1], lo[2], lo[3]);
+    }
   }
   tc::wait_st();
   tc::fence_before_sync();
@@ -162,30 +266,177 @@ __device__ __forceinline__ bool produce_chunk(uint32_t n, const float (&h)[4][4]
   if (last) {  // warp-uniform: the whole converged warp issues, elect.sync picks a lane
     tc::fence_after_sync();
     const uint32_t in_tile = n % kChunksPerTile;
-    issue_chunk_mmas(cx, static_cast<int>(in_tile / kChunks), static_cast<int>(in_tile % kChunks),
-                     slot);
+    issue_chunk_mmas<F16>(cx, static_cast<int>(in_tile / kChunks),
+                          static_cast<int>(in_tile % kChunks), slot);
     __syncwarp();
   }
   return true;
 }
 
+// Small parameter of thread i: W0, b0, b1..b3, w_out, b_out in the order of `small`.
+__device__ __forceinline__ float small_param(const float* __restrict__ params, int i) {
+  if (i < kSmB0) return params[i];                                          // W0
+  if (i < kSmB) return params[kB0 + (i - kSmB0)];                           // b0
+  if (i < kSmWout) {                                                        // b1..b3
+    const int l = (i - kSmB) >> 6, o = (i - kSmB) & 63;
+    return params[kHiddenBase + l * kHiddenStride + kWidth * kWidth + o];
+  }
+  if (i < kSmBout) return params[kOutBase + (i - kSmWout)];                 // w_out
+  if (i == kSmBout) return params[kOutBase + kWidth];                       // b_out
+  return 0.0f;
+}
+
+// tf32 set-up: the small parameters and the hi/lo split of the hidden weights. Element e of
+// an operand, enumerated as (row group, K chunk, row in group, K in chunk), sits at byte 4e of
+// the canonical layout: consecutive threads store consecutive words. All 25 loads of a thread
+// (24 weights, one small parameter) are issued before any is used.
+__device__ __forceinline__ void stage_tf32(const float* __restrict__ params, uint8_t* smem,
+                                           float* small) {
+  using F = Format<false>;
+  const float sv = small_param(params, threadIdx.x);
+  constexpr int kPerThread = kHiddenGemms * kWidth * kWidth / kThreads;  // 24
+  float w[kPerThread];
+#pragma unroll
+  for (int r = 0; r < kPerThread; ++r) {
+    const int idx = threadIdx.x + r * kThreads;
+    const int layer = idx >> 12, e = idx & 4095;
+    const int row = ((e >> 9) << 3) | ((e >> 2) & 7);
+    const int k = (((e >> 5) & 15) << 2) | (e & 3);
+    w[r] = params[kHiddenBase + layer * kHiddenStride + row * kWidth + k];
+  }
+#pragma unroll
+  for (int r = 0; r < kPerThread; ++r) {
+    const int idx = threadIdx.x + r * kThreads;
+    const int layer = idx >> 12, e = idx & 4095;
+    const uint32_t hi = tc::to_tf32(w[r]);
+    const uint32_t lo = tc::to_tf32(w[r] - __uint_as_float(hi));
+    reinterpret_cast<uint32_t*>(smem + (2 * layer) * F::kOperandBytes)[e] = hi;
+    reinterpret_cast<uint32_t*>(smem + (2 * layer + 1) * F::kOperandBytes)[e] = lo;
+  }
+  small[threadIdx.x] = sv;
+}
+
+// f16 set-up: the small parameters, the operand scales, then the split of the hidden weights
+// into 2^11 W_hi, W_hi and W_lo' (tau-scaled). Every load is issued before any is used (one
+// memory round trip): the small parameter, 24 values for the weight-row statistics and 12
+// pairs for the split. Power-of-2 scales keep every f16 operand in range: tau_l maps
+// max|W_l| to <= 16 (so 2^11 W_hi stays finite); sigma_{l,c} maps a bound of component c of
+// the A operand of GEMM l to <= 2^14. Bounds: |v| <= 1; |d/dx|, |d/dy| grow by N_l (max
+// row-abs-sum of W_l) per layer; |L| becomes N_l |L| + (N_l Bx)^2 + (N_l By)^2 (tanh' <= 1,
+// 2 |tanh tanh'| <= 1). Row statistics are fixed-order warp reductions, so every CTA derives
+// the same scales. Contains two block-wide barriers.
+__device__ __forceinline__ void stage_f16(const float* __restrict__ params, uint8_t* smem,
+                                          float* small, float* red, float* scales, int warp,
+                                          int lane) {
+  using F = Format<true>;
+  constexpr int kStatRows = 3 * kWidth / kWarps;                   // 12 rows per warp
+  constexpr int kPairs = kHiddenGemms * kWidth * kWidth / 2;       // 6144
+  constexpr int kPairsPerThread = kPairs / kThreads;               // 12
+  static_assert(kPairs % kThreads == 0, "whole pairs per thread");
+  float wp[kPairsPerThread][2];
+  {
+    const float sv = small_param(params, threadIdx.x);
+    float rs[kStatRows][2];
+#pragma unroll
+    for (int i = 0; i < kStatRows; ++i) {  // row warp + 16 i of the 192 hidden-weight rows
+      const int r = warp + kWarps * i;
+      const float* wr = params + kHiddenBase + (r >> 6) * kHiddenStride + (r & 63) * kWidth;
+      rs[i][0] = wr[lane];
+      rs[i][1] = wr[lane + 32];
+    }
+#pragma unroll
+    for (int k = 0; k < kPairsPerThread; ++k) {
+      const int idx = threadIdx.x + k * kThreads;
+      const int layer = idx >> 11, e = (idx & 2047) * 2;
+      const int row = ((e >> 9) << 3) | ((e >> 3) & 7);
+      const int kk = (((e >> 6) & 7) << 3) | (e & 7);
+      const float* wr = params + kHiddenBase + layer * kHiddenStride + row * kWidth + kk;
+      wp[k][0] = wr[0];
+      wp[k][1] = wr[1];
+    }
+#pragma unroll
+    for (int i = 0; i < kStatRows; ++i) {
+      const float a = fabsf(rs[i][0]), b = fabsf(rs[i][1]);
+      const float sum = warp_sum(a + b), mx = warp_max(fmaxf(a, b));
+      if (lane == 0) {
+        red[warp + kWarps * i] = sum;  // the output-layer buffer is free during set-up
+        red[256 + warp + kWarps * i] = mx;
+      }
+    }
+    small[threadIdx.x] = sv;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    float nrm[3], wmax[3];
+#pragma unroll
+    for (int l = 0; l < 3; ++l) {
+      nrm[l] = warp_max(fmaxf(red[64 * l + lane], red[64 * l + lane + 32]));
+      wmax[l] = warp_max(fmaxf(red[256 + 64 * l + lane], red[256 + 64 * l + lane + 32]));
+    }
+    const float w0x = small[kSmW0 + 2 * lane], w0y = small[kSmW0 + 2 * lane + 1];
+    const float w0x2 = small[kSmW0 + 2 * (lane + 32)], w0y2 = small[kSmW0 + 2 * (lane + 32) + 1];
+    float bx = warp_max(fmaxf(fabsf(w0x), fabsf(w0x2)));
+    float by = warp_max(fmaxf(fabsf(w0y), fabsf(w0y2)));
+    float bl = warp_max(fmaxf(fmaf(w0x, w0x, w0y * w0y), fmaf(w0x2, w0x2, w0y2 * w0y2)));
+    if (lane == 0) {
+      for (int l = 0; l < 3; ++l) {
+        const float tau = pow2_floor(16.0f / fmaxf(wmax[l], 1e-30f));
+        const float bnd[4] = {1.0f, bx, by, bl};
+        for (int c = 0; c < 4; ++c) {
+          const float sig = pow2_floor(16384.0f / fmaxf(bnd[c], 1e-30f));
+          scales[4 * l + c] = sig;
+          scales[12 + 4 * l + c] = 1.0f / (kLoScale * sig * tau);
+        }
+        scales[24 + l] = tau;
+        const float nx = nrm[l] * bx, ny = nrm[l] * by;
+        bl = fmaf(nrm[l], bl, fmaf(nx, nx, ny * ny));
+        bx = nx;
+        by = ny;
+      }
+    }
+  }
+  __syncthreads();
+  // The split: pairs of adjacent K elements, enumerated (row group, K chunk of 8, row in
+  // group, K pair) so consecutive threads store consecutive words of the canonical layout.
+#pragma unroll
+  for (int k = 0; k < kPairsPerThread; ++k) {
+    const int idx = threadIdx.x + k * kThreads;
+    const int layer = idx >> 11, e = (idx & 2047) * 2;
+    const float tau = scales[24 + layer];
+    const float a = wp[k][0] * tau, b = wp[k][1] * tau;
+    const __half2 hi = __floats2half2_rn(a, b);
+    const float2 hf = __half22float2(hi);
+    const __half2 hs = __floats2half2_rn(hf.x * kLoScale, hf.y * kLoScale);
+    const __half2 lo = __floats2half2_rn((a - hf.x) * kLoScale, (b - hf.y) * kLoScale);
+    uint8_t* base = smem + (3 * layer) * F::kOperandBytes + 2 * e;
+    *reinterpret_cast<__half2*>(base) = hs;
+    *reinterpret_cast<__half2*>(base + F::kOperandBytes) = hi;
+    *reinterpret_cast<__half2*>(base + 2 * F::kOperandBytes) = lo;
+  }
+}
+
+template <bool F16>
 __global__ void __launch_bounds__(kThreads, 1)
     forward_tc_kernel(const float* __restrict__ coords, const float* __restrict__ params,
                       float* __restrict__ u_out, float* __restrict__ lap_out, int64_t n,
                       int64_t tiles, unsigned int* status) {
+  using F = Format<F16>;
+  using L = Layout<F16>;
   extern __shared__ __align__(1024) uint8_t smem[];
-  float* small = reinterpret_cast<float*>(smem + kSmallOff);
-  float* red = reinterpret_cast<float*>(smem + kRedOff);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kBarOff);
-  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(smem + kMiscOff);
+  float* small = reinterpret_cast<float*>(smem + L::kSmallOff);
+  float* red = reinterpret_cast<float*>(smem + L::kRedOff);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::kBarOff);
+  uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(smem + L::kMiscOff);
   Ctx cx;
   cx.smem = smem;
   cx.empty = bars;
-  cx.dfull = bars + kRing;
-  cx.red = bars + kRing + 1;
-  cx.count = reinterpret_cast<uint32_t*>(smem + kCountOff);
-  cx.abort_flag = reinterpret_cast<volatile uint32_t*>(smem + kMiscOff + 4);
+  cx.dfull = bars + F::kRing;
+  cx.red = bars + F::kRing + 1;
+  cx.count = reinterpret_cast<uint32_t*>(smem + L::kCountOff);
+  cx.abort_flag = reinterpret_cast<volatile uint32_t*>(smem + L::kMiscOff + 4);
   cx.status = status;
+  cx.sigma = reinterpret_cast<const float*>(smem + L::kScaleOff);
+  cx.unscale = cx.sigma + 12;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -201,46 +452,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
-  // ---- set-up: split weights to TF32 hi/lo in the canonical layout, small params ----
-  // Element e of an operand, enumerated as (row group, K chunk, row in group, K in chunk),
-  // sits at byte 4e of the canonical layout: consecutive threads store consecutive words.
-  // All 25 loads of a thread (24 weights, one small parameter) are issued before any is used.
+  // ---- set-up: small params and the split weight operands ----
   static_assert(kSmallFloats == kThreads, "one small parameter per thread");
-  {
-    float sv = 0.0f;
-    {
-      const int i = threadIdx.x;
-      if (i < kSmB0) sv = params[i];                                       // W0
-      else if (i < kSmB) sv = params[kB0 + (i - kSmB0)];                   // b0
-      else if (i < kSmWout) {                                              // b1..b3
-        const int l = (i - kSmB) >> 6, o = (i - kSmB) & 63;
-        sv = params[kHiddenBase + l * kHiddenStride + kWidth * kWidth + o];
-      } else if (i < kSmBout) sv = params[kOutBase + (i - kSmWout)];       // w_out
-      else if (i == kSmBout) sv = params[kOutBase + kWidth];               // b_out
-    }
-    constexpr int kPerThread = kHiddenGemms * kWidth * kWidth / kThreads;  // 24
-    float w[kPerThread];
-#pragma unroll
-    for (int r = 0; r < kPerThread; ++r) {
-      const int idx = threadIdx.x + r * kThreads;
-      const int layer = idx >> 12, e = idx & 4095;
-      const int row = ((e >> 9) << 3) | ((e >> 2) & 7);
-      const int k = (((e >> 5) & 15) << 2) | (e & 3);
-      w[r] = params[kHiddenBase + layer * kHiddenStride + row * kWidth + k];
-    }
-#pragma unroll
-    for (int r = 0; r < kPerThread; ++r) {
-      const int idx = threadIdx.x + r * kThreads;
-      const int layer = idx >> 12, e = idx & 4095;
-      const uint32_t hi = tc::to_tf32(w[r]);
-      const uint32_t lo = tc::to_tf32(w[r] - __uint_as_float(hi));
-      reinterpret_cast<uint32_t*>(smem + (2 * layer) * kOperandBytes)[e] = hi;
-      reinterpret_cast<uint32_t*>(smem + (2 * layer + 1) * kOperandBytes)[e] = lo;
-    }
-    small[threadIdx.x] = sv;
+  if constexpr (F16) {
+    stage_f16(params, smem, small, red, reinterpret_cast<float*>(smem + L::kScaleOff), warp,
+              lane);
+  } else {
+    stage_tf32(params, smem, small);
   }
   if (threadIdx.x == 0) {
-    for (int r = 0; r < kRing; ++r) {
+    for (int r = 0; r < F::kRing; ++r) {
       mbar_init(&cx.empty[r], 1);
       cx.count[r] = 0u;
     }
@@ -290,7 +511,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tanh_jet_fast(fmaf(w0, x0, fmaf(w1, x1, small[kSmB0 + o])), w0, w1, 0.0f, h[0][t],
                       h[1][t], h[2][t], h[3][t]);
       }
-      if (!(ok = produce_chunk(chunk++, h, tmem_warp, s, cx))) break;
+      if (!(ok = produce_chunk<F16>(chunk++, h, tmem_warp, s, cx))) break;
     }
 
     for (int l = 0; ok && l < kHiddenGemms; ++l, ++mlayer) {
@@ -306,6 +527,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                     *reinterpret_cast<float(*)[4]>(&d[c][4 * a]));
       tc::wait_ld();
       const float* bias = small + kSmB + 64 * l;
+      if constexpr (F16) {  // remove the operand scales: an exact power of 2
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const float us = cx.unscale[4 * l + c];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) d[c][i] *= us;
+        }
+      }
 #pragma unroll
       for (int i = 0; i < 16; ++i) d[0][i] += bias[16 * (i >> 2) + 4 * s + (i & 3)];
 
@@ -319,7 +548,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tanh_jet_fast(d[0][i], d[1][i], d[2][i], d[3][i], h[0][t], h[1][t], h[2][t],
                           h[3][t]);
           }
-          if (!(ok = produce_chunk(chunk++, h, tmem_warp, s, cx))) break;
+          if (!(ok = produce_chunk<F16>(chunk++, h, tmem_warp, s, cx))) break;
         }
       } else {
         // output layer: u = w.v + b, lap = w.L, over this warp's 16 neurons
@@ -375,16 +604,25 @@ __global__ void __launch_bounds__(kThreads, 1)
 }  // namespace
 
 cudaError_t prepare_forward_tc() {
-  return cudaFuncSetAttribute(forward_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                              kSmemBytes);
+  cudaError_t e = cudaFuncSetAttribute(forward_tc_kernel<false>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(forward_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kSmemBytes);
+  return e;
 }
 
 cudaError_t launch_forward_tc(const float* coords, const float* params, float* u, float* lap,
-                              int64_t n, const DeviceInfo& dev, cudaStream_t stream) {
+                              int64_t n, bool f16, const DeviceInfo& dev, cudaStream_t stream) {
   const int64_t tiles = (n + kTile - 1) / kTile;
   const int grid = static_cast<int>(std::min<int64_t>(tiles, dev.sms));
-  forward_tc_kernel<<<grid, kThreads, kSmemBytes, stream>>>(coords, params, u, lap, n, tiles,
-                                                            dev.status);
+  if (f16) {
+    forward_tc_kernel<true><<<grid, kThreads, kSmemBytes, stream>>>(coords, params, u, lap, n,
+                                                                    tiles, dev.status);
+  } else {
+    forward_tc_kernel<false><<<grid, kThreads, kSmemBytes, stream>>>(coords, params, u, lap, n,
+                                                                     tiles, dev.status);
+  }
   return cudaGetLastError();
 }
 

@@ -130,15 +130,11 @@ cudaError_t launch_forward_fp32(int tile, const float* coords, const float* para
                                 float* lap, int64_t n, const DeviceInfo& dev,
                                 cudaStream_t stream);
 
-// ---- forward_f16.cu ----
-cudaError_t prepare_forward_f16();
-cudaError_t launch_forward_f16(const float* coords, const float* params, float* u, float* lap,
-                               int64_t n, const DeviceInfo& dev, cudaStream_t stream);
-
 // ---- forward_tc.cu ----
 cudaError_t prepare_forward_tc();
+// f16: the 3xFP16 operand format (forward version 3), else 3xTF32 (versions 4, 5).
 cudaError_t launch_forward_tc(const float* coords, const float* params, float* u, float* lap,
-                              int64_t n, const DeviceInfo& dev, cudaStream_t stream);
+                              int64_t n, bool f16, const DeviceInfo& dev, cudaStream_t stream);
 
 // ---- backward_fp32.cu ----
 cudaError_t prepare_backward_fp32();
