@@ -73,6 +73,8 @@ def parse_args():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--exchange", choices=["peer", "nccl"], default="peer",
                    help="how the training step sums gradients over ranks")
+    p.add_argument("--activation", choices=["tanh", "silu"], default="tanh",
+                   help="hidden activation (the BASELINE configs use tanh)")
     return p.parse_args()
 
 
@@ -242,6 +244,7 @@ def run_ours(args) -> None:
     C = fused_hoad.load_extension()
     C.prepare_device(local_rank)
     version = args.version if args.version is not None else 3
+    act = args.activation
     n = args.points
     params = fused_hoad.pack_poisson_parameters(
         (torch.manual_seed(0), fused_hoad.build_mlp())[1]
@@ -266,7 +269,7 @@ def run_ours(args) -> None:
 
     # ---- device-timed eval (headline) ----
     for _ in range(args.warmup):
-        C.fused_forward_laplacian(coords, params, version)
+        C.fused_forward_laplacian(coords, params, version, act)
         flush.zero_()
     events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
               for _ in range(args.steps)]
@@ -275,7 +278,7 @@ def run_ours(args) -> None:
         for start, end in events:
             flush.zero_()
             start.record(stream)
-            C.fused_forward_laplacian(coords, params, version)
+            C.fused_forward_laplacian(coords, params, version, act)
             end.record(stream)
         barrier()
     eval_ms = [s.elapsed_time(e) for s, e in events]
@@ -292,12 +295,13 @@ def run_ours(args) -> None:
 
     def staged_step():  # explicit H2D copy, kernel, D2H copies
         dev_in.copy_(pinned_in, non_blocking=True)
-        u, lap = C.fused_forward_laplacian(dev_in, params, version)
+        u, lap = C.fused_forward_laplacian(dev_in, params, version, act)
         pinned_u.copy_(u, non_blocking=True)
         pinned_lap.copy_(lap, non_blocking=True)
 
     def zero_copy_step():  # the kernel reads/writes the pinned host buffers directly
-        fused_hoad.fused_forward_laplacian_host(pinned_in, params, version, pinned_u, pinned_lap)
+        fused_hoad.fused_forward_laplacian_host(pinned_in, params, version, pinned_u, pinned_lap,
+                                                act)
 
     def time_e2e(step) -> float:
         for _ in range(max(3, args.warmup)):
@@ -315,7 +319,7 @@ def run_ours(args) -> None:
         total = max_over_ranks(sum(s.elapsed_time(e) for s, e in events))
         return n * world * e2e_steps / (total / 1e3)
 
-    reference_lap = C.fused_forward_laplacian(coords, params, version)[1].cpu()
+    reference_lap = C.fused_forward_laplacian(coords, params, version, act)[1].cpu()
     staged_value = time_e2e(staged_step)
     staged_ok = torch.equal(pinned_lap, reference_lap)
     pinned_lap.zero_()
@@ -342,7 +346,7 @@ def run_ours(args) -> None:
         barrier()
         return max_over_ranks(sum(s.elapsed_time(e) for s, e in events))
 
-    trainer = fused_hoad.PoissonTrainer(params.clone(), exchange=args.exchange)
+    trainer = fused_hoad.PoissonTrainer(params.clone(), exchange=args.exchange, activation=act)
     for _ in range(max(3, args.warmup)):
         trainer.step(coords, n * world)
     eager_total = time_train(lambda: trainer.step(coords, n * world))
@@ -375,7 +379,7 @@ def run_ours(args) -> None:
     # DRAM read + write bytes of one forward launch at 65,536 points, from one ncu capture of
     # the same command per kernel family (0-2: FP32 kernel, 3: 3xFP16, 4-5: 3xTF32).
     traffic = None
-    if n == POINTS_PER_GPU:
+    if n == POINTS_PER_GPU and act == "tanh":
         traffic = {0: 611_840, 1: 611_840, 2: 611_840, 3: F16_TRAFFIC, 4: 646_400, 5: 646_400}[version]
     per_launch_s = ms_per_step / 1e3
     achieved_tflops = n * FLOP_FORWARD / per_launch_s / 1e12
@@ -391,7 +395,7 @@ def run_ours(args) -> None:
         }
     else:
         bf16 = peaks["bf16_tflops"]
-        f16 = version == 3
+        f16 = version == 3 and act == "tanh"  # SiLU runs the 3xTF32 format
         roofline = {
             "bound": "tensor", "achieved": achieved_tflops, "peak": bf16, "unit": "TFLOP/s",
             "frac": achieved_tflops / bf16, "traffic": traffic,
@@ -416,6 +420,7 @@ def run_ours(args) -> None:
         "config": {
             "workload": "config1: residual eval (u, lap) of the 2->64->64->64->64->1 tanh MLP",
             "points_per_gpu": n, "global_points": n * world, "forward_version": version,
+            "activation": act,
             "l2": f"flushed between timed steps ({FLUSH_BYTES >> 20} MiB write, outside the events)",
             "parallelism": f"dp{world}",
         },
@@ -438,7 +443,8 @@ def run_ours(args) -> None:
             "exchange": args.exchange,
             "value": train_value, "unit": UNIT, "ms_per_step": train_ms, "steps": train_steps,
             "timing": train_mode, "eager_value": eager_value,
-            "backward_kernel": "backward_tc_kernel (version 6)",
+            "backward_kernel": ("backward_tc_kernel (version 6)" if act == "tanh" else
+                                "backward_fp32_kernel (SiLU: every version)"),
             "points_per_gpu": n,
             "launches_per_step": 3 if args.exchange == "peer" else 4 + (1 if world > 1 else 0),
             "loss_after": final_loss,

@@ -147,7 +147,7 @@ __device__ __forceinline__ void store_jet(float* buf, int o, int lane, float v, 
   dst[3 * kPlane] = l;
 }
 
-template <bool kPoisson>
+template <bool kPoisson, class Act>
 __global__ void __launch_bounds__(kThreads, 1)
     backward_fp32_kernel(const PointSets ps, const float* __restrict__ params,
                          const float* __restrict__ grad_u, const float* __restrict__ grad_lap,
@@ -207,7 +207,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float w0 = sp[2 * o], w1 = sp[2 * o + 1];
       zv0[k] = fmaf(w0, x0, fmaf(w1, x1, sp[kB0 + o]));
       float v, j0, j1, l;
-      tanh_jet(zv0[k], w0, w1, 0.0f, v, j0, j1, l);
+      Act::jet(zv0[k], w0, w1, 0.0f, v, j0, j1, l);
       store_jet(hbuf, o, lane, v, j0, j1, l);
     }
     __syncthreads();
@@ -217,7 +217,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
       float v, j0, j1, l;
-      tanh_jet(z1[0][k], z1[1][k], z1[2][k], z1[3][k], v, j0, j1, l);
+      Act::jet(z1[0][k], z1[1][k], z1[2][k], z1[3][k], v, j0, j1, l);
       store_jet(hbuf, o0 + k, lane, v, j0, j1, l);
     }
     __syncthreads();
@@ -226,7 +226,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
       float v, j0, j1, l;
-      tanh_jet(z2[0][k], z2[1][k], z2[2][k], z2[3][k], v, j0, j1, l);
+      Act::jet(z2[0][k], z2[1][k], z2[2][k], z2[3][k], v, j0, j1, l);
       store_jet(hbuf, o0 + k, lane, v, j0, j1, l);
     }
     __syncthreads();  // hbuf = h2, kept until the layer-3 weight gradient
@@ -239,7 +239,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
         float j0, j1;
-        tanh_jet(z3[0][k], z3[1][k], z3[2][k], z3[3][k], h3v[k], j0, j1, h3l[k]);
+        Act::jet(z3[0][k], z3[1][k], z3[2][k], z3[3][k], h3v[k], j0, j1, h3l[k]);
       }
       float gu, gl;
       if (kPoisson) {
@@ -299,7 +299,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float w = wout[o];
         const float dwo = warp_sum(fmaf(gu, h3v[k], gl * h3l[k]));
         float av = gu * w, aj0 = 0.0f, aj1 = 0.0f, al = gl * w;
-        tanh_jet_adjoint(z3[0][k], z3[1][k], z3[2][k], z3[3][k], av, aj0, aj1, al);
+        Act::adjoint(z3[0][k], z3[1][k], z3[2][k], z3[3][k], av, aj0, aj1, al);
         const float db = warp_sum(av);
         if (lane == 0) {
           small[kSmallWout + o] += dwo;
@@ -317,13 +317,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
       const int o = o0 + k;
-      tanh_jet_adjoint(z2[0][k], z2[1][k], z2[2][k], z2[3][k], hb[0][k], hb[1][k], hb[2][k],
+      Act::adjoint(z2[0][k], z2[1][k], z2[2][k], z2[3][k], hb[0][k], hb[1][k], hb[2][k],
                        hb[3][k]);
       const float db = warp_sum(hb[0][k]);
       if (lane == 0) small[kSmallBias + 2 * kWidth + o] += db;
       store_jet(adj, o, lane, hb[0][k], hb[1][k], hb[2][k], hb[3][k]);
       float v, j0, j1, l;
-      tanh_jet(z1[0][k], z1[1][k], z1[2][k], z1[3][k], v, j0, j1, l);
+      Act::jet(z1[0][k], z1[1][k], z1[2][k], z1[3][k], v, j0, j1, l);
       store_jet(hbuf, o, lane, v, j0, j1, l);
     }
     __syncthreads();  // adj = zbar2, hbuf = h1
@@ -334,14 +334,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
       const int o = o0 + k;
-      tanh_jet_adjoint(z1[0][k], z1[1][k], z1[2][k], z1[3][k], hb[0][k], hb[1][k], hb[2][k],
+      Act::adjoint(z1[0][k], z1[1][k], z1[2][k], z1[3][k], hb[0][k], hb[1][k], hb[2][k],
                        hb[3][k]);
       const float db = warp_sum(hb[0][k]);
       if (lane == 0) small[kSmallBias + 1 * kWidth + o] += db;
       store_jet(adj, o, lane, hb[0][k], hb[1][k], hb[2][k], hb[3][k]);
       const float w0 = sp[2 * o], w1 = sp[2 * o + 1];
       float v, j0, j1, l;
-      tanh_jet(zv0[k], w0, w1, 0.0f, v, j0, j1, l);
+      Act::jet(zv0[k], w0, w1, 0.0f, v, j0, j1, l);
       store_jet(hbuf, o, lane, v, j0, j1, l);
     }
     __syncthreads();  // adj = zbar1, hbuf = h0
@@ -355,7 +355,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int k = 0; k < 8; ++k) {
       const int o = o0 + k;
       const float w0 = sp[2 * o], w1 = sp[2 * o + 1];
-      tanh_jet_adjoint(zv0[k], w0, w1, 0.0f, hb[0][k], hb[1][k], hb[2][k], hb[3][k]);
+      Act::adjoint(zv0[k], w0, w1, 0.0f, hb[0][k], hb[1][k], hb[2][k], hb[3][k]);
       const float zb = active ? hb[0][k] : 0.0f;
       const float db = warp_sum(zb);
       const float d0 = warp_sum(fmaf(zb, x0, active ? hb[1][k] : 0.0f));
@@ -433,16 +433,36 @@ __global__ void __launch_bounds__(kReduceCols * kReduceGroups)
   }
 }
 
+template <bool kPoisson, class Act>
+cudaError_t set_attributes() {
+  return cudaFuncSetAttribute(backward_fp32_kernel<kPoisson, Act>,
+                              cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              static_cast<int>(kSmem));
+}
+
+template <class Act>
+void launch_act(const PointSets& ps, const float* params, const float* grad_u,
+                const float* grad_lap, float* grad_coords, float* lap_out, float* partials,
+                bool poisson, int grid, int64_t tiles, int aligned, const DeviceInfo& dev,
+                cudaStream_t stream) {
+  if (poisson) {
+    backward_fp32_kernel<true, Act><<<grid, kThreads, kSmem, stream>>>(
+        ps, params, nullptr, nullptr, grad_coords, lap_out, partials, tiles, aligned,
+        dev.status);
+  } else {
+    backward_fp32_kernel<false, Act><<<grid, kThreads, kSmem, stream>>>(
+        ps, params, grad_u, grad_lap, grad_coords, nullptr, partials, tiles, aligned,
+        dev.status);
+  }
+}
+
 }  // namespace
 
 cudaError_t prepare_backward_fp32() {
-  cudaError_t e = cudaFuncSetAttribute(backward_fp32_kernel<false>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(kSmem));
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(backward_fp32_kernel<true>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(kSmem));
+  cudaError_t e = cudaSuccess;
+  for (cudaError_t r : {set_attributes<false, TanhAct>(), set_attributes<true, TanhAct>(),
+                        set_attributes<false, SiluAct>(), set_attributes<true, SiluAct>()})
+    if (e == cudaSuccess) e = r;
   return e;
 }
 
@@ -454,21 +474,19 @@ int backward_grid(int64_t n, int64_t nb, const DeviceInfo& dev) {
 cudaError_t launch_backward_fp32(const PointSets& points, const float* params,
                                  const float* grad_u, const float* grad_lap,
                                  float* grad_coords, float* lap_out, float* partials,
-                                 bool poisson, const DeviceInfo& dev, cudaStream_t stream) {
+                                 bool poisson, int activation, const DeviceInfo& dev,
+                                 cudaStream_t stream) {
   PointSets ps = points;
   ps.tiles = (ps.n + kTile - 1) / kTile;
   const int64_t tiles = ps.tiles + (ps.nb + kTile - 1) / kTile;
   const int grid = backward_grid(ps.n, ps.nb, dev);
   const int aligned = (reinterpret_cast<uintptr_t>(params) % 16) == 0;
-  if (poisson) {
-    backward_fp32_kernel<true><<<grid, kThreads, kSmem, stream>>>(
-        ps, params, nullptr, nullptr, grad_coords, lap_out, partials, tiles, aligned,
-        dev.status);
-  } else {
-    backward_fp32_kernel<false><<<grid, kThreads, kSmem, stream>>>(
-        ps, params, grad_u, grad_lap, grad_coords, nullptr, partials, tiles, aligned,
-        dev.status);
-  }
+  if (activation == FHB_ACTIVATION_SILU)
+    launch_act<SiluAct>(ps, params, grad_u, grad_lap, grad_coords, lap_out, partials, poisson,
+                        grid, tiles, aligned, dev, stream);
+  else
+    launch_act<TanhAct>(ps, params, grad_u, grad_lap, grad_coords, lap_out, partials, poisson,
+                        grid, tiles, aligned, dev, stream);
   return cudaGetLastError();
 }
 

@@ -9,6 +9,7 @@
 #include <cuda_runtime.h>
 #include <torch/extension.h>
 
+#include <string>
 #include <vector>
 
 #include "../../include/fused_hoad_b200.h"
@@ -49,6 +50,15 @@ void check_status(int code, const char* op) {
   TORCH_CHECK(false, op, " failed: ", fhb_status_string(code));
 }
 
+// Hidden activation by name: "tanh" (the reference kernels' activation, the default) or
+// "silu" (the other jet of the reference's PyTorch forward-Laplacian backend).
+int activation_code(const std::string& activation) {
+  if (activation == "tanh") return FHB_ACTIVATION_TANH;
+  if (activation == "silu") return FHB_ACTIVATION_SILU;
+  TORCH_CHECK(false, "activation must be \"tanh\" or \"silu\"");
+  return -1;
+}
+
 torch::Tensor workspace_for(int64_t batch, const torch::Tensor& like) {
   const size_t bytes = fhb_backward_workspace_bytes(batch);
   return torch::empty({static_cast<int64_t>((bytes + 15) / 16) * 4}, like.options());
@@ -57,17 +67,20 @@ torch::Tensor workspace_for(int64_t batch, const torch::Tensor& like) {
 }  // namespace
 
 std::vector<torch::Tensor> fused_forward_laplacian(torch::Tensor coordinates,
-                                                   torch::Tensor parameters, int64_t version) {
+                                                   torch::Tensor parameters, int64_t version,
+                                                   const std::string& activation) {
   TORCH_CHECK(version >= 0 && version <= 5, "version must be 0 to 5");
   check_inputs(coordinates, parameters);
+  const int act = activation_code(activation);
   const c10::cuda::CUDAGuard device_guard(coordinates.device());
   const int64_t batch = coordinates.size(0);
   auto output = torch::empty({batch, 1}, coordinates.options());
   auto laplacian = torch::empty({batch, 1}, coordinates.options());
   if (batch == 0) return {output, laplacian};
-  check_status(fhb_forward(coordinates.data_ptr<float>(), parameters.data_ptr<float>(),
-                           output.data_ptr<float>(), laplacian.data_ptr<float>(), batch,
-                           static_cast<int>(version), at::cuda::getCurrentCUDAStream()),
+  check_status(fhb_forward_ex(coordinates.data_ptr<float>(), parameters.data_ptr<float>(),
+                              output.data_ptr<float>(), laplacian.data_ptr<float>(), batch,
+                              static_cast<int>(version), act,
+                              at::cuda::getCurrentCUDAStream()),
                "fused_forward_laplacian");
   return {output, laplacian};
 }
@@ -76,9 +89,11 @@ std::vector<torch::Tensor> fused_forward_laplacian_backward(torch::Tensor coordi
                                                             torch::Tensor parameters,
                                                             torch::Tensor grad_output,
                                                             torch::Tensor grad_laplacian,
-                                                            int64_t version) {
+                                                            int64_t version,
+                                                            const std::string& activation) {
   TORCH_CHECK(version >= 1 && version <= 6, "backward version must be 1 to 6");
   check_inputs(coordinates, parameters);
+  const int act = activation_code(activation);
   for (const auto& grad : {grad_output, grad_laplacian}) {
     TORCH_CHECK(grad.is_cuda() && grad.is_contiguous() && grad.scalar_type() == torch::kFloat32,
                 "upstream gradients must be contiguous float32 CUDA tensors");
@@ -91,12 +106,12 @@ std::vector<torch::Tensor> fused_forward_laplacian_backward(torch::Tensor coordi
   auto grad_parameters = torch::empty_like(parameters);
   auto workspace = workspace_for(batch, parameters);
   check_status(
-      fhb_backward(coordinates.data_ptr<float>(), parameters.data_ptr<float>(),
-                   grad_output.data_ptr<float>(), grad_laplacian.data_ptr<float>(),
-                   grad_parameters.data_ptr<float>(), grad_coordinates.data_ptr<float>(), batch,
-                   static_cast<int>(version), workspace.data_ptr<float>(),
-                   static_cast<size_t>(workspace.numel()) * sizeof(float),
-                   at::cuda::getCurrentCUDAStream()),
+      fhb_backward_ex(coordinates.data_ptr<float>(), parameters.data_ptr<float>(),
+                      grad_output.data_ptr<float>(), grad_laplacian.data_ptr<float>(),
+                      grad_parameters.data_ptr<float>(), grad_coordinates.data_ptr<float>(),
+                      batch, static_cast<int>(version), act, workspace.data_ptr<float>(),
+                      static_cast<size_t>(workspace.numel()) * sizeof(float),
+                      at::cuda::getCurrentCUDAStream()),
       "fused_forward_laplacian_backward");
   return {grad_parameters, grad_coordinates};
 }
@@ -112,8 +127,10 @@ std::vector<torch::Tensor> fused_forward_laplacian_host(torch::Tensor coordinate
                                                         torch::Tensor parameters,
                                                         int64_t version,
                                                         c10::optional<torch::Tensor> output,
-                                                        c10::optional<torch::Tensor> laplacian) {
+                                                        c10::optional<torch::Tensor> laplacian,
+                                                        const std::string& activation) {
   TORCH_CHECK(version >= 0 && version <= 5, "version must be 0 to 5");
+  const int act = activation_code(activation);
   TORCH_CHECK(!coordinates.is_cuda() && coordinates.is_pinned(),
               "coordinates must be a pinned host tensor");
   TORCH_CHECK(parameters.is_cuda(), "parameters must be a CUDA tensor");
@@ -137,9 +154,9 @@ std::vector<torch::Tensor> fused_forward_laplacian_host(torch::Tensor coordinate
   }
   if (batch == 0) return {u, lap};
   const c10::cuda::CUDAGuard device_guard(parameters.device());
-  check_status(fhb_forward(coordinates.data_ptr<float>(), parameters.data_ptr<float>(),
-                           u.data_ptr<float>(), lap.data_ptr<float>(), batch,
-                           static_cast<int>(version), at::cuda::getCurrentCUDAStream()),
+  check_status(fhb_forward_ex(coordinates.data_ptr<float>(), parameters.data_ptr<float>(),
+                              u.data_ptr<float>(), lap.data_ptr<float>(), batch,
+                              static_cast<int>(version), act, at::cuda::getCurrentCUDAStream()),
                "fused_forward_laplacian_host");
   return {u, lap};
 }
@@ -186,7 +203,8 @@ std::vector<torch::Tensor> poisson_step_gradients(torch::Tensor coordinates,
 torch::Tensor pinn_step_gradients(torch::Tensor coordinates, torch::Tensor boundary,
                                   torch::Tensor parameters, int64_t total_points,
                                   int64_t boundary_total, double boundary_weight,
-                                  int64_t version) {
+                                  int64_t version, const std::string& activation) {
+  const int act = activation_code(activation);
   check_inputs(coordinates, parameters);
   check_inputs(boundary, parameters);
   const c10::cuda::CUDAGuard device_guard(coordinates.device());
@@ -204,7 +222,7 @@ torch::Tensor pinn_step_gradients(torch::Tensor coordinates, torch::Tensor bound
                    coordinates.data_ptr<float>(), batch, total_points,
                    boundary.data_ptr<float>(), nb, boundary_total,
                    static_cast<float>(boundary_weight), parameters.data_ptr<float>(), out,
-                   out + kParameterCount, static_cast<int>(version),
+                   out + kParameterCount, static_cast<int>(version), act,
                    bytes ? workspace.data_ptr<float>() : nullptr,
                    static_cast<size_t>(workspace.numel()) * sizeof(float),
                    at::cuda::getCurrentCUDAStream()),
@@ -290,7 +308,8 @@ torch::Tensor train_step(torch::Tensor coordinates, torch::Tensor boundary,
                          torch::Tensor exp_avg_sq, torch::Tensor step, double lr, double beta1,
                          double beta2, double eps, int64_t total_points, int64_t boundary_total,
                          double boundary_weight, int64_t exchange, int64_t version,
-                         c10::optional<torch::Tensor> grad_out) {
+                         c10::optional<torch::Tensor> grad_out, const std::string& activation) {
+  const int act = activation_code(activation);
   check_inputs(coordinates, parameters);
   check_inputs(boundary, parameters);
   check_vector(exp_avg, parameters, kParameterCount, "exp_avg");
@@ -317,7 +336,8 @@ torch::Tensor train_step(torch::Tensor coordinates, torch::Tensor boundary,
                      static_cast<float>(beta1), static_cast<float>(beta2),
                      static_cast<float>(eps), as_exchange(exchange),
                      grad_out ? grad_out->data_ptr<float>() : nullptr, loss.data_ptr<float>(),
-                     static_cast<int>(version), bytes ? workspace.data_ptr<float>() : nullptr,
+                     static_cast<int>(version), act,
+                     bytes ? workspace.data_ptr<float>() : nullptr,
                      static_cast<size_t>(workspace.numel()) * sizeof(float),
                      at::cuda::getCurrentCUDAStream()),
       "train_step");
@@ -338,25 +358,25 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, module) {
   module.def("fused_forward_laplacian", &fused_forward_laplacian,
              "Fixed MLP forward pass and input Laplacian (CUDA, sm_100a)",
              pybind11::arg("coordinates"), pybind11::arg("parameters"),
-             pybind11::arg("version") = 2);
+             pybind11::arg("version") = 2, pybind11::arg("activation") = "tanh");
   module.def("fused_forward_laplacian_backward", &fused_forward_laplacian_backward,
              "Gradients of the fused forward Laplacian w.r.t. parameters and coordinates "
              "(CUDA, sm_100a)",
              pybind11::arg("coordinates"), pybind11::arg("parameters"),
              pybind11::arg("grad_output"), pybind11::arg("grad_laplacian"),
-             pybind11::arg("version") = 6);
+             pybind11::arg("version") = 6, pybind11::arg("activation") = "tanh");
   module.def("fused_forward_laplacian_host", &fused_forward_laplacian_host,
              "Forward Laplacian of points in pinned host memory, read and written by the "
              "kernel over the host link (zero-copy)",
              pybind11::arg("coordinates"), pybind11::arg("parameters"),
              pybind11::arg("version") = 3, pybind11::arg("output") = pybind11::none(),
-             pybind11::arg("laplacian") = pybind11::none());
+             pybind11::arg("laplacian") = pybind11::none(), pybind11::arg("activation") = "tanh");
   module.def("pinn_step_gradients", &pinn_step_gradients,
              "Fused gradients of the Poisson PINN loss (interior residual + boundary term)",
              pybind11::arg("coordinates"), pybind11::arg("boundary"),
              pybind11::arg("parameters"), pybind11::arg("total_points"),
              pybind11::arg("boundary_total"), pybind11::arg("boundary_weight") = 100.0,
-             pybind11::arg("version") = 6);
+             pybind11::arg("version") = 6, pybind11::arg("activation") = "tanh");
   module.def("poisson_step_gradients", &poisson_step_gradients,
              "Fused forward + interior Poisson loss + backward in one persistent kernel",
              pybind11::arg("coordinates"), pybind11::arg("parameters"),
@@ -392,7 +412,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, module) {
              pybind11::arg("beta1"), pybind11::arg("beta2"), pybind11::arg("eps"),
              pybind11::arg("total_points"), pybind11::arg("boundary_total"),
              pybind11::arg("boundary_weight"), pybind11::arg("exchange"),
-             pybind11::arg("version") = 6, pybind11::arg("grad_out") = pybind11::none());
+             pybind11::arg("version") = 6, pybind11::arg("grad_out") = pybind11::none(),
+             pybind11::arg("activation") = "tanh");
   module.def("prepare_device", &prepare_device, "One-time per-device kernel set-up",
              pybind11::arg("device"));
   module.def("read_device_status", &read_device_status,

@@ -86,6 +86,10 @@ size_t backward_workspace_bytes(int64_t n, int64_t nb, const fhb::DeviceInfo& de
 
 bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
+bool valid_activation(int activation) {
+  return activation == FHB_ACTIVATION_TANH || activation == FHB_ACTIVATION_SILU;
+}
+
 bool valid_adam(float lr, float beta1, float beta2, float eps) {
   return lr >= 0.0f && beta1 >= 0.0f && beta1 < 1.0f && beta2 >= 0.0f && beta2 < 1.0f &&
          eps >= 0.0f;
@@ -165,9 +169,10 @@ int fhb_parameter_count(void) { return fhb::kParamCount; }
 
 int fhb_prepare_device(int device) { return prepare(device); }
 
-int fhb_forward(const float* coords, const float* params, float* u, float* lap, int64_t n,
-                int version, fhb_stream_t stream) {
-  if (version < FHB_FORWARD_VERSION_MIN || version > FHB_FORWARD_VERSION_MAX || n < 0)
+int fhb_forward_ex(const float* coords, const float* params, float* u, float* lap, int64_t n,
+                   int version, int activation, fhb_stream_t stream) {
+  if (version < FHB_FORWARD_VERSION_MIN || version > FHB_FORWARD_VERSION_MAX || n < 0 ||
+      !valid_activation(activation))
     return FHB_ERR_INVALID_ARGUMENT;
   if (n == 0) return FHB_OK;
   if (!coords || !params || !u || !lap) return FHB_ERR_INVALID_ARGUMENT;
@@ -178,11 +183,16 @@ int fhb_forward(const float* coords, const float* params, float* u, float* lap, 
   if (code != FHB_OK) return code;
   cudaError_t e;
   if (version <= 2)
-    e = fhb::launch_forward_fp32(version, coords, params, u, lap, n, *dev, stream);
+    e = fhb::launch_forward_fp32(version, coords, params, u, lap, n, activation, *dev, stream);
   else
     e = fhb::launch_forward_tc(coords, params, u, lap, n, version == FHB_FORWARD_VERSION_F16,
-                               *dev, stream);
+                               activation, *dev, stream);
   return record(e);
+}
+
+int fhb_forward(const float* coords, const float* params, float* u, float* lap, int64_t n,
+                int version, fhb_stream_t stream) {
+  return fhb_forward_ex(coords, params, u, lap, n, version, FHB_ACTIVATION_TANH, stream);
 }
 
 size_t fhb_backward_workspace_bytes(int64_t n) {
@@ -196,10 +206,12 @@ size_t fhb_backward_workspace_bytes(int64_t n) {
 static cudaError_t launch_gradient_kernel(const fhb::PointSets& ps, const float* params,
                                           const float* grad_u, const float* grad_lap,
                                           float* grad_coords, float* lap_out, bool poisson,
-                                          bool tensor_core, float* ws,
+                                          bool tensor_core, int activation, float* ws,
                                           const fhb::DeviceInfo& dev, cudaStream_t stream,
                                           const float** partials, int* rows) {
-  if (tensor_core) {
+  // The tensor-core kernel keeps the activations, not the pre-activations, for its adjoint
+  // (tanh's derivatives are functions of tanh); other activations run the FP32 kernel.
+  if (tensor_core && activation == FHB_ACTIVATION_TANH) {
     *partials = fhb::backward_tc_partials(ws);
     *rows = fhb::backward_tc_grid(ps.n, ps.nb, dev);
     return fhb::launch_backward_tc(ps, params, grad_u, grad_lap, grad_coords, lap_out, ws,
@@ -208,7 +220,7 @@ static cudaError_t launch_gradient_kernel(const fhb::PointSets& ps, const float*
   *partials = ws;
   *rows = fhb::backward_grid(ps.n, ps.nb, dev);
   return fhb::launch_backward_fp32(ps, params, grad_u, grad_lap, grad_coords, lap_out, ws,
-                                   poisson, dev, stream);
+                                   poisson, activation, dev, stream);
 }
 
 // Checks the point sets, parameters and workspace of a gradient launch.
@@ -228,7 +240,8 @@ static int check_gradient_inputs(const fhb::PointSets& ps, const float* params, 
 static int backward_common(const fhb::PointSets& ps, const float* params, const float* grad_u,
                            const float* grad_lap, float* grad_params, float* grad_coords,
                            float* lap_out, float* loss, bool poisson, bool tensor_core,
-                           void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+                           int activation, void* workspace, size_t workspace_bytes,
+                           cudaStream_t stream) {
   if (ps.n < 0 || ps.nb < 0 || !params || !grad_params) return FHB_ERR_INVALID_ARGUMENT;
   if (poisson && !loss) return FHB_ERR_INVALID_ARGUMENT;
   const fhb::DeviceInfo* dev = nullptr;
@@ -244,8 +257,9 @@ static int backward_common(const fhb::PointSets& ps, const float* params, const 
   const float* partials = nullptr;
   int rows = 0;
   cudaError_t e = launch_gradient_kernel(ps, params, grad_u, grad_lap, grad_coords, lap_out,
-                                         poisson, tensor_core, static_cast<float*>(workspace),
-                                         *dev, stream, &partials, &rows);
+                                         poisson, tensor_core, activation,
+                                         static_cast<float*>(workspace), *dev, stream,
+                                         &partials, &rows);
   if (e == cudaSuccess)
     e = fhb::launch_reduce_rows(partials, rows, grad_params, poisson ? loss : nullptr, stream);
   return record(e);
@@ -259,15 +273,24 @@ static fhb::PointSets interior_only(const float* coords, int64_t n, int64_t n_to
   return ps;
 }
 
-int fhb_backward(const float* coords, const float* params, const float* grad_u,
-                 const float* grad_lap, float* grad_params, float* grad_coords, int64_t n,
-                 int version, void* workspace, size_t workspace_bytes, fhb_stream_t stream) {
-  if (version < FHB_BACKWARD_VERSION_MIN || version > FHB_BACKWARD_VERSION_MAX)
+int fhb_backward_ex(const float* coords, const float* params, const float* grad_u,
+                    const float* grad_lap, float* grad_params, float* grad_coords, int64_t n,
+                    int version, int activation, void* workspace, size_t workspace_bytes,
+                    fhb_stream_t stream) {
+  if (version < FHB_BACKWARD_VERSION_MIN || version > FHB_BACKWARD_VERSION_MAX ||
+      !valid_activation(activation))
     return FHB_ERR_INVALID_ARGUMENT;
   return backward_common(interior_only(coords, n, n), params, grad_u, grad_lap, grad_params,
                          grad_coords, nullptr, nullptr, false,
-                         version == FHB_BACKWARD_VERSION_TENSOR_CORE, workspace,
+                         version == FHB_BACKWARD_VERSION_TENSOR_CORE, activation, workspace,
                          workspace_bytes, stream);
+}
+
+int fhb_backward(const float* coords, const float* params, const float* grad_u,
+                 const float* grad_lap, float* grad_params, float* grad_coords, int64_t n,
+                 int version, void* workspace, size_t workspace_bytes, fhb_stream_t stream) {
+  return fhb_backward_ex(coords, params, grad_u, grad_lap, grad_params, grad_coords, n, version,
+                         FHB_ACTIVATION_TANH, workspace, workspace_bytes, stream);
 }
 
 int fhb_poisson_step_gradients(const float* coords, const float* params, int64_t n,
@@ -279,8 +302,8 @@ int fhb_poisson_step_gradients(const float* coords, const float* params, int64_t
     return FHB_ERR_INVALID_ARGUMENT;
   return backward_common(interior_only(coords, n, n_total), params, nullptr, nullptr,
                          grad_params, grad_coords, lap_out, loss, true,
-                         version == FHB_BACKWARD_VERSION_TENSOR_CORE, workspace,
-                         workspace_bytes, stream);
+                         version == FHB_BACKWARD_VERSION_TENSOR_CORE, FHB_ACTIVATION_TANH,
+                         workspace, workspace_bytes, stream);
 }
 
 size_t fhb_pinn_step_workspace_bytes(int64_t n, int64_t n_boundary) {
@@ -293,8 +316,10 @@ int fhb_pinn_step_gradients(const float* coords, int64_t n, int64_t n_total,
                             const float* boundary, int64_t n_boundary,
                             int64_t n_boundary_total, float boundary_weight,
                             const float* params, float* grad_params, float* loss, int version,
-                            void* workspace, size_t workspace_bytes, fhb_stream_t stream) {
+                            int activation, void* workspace, size_t workspace_bytes,
+                            fhb_stream_t stream) {
   if (version < FHB_BACKWARD_VERSION_MIN || version > FHB_BACKWARD_VERSION_MAX || n < 0 ||
+      !valid_activation(activation) ||
       n_boundary < 0 || n_total < n || n_boundary_total < n_boundary ||
       !(boundary_weight >= 0.0f))
     return FHB_ERR_INVALID_ARGUMENT;
@@ -306,8 +331,8 @@ int fhb_pinn_step_gradients(const float* coords, int64_t n, int64_t n_total,
                       : 0.0f;
   ps.bweight = boundary_weight;
   return backward_common(ps, params, nullptr, nullptr, grad_params, nullptr, nullptr, loss,
-                         true, version == FHB_BACKWARD_VERSION_TENSOR_CORE, workspace,
-                         workspace_bytes, stream);
+                         true, version == FHB_BACKWARD_VERSION_TENSOR_CORE, activation,
+                         workspace, workspace_bytes, stream);
 }
 
 int fhb_adam_step(float* params, const float* grad, float* exp_avg, float* exp_avg_sq,
@@ -430,9 +455,10 @@ int fhb_train_step(const float* coords, int64_t n, int64_t n_total, const float*
                    int64_t n_boundary, int64_t n_boundary_total, float boundary_weight,
                    float* params, float* exp_avg, float* exp_avg_sq, int64_t* step, float lr,
                    float beta1, float beta2, float eps, fhb_exchange* exchange,
-                   float* grad_out, float* loss_out, int version, void* workspace,
-                   size_t workspace_bytes, fhb_stream_t stream) {
+                   float* grad_out, float* loss_out, int version, int activation,
+                   void* workspace, size_t workspace_bytes, fhb_stream_t stream) {
   if (version < FHB_BACKWARD_VERSION_MIN || version > FHB_BACKWARD_VERSION_MAX || n < 0 ||
+      !valid_activation(activation) ||
       n_boundary < 0 || n_total < n || n_boundary_total < n_boundary ||
       !(boundary_weight >= 0.0f) || !params || !exp_avg || !exp_avg_sq || !step ||
       !valid_adam(lr, beta1, beta2, eps) || !exchange || !exchange->connected)
@@ -460,7 +486,7 @@ int fhb_train_step(const float* coords, int64_t n, int64_t n_total, const float*
     code = check_gradient_inputs(ps, params, true, nullptr, workspace, workspace_bytes, *dev);
     if (code != FHB_OK) return code;
     e = launch_gradient_kernel(ps, params, nullptr, nullptr, nullptr, nullptr, true,
-                               version == FHB_BACKWARD_VERSION_TENSOR_CORE,
+                               version == FHB_BACKWARD_VERSION_TENSOR_CORE, activation,
                                static_cast<float*>(workspace), *dev, stream, &partials, &rows);
     if (e != cudaSuccess) return record(e);
   } else if (!aligned(params, 4)) {

@@ -204,6 +204,101 @@ __device__ __forceinline__ void tanh_jet_fast(float zv, float zj0, float zj1, fl
   l = fmaf(s, zl, -2.0f * a * s * q);
 }
 
+// ---- the SiLU jet and its adjoint ----
+//
+// Reference src/fused_hoad/backends/forward_laplacian.py:34-38 (_silu_jet) with :60-67: for
+// phi(z) = z sigma(z), p = sigma (1 - sigma),
+//   phi' = sigma + z p,   phi'' = p (2 + z (1 - 2 sigma)),
+//   phi''' = p ((1 - 2 sigma)(3 + z (1 - 2 sigma)) - 2 z p)   (the derivative of phi'');
+// the jet is v = phi, J_d = phi' z_Jd, L = phi' z_L + phi'' |z_J|^2, and its adjoint has the
+// tanh adjoint's form with (s, s2, s3) = (phi', phi'', phi''').
+__device__ __forceinline__ float sigmoid(float z) { return 1.0f / (1.0f + expf(-z)); }
+
+// sigmoid from 1 / (1 + 2^(-z log2(e))) on the special-function unit (ex2.approx, rcp.approx),
+// the SiLU counterpart of tanh_fast: a few 1e-7 absolute; saturates to exactly 0 and 1.
+__device__ __forceinline__ float sigmoid_fast(float z) {
+  float e, r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(z * -1.4426950408889634f));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(e + 1.0f));
+  return r;
+}
+
+__device__ __forceinline__ void silu_jet_from_sigmoid(float sg, float zv, float zj0, float zj1,
+                                                      float zl, float& v, float& j0, float& j1,
+                                                      float& l) {
+  const float p = sg * (1.0f - sg);
+  const float d1 = fmaf(zv, p, sg);
+  const float d2 = p * fmaf(zv, fmaf(-2.0f, sg, 1.0f), 2.0f);
+  const float q = fmaf(zj0, zj0, zj1 * zj1);
+  v = zv * sg;
+  j0 = d1 * zj0;
+  j1 = d1 * zj1;
+  l = fmaf(d1, zl, d2 * q);
+}
+
+__device__ __forceinline__ void silu_jet(float zv, float zj0, float zj1, float zl, float& v,
+                                         float& j0, float& j1, float& l) {
+  silu_jet_from_sigmoid(sigmoid(zv), zv, zj0, zj1, zl, v, j0, j1, l);
+}
+
+__device__ __forceinline__ void silu_jet_fast(float zv, float zj0, float zj1, float zl, float& v,
+                                              float& j0, float& j1, float& l) {
+  silu_jet_from_sigmoid(sigmoid_fast(zv), zv, zj0, zj1, zl, v, j0, j1, l);
+}
+
+// Maps (vbar, J0bar, J1bar, Lbar) in place to (zbar_v, zbar_J0, zbar_J1, zbar_L).
+__device__ __forceinline__ void silu_jet_adjoint(float zv, float zj0, float zj1, float zl,
+                                                 float& av, float& aj0, float& aj1, float& al) {
+  const float sg = sigmoid(zv);
+  const float p = sg * (1.0f - sg);
+  const float m = fmaf(-2.0f, sg, 1.0f);  // 1 - 2 sigma
+  const float s = fmaf(zv, p, sg);
+  const float s2 = p * fmaf(zv, m, 2.0f);
+  const float s3 = p * fmaf(m, fmaf(zv, m, 3.0f), -2.0f * zv * p);
+  const float q = fmaf(zj0, zj0, zj1 * zj1);
+  const float gv = av * s + fmaf(aj0, zj0, aj1 * zj1) * s2 + al * fmaf(zl, s2, q * s3);
+  const float l2 = 2.0f * al * s2;
+  const float g0 = fmaf(aj0, s, l2 * zj0);
+  const float g1 = fmaf(aj1, s, l2 * zj1);
+  av = gv;
+  aj0 = g0;
+  aj1 = g1;
+  al = al * s;
+}
+
+// Activation policies for the kernel templates: jet (accurate), jet_fast (special-function
+// unit, tensor-core epilogues) and the adjoint in terms of the pre-activation jet.
+struct TanhAct {
+  static constexpr int kCode = FHB_ACTIVATION_TANH;
+  static __device__ __forceinline__ void jet(float zv, float zj0, float zj1, float zl, float& v,
+                                             float& j0, float& j1, float& l) {
+    tanh_jet(zv, zj0, zj1, zl, v, j0, j1, l);
+  }
+  static __device__ __forceinline__ void jet_fast(float zv, float zj0, float zj1, float zl,
+                                                  float& v, float& j0, float& j1, float& l) {
+    tanh_jet_fast(zv, zj0, zj1, zl, v, j0, j1, l);
+  }
+  static __device__ __forceinline__ void adjoint(float zv, float zj0, float zj1, float zl,
+                                                 float& av, float& aj0, float& aj1, float& al) {
+    tanh_jet_adjoint(zv, zj0, zj1, zl, av, aj0, aj1, al);
+  }
+};
+struct SiluAct {
+  static constexpr int kCode = FHB_ACTIVATION_SILU;
+  static __device__ __forceinline__ void jet(float zv, float zj0, float zj1, float zl, float& v,
+                                             float& j0, float& j1, float& l) {
+    silu_jet(zv, zj0, zj1, zl, v, j0, j1, l);
+  }
+  static __device__ __forceinline__ void jet_fast(float zv, float zj0, float zj1, float zl,
+                                                  float& v, float& j0, float& j1, float& l) {
+    silu_jet_fast(zv, zj0, zj1, zl, v, j0, j1, l);
+  }
+  static __device__ __forceinline__ void adjoint(float zv, float zj0, float zj1, float zl,
+                                                 float& av, float& aj0, float& aj1, float& al) {
+    silu_jet_adjoint(zv, zj0, zj1, zl, av, aj0, aj1, al);
+  }
+};
+
 // Warp-wide sum with a fixed butterfly order (deterministic).
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll

@@ -2,7 +2,9 @@
 //
 // Same math as the reference's fwd v0-v2 (csrc/fused_residual.cu:61-279): the jet
 // (value, d/dx, d/dy, Laplacian) of every hidden neuron is carried through the 2->64x4->1
-// tanh MLP. Design for sm_100a:
+// MLP, with tanh (the reference kernels' activation) or SiLU (the other activation of the
+// reference's PyTorch forward-Laplacian backend) as the Act template parameter. Design for
+// sm_100a:
 //   * persistent grid, one 256-thread CTA per SM; the whole 51 KB parameter buffer is
 //     staged into shared memory ONCE per CTA by one bulk (TMA) copy, not once per tile;
 //   * a tile holds 32*PPL points; warp w owns neurons 8w..8w+7, lane l owns points
@@ -69,7 +71,7 @@ __device__ __forceinline__ float lane_of(const float4& w, int j) {
   return j == 0 ? w.x : j == 1 ? w.y : j == 2 ? w.z : w.w;
 }
 
-template <int PPL>
+template <int PPL, class Act>
 __global__ void __launch_bounds__(kThreads, 1)
     forward_fp32_kernel(const float* __restrict__ coords, const float* __restrict__ params,
                         float* __restrict__ u_out, float* __restrict__ lap_out, int64_t n,
@@ -118,7 +120,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       float hv[PPL], hj0[PPL], hj1[PPL], hl[PPL];
 #pragma unroll
       for (int q = 0; q < PPL; ++q)
-        tanh_jet(fmaf(w0, x0[q], fmaf(w1, x1[q], b)), w0, w1, 0.0f, hv[q], hj0[q], hj1[q],
+        Act::jet(fmaf(w0, x0[q], fmaf(w1, x1[q], b)), w0, w1, 0.0f, hv[q], hj0[q], hj1[q],
                  hl[q]);
       float* dst = jet + o * C::kTile + col;
       st_pts<PPL>(dst, hv);
@@ -175,7 +177,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           float hv[PPL], hj0[PPL], hj1[PPL], hl[PPL];
 #pragma unroll
           for (int q = 0; q < PPL; ++q)
-            tanh_jet(acc[0][k][q], acc[1][k][q], acc[2][k][q], acc[3][k][q], hv[q], hj0[q],
+            Act::jet(acc[0][k][q], acc[1][k][q], acc[2][k][q], acc[3][k][q], hv[q], hj0[q],
                      hj1[q], hl[q]);
           float* dst = jet + (o0 + k) * C::kTile + col;
           st_pts<PPL>(dst, hv);
@@ -194,7 +196,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int q = 0; q < PPL; ++q) {
             float v, j0, j1, l;
-            tanh_jet(acc[0][k][q], acc[1][k][q], acc[2][k][q], acc[3][k][q], v, j0, j1, l);
+            Act::jet(acc[0][k][q], acc[1][k][q], acc[2][k][q], acc[3][k][q], v, j0, j1, l);
             pu[q] = fmaf(wo, v, pu[q]);
             pl[q] = fmaf(wo, l, pl[q]);
           }
@@ -222,14 +224,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <int PPL>
+template <int PPL, class Act>
 cudaError_t set_attributes() {
-  return cudaFuncSetAttribute(forward_fp32_kernel<PPL>,
+  return cudaFuncSetAttribute(forward_fp32_kernel<PPL, Act>,
                               cudaFuncAttributeMaxDynamicSharedMemorySize,
                               static_cast<int>(Cfg<PPL>::kSmem));
 }
 
-template <int PPL>
+template <int PPL, class Act>
 cudaError_t launch(const float* coords, const float* params, float* u, float* lap, int64_t n,
                    const DeviceInfo& dev, cudaStream_t stream) {
   using C = Cfg<PPL>;
@@ -237,28 +239,38 @@ cudaError_t launch(const float* coords, const float* params, float* u, float* la
   const int grid = static_cast<int>(std::min<int64_t>(tiles, dev.sms));
   const int params_aligned = (reinterpret_cast<uintptr_t>(params) % 16) == 0;
   const int coords_aligned = (reinterpret_cast<uintptr_t>(coords) % 16) == 0;
-  forward_fp32_kernel<PPL><<<grid, kThreads, C::kSmem, stream>>>(
+  forward_fp32_kernel<PPL, Act><<<grid, kThreads, C::kSmem, stream>>>(
       coords, params, u, lap, n, tiles, params_aligned, coords_aligned, dev.status);
   return cudaGetLastError();
+}
+
+template <class Act>
+cudaError_t launch_act(int tile, const float* coords, const float* params, float* u, float* lap,
+                       int64_t n, const DeviceInfo& dev, cudaStream_t stream) {
+  switch (tile) {
+    case 0: return launch<1, Act>(coords, params, u, lap, n, dev, stream);
+    case 1: return launch<4, Act>(coords, params, u, lap, n, dev, stream);
+    default: return launch<2, Act>(coords, params, u, lap, n, dev, stream);
+  }
 }
 
 }  // namespace
 
 cudaError_t prepare_forward_fp32() {
-  cudaError_t e = set_attributes<1>();
-  if (e == cudaSuccess) e = set_attributes<2>();
-  if (e == cudaSuccess) e = set_attributes<4>();
+  cudaError_t e = cudaSuccess;
+  for (cudaError_t r : {set_attributes<1, TanhAct>(), set_attributes<2, TanhAct>(),
+                        set_attributes<4, TanhAct>(), set_attributes<1, SiluAct>(),
+                        set_attributes<2, SiluAct>(), set_attributes<4, SiluAct>()})
+    if (e == cudaSuccess) e = r;
   return e;
 }
 
 cudaError_t launch_forward_fp32(int tile, const float* coords, const float* params, float* u,
-                                float* lap, int64_t n, const DeviceInfo& dev,
+                                float* lap, int64_t n, int activation, const DeviceInfo& dev,
                                 cudaStream_t stream) {
-  switch (tile) {
-    case 0: return launch<1>(coords, params, u, lap, n, dev, stream);
-    case 1: return launch<4>(coords, params, u, lap, n, dev, stream);
-    default: return launch<2>(coords, params, u, lap, n, dev, stream);
-  }
+  return activation == FHB_ACTIVATION_SILU
+             ? launch_act<SiluAct>(tile, coords, params, u, lap, n, dev, stream)
+             : launch_act<TanhAct>(tile, coords, params, u, lap, n, dev, stream);
 }
 
 }  // namespace fhb

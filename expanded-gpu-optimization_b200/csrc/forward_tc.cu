@@ -415,13 +415,15 @@ __device__ __forceinline__ void stage_f16(const float* __restrict__ params, uint
   }
 }
 
-template <bool F16>
+template <bool F16, class Act>
 __global__ void __launch_bounds__(kThreads, 1)
     forward_tc_kernel(const float* __restrict__ coords, const float* __restrict__ params,
                       float* __restrict__ u_out, float* __restrict__ lap_out, int64_t n,
                       int64_t tiles, unsigned int* status) {
   using F = Format<F16>;
   using L = Layout<F16>;
+  // The f16 range scales bound the jets with |tanh| <= 1 and tanh' <= 1: tanh only.
+  static_assert(!F16 || Act::kCode == FHB_ACTIVATION_TANH, "3xFP16 operands need the tanh bounds");
   extern __shared__ __align__(1024) uint8_t smem[];
   float* small = reinterpret_cast<float*>(smem + L::kSmallOff);
   float* red = reinterpret_cast<float*>(smem + L::kRedOff);
@@ -508,7 +510,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int t = 0; t < 4; ++t) {
         const int o = 16 * j + 4 * s + t;
         const float w0 = small[kSmW0 + 2 * o], w1 = small[kSmW0 + 2 * o + 1];
-        tanh_jet_fast(fmaf(w0, x0, fmaf(w1, x1, small[kSmB0 + o])), w0, w1, 0.0f, h[0][t],
+        Act::jet_fast(fmaf(w0, x0, fmaf(w1, x1, small[kSmB0 + o])), w0, w1, 0.0f, h[0][t],
                       h[1][t], h[2][t], h[3][t]);
       }
       if (!(ok = produce_chunk<F16>(chunk++, h, tmem_warp, s, cx))) break;
@@ -545,7 +547,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int t = 0; t < 4; ++t) {
             const int i = 4 * j + t;
-            tanh_jet_fast(d[0][i], d[1][i], d[2][i], d[3][i], h[0][t], h[1][t], h[2][t],
+            Act::jet_fast(d[0][i], d[1][i], d[2][i], d[3][i], h[0][t], h[1][t], h[2][t],
                           h[3][t]);
           }
           if (!(ok = produce_chunk<F16>(chunk++, h, tmem_warp, s, cx))) break;
@@ -556,7 +558,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           float v, j0, j1, lv;
-          tanh_jet_fast(d[0][i], d[1][i], d[2][i], d[3][i], v, j0, j1, lv);
+          Act::jet_fast(d[0][i], d[1][i], d[2][i], d[3][i], v, j0, j1, lv);
           const float w = small[kSmWout + 16 * (i >> 2) + 4 * s + (i & 3)];
           pu = fmaf(w, v, pu);
           pl = fmaf(w, lv, pl);
@@ -603,25 +605,34 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 }  // namespace
 
+template <bool F16, class Act>
+cudaError_t set_attributes() {
+  return cudaFuncSetAttribute(forward_tc_kernel<F16, Act>,
+                              cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+}
+
 cudaError_t prepare_forward_tc() {
-  cudaError_t e = cudaFuncSetAttribute(forward_tc_kernel<false>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(forward_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             kSmemBytes);
+  cudaError_t e = cudaSuccess;
+  for (cudaError_t r : {set_attributes<true, TanhAct>(), set_attributes<false, TanhAct>(),
+                        set_attributes<false, SiluAct>()})
+    if (e == cudaSuccess) e = r;
   return e;
 }
 
 cudaError_t launch_forward_tc(const float* coords, const float* params, float* u, float* lap,
-                              int64_t n, bool f16, const DeviceInfo& dev, cudaStream_t stream) {
+                              int64_t n, bool f16, int activation, const DeviceInfo& dev,
+                              cudaStream_t stream) {
   const int64_t tiles = (n + kTile - 1) / kTile;
   const int grid = static_cast<int>(std::min<int64_t>(tiles, dev.sms));
-  if (f16) {
-    forward_tc_kernel<true><<<grid, kThreads, kSmemBytes, stream>>>(coords, params, u, lap, n,
-                                                                    tiles, dev.status);
+  if (activation == FHB_ACTIVATION_SILU) {  // unbounded activations: the 3xTF32 format
+    forward_tc_kernel<false, SiluAct><<<grid, kThreads, kSmemBytes, stream>>>(
+        coords, params, u, lap, n, tiles, dev.status);
+  } else if (f16) {
+    forward_tc_kernel<true, TanhAct><<<grid, kThreads, kSmemBytes, stream>>>(
+        coords, params, u, lap, n, tiles, dev.status);
   } else {
-    forward_tc_kernel<false><<<grid, kThreads, kSmemBytes, stream>>>(coords, params, u, lap, n,
-                                                                     tiles, dev.status);
+    forward_tc_kernel<false, TanhAct><<<grid, kThreads, kSmemBytes, stream>>>(
+        coords, params, u, lap, n, tiles, dev.status);
   }
   return cudaGetLastError();
 }

@@ -126,15 +126,19 @@ struct DeviceInfo {
 // ---- forward_fp32.cu ----
 cudaError_t prepare_forward_fp32();
 // tile: 0 -> 32-point tiles, 1 -> 128-point tiles, 2 -> 64-point tiles
+// activation: FHB_ACTIVATION_TANH or FHB_ACTIVATION_SILU
 cudaError_t launch_forward_fp32(int tile, const float* coords, const float* params, float* u,
-                                float* lap, int64_t n, const DeviceInfo& dev,
+                                float* lap, int64_t n, int activation, const DeviceInfo& dev,
                                 cudaStream_t stream);
 
 // ---- forward_tc.cu ----
 cudaError_t prepare_forward_tc();
-// f16: the 3xFP16 operand format (forward version 3), else 3xTF32 (versions 4, 5).
+// f16: the 3xFP16 operand format (forward version 3), else 3xTF32 (versions 4, 5). SiLU
+// always runs the 3xTF32 format (its activations are unbounded, so no weight-derived f16
+// range scale exists).
 cudaError_t launch_forward_tc(const float* coords, const float* params, float* u, float* lap,
-                              int64_t n, bool f16, const DeviceInfo& dev, cudaStream_t stream);
+                              int64_t n, bool f16, int activation, const DeviceInfo& dev,
+                              cudaStream_t stream);
 
 // ---- backward_fp32.cu ----
 cudaError_t prepare_backward_fp32();
@@ -144,7 +148,8 @@ int backward_grid(int64_t n, int64_t nb, const DeviceInfo& dev);
 cudaError_t launch_backward_fp32(const PointSets& points, const float* params,
                                  const float* grad_u, const float* grad_lap,
                                  float* grad_coords, float* lap_out, float* partials,
-                                 bool poisson, const DeviceInfo& dev, cudaStream_t stream);
+                                 bool poisson, int activation, const DeviceInfo& dev,
+                                 cudaStream_t stream);
 cudaError_t launch_reduce_rows(const float* partials, int rows, float* grad_params,
                                float* loss, cudaStream_t stream);
 

@@ -78,7 +78,7 @@ extern "C" int fhb_backward_noalloc(const float* coords, const float* params,
   ps.interior = coords;
   ps.n = n;
   e = fhb::launch_backward_fp32(ps, params, grad_u, grad_lap, grad_coords, nullptr, st.rows,
-                                false, st.info, stream);
+                                false, FHB_ACTIVATION_TANH, st.info, stream);
   if (e == cudaSuccess) e = fhb::launch_reduce_rows(st.rows, rows, grad_params, nullptr, stream);
   return e == cudaSuccess ? FHB_OK : FHB_ERR_CUDA;
 }

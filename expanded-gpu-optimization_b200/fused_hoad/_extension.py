@@ -38,15 +38,19 @@ def extension_available() -> bool:
 
 
 def fused_forward_laplacian(
-    coordinates: Tensor, parameters: Tensor, version: int = 2
+    coordinates: Tensor, parameters: Tensor, version: int = 2, activation: str = "tanh"
 ) -> tuple[Tensor, Tensor]:
     """Evaluate the fixed MLP and its input Laplacian: ``(u [N,1], lap [N,1])``.
 
     ``version`` 0, 1, 2: the FP32 CUDA-core kernel with 32-, 128- and 64-point tiles (2 is
-    the default, as in the reference). 3, 4, 5: the 3xTF32 tcgen05/TMEM tensor-core kernel,
-    which holds the same FP32 tolerance (the reference's single-TF32 v3-v5 did not).
+    the default, as in the reference). 3: the 3xFP16 tcgen05/TMEM tensor-core kernel; 4, 5:
+    the 3xTF32 one; both hold the FP32 tolerance (the reference's single-TF32 v3-v5 did
+    not). ``activation`` is ``"tanh"`` (the reference kernels') or ``"silu"`` (the other jet
+    of the reference's PyTorch forward-Laplacian backend; versions 3-5 then run 3xTF32).
     """
-    output, laplacian = load_extension().fused_forward_laplacian(coordinates, parameters, version)
+    output, laplacian = load_extension().fused_forward_laplacian(
+        coordinates, parameters, version, activation
+    )
     return output, laplacian
 
 
@@ -56,12 +60,13 @@ def fused_forward_laplacian_backward(
     grad_output: Tensor,
     grad_laplacian: Tensor,
     version: int = 6,
+    activation: str = "tanh",
 ) -> tuple[Tensor, Tensor]:
     """Return ``(grad_parameters [12737], grad_coordinates [N,2])``.
 
-    Every version 1..6 runs the same persistent adjoint-jet kernel, whose fixed-order
-    reduction makes the gradients bitwise reproducible; the argument is kept so callers of
-    the reference's versions keep working.
+    Version 6 (the default) runs the tensor-core adjoint kernel, 1..5 the FP32 CUDA-core one;
+    both reduce in a fixed order, so the gradients are bitwise reproducible. SiLU runs the
+    FP32 kernel for every version.
     """
     grad_parameters, grad_coordinates = load_extension().fused_forward_laplacian_backward(
         coordinates,
@@ -69,6 +74,7 @@ def fused_forward_laplacian_backward(
         grad_output.reshape(-1).contiguous(),
         grad_laplacian.reshape(-1).contiguous(),
         version,
+        activation,
     )
     return grad_parameters, grad_coordinates
 
@@ -79,6 +85,7 @@ def fused_forward_laplacian_host(
     version: int = 3,
     output: Tensor | None = None,
     laplacian: Tensor | None = None,
+    activation: str = "tanh",
 ) -> tuple[Tensor, Tensor]:
     """``(u, lap)`` for points in pinned host memory, without staging copies.
 
@@ -87,6 +94,6 @@ def fused_forward_laplacian_host(
     valid once the current CUDA stream of ``parameters``' device has completed.
     """
     u, lap = load_extension().fused_forward_laplacian_host(
-        coordinates, parameters, version, output, laplacian
+        coordinates, parameters, version, output, laplacian, activation
     )
     return u, lap

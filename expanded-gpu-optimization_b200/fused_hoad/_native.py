@@ -21,10 +21,15 @@ _SIGNATURES: dict[str, tuple[object, list]] = {
     "fhb_parameter_count": (ctypes.c_int, []),
     "fhb_prepare_device": (ctypes.c_int, [ctypes.c_int]),
     "fhb_forward": (ctypes.c_int, [_p, _p, _p, _p, _i64, ctypes.c_int, _p]),
+    "fhb_forward_ex": (ctypes.c_int, [_p, _p, _p, _p, _i64, ctypes.c_int, ctypes.c_int, _p]),
     "fhb_backward_workspace_bytes": (ctypes.c_size_t, [_i64]),
     "fhb_backward": (
         ctypes.c_int,
         [_p, _p, _p, _p, _p, _p, _i64, ctypes.c_int, _p, ctypes.c_size_t, _p],
+    ),
+    "fhb_backward_ex": (
+        ctypes.c_int,
+        [_p, _p, _p, _p, _p, _p, _i64, ctypes.c_int, ctypes.c_int, _p, ctypes.c_size_t, _p],
     ),
     "fhb_backward_noalloc": (ctypes.c_int, [_p, _p, _p, _p, _p, _p, _i64, _p]),
     "fhb_poisson_step_gradients": (
@@ -34,8 +39,8 @@ _SIGNATURES: dict[str, tuple[object, list]] = {
     "fhb_pinn_step_workspace_bytes": (ctypes.c_size_t, [_i64, _i64]),
     "fhb_pinn_step_gradients": (
         ctypes.c_int,
-        [_p, _i64, _i64, _p, _i64, _i64, ctypes.c_float, _p, _p, _p, ctypes.c_int, _p,
-         ctypes.c_size_t, _p],
+        [_p, _i64, _i64, _p, _i64, _i64, ctypes.c_float, _p, _p, _p, ctypes.c_int,
+         ctypes.c_int, _p, ctypes.c_size_t, _p],
     ),
     "fhb_adam_step": (
         ctypes.c_int,
@@ -54,8 +59,8 @@ _SIGNATURES: dict[str, tuple[object, list]] = {
     "fhb_train_step": (
         ctypes.c_int,
         [_p, _i64, _i64, _p, _i64, _i64, ctypes.c_float, _p, _p, _p, _p, ctypes.c_float,
-         ctypes.c_float, ctypes.c_float, ctypes.c_float, _p, _p, _p, ctypes.c_int, _p,
-         ctypes.c_size_t, _p],
+         ctypes.c_float, ctypes.c_float, ctypes.c_float, _p, _p, _p, ctypes.c_int,
+         ctypes.c_int, _p, ctypes.c_size_t, _p],
     ),
     "fhb_read_device_status": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_uint)]),
     "fhb_debug_bounded_wait_selftest": (ctypes.c_int, [ctypes.c_uint64, _p]),

@@ -16,6 +16,7 @@ from torch import Tensor, nn
 
 from fused_hoad._extension import fused_forward_laplacian, fused_forward_laplacian_backward
 from fused_hoad.parameters import pack_poisson_parameters
+from fused_hoad.problem import ACTIVATIONS
 
 _cache: dict[str, object] = {}
 
@@ -36,10 +37,18 @@ class FusedForwardLaplacian(torch.autograd.Function):
     """Fused-kernel forward ``(u, lap)``; fused-kernel backward to ``(coords, params)``."""
 
     @staticmethod
-    def forward(ctx, coordinates: Tensor, parameters: Tensor, version: int, backward: str):
+    def forward(
+        ctx,
+        coordinates: Tensor,
+        parameters: Tensor,
+        version: int,
+        backward: str,
+        activation: str = "tanh",
+    ):
         ctx.save_for_backward(coordinates, parameters)
         ctx.backward_mode = backward
-        return fused_forward_laplacian(coordinates, parameters, version)
+        ctx.activation = activation
+        return fused_forward_laplacian(coordinates, parameters, version, activation)
 
     @staticmethod
     def backward(ctx, grad_output: Tensor | None, grad_laplacian: Tensor | None):
@@ -55,10 +64,12 @@ class FusedForwardLaplacian(torch.autograd.Function):
             grad_output,
             grad_laplacian,
             _CUDA_BACKWARD_VERSIONS[ctx.backward_mode],
+            ctx.activation,
         )
         return (
             grad_coordinates if needs_coordinates else None,
             grad_parameters if needs_parameters else None,
+            None,
             None,
             None,
         )
@@ -83,17 +94,30 @@ def _packed_parameters(model: nn.Module) -> Tensor:
     return _cache["packed"]
 
 
+def model_activation(model: nn.Module) -> str:
+    """Name of the model's hidden activation (``"tanh"`` or ``"silu"``), all layers alike."""
+    kinds = {name for module in model.modules() for name, cls in ACTIVATIONS.items()
+             if type(module) is cls}
+    if len(kinds) != 1:
+        raise TypeError(f"the fused kernels need one hidden activation out of {tuple(ACTIVATIONS)}")
+    return kinds.pop()
+
+
 def fused_laplacian(
     model: nn.Module, coordinates: Tensor, version: int = 2, backward: str = "cuda"
 ) -> tuple[Tensor, Tensor]:
     """Evaluate the fixed Poisson MLP and its input Laplacian with one CUDA kernel.
 
     ``backward`` names the gradient path when autograd is active (``"cuda"`` or
-    ``"cuda_vN"``; all run the fused adjoint kernel).
+    ``"cuda_vN"``; all run the fused adjoint kernel). The hidden activation (tanh or SiLU)
+    is read from the model.
     """
     if backward not in BACKWARD_MODES:
         raise ValueError(f"backward must be one of {BACKWARD_MODES}")
+    activation = model_activation(model)
     parameters = _packed_parameters(model)
     if parameters.requires_grad or coordinates.requires_grad:
-        return FusedForwardLaplacian.apply(coordinates.contiguous(), parameters, version, backward)
-    return fused_forward_laplacian(coordinates.contiguous(), parameters, version)
+        return FusedForwardLaplacian.apply(
+            coordinates.contiguous(), parameters, version, backward, activation
+        )
+    return fused_forward_laplacian(coordinates.contiguous(), parameters, version, activation)

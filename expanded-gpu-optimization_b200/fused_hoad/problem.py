@@ -16,6 +16,11 @@ import torch
 from torch import Tensor, nn
 
 
+# Hidden activations with a fused jet (reference src/fused_hoad/models.py:9-12): tanh, the
+# reference kernels' activation, and SiLU, the other jet of its forward-Laplacian backend.
+ACTIVATIONS: dict[str, type[nn.Module]] = {"tanh": nn.Tanh, "silu": nn.SiLU}
+
+
 @dataclass(frozen=True, slots=True)
 class MLPConfig:
     """Shape contract of the MLP targeted by the fused kernels."""
@@ -30,19 +35,20 @@ class MLPConfig:
         for name in ("input_dim", "hidden_dim", "hidden_layers", "output_dim"):
             if getattr(self, name) < 1:
                 raise ValueError(f"{name} must be positive")
-        if self.activation != "tanh":
-            raise ValueError("the fused kernels implement the tanh jet only")
+        if self.activation not in ACTIVATIONS:
+            raise ValueError(f"activation must be one of {tuple(ACTIVATIONS)}")
 
 
 DEFAULT_POISSON_MLP = MLPConfig(input_dim=2, hidden_dim=64, hidden_layers=4)
 
 
 def build_mlp(config: MLPConfig = DEFAULT_POISSON_MLP) -> nn.Sequential:
-    """``Linear, Tanh`` x hidden_layers then ``Linear``, with nn.Linear's default init."""
+    """``Linear, activation`` x hidden_layers then ``Linear``, with nn.Linear's default init
+    (reference ``src/fused_hoad/models.py:15-26``)."""
     layers: list[nn.Module] = []
     width = config.input_dim
     for _ in range(config.hidden_layers):
-        layers += [nn.Linear(width, config.hidden_dim), nn.Tanh()]
+        layers += [nn.Linear(width, config.hidden_dim), ACTIVATIONS[config.activation]()]
         width = config.hidden_dim
     layers.append(nn.Linear(width, config.output_dim))
     return nn.Sequential(*layers)

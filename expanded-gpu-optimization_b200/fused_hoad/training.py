@@ -33,6 +33,8 @@ from torch import Tensor, nn
 
 from fused_hoad._extension import load_extension
 from fused_hoad.distributed import PeerExchange, allreduce_sum_, world
+from fused_hoad.problem import ACTIVATIONS
+from fused_hoad.backends.fused import model_activation
 from fused_hoad.parameters import (
     POISSON_PARAMETER_COUNT,
     bind_model_to_flat,
@@ -85,7 +87,9 @@ class PoissonTrainer:
     and Adam launches. With ``"peer"`` and more than one rank, every rank must construct its
     trainer in the same order and call :meth:`close` after its last step.
 
-    The loss is the interior Poisson residual ``mean((lap - f)^2)`` (the benchmark's,
+    ``activation`` (``"tanh"`` or ``"silu"``) is read from a module, else defaults to tanh;
+    SiLU runs the FP32 gradient kernel. The loss is the interior Poisson residual
+    ``mean((lap - f)^2)`` (the benchmark's,
     benchmarks/benchmark_training.py:46-48); passing ``boundary`` points to :meth:`step`
     adds the PINN boundary term ``boundary_weight * mean(u^2)`` of the reference's training
     driver (src/fused_hoad/training.py:68-94), in the same kernel launch.
@@ -103,13 +107,21 @@ class PoissonTrainer:
         boundary_weight: float = 100.0,
         exchange: str = "peer",
         wait_limit_s: float = 30.0,
+        activation: str | None = None,
     ) -> None:
         self._C = load_extension()
         if isinstance(parameters, nn.Module):
+            model_act = model_activation(parameters)
+            if activation is not None and activation != model_act:
+                raise ValueError(f"activation {activation!r} does not match the model's {model_act!r}")
+            activation = model_act
             flat = pack_poisson_parameters(parameters).contiguous()
             bind_model_to_flat(parameters, flat)
         else:
             flat = parameters
+        self.activation = activation or "tanh"
+        if self.activation not in ACTIVATIONS:
+            raise ValueError(f"activation must be one of {tuple(ACTIVATIONS)}")
         if not (flat.is_cuda and flat.dtype == torch.float32 and flat.is_contiguous()):
             raise ValueError("parameters must be a contiguous float32 CUDA tensor")
         if flat.numel() != POISSON_PARAMETER_COUNT:
@@ -147,17 +159,14 @@ class PoissonTrainer:
         boundary_total: int | None = None,
     ) -> Tensor:
         """Flat ``[12738]`` buffer: the gradient summed over ranks, then the loss."""
-        if boundary is None:
-            out, _, _ = self._C.poisson_step_gradients(
-                coordinates, self.params, total_points, version=self.backward_version
-            )
-        else:
-            if boundary_total is None:
-                boundary_total = boundary.shape[0] * world()[1]
-            out = self._C.pinn_step_gradients(
-                coordinates, boundary, self.params, total_points, boundary_total,
-                self.boundary_weight, self.backward_version,
-            )
+        if boundary is None:  # the PINN step without a boundary set is the Poisson step
+            boundary, boundary_total = self._no_boundary, 0
+        elif boundary_total is None:
+            boundary_total = boundary.shape[0] * world()[1]
+        out = self._C.pinn_step_gradients(
+            coordinates, boundary, self.params, total_points, boundary_total,
+            self.boundary_weight, self.backward_version, self.activation,
+        )
         return allreduce_sum_(out, self.group)
 
     def step(
@@ -182,7 +191,7 @@ class PoissonTrainer:
                 coordinates, boundary, self.params, self.exp_avg, self.exp_avg_sq,
                 self.step_count, self.lr, self.betas[0], self.betas[1], self.eps,
                 total_points, boundary_total, self.boundary_weight, self._peer.handle,
-                self.backward_version,
+                self.backward_version, None, self.activation,
             )
         out = self.gradients(coordinates, total_points, boundary, boundary_total)
         self._C.adam_step(

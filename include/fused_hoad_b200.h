@@ -59,6 +59,12 @@ typedef struct CUstream_st* fhb_stream_t;
  * in 3xTF32). Both reduce in a fixed order. */
 #define FHB_BACKWARD_VERSION_TENSOR_CORE 6
 
+/* Hidden-layer activations (reference src/fused_hoad/specs.py:17, models.py:9-12). The
+ * reference's fused CUDA path is tanh only; SiLU is the jet of its PyTorch forward-Laplacian
+ * backend (src/fused_hoad/backends/forward_laplacian.py:34-38). */
+#define FHB_ACTIVATION_TANH 0
+#define FHB_ACTIVATION_SILU 1
+
 const char* fhb_status_string(int code);
 /* Last CUDA runtime error seen by this library on the calling thread (cudaError_t). */
 int fhb_last_cuda_error(void);
@@ -86,6 +92,15 @@ int fhb_prepare_device(int device);
  */
 int fhb_forward(const float* coords, const float* params, float* u, float* lap, int64_t n,
                 int version, fhb_stream_t stream);
+/*
+ * fhb_forward with the hidden activation chosen (FHB_ACTIVATION_*); fhb_forward is this call
+ * with FHB_ACTIVATION_TANH. SiLU is the jet of the reference's PyTorch forward-Laplacian
+ * backend (src/fused_hoad/backends/forward_laplacian.py:34-38); versions 0..2 run the FP32
+ * kernel with it, versions 3..5 the 3xTF32 tensor-core kernel (SiLU's activations are
+ * unbounded, so the 3xFP16 operand scales, derived from weights alone, do not apply).
+ */
+int fhb_forward_ex(const float* coords, const float* params, float* u, float* lap, int64_t n,
+                   int version, int activation, fhb_stream_t stream);
 
 /*
  * Workspace the backward needs for n points on the current device, in bytes (0 for n==0),
@@ -109,6 +124,15 @@ size_t fhb_backward_workspace_bytes(int64_t n);
 int fhb_backward(const float* coords, const float* params, const float* grad_u,
                  const float* grad_lap, float* grad_params, float* grad_coords, int64_t n,
                  int version, void* workspace, size_t workspace_bytes, fhb_stream_t stream);
+/*
+ * fhb_backward with the hidden activation chosen; fhb_backward is this call with
+ * FHB_ACTIVATION_TANH. SiLU runs the FP32 CUDA-core adjoint kernel for every version (its
+ * adjoint needs the pre-activations, which that kernel keeps in registers).
+ */
+int fhb_backward_ex(const float* coords, const float* params, const float* grad_u,
+                    const float* grad_lap, float* grad_params, float* grad_coords, int64_t n,
+                    int version, int activation, void* workspace, size_t workspace_bytes,
+                    fhb_stream_t stream);
 
 /*
  * fhb_backward without a workspace argument: no counterpart in the reference (its backward
@@ -154,7 +178,8 @@ int fhb_poisson_step_gradients(const float* coords, const float* params, int64_t
  * n_boundary_total, grad_lap = 0), so one reduction gives grad_params[12737] and *loss of
  * both terms (this shard's contributions; the totals >= the local counts let data-parallel
  * shards sum to the global values). No counterpart entry in the reference, whose boundary
- * term is a separate eager forward and autograd backward. `version` as for fhb_backward.
+ * term is a separate eager forward and autograd backward. `version` as for fhb_backward,
+ * `activation` an FHB_ACTIVATION_* (SiLU runs the FP32 kernel).
  * Workspace: fhb_pinn_step_workspace_bytes(n, n_boundary) bytes, 16-byte aligned.
  */
 size_t fhb_pinn_step_workspace_bytes(int64_t n, int64_t n_boundary);
@@ -162,7 +187,8 @@ int fhb_pinn_step_gradients(const float* coords, int64_t n, int64_t n_total,
                             const float* boundary, int64_t n_boundary,
                             int64_t n_boundary_total, float boundary_weight,
                             const float* params, float* grad_params, float* loss, int version,
-                            void* workspace, size_t workspace_bytes, fhb_stream_t stream);
+                            int activation, void* workspace, size_t workspace_bytes,
+                            fhb_stream_t stream);
 
 /*
  * One Adam step on a flat buffer, torch.optim.Adam semantics (no weight decay, no amsgrad),
@@ -231,7 +257,8 @@ int fhb_exchange_destroy(fhb_exchange* exchange);
  * fhb_poisson_step_gradients), then one update kernel that sums the partial rows, sums over
  * the exchange's ranks and applies Adam (as fhb_adam_step) to params / exp_avg / exp_avg_sq /
  * step. grad_out (NULL or 12,738 floats) receives the global gradient and then the global
- * loss; loss_out (NULL or 1 float) the global loss. The totals are the global counts. If a
+ * loss; loss_out (NULL or 1 float) the global loss. `activation` is an FHB_ACTIVATION_*
+ * (SiLU runs the FP32 gradient kernel). The totals are the global counts. If a
  * peer wait gives up, FHB_STATUS_PEER_TIMEOUT is set, the parameters whose wait gave up are
  * left unchanged and the replicas are no longer consistent: stop or reload a checkpoint.
  * Workspace: fhb_pinn_step_workspace_bytes(n, n_boundary) bytes, 16-byte aligned.
@@ -240,8 +267,8 @@ int fhb_train_step(const float* coords, int64_t n, int64_t n_total, const float*
                    int64_t n_boundary, int64_t n_boundary_total, float boundary_weight,
                    float* params, float* exp_avg, float* exp_avg_sq, int64_t* step, float lr,
                    float beta1, float beta2, float eps, fhb_exchange* exchange,
-                   float* grad_out, float* loss_out, int version, void* workspace,
-                   size_t workspace_bytes, fhb_stream_t stream);
+                   float* grad_out, float* loss_out, int version, int activation,
+                   void* workspace, size_t workspace_bytes, fhb_stream_t stream);
 
 /* Reads and clears the status word of `device` (synchronises that device). */
 int fhb_read_device_status(int device, unsigned int* status_out);

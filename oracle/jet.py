@@ -8,7 +8,8 @@ Jet convention (``src/fused_hoad/backends/forward_laplacian.py:3-16``): each hid
 is ``[batch, dims + 2, width]`` = (value, d/dx_0, d/dx_1, Laplacian). A linear layer is one
 matmul with the bias added to the value row only (``:52-57``); tanh applies
 ``h_v = a, h_J = s z_J, h_L = s z_L - 2 a s |z_J|^2`` with ``a = tanh(z_v), s = 1 - a^2``
-(``:28-31, :60-67``).
+(``:28-31, :60-67``); SiLU applies ``h_v = phi, h_J = phi' z_J, h_L = phi' z_L +
+phi'' |z_J|^2`` with ``phi = z sigma(z)`` (``:34-38``).
 """
 
 from __future__ import annotations
@@ -76,6 +77,24 @@ def _tanh_jet(jet: Tensor) -> Tensor:
     return out
 
 
+def _silu_jet(jet: Tensor) -> Tensor:
+    # forward_laplacian.py:34-38 (_silu_jet) and :60-67 (_activation): phi = z sigma,
+    # phi' = sigma (1 + z (1 - sigma)), phi'' = sigma (1 - sigma) (2 + z (1 - 2 sigma))
+    z_v, z_j = jet[:, :1], jet[:, 1:-1]
+    sigma = torch.sigmoid(z_v)
+    first = sigma * (1.0 + z_v * (1.0 - sigma))
+    second = sigma * (1.0 - sigma) * (2.0 + z_v * (1.0 - 2.0 * sigma))
+    out = first * jet
+    out[:, -1:].add_(second * (z_j * z_j).sum(dim=1, keepdim=True))
+    out[:, :1].copy_(z_v * sigma)
+    return out
+
+
+# Hidden activations (reference src/fused_hoad/models.py:9-12) and their jets.
+ACTIVATION_JETS = {"tanh": _tanh_jet, "silu": _silu_jet}
+_ACTIVATION_FNS = {"tanh": torch.tanh, "silu": torch.nn.functional.silu}
+
+
 def _linear(jet: Tensor, weight: Tensor, bias: Tensor) -> Tensor:
     # forward_laplacian.py:52-57: bias on the value row only
     out = jet @ weight.T
@@ -83,8 +102,11 @@ def _linear(jet: Tensor, weight: Tensor, bias: Tensor) -> Tensor:
     return out
 
 
-def forward_laplacian_from_linears(linears, coords: Tensor) -> tuple[Tensor, Tensor]:
+def forward_laplacian_from_linears(
+    linears, coords: Tensor, activation: str = "tanh"
+) -> tuple[Tensor, Tensor]:
     """(u, lap) each ``[n, 1]``; forward_laplacian.py:84-92 with :116-132."""
+    act_jet = ACTIVATION_JETS[activation]
     n, dims = coords.shape
     jet = coords.new_zeros(n, dims + 2, dims)
     jet[:, 0] = coords
@@ -92,16 +114,20 @@ def forward_laplacian_from_linears(linears, coords: Tensor) -> tuple[Tensor, Ten
     for index, (weight, bias) in enumerate(linears):
         jet = _linear(jet, weight, bias)
         if index < len(linears) - 1:
-            jet = _tanh_jet(jet)
+            jet = act_jet(jet)
     return jet[:, 0], jet[:, -1]
 
 
-def forward_laplacian(params: Tensor, coords: Tensor) -> tuple[Tensor, Tensor]:
+def forward_laplacian(
+    params: Tensor, coords: Tensor, activation: str = "tanh"
+) -> tuple[Tensor, Tensor]:
     """Forward Laplacian of the packed MLP at ``coords [n, 2]`` in their dtype."""
-    return forward_laplacian_from_linears(unpack(params.to(coords.dtype)), coords)
+    return forward_laplacian_from_linears(unpack(params.to(coords.dtype)), coords, activation)
 
 
-def eager_laplacian(params: Tensor, coords: Tensor) -> tuple[Tensor, Tensor]:
+def eager_laplacian(
+    params: Tensor, coords: Tensor, activation: str = "tanh"
+) -> tuple[Tensor, Tensor]:
     """Nested-autograd Laplacian; src/fused_hoad/autodiff.py:16-40, reference.py:9-20."""
     linears = unpack(params.to(coords.dtype))
     x = coords.detach().clone().requires_grad_(True)
@@ -110,7 +136,7 @@ def eager_laplacian(params: Tensor, coords: Tensor) -> tuple[Tensor, Tensor]:
         for index, (weight, bias) in enumerate(linears):
             h = h @ weight.T + bias
             if index < len(linears) - 1:
-                h = torch.tanh(h)
+                h = _ACTIVATION_FNS[activation](h)
         (first,) = torch.autograd.grad(h.sum(), x, create_graph=True)
         lap = torch.zeros_like(h)
         for d in range(x.shape[1]):
@@ -120,7 +146,7 @@ def eager_laplacian(params: Tensor, coords: Tensor) -> tuple[Tensor, Tensor]:
 
 
 def recompute_backward(
-    params: Tensor, coords: Tensor, grad_u: Tensor, grad_lap: Tensor
+    params: Tensor, coords: Tensor, grad_u: Tensor, grad_lap: Tensor, activation: str = "tanh"
 ) -> tuple[Tensor, Tensor]:
     """(grad_params [12737], grad_coords [n, 2]); backends/fused.py:76-101.
 
@@ -131,7 +157,7 @@ def recompute_backward(
     with torch.enable_grad():
         x = coords.detach().clone().requires_grad_(True)
         flat = params.detach().to(dtype).clone().requires_grad_(True)
-        outputs = forward_laplacian_from_linears(unpack(flat), x)
+        outputs = forward_laplacian_from_linears(unpack(flat), x, activation)
         grad_x, grad_p = torch.autograd.grad(
             outputs,
             [x, flat],
@@ -152,7 +178,7 @@ def manufactured_source(coords: Tensor) -> Tensor:
 
 
 def poisson_step_gradients(
-    params: Tensor, coords: Tensor, total_points: int | None = None
+    params: Tensor, coords: Tensor, total_points: int | None = None, activation: str = "tanh"
 ) -> tuple[Tensor, Tensor, Tensor]:
     """Gradients of ``L = sum((lap - f)^2) / total_points`` (benchmark_training.py:46-48).
 
@@ -163,11 +189,13 @@ def poisson_step_gradients(
     """
     n = coords.shape[0]
     total = n if total_points is None else total_points
-    _, lap = forward_laplacian(params, coords)
+    _, lap = forward_laplacian(params, coords, activation)
     residual = lap - manufactured_source(coords)
     loss = (residual * residual).sum() / total
     grad_lap = 2.0 * residual / total
-    grad_p, grad_x = recompute_backward(params, coords, torch.zeros_like(lap), grad_lap)
+    grad_p, grad_x = recompute_backward(
+        params, coords, torch.zeros_like(lap), grad_lap, activation
+    )
     return loss, grad_p, grad_x
 
 
@@ -192,6 +220,7 @@ def pinn_step_gradients(
     interior_total: int | None = None,
     boundary_total: int | None = None,
     boundary_weight: float = 100.0,
+    activation: str = "tanh",
 ) -> tuple[Tensor, Tensor]:
     """Gradient of the Poisson PINN loss of src/fused_hoad/training.py:68-94:
     ``sum((lap - f)^2) / interior_total + boundary_weight * sum(u_b^2) / boundary_total``,
@@ -201,13 +230,13 @@ def pinn_step_gradients(
     """
     nb = boundary.shape[0]
     btotal = nb if boundary_total is None else boundary_total
-    loss_i, grad_i, _ = poisson_step_gradients(params, interior, interior_total)
+    loss_i, grad_i, _ = poisson_step_gradients(params, interior, interior_total, activation)
     if nb == 0:
         return loss_i, grad_i
-    u_b, _ = forward_laplacian(params, boundary)
+    u_b, _ = forward_laplacian(params, boundary, activation)
     loss_b = boundary_weight * (u_b * u_b).sum() / btotal
     grad_u = 2.0 * boundary_weight * u_b / btotal
-    grad_b, _ = recompute_backward(params, boundary, grad_u, torch.zeros_like(u_b))
+    grad_b, _ = recompute_backward(params, boundary, grad_u, torch.zeros_like(u_b), activation)
     return loss_i + loss_b, grad_i + grad_b
 
 

@@ -16,7 +16,11 @@ Imports ``fused_hoad`` from the reference checkout's ``src/`` (default: the path
   ``mean((lap - f)^2)`` (``benchmarks/benchmark_training.py:39-57``);
 * the full PINN loss of ``poisson_loss_fn`` (``src/fused_hoad/training.py:68-94``: interior
   residual + 100 * mean(u^2) on ``boundary_points``, ``:45-53``) through the FL backend, and
-  its parameter gradients.
+  its parameter gradients;
+* for the SiLU MLP (``MLPConfig(activation="silu")``, ``src/fused_hoad/models.py:9-12``): FL
+  forwards in FP32/FP64 and the FP64 eager Laplacian, an x3-scaled FP64 forward, FP64
+  gradients by autograd through FL (the reference's fused backward is tanh-only), and the
+  5-step Adam trajectory.
 
 Inputs come from CPU generators (points: seed 1, ``rand*2-1``; upstream grads: seed 2).
 The result is ``tests/golden/golden.npz``; nothing at test time reads the reference.
@@ -41,6 +45,8 @@ ADAM_BATCH = 512
 ADAM_STEPS = 5
 PINN_INTERIOR = 256
 PINN_BOUNDARY = 64
+SILU_FORWARD_BATCHES = (1, 33, 129, 1000)
+SILU_BACKWARD_BATCHES = (33, 1000)
 
 
 def main() -> None:
@@ -162,6 +168,68 @@ def main() -> None:
     out["pinn_x"], out["pinn_xb"] = xi.numpy(), xb.numpy()
     out["pinn_loss"] = np.array(loss.item(), dtype=np.float64)
     out["pinn_grad"] = torch.cat(grads).detach().numpy()
+
+    # SiLU (the reference's other activation: MLPConfig(activation="silu"), models.py:9-12,
+    # forward_laplacian.py:34-38). Its fused backend is tanh-only, so the gradients come from
+    # autograd through the reference's forward_laplacian on the SiLU model.
+    import dataclasses
+
+    silu_config = dataclasses.replace(DEFAULT_POISSON_MLP, activation="silu")
+
+    def silu_model(seed: int, scale: float = 1.0):
+        torch.manual_seed(seed)
+        m = build_mlp(silu_config).requires_grad_(False)
+        if scale != 1.0:
+            for p in m.parameters():
+                p.mul_(scale)
+        return m
+
+    ms = silu_model(0)
+    out["silu_params_seed0"] = pack_poisson_parameters(ms).numpy()
+    for n in SILU_FORWARD_BATCHES:
+        x = points(n)
+        u32, l32 = forward_laplacian(ms, x)
+        u64, l64 = forward_laplacian(ms.double(), x.double())
+        _, le64 = eager_laplacian(ms.double(), x.double())
+        ms.float()
+        out[f"silufwd{n}_x"] = x.numpy()
+        out[f"silufwd{n}_u32"], out[f"silufwd{n}_lap32"] = u32.numpy(), l32.numpy()
+        out[f"silufwd{n}_u64"], out[f"silufwd{n}_lap64"] = u64.numpy(), l64.numpy()
+        out[f"silufwd{n}_eager_lap64"] = le64.detach().numpy()
+    ms3 = silu_model(1, 3.0)
+    out["silu_params_seed1_x3"] = pack_poisson_parameters(ms3).numpy()
+    xs = points(SATURATED_BATCH)
+    u64, l64 = forward_laplacian(ms3.double(), xs.double())
+    out["silusat_x"], out["silusat_u64"], out["silusat_lap64"] = xs.numpy(), u64.numpy(), l64.numpy()
+
+    for n in SILU_BACKWARD_BATCHES:
+        grad_model = silu_model(0).double().requires_grad_(True)
+        x = points(n).double().requires_grad_(True)
+        gu, gl = upstream(n)
+        u, lap = forward_laplacian(grad_model, x)
+        torch.autograd.backward([u, lap], [gu.double(), gl.double()])
+        gp = torch.cat([torch.cat([grad_model[k].weight.grad.reshape(-1),
+                                   grad_model[k].bias.grad.reshape(-1)])
+                        for k in range(0, len(grad_model), 2)])
+        out[f"silubwd{n}_x"] = x.detach().float().numpy()
+        out[f"silubwd{n}_gu"], out[f"silubwd{n}_gl"] = gu.numpy(), gl.numpy()
+        out[f"silubwd{n}_gp64"] = gp.detach().numpy()
+        out[f"silubwd{n}_gx64"] = x.grad.detach().numpy()
+
+    train = silu_model(0).requires_grad_(True)
+    x = points(ADAM_BATCH)
+    source = manufactured_source(x)
+    optimizer = torch.optim.Adam(train.parameters(), lr=1e-3, betas=(0.9, 0.999))
+    losses = []
+    for _ in range(ADAM_STEPS):
+        optimizer.zero_grad()
+        _, lap = forward_laplacian(train, x)
+        loss = (lap - source).pow(2).mean()
+        loss.backward()
+        optimizer.step()
+        losses.append(loss.item())
+    out["siluadam_losses"] = np.array(losses, dtype=np.float64)
+    out["siluadam_params_final"] = pack_poisson_parameters(train).detach().numpy()
 
     np.savez_compressed(OUT, **out)
     print(f"wrote {OUT} ({OUT.stat().st_size / 1024:.0f} KiB, {len(out)} arrays)")

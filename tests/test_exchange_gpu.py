@@ -123,7 +123,7 @@ def test_train_step_through_the_c_abi_matches_the_oracle() -> None:
         for _ in range(2):
             code = lib.fhb_train_step(
                 ptr(x), len(x), len(x), None, 0, 0, 100.0, ptr(p), ptr(m), ptr(v), ptr(step),
-                1e-3, 0.9, 0.999, 1e-8, handle, None, ptr(loss), 6, ptr(ws), ws_bytes,
+                1e-3, 0.9, 0.999, 1e-8, handle, None, ptr(loss), 6, 0, ptr(ws), ws_bytes,
                 stream_handle())
             _native.check(code, "fhb_train_step")
     finally:
@@ -139,7 +139,7 @@ def test_train_step_through_the_c_abi_matches_the_oracle() -> None:
     # argument checks: a missing exchange and an unconnected one are rejected
     assert lib.fhb_train_step(ptr(x), len(x), len(x), None, 0, 0, 100.0, ptr(p), ptr(m),
                               ptr(v), ptr(step), 1e-3, 0.9, 0.999, 1e-8, None, None,
-                              ptr(loss), 6, ptr(ws), ws_bytes, stream_handle()) == 1
+                              ptr(loss), 6, 0, ptr(ws), ws_bytes, stream_handle()) == 1
 
 
 @pytest.mark.parametrize("kernel", [5, 6])

@@ -135,3 +135,64 @@ def test_known_answers() -> None:
     assert torch.all(u == 0.25) and torch.all(lap == 0.0)
     cu, cl = cjet.forward(params.numpy(), x.numpy())
     assert np.all(cu == 0.25) and np.all(cl == 0.0)
+
+
+# ---------------------------------------------------------------- SiLU (f rank 4) ----
+
+SILU_FORWARD_BATCHES = (1, 33, 129, 1000)
+
+
+def test_silu_parameters_match_reference_pack(golden) -> None:
+    # nn.Linear init does not depend on the activation module, so the SiLU MLP of seed 0
+    # packs to the tanh MLP's buffer
+    np.testing.assert_array_equal(golden["silu_params_seed0"], golden["params_seed0"])
+
+
+@pytest.mark.parametrize("n", SILU_FORWARD_BATCHES)
+def test_torch_oracle_silu_forward_matches_reference(golden, n: int) -> None:
+    params = torch.from_numpy(golden["silu_params_seed0"])
+    x = torch.from_numpy(golden[f"silufwd{n}_x"])
+    u, lap = jet.forward_laplacian(params, x, "silu")
+    np.testing.assert_allclose(u.numpy(), golden[f"silufwd{n}_u32"], rtol=1e-6, atol=1e-7)
+    np.testing.assert_allclose(lap.numpy(), golden[f"silufwd{n}_lap32"], rtol=1e-6, atol=1e-7)
+    u, lap = jet.forward_laplacian(params.double(), x.double(), "silu")
+    np.testing.assert_allclose(u.numpy(), golden[f"silufwd{n}_u64"], rtol=1e-12, atol=1e-14)
+    np.testing.assert_allclose(lap.numpy(), golden[f"silufwd{n}_lap64"], rtol=1e-12, atol=1e-14)
+    _, lap = jet.eager_laplacian(params.double(), x.double(), "silu")
+    np.testing.assert_allclose(lap.numpy(), golden[f"silufwd{n}_eager_lap64"], rtol=1e-10,
+                               atol=1e-12)
+
+
+def test_torch_oracle_silu_saturated_forward_matches_reference(golden) -> None:
+    params = torch.from_numpy(golden["silu_params_seed1_x3"]).double()
+    u, lap = jet.forward_laplacian(params, torch.from_numpy(golden["silusat_x"]).double(), "silu")
+    assert_scaled_close(u.numpy(), golden["silusat_u64"], 1e-12, "u")
+    assert_scaled_close(lap.numpy(), golden["silusat_lap64"], 1e-12, "lap")
+
+
+@pytest.mark.parametrize("n", (33, 1000))
+def test_torch_oracle_silu_backward_matches_reference(golden, n: int) -> None:
+    params = torch.from_numpy(golden["silu_params_seed0"]).double()
+    gp, gx = jet.recompute_backward(
+        params,
+        torch.from_numpy(golden[f"silubwd{n}_x"]).double(),
+        torch.from_numpy(golden[f"silubwd{n}_gu"]).double(),
+        torch.from_numpy(golden[f"silubwd{n}_gl"]).double(),
+        "silu",
+    )
+    assert_scaled_close(gp.numpy(), golden[f"silubwd{n}_gp64"], 1e-11, "grad params")
+    assert_scaled_close(gx.numpy(), golden[f"silubwd{n}_gx64"], 1e-11, "grad coords")
+
+
+def test_oracle_silu_adam_trajectory_matches_reference(golden) -> None:
+    p = torch.from_numpy(golden["silu_params_seed0"]).clone()
+    x = torch.from_numpy(golden["adam_x"])
+    m, v = torch.zeros_like(p), torch.zeros_like(p)
+    losses = []
+    for step in range(1, len(golden["siluadam_losses"]) + 1):
+        loss, grad, _ = jet.poisson_step_gradients(p, x, activation="silu")
+        losses.append(loss.item())
+        jet.adam_update(p, grad, m, v, step)
+    np.testing.assert_allclose(losses, golden["siluadam_losses"], rtol=1e-5)
+    diff = np.abs(p.numpy() - golden["siluadam_params_final"])
+    assert np.mean(diff > 1e-6) < 1e-3, float(diff.max())
