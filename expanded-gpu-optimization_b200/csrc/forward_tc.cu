@@ -10,26 +10,26 @@
 // split x = hi + lo into two low-precision parts and three products per product:
 //   * 3xTF32 (kind::tf32, K = 8): hi = tf32(x), lo = x - hi;
 //     Z += H_hi W_hi + H_lo W_hi + H_hi W_lo; a 16-neuron chunk is 24 MMAs;
-//   * 3xFP16 (kind::f16, K = 16): hi = f16(x), lo' = f16(2^11 (x - hi)) -- 11 + 11 significant
-//     bits, the precision of the tf32 split --; D = H_hi (2^11 W_hi) + H_lo' W_hi + H_hi W_lo'
-//     = 2^11 H W; a chunk is 12 MMAs and writes half the bytes into TMEM. The tf32 form spends
-//     its layer time on the MMAs and on the TMEM traffic between the chunk stores and the MMAs
-//     (a chunk's 24 MMAs take 0.57-0.74 us instead of 0.39 us while 16 warps store the next
-//     chunk), which this halves.
-//     Range: f16 holds magnitudes below 65,504, and the Laplacian jet grows fast with the
-//     weight scale. Each launch derives power-of-2 scales from the weights: tau_l maps
-//     max|W_l| to <= 16 (so 2^11 W_hi stays finite); sigma_{l,c} maps an upper bound of
-//     component c of GEMM l's A operand to <= 2^14. They are applied before the split and
-//     removed exactly from the accumulators (times 1 / (2^11 sigma tau), a power of 2). The
-//     bounds: |v| <= 1; |dv/dx|, |dv/dy| grow by N_l = max row-abs-sum of W_l per layer; |Lv|
-//     becomes N_l |Lv| + (N_l Bx)^2 + (N_l By)^2 (tanh' <= 1 and 2 |tanh tanh'| <= 1). A value
-//     keeps full relative precision until it is 2^28 times below its bound. The scales depend
-//     on the weights only (fixed-order warp reductions), so every CTA and every shard of a
-//     batch uses the same ones.
+//   * 3xFP16 (kind::f16, K = 16): hi = x rounded to 11 significant bits (tf32 rounding, exact
+//     in f16), lo = f16(x - hi) -- 11 + 11 significant bits, the precision of the tf32 split --;
+//     Z += H_hi W_hi + H_lo W_hi + H_hi W_lo; a chunk is 12 MMAs and writes half the bytes into
+//     TMEM. The tf32 form spends its layer time on the MMAs and on the TMEM traffic between the
+//     chunk stores and the MMAs (a chunk's 24 MMAs take 0.57-0.74 us instead of 0.39 us while
+//     16 warps store the next chunk), which this halves.
+//     Range: f16 holds magnitudes below 65,504 (normal from 2^-14), and the Laplacian jet grows
+//     fast with the weight scale. Each launch derives power-of-2 scales from the weights:
+//     tau_l maps max|W_l| to <= 16; sigma_{l,c} maps an upper bound of component c of GEMM l's
+//     A operand to <= 2^14, so lo stays a normal f16 for every value within 2^17 of its bound
+//     and the rest lose at most 2^-25 (scaled units). The bounds: |v| <= 1; |dv/dx|, |dv/dy|
+//     grow by N_l = max row-abs-sum of W_l per layer; |Lv| becomes N_l |Lv| + 2 (N_l B_J)^2
+//     (tanh' <= 1 and 2 |tanh tanh'| <= 1). The epilogue folds the scales into the jet
+//     arithmetic (F16Consts: accumulators times exact powers of 2 in, the next GEMM's scaled
+//     operand out). The scales depend on the weights only (fixed-order warp reductions), so
+//     every CTA and every shard of a batch uses the same ones.
 //
 // Where the data lives (per CTA, one CTA per SM, persistent over tiles):
 //   * weights: all three hidden layers pre-split once per CTA into the K-major no-swizzle
-//     canonical layout in shared memory (tf32: hi, lo, 96 KB; f16: 2^11 hi, hi, lo', 72 KB);
+//     canonical layout in shared memory (hi, lo; tf32 96 KB, f16 48 KB);
 //   * TMEM (512 columns x 128 lanes, lane = point):
 //       [0, 256)   accumulators D_c, component c at columns 64c..64c+63;
 //       [256, 512) a ring of A-operand chunks; a chunk is 16 input neurons of the next
@@ -75,7 +75,6 @@ constexpr int kChunks = 4;            // chunks of 16 neurons per 64-wide layer
 constexpr int kChunksPerTile = kHiddenGemms * kChunks;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kRingCol = 256;
-constexpr float kLoScale = 2048.0f;   // f16: lo' = 2^11 (x - hi)
 constexpr uint32_t kLbo = 128;        // K-adjacent core matrices of the canonical layout
 
 // Operand formats. One [64 x 64] weight operand is kOperandBytes in the K-major no-swizzle
@@ -95,10 +94,10 @@ struct Format<false> {  // 3xTF32, kind::tf32, K = 8 per MMA
 template <>
 struct Format<true> {  // 3xFP16, kind::f16, K = 16 per MMA
   static constexpr int kRing = 4;
-  static constexpr uint32_t kSlotCols = 64;   // 4 components x {hi, lo'} x 8 columns of pairs
+  static constexpr uint32_t kSlotCols = 64;   // 4 components x {hi, lo} x 8 columns of pairs
   static constexpr uint32_t kIdesc = tc::idesc_f16(128, 64);
   static constexpr int kOperandBytes = kWidth * kWidth * 2;  // 8 KB
-  static constexpr int kOperands = 3;                        // 2^11 W_hi, W_hi, W_lo'
+  static constexpr int kOperands = 2;                        // W_hi, W_lo (tau-scaled)
   static constexpr uint32_t kSbo = 1024;
 };
 
@@ -110,8 +109,8 @@ struct Layout {
   static constexpr int kBarOff = kRedOff + 8 * kTile * 4;  // mbarriers: empty[kRing], dfull, red
   static constexpr int kCountOff = kBarOff + 8 * 8;        // per-slot contribution counters
   static constexpr int kMiscOff = kCountOff + 4 * 4;       // TMEM base, abort flag
-  static constexpr int kScaleOff = kMiscOff + 16;          // f16: sigma[3][4], unscale[3][4], tau[3]
-  static constexpr int kSmemUsed = kScaleOff + 32 * 4;
+  static constexpr int kScaleOff = kMiscOff + 16;          // f16: F16Consts
+  static constexpr int kSmemUsed = kScaleOff + 256 * 4;
 };
 constexpr int kSmW0 = 0, kSmB0 = 128, kSmB = 192, kSmWout = 384, kSmBout = 448;
 constexpr int kSmallFloats = 512;
@@ -130,8 +129,25 @@ struct Ctx {
   volatile uint32_t* abort_flag;
   unsigned int* status;
   uint32_t tmem;
-  const float* sigma;         // f16: [3][4] A-operand scale of GEMM l, component c (power of 2)
-  const float* unscale;       // f16: [3][4] 1 / (2^11 sigma tau) for the accumulators of GEMM l
+  const float* f16c;          // f16: the F16Consts words
+};
+
+// f16 scale constants in shared memory (floats at Layout::kScaleOff). GEMM l's A operand,
+// component c, is the true activation times sigma[l][c] (a power of 2; sigma_x = sigma_y),
+// its weights are times tau[l], so its accumulators are the true products times
+// sigma tau. The epilogue of GEMM l (l = 0, 1) turns accumulators D straight into the next
+// GEMM's scaled operand: with us = 1 / (sigma_l tau_l) and s' = sigma_{l+1},
+//   z_v = D_v us_v + b,  a = tanh z_v = 1 - 2r,  s = 1 - a^2,
+//   v' = s'_v a,  J' = s (s'_J us_J) D_J,  L' = s (s'_L us_L D_L - 2 s'_L us_J^2 a |D_J|^2).
+struct F16Consts {
+  static constexpr int kUnscale = 0;   // [3][4] 1 / (sigma tau) of GEMM l's accumulators
+  static constexpr int kTau = 12;      // [3]
+  static constexpr int kEpi = 16;      // [2][4]: s'_v, s'_J us_J, s'_L us_L, -2 s'_L us_J^2
+  static constexpr int kSigma0 = 24;   // s_v of GEMM 0 (layer-0 jets)
+  static constexpr int kW0 = 32;       // [64] sigma_J0 W0[o][0]
+  static constexpr int kW1 = 96;       // [64] sigma_J0 W0[o][1]
+  static constexpr int kC0 = 160;      // [64] -2 sigma_L0 (W0[o][0]^2 + W0[o][1]^2)
+  static constexpr int kWords = 224;
 };
 
 // Bounded wait that also gives up when another warp has aborted the CTA.
@@ -168,38 +184,46 @@ __device__ __forceinline__ float pow2_floor(float x) {
   return __uint_as_float(__float_as_uint(x) & 0x7F800000u);
 }
 
-// f16 pairs of the A operand: hi = f16(x) and lo' = f16(2^11 (x - hi)), element a (even K)
-// in the low half.
-__device__ __forceinline__ uint32_t pack_hi(float a, float b) {
-  const __half2 h = __floats2half2_rn(a, b);
-  return *reinterpret_cast<const uint32_t*>(&h);
+// f16 pairs of a split: hi = x rounded to 11 significant bits (tf32 rounding; exact in f16
+// inside the scaled range), lo = x - hi (exact in FP32, rounded to f16); element a (even K)
+// in the low halves. Values below f16's normal range (2^-14, 2^28 below a scaled bound) lose
+// precision, an absolute error of at most 2^-25 in scaled units.
+__device__ __forceinline__ void split_f16_pair(float a, float b, uint32_t& hi, uint32_t& lo) {
+  const float ha = __uint_as_float(tc::to_tf32(a)), hb = __uint_as_float(tc::to_tf32(b));
+  const __half2 h = __floats2half2_rn(ha, hb);
+  const __half2 l = __floats2half2_rn(a - ha, b - hb);
+  hi = *reinterpret_cast<const uint32_t*>(&h);
+  lo = *reinterpret_cast<const uint32_t*>(&l);
 }
-__device__ __forceinline__ uint32_t pack_lo(float a, float b) {
-  const float ha = __half2float(__float2half_rn(a)), hb = __half2float(__float2half_rn(b));
-  const __half2 h = __floats2half2_rn((a - ha) * kLoScale, (b - hb) * kLoScale);
-  return *reinterpret_cast<const uint32_t*>(&h);
+
+// tanh through 1 - 2r, r = 1 / (exp(2x) + 1) on the special-function unit (tanh_fast's
+// formula, which returns 1 - 2r): the f16 epilogue folds its operand scale into 1 - 2r.
+__device__ __forceinline__ float tanh_fast_r(float x) {
+  float e, r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(x * 2.8853900817779268f));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(e + 1.0f));
+  return r;
 }
 
 // The MMAs of chunk j (input neurons 16j..16j+15) of hidden GEMM `layer`, A from ring slot
 // `slot`, then a commit that frees the slot (and after the 4th chunk one that marks D
 // complete). tf32: 2 K steps x 4 components x (H_hi W_hi + H_lo W_hi + H_hi W_lo), A block
 // (component c, hi/lo sp, K step kk) at columns 32c + 16sp + 8kk of the slot. f16: 4
-// components x (H_hi 2^11 W_hi + H_lo' W_hi + H_hi W_lo'), A block (c, sp) at 16c + 8sp.
+// components x (H_hi W_hi + H_lo W_hi + H_hi W_lo), A block (c, sp) at 16c + 8sp.
 template <bool F16>
 __device__ __forceinline__ void issue_chunk_mmas(const Ctx& cx, int layer, int j, uint32_t slot) {
   using F = Format<F16>;
   const uint32_t slot_col = cx.tmem + kRingCol + F::kSlotCols * slot;
   if constexpr (F16) {
-    const uint32_t w0 = smem_u32(cx.smem + (3 * layer) * F::kOperandBytes + 256 * j);
-    const uint64_t b_hs = tc::smem_desc_kmajor(w0, kLbo, F::kSbo);
-    const uint64_t b_hi = tc::smem_desc_kmajor(w0 + F::kOperandBytes, kLbo, F::kSbo);
-    const uint64_t b_lo = tc::smem_desc_kmajor(w0 + 2 * F::kOperandBytes, kLbo, F::kSbo);
+    const uint32_t w0 = smem_u32(cx.smem + (2 * layer) * F::kOperandBytes + 256 * j);
+    const uint64_t b_hi = tc::smem_desc_kmajor(w0, kLbo, F::kSbo);
+    const uint64_t b_lo = tc::smem_desc_kmajor(w0 + F::kOperandBytes, kLbo, F::kSbo);
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
       const uint32_t d = cx.tmem + 64u * c;
       const uint32_t a_hi = slot_col + 16u * c;
       const uint32_t a_lo = a_hi + 8u;
-      tc::mma_f16_ts_warp(d, a_hi, b_hs, F::kIdesc, j > 0 ? 1u : 0u);
+      tc::mma_f16_ts_warp(d, a_hi, b_hi, F::kIdesc, j > 0 ? 1u : 0u);
       tc::mma_f16_ts_warp(d, a_lo, b_hi, F::kIdesc, 1u);
       tc::mma_f16_ts_warp(d, a_hi, b_lo, F::kIdesc, 1u);
     }
@@ -225,8 +249,8 @@ __device__ __forceinline__ void issue_chunk_mmas(const Ctx& cx, int layer, int j
   if (j == kChunks - 1) tc::commit_warp(cx.dfull);
 }
 
-// Write chunk `n` (this warp's 4 neurons x 4 components as hi/lo parts; f16: scaled by sigma
-// of their GEMM first) into ring slot n % kRing; the warp completing the chunk last issues its
+// Write chunk `n` (this warp's 4 neurons x 4 components as hi/lo parts; f16: h is already
+// the scaled operand) into ring slot n % kRing; the warp completing the chunk last issues its
 // MMAs. False if aborted.
 template <bool F16>
 __device__ __forceinline__ bool produce_chunk(uint32_t n, const float (&h)[4][4],
@@ -238,13 +262,13 @@ __device__ __forceinline__ bool produce_chunk(uint32_t n, const float (&h)[4][4]
   const uint32_t slot_col = tmem_warp + kRingCol + F::kSlotCols * slot;
   if constexpr (F16) {
     const uint32_t base = slot_col + 2u * s;
-    const float* sig = cx.sigma + 4 * ((n % kChunksPerTile) / kChunks);
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
-      const float g = sig[c];
-      const float a0 = h[c][0] * g, a1 = h[c][1] * g, a2 = h[c][2] * g, a3 = h[c][3] * g;
-      tc::st_x2(base + 16u * c, pack_hi(a0, a1), pack_hi(a2, a3));
-      tc::st_x2(base + 16u * c + 8u, pack_lo(a0, a1), pack_lo(a2, a3));
+      uint32_t hi0, lo0, hi1, lo1;
+      split_f16_pair(h[c][0], h[c][1], hi0, lo0);
+      split_f16_pair(h[c][2], h[c][3], hi1, lo1);
+      tc::st_x2(base + 16u * c, hi0, hi1);
+      tc::st_x2(base + 16u * c + 8u, lo0, lo1);
     }
   } else {
     const uint32_t base = slot_col + 4u * s;
@@ -316,23 +340,25 @@ __device__ __forceinline__ void stage_tf32(const float* __restrict__ params, uin
   small[threadIdx.x] = sv;
 }
 
-// f16 set-up: the small parameters, the operand scales, then the split of the hidden weights
-// into 2^11 W_hi, W_hi and W_lo' (tau-scaled). Every load is issued before any is used (one
-// memory round trip): the small parameter, 24 values for the weight-row statistics and 12
-// pairs for the split. Power-of-2 scales keep every f16 operand in range: tau_l maps
-// max|W_l| to <= 16 (so 2^11 W_hi stays finite); sigma_{l,c} maps a bound of component c of
-// the A operand of GEMM l to <= 2^14. Bounds: |v| <= 1; |d/dx|, |d/dy| grow by N_l (max
-// row-abs-sum of W_l) per layer; |L| becomes N_l |L| + (N_l Bx)^2 + (N_l By)^2 (tanh' <= 1,
-// 2 |tanh tanh'| <= 1). Row statistics are fixed-order warp reductions, so every CTA derives
-// the same scales. Contains two block-wide barriers.
+// f16 set-up: the small parameters, the operand scales and the epilogue constants
+// (F16Consts), then the split of the tau-scaled hidden weights into W_hi and W_lo. Every load
+// is issued before any is used (one memory round trip): the small parameter, 24 values for the
+// weight-row statistics and 12 pairs for the split. Power-of-2 scales keep every f16 operand
+// in range: tau_l maps max|W_l| to <= 16; sigma_{l,c} maps a bound of component c of GEMM l's
+// A operand to <= 2^14 (one sigma for d/dx and d/dy, from the larger bound). Bounds: |v| <= 1;
+// |d/dx|, |d/dy| grow by N_l (max row-abs-sum of W_l) per layer; |L| becomes
+// N_l |L| + (N_l Bx)^2 + (N_l By)^2 (tanh' <= 1, 2 |tanh tanh'| <= 1). Row statistics are
+// fixed-order warp reductions, so every CTA derives the same scales. Contains two block-wide
+// barriers.
 __device__ __forceinline__ void stage_f16(const float* __restrict__ params, uint8_t* smem,
-                                          float* small, float* red, float* scales, int warp,
+                                          float* small, float* red, float* cst, int warp,
                                           int lane) {
   using F = Format<true>;
   constexpr int kStatRows = 3 * kWidth / kWarps;                   // 12 rows per warp
   constexpr int kPairs = kHiddenGemms * kWidth * kWidth / 2;       // 6144
   constexpr int kPairsPerThread = kPairs / kThreads;               // 12
   static_assert(kPairs % kThreads == 0, "whole pairs per thread");
+  using C = F16Consts;
   float wp[kPairsPerThread][2];
   {
     const float sv = small_param(params, threadIdx.x);
@@ -366,6 +392,7 @@ __device__ __forceinline__ void stage_f16(const float* __restrict__ params, uint
     small[threadIdx.x] = sv;
   }
   __syncthreads();
+  float* sigma = red + 512;  // [3][4] scratch for the layer-0 constants below
   if (warp == 0) {
     float nrm[3], wmax[3];
 #pragma unroll
@@ -375,43 +402,59 @@ __device__ __forceinline__ void stage_f16(const float* __restrict__ params, uint
     }
     const float w0x = small[kSmW0 + 2 * lane], w0y = small[kSmW0 + 2 * lane + 1];
     const float w0x2 = small[kSmW0 + 2 * (lane + 32)], w0y2 = small[kSmW0 + 2 * (lane + 32) + 1];
-    float bx = warp_max(fmaxf(fabsf(w0x), fabsf(w0x2)));
-    float by = warp_max(fmaxf(fabsf(w0y), fabsf(w0y2)));
+    float bj = warp_max(fmaxf(fmaxf(fabsf(w0x), fabsf(w0x2)), fmaxf(fabsf(w0y), fabsf(w0y2))));
     float bl = warp_max(fmaxf(fmaf(w0x, w0x, w0y * w0y), fmaf(w0x2, w0x2, w0y2 * w0y2)));
     if (lane == 0) {
+      float tau[3], sig[3][3];  // sig[l]: v, J, L
       for (int l = 0; l < 3; ++l) {
-        const float tau = pow2_floor(16.0f / fmaxf(wmax[l], 1e-30f));
-        const float bnd[4] = {1.0f, bx, by, bl};
-        for (int c = 0; c < 4; ++c) {
-          const float sig = pow2_floor(16384.0f / fmaxf(bnd[c], 1e-30f));
-          scales[4 * l + c] = sig;
-          scales[12 + 4 * l + c] = 1.0f / (kLoScale * sig * tau);
-        }
-        scales[24 + l] = tau;
-        const float nx = nrm[l] * bx, ny = nrm[l] * by;
-        bl = fmaf(nrm[l], bl, fmaf(nx, nx, ny * ny));
-        bx = nx;
-        by = ny;
+        tau[l] = pow2_floor(16.0f / fmaxf(wmax[l], 1e-30f));
+        sig[l][0] = pow2_floor(16384.0f);
+        sig[l][1] = pow2_floor(16384.0f / fmaxf(bj, 1e-30f));
+        sig[l][2] = pow2_floor(16384.0f / fmaxf(bl, 1e-30f));
+        const float nj = nrm[l] * bj;
+        bl = fmaf(nrm[l], bl, 2.0f * nj * nj);
+        bj = nj;
       }
+      for (int l = 0; l < 3; ++l) {
+        const float us[3] = {1.0f / (sig[l][0] * tau[l]), 1.0f / (sig[l][1] * tau[l]),
+                             1.0f / (sig[l][2] * tau[l])};
+        cst[C::kUnscale + 4 * l + 0] = us[0];
+        cst[C::kUnscale + 4 * l + 1] = us[1];
+        cst[C::kUnscale + 4 * l + 2] = us[1];
+        cst[C::kUnscale + 4 * l + 3] = us[2];
+        cst[C::kTau + l] = tau[l];
+        if (l < 2) {
+          cst[C::kEpi + 4 * l + 0] = sig[l + 1][0];
+          cst[C::kEpi + 4 * l + 1] = sig[l + 1][1] * us[1];
+          cst[C::kEpi + 4 * l + 2] = sig[l + 1][2] * us[2];
+          cst[C::kEpi + 4 * l + 3] = -2.0f * sig[l + 1][2] * us[1] * us[1];
+        }
+      }
+      cst[C::kSigma0] = sig[0][0];
+      sigma[0] = sig[0][1];
+      sigma[1] = sig[0][2];
     }
   }
   __syncthreads();
+  if (threadIdx.x < kWidth) {  // layer-0 jets: J = W0 columns, L = -2 a s |W0 row|^2
+    const int o = threadIdx.x;
+    const float w0 = small[kSmW0 + 2 * o], w1 = small[kSmW0 + 2 * o + 1];
+    cst[C::kW0 + o] = sigma[0] * w0;
+    cst[C::kW1 + o] = sigma[0] * w1;
+    cst[C::kC0 + o] = -2.0f * sigma[1] * fmaf(w0, w0, w1 * w1);
+  }
   // The split: pairs of adjacent K elements, enumerated (row group, K chunk of 8, row in
   // group, K pair) so consecutive threads store consecutive words of the canonical layout.
 #pragma unroll
   for (int k = 0; k < kPairsPerThread; ++k) {
     const int idx = threadIdx.x + k * kThreads;
     const int layer = idx >> 11, e = (idx & 2047) * 2;
-    const float tau = scales[24 + layer];
-    const float a = wp[k][0] * tau, b = wp[k][1] * tau;
-    const __half2 hi = __floats2half2_rn(a, b);
-    const float2 hf = __half22float2(hi);
-    const __half2 hs = __floats2half2_rn(hf.x * kLoScale, hf.y * kLoScale);
-    const __half2 lo = __floats2half2_rn((a - hf.x) * kLoScale, (b - hf.y) * kLoScale);
-    uint8_t* base = smem + (3 * layer) * F::kOperandBytes + 2 * e;
-    *reinterpret_cast<__half2*>(base) = hs;
-    *reinterpret_cast<__half2*>(base + F::kOperandBytes) = hi;
-    *reinterpret_cast<__half2*>(base + 2 * F::kOperandBytes) = lo;
+    const float tau = cst[C::kTau + layer];
+    uint32_t hi, lo;
+    split_f16_pair(wp[k][0] * tau, wp[k][1] * tau, hi, lo);
+    uint8_t* base = smem + (2 * layer) * F::kOperandBytes + 2 * e;
+    *reinterpret_cast<uint32_t*>(base) = hi;
+    *reinterpret_cast<uint32_t*>(base + F::kOperandBytes) = lo;
   }
 }
 
@@ -437,8 +480,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   cx.count = reinterpret_cast<uint32_t*>(smem + L::kCountOff);
   cx.abort_flag = reinterpret_cast<volatile uint32_t*>(smem + L::kMiscOff + 4);
   cx.status = status;
-  cx.sigma = reinterpret_cast<const float*>(smem + L::kScaleOff);
-  cx.unscale = cx.sigma + 12;
+  cx.f16c = reinterpret_cast<const float*>(smem + L::kScaleOff);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -502,7 +544,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
 
-    // layer 0: z = W0 x + b0, z_J = W0 columns, z_L = 0
+    // layer 0: z = W0 x + b0, z_J = W0 columns, z_L = 0 (f16: the scaled operand directly)
 #pragma unroll
     for (int j = 0; j < kChunks; ++j) {
       float h[4][4];
@@ -510,8 +552,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int t = 0; t < 4; ++t) {
         const int o = 16 * j + 4 * s + t;
         const float w0 = small[kSmW0 + 2 * o], w1 = small[kSmW0 + 2 * o + 1];
-        Act::jet_fast(fmaf(w0, x0, fmaf(w1, x1, small[kSmB0 + o])), w0, w1, 0.0f, h[0][t],
-                      h[1][t], h[2][t], h[3][t]);
+        const float z = fmaf(w0, x0, fmaf(w1, x1, small[kSmB0 + o]));
+        if constexpr (F16) {
+          using C = F16Consts;
+          const float r = tanh_fast_r(z), sv = cx.f16c[C::kSigma0];
+          const float a = fmaf(-2.0f, r, 1.0f), sd = fmaf(-a, a, 1.0f);
+          h[0][t] = fmaf(-2.0f * sv, r, sv);
+          h[1][t] = sd * cx.f16c[C::kW0 + o];
+          h[2][t] = sd * cx.f16c[C::kW1 + o];
+          h[3][t] = cx.f16c[C::kC0 + o] * (a * sd);
+        } else {
+          Act::jet_fast(z, w0, w1, 0.0f, h[0][t], h[1][t], h[2][t], h[3][t]);
+        }
       }
       if (!(ok = produce_chunk<F16>(chunk++, h, tmem_warp, s, cx))) break;
     }
@@ -529,17 +581,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                     *reinterpret_cast<float(*)[4]>(&d[c][4 * a]));
       tc::wait_ld();
       const float* bias = small + kSmB + 64 * l;
-      if constexpr (F16) {  // remove the operand scales: an exact power of 2
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const float us = cx.unscale[4 * l + c];
-#pragma unroll
-          for (int i = 0; i < 16; ++i) d[c][i] *= us;
-        }
-      }
-#pragma unroll
-      for (int i = 0; i < 16; ++i) d[0][i] += bias[16 * (i >> 2) + 4 * s + (i & 3)];
-
       if (l + 1 < kHiddenGemms) {
 #pragma unroll
         for (int j = 0; j < kChunks; ++j) {
@@ -547,12 +588,36 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int t = 0; t < 4; ++t) {
             const int i = 4 * j + t;
-            Act::jet_fast(d[0][i], d[1][i], d[2][i], d[3][i], h[0][t], h[1][t], h[2][t],
-                          h[3][t]);
+            const float b = bias[16 * j + 4 * s + t];
+            if constexpr (F16) {  // accumulators -> the next GEMM's scaled operand
+              using C = F16Consts;
+              const float* e = cx.f16c + C::kEpi + 4 * l;
+              const float r = tanh_fast_r(fmaf(d[0][i], cx.f16c[C::kUnscale + 4 * l], b));
+              const float a = fmaf(-2.0f, r, 1.0f), sd = fmaf(-a, a, 1.0f);
+              const float sk = sd * e[1];
+              const float q = fmaf(d[1][i], d[1][i], d[2][i] * d[2][i]);
+              h[0][t] = fmaf(-2.0f * e[0], r, e[0]);
+              h[1][t] = sk * d[1][i];
+              h[2][t] = sk * d[2][i];
+              h[3][t] = sd * fmaf(e[3] * a, q, e[2] * d[3][i]);
+            } else {
+              Act::jet_fast(d[0][i] + b, d[1][i], d[2][i], d[3][i], h[0][t], h[1][t],
+                            h[2][t], h[3][t]);
+            }
           }
           if (!(ok = produce_chunk<F16>(chunk++, h, tmem_warp, s, cx))) break;
         }
       } else {
+        if constexpr (F16) {  // remove the operand scales: exact powers of 2
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const float us = cx.f16c[F16Consts::kUnscale + 4 * l + c];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) d[c][i] *= us;
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < 16; ++i) d[0][i] += bias[16 * (i >> 2) + 4 * s + (i & 3)];
         // output layer: u = w.v + b, lap = w.L, over this warp's 16 neurons
         float pu = 0.0f, pl = 0.0f;
 #pragma unroll
