@@ -50,7 +50,7 @@ UNIT = "pts/s"
 FLOP_FORWARD = 101_888  # per point: 3 hidden 64x64 jet GEMMs x 4 comps + layer 0/out + tanh jet
 FLOP_STEP = 98_304 * 3 + 256 * 2 + 6_000  # forward + input adjoint + weight gradient + small
 POINTS_PER_GPU = 65_536
-F16_TRAFFIC = 657_920  # DRAM bytes of one version-3 launch at 65,536 points (ncu)
+F16_TRAFFIC = 656_896  # DRAM bytes of one version-3 launch at 65,536 points (ncu)
 FLUSH_BYTES = 192 << 20
 PEAKS_FILE = ROOT / "MEASURED_PEAKS.json"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
