@@ -32,6 +32,8 @@ TC_VERSIONS = [3, 4, 5]  # 3: 3xFP16 kernel; 4, 5: 3xTF32 kernel
 ALL_VERSIONS = FP32_VERSIONS + TC_VERSIONS
 BATCHES = [1, 2, 31, 32, 33, 63, 64, 65, 127, 128, 129, 1_000, 65_536]
 ROUTES = ["capi", "torch"]
+# backward kernels: version 5 runs the FP32 CUDA-core kernel, 6 the tensor-core one
+BACKWARD_KERNELS = [pytest.param(5, id="fp32"), pytest.param(6, id="tc")]
 
 
 @pytest.fixture(scope="module", autouse=True)
@@ -182,6 +184,47 @@ def test_forward_large_batches_sampled_against_oracle(batch: int, version: int) 
     assert torch.isfinite(lap).all()
 
 
+@pytest.mark.parametrize("version", [2, 3, 4])
+def test_forward_at_the_largest_config_size(version: int) -> None:
+    """16,777,216 points (config 3's largest, one GPU): a strided sample against the oracle,
+    and pointwise evaluation -- a shard evaluated alone gives bitwise the full batch's
+    values."""
+    batch = 16_777_216
+    params = _params()
+    coords = uniform_points(batch, seed=7).cuda()
+    u, lap = fused_forward_laplacian(coords, params, version)
+    idx = torch.arange(0, batch, batch // 4096 + 7, device="cuda")
+    eu, el = _oracle_forward(params, coords[idx])
+    torch.testing.assert_close(lap[idx].cpu(), el, atol=1e-5, rtol=1e-4)
+    torch.testing.assert_close(u[idx].cpu(), eu, atol=1e-5, rtol=1e-4)
+    a, b = 5_000_003, 5_131_077
+    su, sl = fused_forward_laplacian(coords[a:b].contiguous(), params, version)
+    assert torch.equal(su, u[a:b]) and torch.equal(sl, lap[a:b])
+    assert bool(torch.isfinite(u).all() and torch.isfinite(lap).all())
+
+
+@pytest.mark.parametrize("kernel", BACKWARD_KERNELS)
+def test_step_at_the_per_gpu_config_size(kernel: int) -> None:
+    """2,097,152 points (config 4's batch per GPU at 8 GPUs): the fused step's loss equals
+    the loss formed from the forward kernel's Laplacian, and the gradient equals the sum of
+    the gradients of four shards."""
+    n = 2_097_152
+    params = _params()
+    coords = uniform_points(n, seed=8).cuda()
+    C = fused_hoad.load_extension()
+    full = C.poisson_step_gradients(coords, params, n, version=kernel)[0]
+    _, lap = fused_forward_laplacian(coords, params, 4)
+    f = fused_hoad.manufactured_source(coords)
+    loss = ((lap.double() - f.double()) ** 2).sum() / n
+    np.testing.assert_allclose(full[-1].item(), loss.item(), rtol=1e-5)
+    parts = torch.zeros_like(full)
+    for r in range(4):
+        a, b = fused_hoad.shard_range(n, r, 4)
+        parts += C.poisson_step_gradients(coords[a:b].contiguous(), params, n, version=kernel)[0]
+    assert_scaled(parts[:-1].cpu(), full[:-1].cpu(), 1e-5, "grad")
+    assert bool(torch.isfinite(full).all())
+
+
 def test_backend_repacks_after_in_place_weight_update() -> None:
     torch.manual_seed(0)
     model = build_mlp().cuda().requires_grad_(False)
@@ -206,8 +249,6 @@ def test_inference_path_stays_out_of_autograd() -> None:
 # ---------------------------------------------------------------- backward ----
 
 BACKWARD_BATCHES = [1, 15, 16, 17, 31, 32, 33, 127, 128, 129, 1_000, 65_536]
-# Backward kernels: 5 = FP32 CUDA-core kernel (versions 1..5), 6 = tensor-core kernel.
-BACKWARD_KERNELS = [pytest.param(5, id="fp32"), pytest.param(6, id="tc")]
 
 
 def _upstream(batch: int, seed: int = 2):
