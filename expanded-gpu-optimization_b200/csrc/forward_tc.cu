@@ -29,7 +29,10 @@
 //
 // Where the data lives (per CTA, one CTA per SM, persistent over tiles):
 //   * weights: all three hidden layers pre-split once per CTA into the K-major no-swizzle
-//     canonical layout in shared memory (hi, lo; tf32 96 KB, f16 48 KB);
+//     canonical layout in shared memory (hi, lo; tf32 96 KB, f16 48 KB), from a copy of the
+//     whole parameter buffer that one bulk (TMA) copy brings into shared memory while warp 0
+//     allocates TMEM (staging from the copy instead of ~50 scattered global loads per thread
+//     took the set-up from ~6 to ~3 us after an L2 flush);
 //   * TMEM (512 columns x 128 lanes, lane = point):
 //       [0, 256)   accumulators D_c, component c at columns 64c..64c+63;
 //       [256, 512) a ring of A-operand chunks; a chunk is 16 input neurons of the next
@@ -38,21 +41,28 @@
 //                  32-bit column (K 2j in the low half of column j).
 //     The A operand lives in TMEM, not shared memory: with N = 64 an A tile read from
 //     shared memory would need ~1.5x the shared-memory bandwidth an SM has.
-//   * 16 warps: warp w serves TMEM lanes 32(w%4)..+31 (its quadrant) and, with s = w/4,
-//     neurons 16a+4s+t. Per layer it loads its 4 x 16 accumulators (16 x tcgen05.ld.x4),
-//     applies the tanh jet in registers and writes hi/lo activations chunk by chunk into the
-//     ring (tcgen05.st) for the next layer. Warp s owns the strided neurons 16a+4s+{0..3}
-//     (a = 0..3), so chunk j (neurons 16j..16j+15, natural K order) gets 4 neurons from every
-//     warp and all 16 warps contribute to every chunk;
-//   * the warp that completes a chunk last (an acq_rel counter per ring slot) issues its
-//     MMAs as a converged warp (elect.sync picks the issuing lane; issued from a divergent
-//     lane these small MMAs cost ~4x their execution time), then tcgen05.commit to free the
-//     slot, and after a layer's 4th chunk a commit that marks D complete. A warp contributes
-//     to chunk 0 of layer l+1 only after it has read D of layer l, so when the last
-//     contribution arrives D may be overwritten -- no separate "D free" barrier.
+//   * 16 epilogue warps (warpgroups 0-3): warp w serves TMEM lanes 32(w%4)..+31 (its
+//     quadrant) and, with s = w/4, neurons 16a+4s+t. Per layer it loads its 4 x 16
+//     accumulators (16 x tcgen05.ld.x4), applies the tanh jet in registers and writes hi/lo
+//     activations chunk by chunk into the ring (tcgen05.st) for the next layer, then arrives
+//     on the slot's "full" mbarrier. Warp s owns the strided neurons 16a+4s+{0..3} (a = 0..3),
+//     so chunk j (neurons 16j..16j+15, natural K order) gets 4 neurons from every warp;
+//   * an MMA warpgroup (warps 16-19; warp 16 issues, 17-19 idle): for each chunk in order it
+//     waits for the slot's 16 arrivals, issues the MMAs as a converged warp (elect.sync picks
+//     the lane; issued from a divergent lane these small MMAs cost ~4x their execution time),
+//     then tcgen05.commit to free the slot, and after a layer's 4th chunk a commit that marks
+//     D complete. A warp contributes to chunk 0 of layer l+1 only after it has read D of
+//     layer l, so once chunk 0 is full D may be overwritten -- no separate "D free" barrier.
 //   So the MMAs of layer l+1 consume chunk j while the epilogue of layer l produces chunk
-//   j+1. (Measured alternatives, all slower or no faster: a dedicated MMA warp -- 17 warps
-//   cap registers at 96 --, 8 epilogue warps plus an issuer, one warp per whole chunk.)
+//   j+1. The tensor core has no deep instruction queue: issuing a chunk's MMAs occupies the
+//   issuing warp for their whole execution (500-1100 cycles beside the epilogue's TMEM
+//   stores). Issued by the epilogue warp that completed the chunk (an earlier form), that
+//   warp fell behind, completed the next chunk last and issued again, putting every MMA on
+//   the epilogue's critical path. A fifth warp per SM sub-partition caps registers at 96,
+//   so the MMA warpgroup gives its registers to the epilogue with setmaxnreg: launched at 96
+//   per thread (640 x 96), it drops to 24 and the epilogue warpgroups rise to 112
+//   (128 x 72 freed >= 512 x 16 taken). The host checks that the kernel was built with 96
+//   registers per thread: with fewer, the raise could never be granted.
 // Layer 0 (2 inputs) and the output layer (1 output) are elementwise/epilogue work: tanh_fast
 // (SFU exp2 + reciprocal), the split, and 16-neuron chunks to halve the synchronisation.
 // Every mbarrier wait is bounded; a wait that gives up raises FHB_STATUS_MMA_TIMEOUT, sets
@@ -69,8 +79,15 @@ namespace fhb {
 namespace {
 
 constexpr int kTile = 128;            // points per tile = MMA M = TMEM lanes
-constexpr int kWarps = 16;            // 4 per TMEM lane quadrant
-constexpr int kThreads = kWarps * 32;
+constexpr int kWarps = 16;              // epilogue warps, 4 per TMEM lane quadrant
+constexpr int kThreads = kWarps * 32;   // epilogue threads
+constexpr int kMmaWarp = kWarps;        // warp 16: first warp of the MMA warpgroup
+constexpr int kBlockThreads = kThreads + 128;
+// Registers per thread: at launch (__launch_bounds__(640, 1) caps ptxas at 96), the MMA
+// warpgroup after setmaxnreg.dec, the epilogue warpgroups after setmaxnreg.inc.
+constexpr int kLaunchRegs = 96, kMmaRegs = 24, kEpiRegs = 112;
+static_assert((kLaunchRegs - kMmaRegs) * 128 >= (kEpiRegs - kLaunchRegs) * kThreads,
+              "register split exceeds the launch's registers");
 constexpr int kChunks = 4;            // chunks of 16 neurons per 64-wide layer
 constexpr int kChunksPerTile = kHiddenGemms * kChunks;
 constexpr uint32_t kTmemCols = 512;
@@ -104,28 +121,31 @@ struct Format<true> {  // 3xFP16, kind::f16, K = 16 per MMA
 // Shared memory layout (bytes): the weight operands, then the rest.
 template <bool F16>
 struct Layout {
-  static constexpr int kSmallOff = kHiddenGemms * Format<F16>::kOperands * Format<F16>::kOperandBytes;
+  static constexpr int kSmallOff =
+      kHiddenGemms * Format<F16>::kOperands * Format<F16>::kOperandBytes;
   static constexpr int kRedOff = kSmallOff + 512 * 4;     // small params, then [8][128] sums
-  static constexpr int kBarOff = kRedOff + 8 * kTile * 4;  // mbarriers: empty[kRing], dfull, red
-  static constexpr int kCountOff = kBarOff + 8 * 8;        // per-slot contribution counters
-  static constexpr int kMiscOff = kCountOff + 4 * 4;       // TMEM base, abort flag
+  // mbarriers: empty[kRing], full[kRing], dfull, red, the parameter copy
+  static constexpr int kBarOff = kRedOff + 8 * kTile * 4;
+  static constexpr int kMiscOff = kBarOff + 16 * 8;        // TMEM base, abort flag
   static constexpr int kScaleOff = kMiscOff + 16;          // f16: F16Consts
-  static constexpr int kSmemUsed = kScaleOff + 256 * 4;
+  static constexpr int kParamOff = kScaleOff + 256 * 4;    // staged parameter buffer
+  static constexpr int kSmemUsed = kParamOff + kParamSmemFloats * 4;
+  // Padded so two CTAs never share an SM (each allocates all 512 TMEM columns).
+  static constexpr int kSmemBytes = kSmemUsed > 120 * 1024 ? (kSmemUsed + 1023) / 1024 * 1024
+                                                           : 120 * 1024;
 };
 constexpr int kSmW0 = 0, kSmB0 = 128, kSmB = 192, kSmWout = 384, kSmBout = 448;
 constexpr int kSmallFloats = 512;
-// Padded so two CTAs never share an SM (each allocates all 512 TMEM columns).
-constexpr int kSmemBytes = 120 * 1024;
-static_assert(Layout<false>::kSmemUsed <= kSmemBytes && Layout<true>::kSmemUsed <= kSmemBytes,
+static_assert(Layout<false>::kSmemBytes <= 227 * 1024 && Layout<true>::kSmemBytes <= 227 * 1024,
               "shared memory layout overflow");
-static_assert(Format<true>::kRing <= 4, "bar and counter space");
+static_assert(2 * Format<true>::kRing + 3 <= 16, "mbarrier space");
 
 struct Ctx {
   uint8_t* smem;
   uint64_t* empty;            // [kRing] ring slot consumed by its MMAs (tcgen05.commit)
+  uint64_t* full;             // [kRing] ring slot written by the 16 epilogue warps
   uint64_t* dfull;            // accumulators complete (tcgen05.commit)
   uint64_t* red;              // output-layer partial sums written (16 warps arrive)
-  uint32_t* count;            // [kRing] contributions to each slot, monotonic
   volatile uint32_t* abort_flag;
   unsigned int* status;
   uint32_t tmem;
@@ -149,6 +169,7 @@ struct F16Consts {
   static constexpr int kC0 = 160;      // [64] -2 sigma_L0 (W0[o][0]^2 + W0[o][1]^2)
   static constexpr int kWords = 224;
 };
+static_assert(F16Consts::kWords <= 256, "the F16Consts words fit the scale region");
 
 // Bounded wait that also gives up when another warp has aborted the CTA.
 __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, const Ctx& cx) {
@@ -178,10 +199,15 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
-// Largest power of 2 <= x for x in [2^-126, 2^127]; clamped to that range otherwise.
-__device__ __forceinline__ float pow2_floor(float x) {
-  x = fminf(fmaxf(x, 1.17549435e-38f), 1.7e38f);
-  return __uint_as_float(__float_as_uint(x) & 0x7F800000u);
+// The largest power of 2 <= 2^c / y, y = max(x, 1e-30), clamped to [2^-126, 2^127], from the
+// exponent and mantissa bits alone: for y = m 2^e (m in [1, 2)) the quotient is 2^(c-e) when
+// m = 1 and lies in (2^(c-e-1), 2^(c-e)) otherwise (a correctly rounded division never reaches
+// 2^(c-e) then, so this equals flooring the divided value).
+__device__ __forceinline__ float pow2_floor_ratio(int c, float x) {
+  const uint32_t b = __float_as_uint(fmaxf(x, 1e-30f));
+  int k = c - (static_cast<int>(b >> 23) - 127) - ((b & 0x7FFFFFu) != 0u ? 1 : 0);
+  k = min(max(k, -126), 127);
+  return __uint_as_float(static_cast<uint32_t>(k + 127) << 23);
 }
 
 // f16 pairs of a split: hi = x rounded to 11 significant bits (tf32 rounding; exact in f16
@@ -284,17 +310,22 @@ __device__ __forceinline__ bool produce_chunk(uint32_t n, const float (&h)[4][4]
   tc::wait_st();
   tc::fence_before_sync();
   __syncwarp();
-  uint32_t last = 0;
-  if ((threadIdx.x & 31) == 0) last = (count_contribution(&cx.count[slot]) % kWarps) == kWarps - 1;
-  last = __shfl_sync(0xffffffffu, last, 0);
-  if (last) {  // warp-uniform: the whole converged warp issues, elect.sync picks a lane
-    tc::fence_after_sync();
-    const uint32_t in_tile = n % kChunksPerTile;
-    issue_chunk_mmas<F16>(cx, static_cast<int>(in_tile / kChunks),
-                          static_cast<int>(in_tile % kChunks), slot);
-    __syncwarp();
-  }
+  if ((threadIdx.x & 31) == 0) mbar_arrive(&cx.full[slot]);
   return true;
+}
+
+// Barrier 1 over the 16 epilogue warps (the MMA warpgroup skips the weight staging).
+__device__ __forceinline__ void epi_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(kThreads) : "memory");
+}
+// Register reallocation within the block's launch budget (whole warpgroups, warp-uniform).
+template <uint32_t N>
+__device__ __forceinline__ void regs_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void regs_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
 }
 
 // Small parameter of thread i: W0, b0, b1..b3, w_out, b_out in the order of `small`.
@@ -391,7 +422,7 @@ __device__ __forceinline__ void stage_f16(const float* __restrict__ params, uint
     }
     small[threadIdx.x] = sv;
   }
-  __syncthreads();
+  epi_sync();
   float* sigma = red + 512;  // [3][4] scratch for the layer-0 constants below
   if (warp == 0) {
     float nrm[3], wmax[3];
@@ -407,10 +438,10 @@ __device__ __forceinline__ void stage_f16(const float* __restrict__ params, uint
     if (lane == 0) {
       float tau[3], sig[3][3];  // sig[l]: v, J, L
       for (int l = 0; l < 3; ++l) {
-        tau[l] = pow2_floor(16.0f / fmaxf(wmax[l], 1e-30f));
-        sig[l][0] = pow2_floor(16384.0f);
-        sig[l][1] = pow2_floor(16384.0f / fmaxf(bj, 1e-30f));
-        sig[l][2] = pow2_floor(16384.0f / fmaxf(bl, 1e-30f));
+        tau[l] = pow2_floor_ratio(4, wmax[l]);
+        sig[l][0] = 16384.0f;
+        sig[l][1] = pow2_floor_ratio(14, bj);
+        sig[l][2] = pow2_floor_ratio(14, bl);
         const float nj = nrm[l] * bj;
         bl = fmaf(nrm[l], bl, 2.0f * nj * nj);
         bj = nj;
@@ -435,7 +466,7 @@ __device__ __forceinline__ void stage_f16(const float* __restrict__ params, uint
       sigma[1] = sig[0][2];
     }
   }
-  __syncthreads();
+  epi_sync();
   if (threadIdx.x < kWidth) {  // layer-0 jets: J = W0 columns, L = -2 a s |W0 row|^2
     const int o = threadIdx.x;
     const float w0 = small[kSmW0 + 2 * o], w1 = small[kSmW0 + 2 * o + 1];
@@ -459,10 +490,10 @@ __device__ __forceinline__ void stage_f16(const float* __restrict__ params, uint
 }
 
 template <bool F16, class Act>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kBlockThreads, 1)
     forward_tc_kernel(const float* __restrict__ coords, const float* __restrict__ params,
                       float* __restrict__ u_out, float* __restrict__ lap_out, int64_t n,
-                      int64_t tiles, unsigned int* status) {
+                      int64_t tiles, int params_aligned, unsigned int* status) {
   using F = Format<F16>;
   using L = Layout<F16>;
   // The f16 range scales bound the jets with |tanh| <= 1 and tanh' <= 1: tanh only.
@@ -475,9 +506,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   Ctx cx;
   cx.smem = smem;
   cx.empty = bars;
-  cx.dfull = bars + F::kRing;
-  cx.red = bars + F::kRing + 1;
-  cx.count = reinterpret_cast<uint32_t*>(smem + L::kCountOff);
+  cx.full = bars + F::kRing;
+  cx.dfull = bars + 2 * F::kRing;
+  cx.red = bars + 2 * F::kRing + 1;
   cx.abort_flag = reinterpret_cast<volatile uint32_t*>(smem + L::kMiscOff + 4);
   cx.status = status;
   cx.f16c = reinterpret_cast<const float*>(smem + L::kScaleOff);
@@ -488,7 +519,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // The first tile's point, requested first: its latency overlaps the set-up below.
   const int row0 = 32 * (warp & 3) + lane;
   float nx0 = 0.0f, nx1 = 0.0f;
-  {
+  if (warp < kWarps) {
     const int64_t p = static_cast<int64_t>(blockIdx.x) * kTile + row0;
     if (p < n) {
       nx0 = coords[2 * p];
@@ -496,27 +527,47 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
-  // ---- set-up: small params and the split weight operands ----
-  static_assert(kSmallFloats == kThreads, "one small parameter per thread");
-  if constexpr (F16) {
-    stage_f16(params, smem, small, red, reinterpret_cast<float*>(smem + L::kScaleOff), warp,
-              lane);
-  } else {
-    stage_tf32(params, smem, small);
-  }
+  // ---- set-up ----
+  // Barriers first, then one bulk copy of the parameter buffer into shared memory and the
+  // TMEM allocation while it is in flight; the statistics and the split read the staged copy.
+  float* sp = reinterpret_cast<float*>(smem + L::kParamOff);
+  uint64_t* pbar = bars + 2 * F::kRing + 2;
   if (threadIdx.x == 0) {
     for (int r = 0; r < F::kRing; ++r) {
       mbar_init(&cx.empty[r], 1);
-      cx.count[r] = 0u;
+      mbar_init(&cx.full[r], kWarps);
     }
     mbar_init(cx.dfull, 1);
     mbar_init(cx.red, kWarps);
+    mbar_init(pbar, 1);
     *cx.abort_flag = 0u;
     fence_barrier_init();
+    if (params_aligned) {
+      mbar_arrive_expect_tx(pbar, kParamBulkFloats * 4);
+      bulk_copy_g2s(sp, params, kParamBulkFloats * 4, pbar);
+    }
   }
   if (warp == 0) {
     tc::tmem_alloc(tmem_base_slot, kTmemCols);
     tc::tmem_relinquish();
+  }
+  if (!params_aligned) {
+    for (int k = threadIdx.x; k < kParamCount; k += kBlockThreads) sp[k] = params[k];
+  } else if (threadIdx.x == 32) {
+    for (int k = kParamBulkFloats; k < kParamCount; ++k) sp[k] = params[k];
+  }
+  __syncthreads();  // barriers initialised; plain-loaded parameters written
+  const bool staged =
+      !params_aligned || mbar_wait_bounded(pbar, 0, status, FHB_STATUS_STAGE_TIMEOUT);
+  if (__syncthreads_and(staged ? 1 : 0) == 0) {
+    if (threadIdx.x == 0) *cx.abort_flag = 1u;
+  } else if (warp < kWarps) {
+    static_assert(kSmallFloats == kThreads, "one small parameter per thread");
+    if constexpr (F16) {
+      stage_f16(sp, smem, small, red, reinterpret_cast<float*>(smem + L::kScaleOff), warp, lane);
+    } else {
+      stage_tf32(sp, smem, small);
+    }
   }
   tc::fence_proxy_async_smem();  // weight operands visible to the tensor core
   tc::fence_before_sync();
@@ -524,133 +575,154 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc::fence_after_sync();
   cx.tmem = *tmem_base_slot;
 
-  const int q = warp & 3;   // TMEM lane quadrant
-  const int s = warp >> 2;  // neuron block 16s..16s+15
-  const uint32_t tmem_warp = cx.tmem + (static_cast<uint32_t>(32 * q) << 16);
-  const int row = 32 * q + lane;
-  uint32_t chunk = 0, mlayer = 0, tile_count = 0;
-  bool ok = true;
-  // Points of the next tile are loaded one tile ahead, so the load latency (long when the
-  // points sit in pinned host memory read over the host link) overlaps a tile of work.
-  for (int64_t tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x, ++tile_count) {
-    const int64_t p = tile * kTile + row;
-    const bool active = p < n;
-    const float x0 = nx0, x1 = nx1;
-    {
-      const int64_t pn = p + static_cast<int64_t>(gridDim.x) * kTile;
-      if (pn < n) {
-        nx0 = coords[2 * pn];
-        nx1 = coords[2 * pn + 1];
-      }
-    }
-
-    // layer 0: z = W0 x + b0, z_J = W0 columns, z_L = 0 (f16: the scaled operand directly)
-#pragma unroll
-    for (int j = 0; j < kChunks; ++j) {
-      float h[4][4];
-#pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        const int o = 16 * j + 4 * s + t;
-        const float w0 = small[kSmW0 + 2 * o], w1 = small[kSmW0 + 2 * o + 1];
-        const float z = fmaf(w0, x0, fmaf(w1, x1, small[kSmB0 + o]));
-        if constexpr (F16) {
-          using C = F16Consts;
-          const float r = tanh_fast_r(z), sv = cx.f16c[C::kSigma0];
-          const float a = fmaf(-2.0f, r, 1.0f), sd = fmaf(-a, a, 1.0f);
-          h[0][t] = fmaf(-2.0f * sv, r, sv);
-          h[1][t] = sd * cx.f16c[C::kW0 + o];
-          h[2][t] = sd * cx.f16c[C::kW1 + o];
-          h[3][t] = cx.f16c[C::kC0 + o] * (a * sd);
-        } else {
-          Act::jet_fast(z, w0, w1, 0.0f, h[0][t], h[1][t], h[2][t], h[3][t]);
-        }
-      }
-      if (!(ok = produce_chunk<F16>(chunk++, h, tmem_warp, s, cx))) break;
-    }
-
-    for (int l = 0; ok && l < kHiddenGemms; ++l, ++mlayer) {
-      if (!(ok = warp_wait(cx.dfull, mlayer & 1u, cx))) break;
-      tc::fence_after_sync();
-      // d[c][4a + t] = component c of neuron 16a + 4s + t
-      float d[4][16];
-#pragma unroll
-      for (int c = 0; c < 4; ++c)
-#pragma unroll
-        for (int a = 0; a < 4; ++a)
-          tc::ld_x4(tmem_warp + 64u * c + 16u * a + 4u * s,
-                    *reinterpret_cast<float(*)[4]>(&d[c][4 * a]));
-      tc::wait_ld();
-      const float* bias = small + kSmB + 64 * l;
-      if (l + 1 < kHiddenGemms) {
-#pragma unroll
-        for (int j = 0; j < kChunks; ++j) {
-          float h[4][4];
-#pragma unroll
-          for (int t = 0; t < 4; ++t) {
-            const int i = 4 * j + t;
-            const float b = bias[16 * j + 4 * s + t];
-            if constexpr (F16) {  // accumulators -> the next GEMM's scaled operand
-              using C = F16Consts;
-              const float* e = cx.f16c + C::kEpi + 4 * l;
-              const float r = tanh_fast_r(fmaf(d[0][i], cx.f16c[C::kUnscale + 4 * l], b));
-              const float a = fmaf(-2.0f, r, 1.0f), sd = fmaf(-a, a, 1.0f);
-              const float sk = sd * e[1];
-              const float q = fmaf(d[1][i], d[1][i], d[2][i] * d[2][i]);
-              h[0][t] = fmaf(-2.0f * e[0], r, e[0]);
-              h[1][t] = sk * d[1][i];
-              h[2][t] = sk * d[2][i];
-              h[3][t] = sd * fmaf(e[3] * a, q, e[2] * d[3][i]);
-            } else {
-              Act::jet_fast(d[0][i] + b, d[1][i], d[2][i], d[3][i], h[0][t], h[1][t],
-                            h[2][t], h[3][t]);
-            }
-          }
-          if (!(ok = produce_chunk<F16>(chunk++, h, tmem_warp, s, cx))) break;
-        }
-      } else {
-        if constexpr (F16) {  // remove the operand scales: exact powers of 2
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            const float us = cx.f16c[F16Consts::kUnscale + 4 * l + c];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) d[c][i] *= us;
-          }
-        }
-#pragma unroll
-        for (int i = 0; i < 16; ++i) d[0][i] += bias[16 * (i >> 2) + 4 * s + (i & 3)];
-        // output layer: u = w.v + b, lap = w.L, over this warp's 16 neurons
-        float pu = 0.0f, pl = 0.0f;
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          float v, j0, j1, lv;
-          Act::jet_fast(d[0][i], d[1][i], d[2][i], d[3][i], v, j0, j1, lv);
-          const float w = small[kSmWout + 16 * (i >> 2) + 4 * s + (i & 3)];
-          pu = fmaf(w, v, pu);
-          pl = fmaf(w, lv, pl);
-        }
-        red[s * kTile + row] = pu;
-        red[(4 + s) * kTile + row] = pl;
+  const bool run = *cx.abort_flag == 0u;
+  if (warp >= kWarps) {
+    // ---- MMA warpgroup: warp 16 issues every chunk of this CTA's tiles in order ----
+    regs_dec<kMmaRegs>();
+    if (warp == kMmaWarp && run) {
+      const int64_t mine = blockIdx.x < tiles ? (tiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+      const uint32_t total = static_cast<uint32_t>(mine) * kChunksPerTile;
+      for (uint32_t n = 0; n < total; ++n) {
+        const uint32_t slot = n % F::kRing;
+        if (!warp_wait(&cx.full[slot], (n / F::kRing) & 1u, cx)) break;
+        tc::fence_after_sync();
+        const uint32_t in_tile = n % kChunksPerTile;
+        issue_chunk_mmas<F16>(cx, static_cast<int>(in_tile / kChunks),
+                              static_cast<int>(in_tile % kChunks), slot);
         __syncwarp();
-        if (lane == 0) mbar_arrive(cx.red);
-        // The s = 0 warps finish the tile. Nobody rewrites `red` before they are done:
-        // the next tile's output stage needs the next tile's chunks from them first.
-        if (s == 0) {
-          if (!(ok = warp_wait(cx.red, tile_count & 1u, cx))) break;
-          if (active) {
-            float uu = small[kSmBout], ll = 0.0f;
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              uu += red[k * kTile + row];
-              ll += red[(4 + k) * kTile + row];
+      }
+    }
+  } else {
+    // ---- epilogue warpgroups ----
+    regs_inc<kEpiRegs>();
+    const int q = warp & 3;   // TMEM lane quadrant
+    const int s = warp >> 2;  // neuron block 16s..16s+15
+    const uint32_t tmem_warp = cx.tmem + (static_cast<uint32_t>(32 * q) << 16);
+    const int row = 32 * q + lane;
+    uint32_t chunk = 0, mlayer = 0, tile_count = 0;
+    bool ok = run;
+    // Points of the next tile are loaded one tile ahead, so the load latency (long when the
+    // points sit in pinned host memory read over the host link) overlaps a tile of work.
+    for (int64_t tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x, ++tile_count) {
+      const int64_t p = tile * kTile + row;
+      const bool active = p < n;
+      const float x0 = nx0, x1 = nx1;
+      {
+        const int64_t pn = p + static_cast<int64_t>(gridDim.x) * kTile;
+        if (pn < n) {
+          nx0 = coords[2 * pn];
+          nx1 = coords[2 * pn + 1];
+        }
+      }
+
+      // layer 0: z = W0 x + b0, z_J = W0 columns, z_L = 0 (f16: the scaled operand directly)
+  #pragma unroll
+      for (int j = 0; j < kChunks; ++j) {
+        float h[4][4];
+  #pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const int o = 16 * j + 4 * s + t;
+          const float w0 = small[kSmW0 + 2 * o], w1 = small[kSmW0 + 2 * o + 1];
+          const float z = fmaf(w0, x0, fmaf(w1, x1, small[kSmB0 + o]));
+          if constexpr (F16) {
+            using C = F16Consts;
+            const float r = tanh_fast_r(z), sv = cx.f16c[C::kSigma0];
+            const float a = fmaf(-2.0f, r, 1.0f), sd = fmaf(-a, a, 1.0f);
+            h[0][t] = fmaf(-2.0f * sv, r, sv);
+            h[1][t] = sd * cx.f16c[C::kW0 + o];
+            h[2][t] = sd * cx.f16c[C::kW1 + o];
+            h[3][t] = cx.f16c[C::kC0 + o] * (a * sd);
+          } else {
+            Act::jet_fast(z, w0, w1, 0.0f, h[0][t], h[1][t], h[2][t], h[3][t]);
+          }
+        }
+        if (!(ok = produce_chunk<F16>(chunk++, h, tmem_warp, s, cx))) break;
+      }
+
+      for (int l = 0; ok && l < kHiddenGemms; ++l, ++mlayer) {
+        if (!(ok = warp_wait(cx.dfull, mlayer & 1u, cx))) break;
+        tc::fence_after_sync();
+        // d[c][4a + t] = component c of neuron 16a + 4s + t
+        float d[4][16];
+  #pragma unroll
+        for (int c = 0; c < 4; ++c)
+  #pragma unroll
+          for (int a = 0; a < 4; ++a)
+            tc::ld_x4(tmem_warp + 64u * c + 16u * a + 4u * s,
+                      *reinterpret_cast<float(*)[4]>(&d[c][4 * a]));
+        tc::wait_ld();
+        const float* bias = small + kSmB + 64 * l;
+        if (l + 1 < kHiddenGemms) {
+  #pragma unroll
+          for (int j = 0; j < kChunks; ++j) {
+            float h[4][4];
+  #pragma unroll
+            for (int t = 0; t < 4; ++t) {
+              const int i = 4 * j + t;
+              const float b = bias[16 * j + 4 * s + t];
+              if constexpr (F16) {  // accumulators -> the next GEMM's scaled operand
+                using C = F16Consts;
+                const float* e = cx.f16c + C::kEpi + 4 * l;
+                const float r = tanh_fast_r(fmaf(d[0][i], cx.f16c[C::kUnscale + 4 * l], b));
+                const float a = fmaf(-2.0f, r, 1.0f), sd = fmaf(-a, a, 1.0f);
+                const float sk = sd * e[1];
+                const float q = fmaf(d[1][i], d[1][i], d[2][i] * d[2][i]);
+                h[0][t] = fmaf(-2.0f * e[0], r, e[0]);
+                h[1][t] = sk * d[1][i];
+                h[2][t] = sk * d[2][i];
+                h[3][t] = sd * fmaf(e[3] * a, q, e[2] * d[3][i]);
+              } else {
+                Act::jet_fast(d[0][i] + b, d[1][i], d[2][i], d[3][i], h[0][t], h[1][t],
+                              h[2][t], h[3][t]);
+              }
             }
-            u_out[p] = uu;
-            lap_out[p] = ll;
+            if (!(ok = produce_chunk<F16>(chunk++, h, tmem_warp, s, cx))) break;
+          }
+        } else {
+          if constexpr (F16) {  // remove the operand scales: exact powers of 2
+  #pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              const float us = cx.f16c[F16Consts::kUnscale + 4 * l + c];
+  #pragma unroll
+              for (int i = 0; i < 16; ++i) d[c][i] *= us;
+            }
+          }
+  #pragma unroll
+          for (int i = 0; i < 16; ++i) d[0][i] += bias[16 * (i >> 2) + 4 * s + (i & 3)];
+          // output layer: u = w.v + b, lap = w.L, over this warp's 16 neurons
+          float pu = 0.0f, pl = 0.0f;
+  #pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            float v, j0, j1, lv;
+            Act::jet_fast(d[0][i], d[1][i], d[2][i], d[3][i], v, j0, j1, lv);
+            const float w = small[kSmWout + 16 * (i >> 2) + 4 * s + (i & 3)];
+            pu = fmaf(w, v, pu);
+            pl = fmaf(w, lv, pl);
+          }
+          red[s * kTile + row] = pu;
+          red[(4 + s) * kTile + row] = pl;
+          __syncwarp();
+          if (lane == 0) mbar_arrive(cx.red);
+          // The s = 0 warps finish the tile. Nobody rewrites `red` before they are done:
+          // the next tile's output stage needs the next tile's chunks from them first.
+          if (s == 0) {
+            if (!(ok = warp_wait(cx.red, tile_count & 1u, cx))) break;
+            if (active) {
+              float uu = small[kSmBout], ll = 0.0f;
+  #pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                uu += red[k * kTile + row];
+                ll += red[(4 + k) * kTile + row];
+              }
+              u_out[p] = uu;
+              lap_out[p] = ll;
+            }
           }
         }
       }
     }
-  }
 
+  }
   // ---- teardown: every warp arrives here (all waits are bounded); free TMEM ----
   // On the normal path each warp waited for the last dfull phase, so every MMA finished.
   // After an abort, MMAs issued before it may still run: give them time to drain (they
@@ -672,8 +744,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 template <bool F16, class Act>
 cudaError_t set_attributes() {
+  // The setmaxnreg split assumes kLaunchRegs per thread at launch; a build with fewer would
+  // leave the epilogue's register raise waiting forever, so it is refused here.
+  cudaFuncAttributes attr;
+  const cudaError_t e = cudaFuncGetAttributes(&attr, forward_tc_kernel<F16, Act>);
+  if (e != cudaSuccess) return e;
+  if (attr.numRegs != kLaunchRegs) return cudaErrorInvalidKernelImage;
   return cudaFuncSetAttribute(forward_tc_kernel<F16, Act>,
-                              cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+                              cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              Layout<F16>::kSmemBytes);
 }
 
 cudaError_t prepare_forward_tc() {
@@ -689,15 +768,16 @@ cudaError_t launch_forward_tc(const float* coords, const float* params, float* u
                               cudaStream_t stream) {
   const int64_t tiles = (n + kTile - 1) / kTile;
   const int grid = static_cast<int>(std::min<int64_t>(tiles, dev.sms));
+  const int aligned = (reinterpret_cast<uintptr_t>(params) % 16) == 0;
   if (activation == FHB_ACTIVATION_SILU) {  // unbounded activations: the 3xTF32 format
-    forward_tc_kernel<false, SiluAct><<<grid, kThreads, kSmemBytes, stream>>>(
-        coords, params, u, lap, n, tiles, dev.status);
+    forward_tc_kernel<false, SiluAct><<<grid, kBlockThreads, Layout<false>::kSmemBytes, stream>>>(
+        coords, params, u, lap, n, tiles, aligned, dev.status);
   } else if (f16) {
-    forward_tc_kernel<true, TanhAct><<<grid, kThreads, kSmemBytes, stream>>>(
-        coords, params, u, lap, n, tiles, dev.status);
+    forward_tc_kernel<true, TanhAct><<<grid, kBlockThreads, Layout<true>::kSmemBytes, stream>>>(
+        coords, params, u, lap, n, tiles, aligned, dev.status);
   } else {
-    forward_tc_kernel<false, TanhAct><<<grid, kThreads, kSmemBytes, stream>>>(
-        coords, params, u, lap, n, tiles, dev.status);
+    forward_tc_kernel<false, TanhAct><<<grid, kBlockThreads, Layout<false>::kSmemBytes, stream>>>(
+        coords, params, u, lap, n, tiles, aligned, dev.status);
   }
   return cudaGetLastError();
 }
