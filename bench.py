@@ -50,7 +50,7 @@ UNIT = "pts/s"
 FLOP_FORWARD = 101_888  # per point: 3 hidden 64x64 jet GEMMs x 4 comps + layer 0/out + tanh jet
 FLOP_STEP = 98_304 * 3 + 256 * 2 + 6_000  # forward + input adjoint + weight gradient + small
 POINTS_PER_GPU = 65_536
-F16_TRAFFIC = 656_896  # DRAM bytes of one version-3 launch at 65,536 points (ncu)
+F16_TRAFFIC = 643_072  # DRAM bytes of one version-3 launch at 65,536 points (ncu)
 FLUSH_BYTES = 192 << 20
 PEAKS_FILE = ROOT / "MEASURED_PEAKS.json"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
@@ -377,7 +377,8 @@ def run_ours(args) -> None:
         return
 
     # DRAM read + write bytes of one forward launch at 65,536 points, from one ncu capture of
-    # the same command per kernel family (0-2: FP32 kernel, 3: 3xFP16, 4-5: 3xTF32).
+    # the same command per kernel family (0-2: FP32 kernel, 3: 3xFP16, 4-5: 3xTF32; the
+    # 3xTF32 figure predates the bulk-copied parameter staging, which reads the same bytes).
     traffic = None
     if n == POINTS_PER_GPU and act == "tanh":
         traffic = {0: 611_840, 1: 611_840, 2: 611_840, 3: F16_TRAFFIC, 4: 646_400, 5: 646_400}[version]
