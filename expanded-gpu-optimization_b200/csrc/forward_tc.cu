@@ -50,9 +50,11 @@
 //   * an MMA warpgroup (warps 16-19; warp 16 issues, 17-19 idle): for each chunk in order it
 //     waits for the slot's 16 arrivals, issues the MMAs as a converged warp (elect.sync picks
 //     the lane; issued from a divergent lane these small MMAs cost ~4x their execution time),
-//     then tcgen05.commit to free the slot, and after a layer's 4th chunk a commit that marks
-//     D complete. A warp contributes to chunk 0 of layer l+1 only after it has read D of
-//     layer l, so once chunk 0 is full D may be overwritten -- no separate "D free" barrier.
+//     then (tf32) tcgen05.commit to free the slot, and after a layer's 4th chunk a commit that
+//     marks D complete. A warp contributes to chunk 0 of layer l+1 only after it has read D
+//     of layer l, so once chunk 0 is full D may be overwritten -- no separate "D free"
+//     barrier. The f16 ring holds a whole layer, so the "D complete" wait before a layer's
+//     epilogue also frees every slot it writes: f16 has no slot-free commit or wait.
 //   So the MMAs of layer l+1 consume chunk j while the epilogue of layer l produces chunk
 //   j+1. The tensor core has no deep instruction queue: issuing a chunk's MMAs occupies the
 //   issuing warp for their whole execution (500-1100 cycles beside the epilogue's TMEM
@@ -232,8 +234,8 @@ __device__ __forceinline__ float tanh_fast_r(float x) {
 }
 
 // The MMAs of chunk j (input neurons 16j..16j+15) of hidden GEMM `layer`, A from ring slot
-// `slot`, then a commit that frees the slot (and after the 4th chunk one that marks D
-// complete). tf32: 2 K steps x 4 components x (H_hi W_hi + H_lo W_hi + H_hi W_lo), A block
+// `slot`, then (tf32) a commit that frees the slot, and after the 4th chunk one that marks D
+// complete. tf32: 2 K steps x 4 components x (H_hi W_hi + H_lo W_hi + H_hi W_lo), A block
 // (component c, hi/lo sp, K step kk) at columns 32c + 16sp + 8kk of the slot. f16: 4
 // components x (H_hi W_hi + H_lo W_hi + H_hi W_lo), A block (c, sp) at 16c + 8sp.
 template <bool F16>
@@ -271,7 +273,7 @@ __device__ __forceinline__ void issue_chunk_mmas(const Ctx& cx, int layer, int j
       }
     }
   }
-  tc::commit_warp(&cx.empty[slot]);
+  if constexpr (!F16) tc::commit_warp(&cx.empty[slot]);  // f16: see produce_chunk
   if (j == kChunks - 1) tc::commit_warp(cx.dfull);
 }
 
@@ -283,8 +285,14 @@ __device__ __forceinline__ bool produce_chunk(uint32_t n, const float (&h)[4][4]
                                               uint32_t tmem_warp, int s, const Ctx& cx) {
   using F = Format<F16>;
   const uint32_t slot = n % F::kRing;
-  if (!warp_wait(&cx.empty[slot], ((n / F::kRing) & 1u) ^ 1u, cx)) return false;
-  tc::fence_after_sync();
+  // tf32 (2 slots) waits for the MMAs of chunk n - 2 of the same GEMM. The f16 ring holds a
+  // whole layer, so chunk n reuses the slot of chunk n - 4 -- the same chunk of the previous
+  // GEMM -- whose MMAs the "D complete" commit that this warp waited on before computing
+  // chunk n already covers (a wait that could never block measured ~300 cycles per chunk).
+  if constexpr (!F16) {
+    if (!warp_wait(&cx.empty[slot], ((n / F::kRing) & 1u) ^ 1u, cx)) return false;
+    tc::fence_after_sync();
+  }
   const uint32_t slot_col = tmem_warp + kRingCol + F::kSlotCols * slot;
   if constexpr (F16) {
     const uint32_t base = slot_col + 2u * s;
@@ -616,10 +624,10 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
       }
 
       // layer 0: z = W0 x + b0, z_J = W0 columns, z_L = 0 (f16: the scaled operand directly)
-  #pragma unroll
+#pragma unroll
       for (int j = 0; j < kChunks; ++j) {
         float h[4][4];
-  #pragma unroll
+#pragma unroll
         for (int t = 0; t < 4; ++t) {
           const int o = 16 * j + 4 * s + t;
           const float w0 = small[kSmW0 + 2 * o], w1 = small[kSmW0 + 2 * o + 1];
@@ -644,19 +652,19 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
         tc::fence_after_sync();
         // d[c][4a + t] = component c of neuron 16a + 4s + t
         float d[4][16];
-  #pragma unroll
+#pragma unroll
         for (int c = 0; c < 4; ++c)
-  #pragma unroll
+#pragma unroll
           for (int a = 0; a < 4; ++a)
             tc::ld_x4(tmem_warp + 64u * c + 16u * a + 4u * s,
                       *reinterpret_cast<float(*)[4]>(&d[c][4 * a]));
         tc::wait_ld();
         const float* bias = small + kSmB + 64 * l;
         if (l + 1 < kHiddenGemms) {
-  #pragma unroll
+#pragma unroll
           for (int j = 0; j < kChunks; ++j) {
             float h[4][4];
-  #pragma unroll
+#pragma unroll
             for (int t = 0; t < 4; ++t) {
               const int i = 4 * j + t;
               const float b = bias[16 * j + 4 * s + t];
@@ -680,18 +688,18 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
           }
         } else {
           if constexpr (F16) {  // remove the operand scales: exact powers of 2
-  #pragma unroll
+#pragma unroll
             for (int c = 0; c < 4; ++c) {
               const float us = cx.f16c[F16Consts::kUnscale + 4 * l + c];
-  #pragma unroll
+#pragma unroll
               for (int i = 0; i < 16; ++i) d[c][i] *= us;
             }
           }
-  #pragma unroll
+#pragma unroll
           for (int i = 0; i < 16; ++i) d[0][i] += bias[16 * (i >> 2) + 4 * s + (i & 3)];
           // output layer: u = w.v + b, lap = w.L, over this warp's 16 neurons
           float pu = 0.0f, pl = 0.0f;
-  #pragma unroll
+#pragma unroll
           for (int i = 0; i < 16; ++i) {
             float v, j0, j1, lv;
             Act::jet_fast(d[0][i], d[1][i], d[2][i], d[3][i], v, j0, j1, lv);
@@ -709,7 +717,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
             if (!(ok = warp_wait(cx.red, tile_count & 1u, cx))) break;
             if (active) {
               float uu = small[kSmBout], ll = 0.0f;
-  #pragma unroll
+#pragma unroll
               for (int k = 0; k < 4; ++k) {
                 uu += red[k * kTile + row];
                 ll += red[(4 + k) * kTile + row];
