@@ -285,13 +285,18 @@ __device__ __forceinline__ bool produce_chunk(uint32_t n, const float (&h)[4][4]
                                               uint32_t tmem_warp, int s, const Ctx& cx) {
   using F = Format<F16>;
   const uint32_t slot = n % F::kRing;
-  // tf32 (2 slots) waits for the MMAs of chunk n - 2 of the same GEMM. The f16 ring holds a
-  // whole layer, so chunk n reuses the slot of chunk n - 4 -- the same chunk of the previous
-  // GEMM -- whose MMAs the "D complete" commit that this warp waited on before computing
-  // chunk n already covers (a wait that could never block measured ~300 cycles per chunk).
+  // A slot is free once the MMAs of the chunk that used it before have completed. Chunks 0
+  // and 1 of a GEMM (and every f16 chunk: the f16 ring holds a whole layer) reuse a slot of
+  // the previous GEMM, whose MMAs the "D complete" commit that this warp waited on before
+  // computing the chunk already covers; only tf32 chunks 2 and 3, which reuse the slots of
+  // chunks 0 and 1 of the same GEMM, wait for a slot's commit (a wait that cannot block still
+  // measured ~300 cycles per chunk). The commits still come once per chunk, so the parity of
+  // the waits that remain counts every chunk of the slot.
   if constexpr (!F16) {
-    if (!warp_wait(&cx.empty[slot], ((n / F::kRing) & 1u) ^ 1u, cx)) return false;
-    tc::fence_after_sync();
+    if (n % kChunks >= static_cast<uint32_t>(F::kRing)) {
+      if (!warp_wait(&cx.empty[slot], ((n / F::kRing) & 1u) ^ 1u, cx)) return false;
+      tc::fence_after_sync();
+    }
   }
   const uint32_t slot_col = tmem_warp + kRingCol + F::kSlotCols * slot;
   if constexpr (F16) {
