@@ -206,8 +206,15 @@ __device__ __noinline__ bool issue_chunk_mmas(const Ctx& cx, uint32_t tile_index
 __device__ __forceinline__ bool produce_chunk(uint32_t n, const float (&h)[4][4],
                                               uint32_t tmem_warp, int s, const Ctx& cx) {
   const uint32_t slot = n % kRing;
-  if (!warp_wait(bar_empty(slot), ((n / kRing) & 1u) ^ 1u)) return false;
-  tc::fence_after_sync();
+  // Chunks 0 and 1 of a GEMM reuse the slots of chunks 2 and 3 of the previous GEMM (or the
+  // weight-gradient accumulators borrowed in between), which this warp's wait for that GEMM's
+  // "D complete" commit (and the block barrier after emptying the accumulators) already
+  // covers; only chunks 2 and 3 wait for the commit of chunk n - 2. A phase still completes
+  // per chunk, so the parity below counts every chunk of the slot.
+  if (n % kChunks >= static_cast<uint32_t>(kRing)) {
+    if (!warp_wait(bar_empty(slot), ((n / kRing) & 1u) ^ 1u)) return false;
+    tc::fence_after_sync();
+  }
   const uint32_t base = tmem_warp + kRingCol + kSlotCols * slot + 4u * s;
 #pragma unroll
   for (int c = 0; c < 4; ++c) {
