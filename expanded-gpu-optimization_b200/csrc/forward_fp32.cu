@@ -5,9 +5,14 @@
 // MLP, with tanh (the reference kernels' activation) or SiLU (the other activation of the
 // reference's PyTorch forward-Laplacian backend) as the Act template parameter. Design for
 // sm_100a:
-//   * persistent grid, one 256-thread CTA per SM; the whole 51 KB parameter buffer is
-//     staged into shared memory ONCE per CTA by one bulk (TMA) copy, not once per tile;
-//   * a tile holds 32*PPL points; warp w owns neurons 8w..8w+7, lane l owns points
+//   * persistent grid, one CTA per SM; the whole 51 KB parameter buffer is staged into
+//     shared memory ONCE per CTA by one bulk (TMA) copy, not once per tile. A CTA holds two
+//     independent 256-thread tile groups (32- and 64-point tiles; one group for 128-point
+//     tiles, whose 128 accumulators per thread leave no registers for a second), each with
+//     its own jet buffer and named barrier, taking the CTA's tiles in turn: 4 warps per
+//     scheduler instead of 2 hide the FMA and shared-memory latencies that bounded one group
+//     (64-point tiles 174 -> 166 us at 64K points, 32-point tiles 190 -> 169 us);
+//   * a tile holds 32*PPL points; warp w of a group owns neurons 8w..8w+7, lane l owns points
 //     l*PPL..l*PPL+PPL-1, so every 64x64 layer is a register-tiled GEMM with
 //     4 comps x 8 neurons x PPL points = 32*PPL accumulators per thread. Weights are read
 //     row-major as float4 (broadcast within a warp: 8 LDS.128 per 4 inputs), jet columns
@@ -34,9 +39,23 @@ struct Cfg {
   static constexpr int kPlane = kWidth * kTile;  // one jet component, [neuron][point]
   static constexpr int kJetFloats = 4 * kPlane;
   static constexpr int kRedFloats = 2 * kWarps * kTile;
+  // Independent 8-warp tile groups per CTA sharing the staged parameters: two where the
+  // accumulators leave room for 512 threads (<= 128 registers), one for 128-point tiles.
+  static constexpr int kGroups = PPL == 4 ? 1 : 2;
+  static constexpr int kBlock = kGroups * kThreads;
   static constexpr size_t kSmem =
-      (size_t)(kParamSmemFloats + kJetFloats + kRedFloats) * sizeof(float) + 16;
+      (size_t)(kParamSmemFloats + kGroups * (kJetFloats + kRedFloats)) * sizeof(float) + 16;
 };
+
+// Barrier over the 256 threads of one tile group (ids 1, 2; 0 is __syncthreads).
+template <int kGroups>
+__device__ __forceinline__ void group_sync(int group) {
+  if constexpr (kGroups == 1) {
+    __syncthreads();
+  } else {
+    asm volatile("bar.sync %0, 256;" ::"r"(1 + group) : "memory");
+  }
+}
 
 template <int PPL>
 __device__ __forceinline__ void ld_pts(const float* p, float (&v)[PPL]) {
@@ -72,7 +91,7 @@ __device__ __forceinline__ float lane_of(const float4& w, int j) {
 }
 
 template <int PPL, class Act>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(Cfg<PPL>::kBlock, 1)
     forward_fp32_kernel(const float* __restrict__ coords, const float* __restrict__ params,
                         float* __restrict__ u_out, float* __restrict__ lap_out, int64_t n,
                         int64_t tiles, int params_aligned, int coords_aligned,
@@ -80,17 +99,23 @@ __global__ void __launch_bounds__(kThreads, 1)
   using C = Cfg<PPL>;
   extern __shared__ __align__(16) float smem[];
   float* sp = smem;                       // staged parameters, ABI layout
-  float* jet = smem + kParamSmemFloats;   // [4][64][kTile]
-  float* red = jet + C::kJetFloats;       // [2][kWarps][kTile]
-  uint64_t* bar = reinterpret_cast<uint64_t*>(red + C::kRedFloats);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(
+      smem + kParamSmemFloats + C::kGroups * (C::kJetFloats + C::kRedFloats));
   if (!stage_parameters(sp, params, bar, params_aligned != 0, status)) return;
 
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
+  const int group = threadIdx.x / kThreads;
+  const int gt = threadIdx.x % kThreads;  // thread within the group
+  float* jet = smem + kParamSmemFloats + group * (C::kJetFloats + C::kRedFloats);  // [4][64][kTile]
+  float* red = jet + C::kJetFloats;       // [2][kWarps][kTile]
+  const int warp = gt >> 5;
+  const int lane = gt & 31;
   const int o0 = warp * kNeuronsPerWarp;
   const int col = lane * PPL;
 
-  for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+  // The CTA's tiles (blockIdx.x + k gridDim.x) alternate between its groups, so the SM's
+  // share stays balanced and an odd last tile runs with the SM to itself.
+  for (int64_t tile = blockIdx.x + static_cast<int64_t>(group) * gridDim.x; tile < tiles;
+       tile += static_cast<int64_t>(gridDim.x) * C::kGroups) {
     const int64_t first = tile * C::kTile + col;
     float x0[PPL], x1[PPL];
     if (coords_aligned && PPL >= 2 && first + PPL <= n) {
@@ -133,7 +158,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int layer = 0; layer < kHiddenGemms; ++layer) {
       const float* W = sp + kHiddenBase + layer * kHiddenStride;  // [out][in]
       const float* bias = W + kWidth * kWidth;
-      __syncthreads();  // the input jet of this layer is complete
+      group_sync<C::kGroups>(group);  // the input jet of this layer is complete
 
       float acc[4][kNeuronsPerWarp][PPL];
 #pragma unroll
@@ -169,7 +194,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      __syncthreads();  // every read of this layer's input jet is done; update in place
+      group_sync<C::kGroups>(group);  // every read of this layer's input jet is done
 
       if (layer + 1 < kHiddenGemms) {
 #pragma unroll
@@ -205,10 +230,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         st_pts<PPL>(red + (kWarps + warp) * C::kTile + col, pl);
       }
     }
-    __syncthreads();  // partial sums complete
+    group_sync<C::kGroups>(group);  // partial sums complete
 
-    if (threadIdx.x < C::kTile) {
-      const int t = threadIdx.x;
+    if (gt < C::kTile) {
+      const int t = gt;
       const int64_t p = tile * C::kTile + t;
       if (p < n) {
         float uu = 0.0f, ll = 0.0f;
@@ -239,7 +264,7 @@ cudaError_t launch(const float* coords, const float* params, float* u, float* la
   const int grid = static_cast<int>(std::min<int64_t>(tiles, dev.sms));
   const int params_aligned = (reinterpret_cast<uintptr_t>(params) % 16) == 0;
   const int coords_aligned = (reinterpret_cast<uintptr_t>(coords) % 16) == 0;
-  forward_fp32_kernel<PPL, Act><<<grid, kThreads, C::kSmem, stream>>>(
+  forward_fp32_kernel<PPL, Act><<<grid, C::kBlock, C::kSmem, stream>>>(
       coords, params, u, lap, n, tiles, params_aligned, coords_aligned, dev.status);
   return cudaGetLastError();
 }
