@@ -155,6 +155,9 @@ def test_forward_unaligned_views(version: int) -> None:
     eu, el = _oracle_forward(base, coords)
     torch.testing.assert_close(lap.cpu(), el, atol=1e-5, rtol=1e-4)
     torch.testing.assert_close(u.cpu(), eu, atol=1e-5, rtol=1e-4)
+    # the bulk-copy and the plain-load parameter staging give bitwise the same results
+    au, alap = fused_forward_laplacian(coords.contiguous().clone(), base, version)
+    assert torch.equal(au, u) and torch.equal(alap, lap)
 
 
 @pytest.mark.parametrize("version", ALL_VERSIONS)
