@@ -73,7 +73,9 @@ int fhb_parameter_count(void);
 /*
  * One-time per-device set-up (kernel attributes, SM count, status word). Called
  * implicitly by the first call of any entry point on a device; call it explicitly before
- * capturing a CUDA graph on a device that has not run a kernel yet.
+ * capturing a CUDA graph on a device that has not run a kernel yet. Fails (FHB_ERR_CUDA,
+ * no kernel launched) if the tensor-core forward was built with another register count
+ * than its warpgroups' register split assumes.
  */
 int fhb_prepare_device(int device);
 
