@@ -50,6 +50,7 @@ UNIT = "pts/s"
 FLOP_FORWARD = 101_888  # per point: 3 hidden 64x64 jet GEMMs x 4 comps + layer 0/out + tanh jet
 FLOP_STEP = 98_304 * 3 + 256 * 2 + 6_000  # forward + input adjoint + weight gradient + small
 POINTS_PER_GPU = 65_536
+WORKLOAD = "config1: residual eval (u, lap) of the 2->64->64->64->64->1 tanh MLP"
 F16_TRAFFIC = 643_072  # DRAM bytes of one version-3 launch at 65,536 points (ncu)
 FLUSH_BYTES = 192 << 20
 PEAKS_FILE = ROOT / "MEASURED_PEAKS.json"
@@ -218,11 +219,11 @@ def run_reference(args) -> None:
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": total / args.steps * 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (uniform points in [-1,1]^2, CPU generator seed 1; seed-0 nn.Linear init)",
-        "config": {"workload": "config1: residual eval (u, lap), 2->64x4->1 tanh MLP",
+        "config": {"workload": WORKLOAD, "points_per_gpu": points, "global_points": points,
                    "points_per_step": sample, "parallelism": "rank 0 only (CPU)"},
         "impl": "reference",
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
-                         "sample": f"{sample:,} points per step of the 65,536-point config-1 "
+                         "sample": f"{sample:,} points per step of the {points:,}-point "
                                    f"workload; PyTorch forward Laplacian (oracle port of "
                                    f"src/fused_hoad/backends/forward_laplacian.py) on {cores} threads"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -419,7 +420,7 @@ def run_ours(args) -> None:
         "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (uniform points in [-1,1]^2, CPU generator seed 1; seed-0 nn.Linear init)",
         "config": {
-            "workload": "config1: residual eval (u, lap) of the 2->64->64->64->64->1 tanh MLP",
+            "workload": WORKLOAD,
             "points_per_gpu": n, "global_points": n * world, "forward_version": version,
             "activation": act,
             "l2": f"flushed between timed steps ({FLUSH_BYTES >> 20} MiB write, outside the events)",
