@@ -51,6 +51,13 @@ FLOP_FORWARD = 101_888  # per point: 3 hidden 64x64 jet GEMMs x 4 comps + layer 
 FLOP_STEP = 98_304 * 3 + 256 * 2 + 6_000  # forward + input adjoint + weight gradient + small
 POINTS_PER_GPU = 65_536
 WORKLOAD = "config1: residual eval (u, lap) of the 2->64->64->64->64->1 tanh MLP"
+# The reference's only published number for this metric: fused fwd v2 (its default) at
+# 65,536 points, 0.538 ms = 121.9 M pts/s on an RTX A5000 (reference
+# results/2026-11-06-RTX-A5000-8454035/inference.txt:47, README.md:63). It publishes no B200,
+# multi-GPU or larger-N numbers.
+PUBLISHED_PTS_S = 121.9e6
+PUBLISHED_NOTE = ("value / 121.9 M pts/s, the reference's published fused fwd v2 at 65,536 "
+                  "points on an RTX A5000 (its only published hardware)")
 F16_TRAFFIC = 643_072  # DRAM bytes of one version-3 launch at 65,536 points (ncu)
 FLUSH_BYTES = 192 << 20
 PEAKS_FILE = ROOT / "MEASURED_PEAKS.json"
@@ -217,7 +224,8 @@ def run_reference(args) -> None:
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": total / args.steps * 1e3,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": value / PUBLISHED_PTS_S,
+        "vs_baseline_note": PUBLISHED_NOTE, "dtype": "f32",
         "data": "synthetic (uniform points in [-1,1]^2, CPU generator seed 1; seed-0 nn.Linear init)",
         "config": {"workload": WORKLOAD, "points_per_gpu": points, "global_points": points,
                    "points_per_step": sample, "parallelism": "rank 0 only (CPU)"},
@@ -417,7 +425,8 @@ def run_ours(args) -> None:
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "scaling": "weak", "vs_baseline": value / PUBLISHED_PTS_S,
+        "vs_baseline_note": PUBLISHED_NOTE, "dtype": "f32",
         "data": "synthetic (uniform points in [-1,1]^2, CPU generator seed 1; seed-0 nn.Linear init)",
         "config": {
             "workload": WORKLOAD,

@@ -41,6 +41,9 @@ def test_reference_arm_prints_one_contract_line() -> None:
     assert line["config"]["workload"] == bench.WORKLOAD
     assert line["config"]["points_per_gpu"] == 65_536
     assert line["value"] > 0 and line["ms_per_step"] > 0
+    # the reference's published number for this metric (fused fwd v2, 64K points, RTX A5000)
+    assert abs(line["vs_baseline"] - line["value"] / bench.PUBLISHED_PTS_S) < 1e-12
+    assert "A5000" in line["vs_baseline_note"]
     base = line["cpu_baseline"]
     assert base["kind"] in ("port", "reference") and base["cores"] >= 1
     assert base["value"] == line["value"] and base["unit"] == bench.UNIT and base["sample"]
