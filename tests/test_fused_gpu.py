@@ -118,6 +118,37 @@ def test_forward_f16_kernel_tracks_tf32_across_weight_scales(scale: float) -> No
             assert errors[3][k] <= 1e-4 * size, (k, errors)
 
 
+HIDDEN_BASE, HIDDEN_STRIDE = 192, 64 * 64 + 64  # W1 offset, one hidden layer (W + b)
+
+
+def _degenerate_parameters(case: str) -> torch.Tensor:
+    params = jet.init_parameters(0)
+    if case == "zeros":
+        return torch.zeros_like(params)
+    if case == "zero_hidden":  # W1..W3 = 0: the hidden jets are constants, lap = 0
+        for layer in range(3):
+            base = HIDDEN_BASE + layer * HIDDEN_STRIDE
+            params[base:base + 64 * 64] = 0.0
+        return params
+    return params * 1e-6  # "tiny": every power-of-2 operand scale far from 1
+
+
+@pytest.mark.parametrize("case", ["zeros", "zero_hidden", "tiny"])
+@pytest.mark.parametrize("version", ALL_VERSIONS)
+def test_forward_degenerate_parameters(version: int, case: str) -> None:
+    """Extreme parameter buffers stay finite and match the FP64 oracle; the 3xFP16 scales
+    saturate for zero weights (2^103 and beyond) without producing inf or NaN."""
+    params = _degenerate_parameters(case)
+    coords = uniform_points(1_000, seed=71)
+    u, lap = fused_forward_laplacian(coords.cuda(), params.cuda(), version)
+    assert bool(torch.isfinite(u).all() and torch.isfinite(lap).all())
+    u64, lap64 = jet.forward_laplacian(params.double(), coords.double())
+    torch.testing.assert_close(u.cpu().double(), u64, atol=1e-5, rtol=1e-4)
+    torch.testing.assert_close(lap.cpu().double(), lap64, atol=1e-5, rtol=1e-4)
+    if case == "zeros":
+        assert not bool(u.any()) and not bool(lap.any())
+
+
 @pytest.mark.parametrize("version", ALL_VERSIONS)
 def test_forward_empty_batch(version: int) -> None:
     u, lap = fused_forward_laplacian(torch.empty(0, 2, device="cuda"), _params(), version)
