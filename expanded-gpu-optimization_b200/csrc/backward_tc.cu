@@ -31,13 +31,25 @@
 //     read back by the same thread for the adjoint and the weight-gradient staging (h_0 is
 //     recomputed from the point);
 //   * registers: per thread one point (TMEM lane) and the 16 neurons 16a+4s+t.
+// Warps: 16 epilogue warps (all of the elementwise work above; warp w serves TMEM lane
+// quadrant w%4 and, with s = w/4, neurons 16a+4s+t) and an MMA warpgroup (warps 16-19) whose
+// warp 16 issues the 24 MMAs of every chunk in order once the chunk's 16 arrivals are in --
+// the warp that completed a chunk used to issue it and, blocked for the MMAs' execution
+// (~1,000 cycles), completed the next chunk last as well. The weight-gradient rounds stay
+// with one epilogue warp per point half, which issues right after its half's barrier (handing
+// them to the MMA warpgroup serialised them behind two mbarrier wake-ups per round). The MMA
+// warpgroup gives its registers to the epilogue with setmaxnreg (launch 640 x 96, MMA
+// warpgroup 32, epilogue 112), and the adjoint reads h_{l-1} without a group-ahead prefetch,
+// which frees 16 registers and was itself slower: 281 -> 268 us at 64K points, 3.41 -> 3.23
+// ms at 1M, bitwise unchanged. The host refuses a build whose launch register count is not
+// the 96 the split assumes.
 // The adjoint is written in terms of the stored activation h = (a, s z_J, s z_L - 2as|z_J|^2)
 // with s = 1 - a^2, the quantities the forward produced, so no pre-activation is stored.
 // Gradients are accumulated in a fixed order (warp butterflies, quadrants and tiles in
 // index order, the tensor core's own order for the weight gradient, one partial row per CTA
 // summed in row order), so results are bitwise reproducible for a given grid. Every wait
-// is bounded; a wait that gives up sets the CTA abort flag, the warps leave together at
-// the next block-wide barrier, and TMEM is freed.
+// is bounded; a wait that gives up sets the CTA abort flag, the epilogue warps leave
+// together at their next barrier, the MMA warp at its next wait, and TMEM is freed.
 #include <algorithm>
 
 #include "common.cuh"
@@ -49,10 +61,16 @@ namespace {
 
 constexpr int kTile = 128;
 constexpr int kWarps = 16;
-constexpr int kThreads = kWarps * 32;
+constexpr int kThreads = kWarps * 32;          // epilogue threads
+constexpr int kMmaWarp = kWarps;                 // warp 16: first warp of the MMA warpgroup
+constexpr int kBlockThreads = kThreads + 128;
+// Registers per thread: at launch (__launch_bounds__(640, 1) caps ptxas at 96), the MMA
+// warpgroup after setmaxnreg.dec, the epilogue warpgroups after setmaxnreg.inc.
+constexpr int kLaunchRegs = 96, kMmaRegs = 32, kEpiRegs = 112;
+static_assert((kLaunchRegs - kMmaRegs) * 128 >= (kEpiRegs - kLaunchRegs) * kThreads,
+              "register split exceeds the launch's registers");
 constexpr int kChunks = 4;                       // 16-neuron chunks per 64-wide GEMM
 constexpr int kGemmsPerTile = 6;                 // forward W1..W3, backward W3^T, W2^T, W1^T
-constexpr int kChunksPerTile = kGemmsPerTile * kChunks;
 constexpr int kRing = 2;
 constexpr uint32_t kSlotCols = 128;
 constexpr uint32_t kTmemCols = 512;
@@ -94,9 +112,8 @@ constexpr int kPLoss = kPartKinds * 256, kPBout = kPLoss + 4;
 constexpr int kPartFloats = kPBout + 4;
 constexpr int kXsOff = kPartOff + kPartFloats * 4;            // the tile's points x[512], y[512]
 constexpr int kBarOff = kXsOff + 2 * kThreads * 4;            // mbarriers
-constexpr int kNumBars = 8;    // empty[2] dfull red wfull[2] dwdone[2]
-constexpr int kCountOff = kBarOff + kNumBars * 8;
-constexpr int kMiscOff = kCountOff + 4 * 4;                   // TMEM base, abort flag, status
+constexpr int kNumBars = 10;   // empty[2] dfull red wfull[2] dwdone[2] full[2]
+constexpr int kMiscOff = kBarOff + kNumBars * 8;              // TMEM base, abort flag, status
 constexpr int kSmemBytes = kMiscOff + 16;
 static_assert(kSmemBytes <= 227 * 1024, "shared memory layout overflow");
 static_assert(kStageOff % 1024 == 0 && kBarOff % 8 == 0 && (kMiscOff + 8) % 8 == 0,
@@ -117,8 +134,9 @@ __device__ __forceinline__ uint64_t* bar_dfull() { return bar_at(kRing); }
 __device__ __forceinline__ uint64_t* bar_red() { return bar_at(kRing + 1); }
 __device__ __forceinline__ uint64_t* bar_wfull(int k) { return bar_at(kRing + 2 + k); }
 __device__ __forceinline__ uint64_t* bar_dwdone(int half) { return bar_at(kRing + 4 + half); }
-__device__ __forceinline__ uint32_t* ring_count(uint32_t r) {
-  return reinterpret_cast<uint32_t*>(dsmem() + kCountOff) + r;
+// A ring slot written by the 16 epilogue warps.
+__device__ __forceinline__ uint64_t* bar_full(uint32_t r) {
+  return bar_at(kRing + 6 + static_cast<int>(r));
 }
 __device__ __forceinline__ volatile uint32_t* abort_flag() {
   return reinterpret_cast<volatile uint32_t*>(dsmem() + kMiscOff + 4);
@@ -152,9 +170,27 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
 
 
 
-// Block-wide barrier that also tells every warp whether any warp has aborted.
+// Barrier 3 over the 16 epilogue warps that also tells every one of them whether any warp
+// has aborted.
 __device__ __forceinline__ bool barrier_ok() {
-  return __syncthreads_or(*abort_flag() != 0u ? 1 : 0) == 0;
+  uint32_t any;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\t"
+      "barrier.red.or.pred q, 3, %2, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(any)
+      : "r"(*abort_flag()), "n"(kThreads)
+      : "memory");
+  return any == 0;
+}
+
+// Register reallocation within the block's launch budget (whole warpgroups, warp-uniform).
+template <uint32_t N>
+__device__ __forceinline__ void regs_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void regs_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
 }
 
 
@@ -227,18 +263,8 @@ __device__ __forceinline__ bool produce_chunk(uint32_t n, const float (&h)[4][4]
   tc::wait_st();
   tc::fence_before_sync();
   __syncwarp();
-  uint32_t last = 0;
-  if ((threadIdx.x & 31) == 0) last = (count_contribution(ring_count(slot)) % kWarps) == kWarps - 1;
-  last = __shfl_sync(0xffffffffu, last, 0);
-  bool ok = true;
-  if (last) {
-    tc::fence_after_sync();
-    const uint32_t in_tile = n % kChunksPerTile;
-    ok = issue_chunk_mmas(cx, n / kChunksPerTile, static_cast<int>(in_tile / kChunks),
-                          static_cast<int>(in_tile % kChunks), slot);
-    __syncwarp();
-  }
-  return ok;
+  if ((threadIdx.x & 31) == 0) mbar_arrive(bar_full(slot));
+  return true;
 }
 
 // Adjoint of the tanh jet in terms of the activation it produced. With h = (a, h_J0, h_J1,
@@ -279,9 +305,29 @@ __device__ __forceinline__ void issue_dw_mmas(const Ctx& cx, int half, bool firs
   tc::commit_warp(bar_dwdone(half));
 }
 
-// Barrier over the 8 warps (256 threads) of one point half; ids 1 and 2 (0 is __syncthreads).
+// Barrier over the 8 warps (256 threads) of one point half; ids 1 and 2 (0 is __syncthreads,
+// 3 the epilogue barrier).
 __device__ __forceinline__ void half_barrier(int half) {
   asm volatile("bar.sync %0, 256;" ::"r"(1 + half) : "memory");
+}
+
+// The MMA warp: issues, in the epilogue warps' order, the MMAs of every chunk of this CTA's
+// tiles (GEMMs 0..5 of each tile). Returns early when a wait gives up.
+__device__ __forceinline__ void mma_warp(const Ctx& cx, int64_t tiles) {
+  uint32_t n = 0, tile_count = 0;
+  for (int64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++tile_count) {
+#pragma unroll 1
+    for (int g = 0; g < kGemmsPerTile; ++g) {
+#pragma unroll 1
+      for (int j = 0; j < kChunks; ++j, ++n) {
+        const uint32_t slot = n % kRing;
+        if (!warp_wait(bar_full(slot), (n / kRing) & 1u)) return;
+        tc::fence_after_sync();
+        if (!issue_chunk_mmas(cx, tile_count, g, j, slot)) return;
+        __syncwarp();
+      }
+    }
+  }
 }
 
 // Sums v[i] over the 32 lanes of the warp for every i < 16 with a fixed butterfly that
@@ -347,7 +393,7 @@ __global__ void __launch_bounds__(256) prep_weights_kernel(const float* __restri
 }
 
 template <bool kPoisson>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kBlockThreads, 1)
     backward_tc_kernel(const PointSets ps, const float* __restrict__ params,
                        const float* __restrict__ wsplit, const float* __restrict__ grad_u,
                        const float* __restrict__ grad_lap, float* __restrict__ grad_coords,
@@ -382,15 +428,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   // The hidden-layer weight gradients are accumulated in place in this CTA's partial row
   // (red.global.add by the thread that owns the entry, so the order is fixed).
+  if (tid < kThreads) {
 #pragma unroll
-  for (int l = 0; l < 3; ++l)
+    for (int l = 0; l < 3; ++l)
 #pragma unroll
-    for (int j = 0; j < 8; ++j) rowp[kHiddenBase + l * kHiddenStride + tid + kThreads * j] = 0.0f;
+      for (int j = 0; j < 8; ++j)
+        rowp[kHiddenBase + l * kHiddenStride + tid + kThreads * j] = 0.0f;
+  }
   if (tid == 0) {
     for (uint32_t r = 0; r < kRing; ++r) {
       mbar_init(bar_empty(r), 1);
-      *ring_count(r) = 0u;
+      mbar_init(bar_full(r), kWarps);
     }
+
     mbar_init(bar_dfull(), 1);
     mbar_init(bar_red(), kWarps);
     for (int k = 0; k < kWeightSlots; ++k) mbar_init(bar_wfull(k), 1);
@@ -411,368 +461,364 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (tid == 0)
     for (int k = 0; k < kWeightSlots; ++k) load_weight_slot(k, wsplit, weight_block(k));
 
-  const int q = warp & 3;   // TMEM lane quadrant
-  const int s = warp >> 2;  // neurons 16a + 4s + t
-  const uint32_t tmem_warp = cx.tmem + (static_cast<uint32_t>(32 * q) << 16);
-  const int row = 32 * q + lane;
-  float* const hscratch = scratch + static_cast<int64_t>(blockIdx.x) * kScratchFloats + tid;
-  // Weight-gradient staging: this thread's point is K index `lane` of K atom q & 1 of
-  // staging buffer q >> 1; neuron row 16a + 4s + t sits at byte a * 2048 + soff[t] of an
-  // operand (plus 8192 for the zbar_lo rows 64.. of A).
-  uint8_t* const stage = smem + kStageOff + (q >> 1) * kStageBytes;
-  uint32_t soff[4];
+  if (warp >= kWarps) {
+    // ---- MMA warpgroup: warp 16 issues the chunks, 17-19 wait at the final barrier ----
+    regs_dec<kMmaRegs>();
+    if (warp == kMmaWarp) mma_warp(cx, tiles);
+  } else {
+    // ---- epilogue warpgroups ----
+    regs_inc<kEpiRegs>();
+    const int q = warp & 3;   // TMEM lane quadrant
+    const int s = warp >> 2;  // neurons 16a + 4s + t
+    const uint32_t tmem_warp = cx.tmem + (static_cast<uint32_t>(32 * q) << 16);
+    const int row = 32 * q + lane;
+    float* const hscratch = scratch + static_cast<int64_t>(blockIdx.x) * kScratchFloats + tid;
+    // Weight-gradient staging: this thread's point is K index `lane` of K atom q & 1 of
+    // staging buffer q >> 1; neuron row 16a + 4s + t sits at byte a * 2048 + soff[t] of an
+    // operand (plus 8192 for the zbar_lo rows 64.. of A).
+    uint8_t* const stage = smem + kStageOff + (q >> 1) * kStageBytes;
+    uint32_t soff[4];
 #pragma unroll
-  for (int t = 0; t < 4; ++t) {
-    const int r7 = 4 * (s & 1) + t;
-    soff[t] = static_cast<uint32_t>((s >> 1) * 1024 + r7 * 128 + (((lane >> 2) ^ r7) << 4) +
-                                    4 * (lane & 3));
-  }
-  const uint32_t ka = static_cast<uint32_t>(q & 1);
-  const int half = q >> 1;
-
-  uint32_t chunk = 0, mlayer = 0, tile_count = 0, dw_issued = 0;
-  bool alive = true;
-  float nx0 = 0.0f, nx1 = 0.0f;
-  load_point(ps, blockIdx.x, kTile, row, nx0, nx1);
-  for (int64_t tile = blockIdx.x; alive && tile < tiles; tile += gridDim.x, ++tile_count) {
-    const bool has_next = tile + gridDim.x < tiles;
-    const bool btile = tile >= ps.tiles;  // a tile of the boundary set (PINN step)
-    const int64_t p = (btile ? tile - ps.tiles : tile) * kTile + row;
-    const bool active = p < (btile ? ps.nb : ps.n);
-    // This tile's point, loaded during the previous tile, is kept in shared memory so that
-    // no register holds it through the backward sweep.
-    xs[tid] = nx0;
-    xs[kThreads + tid] = nx1;
-
-    // ---- forward recompute: layer 0, then the three hidden GEMMs ----
-#pragma unroll
-    for (int a = 0; a < kChunks; ++a) {
-      float h[4][4];
-#pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        const int o = 16 * a + 4 * s + t;
-        const float w0 = small[kSmW0 + 2 * o], w1 = small[kSmW0 + 2 * o + 1];
-        tanh_jet_fast(fmaf(w0, nx0, fmaf(w1, nx1, small[kSmB0 + o])), w0, w1, 0.0f, h[0][t],
-                      h[1][t], h[2][t], h[3][t]);
-      }
-      produce_chunk(chunk++, h, tmem_warp, s, cx);
+    for (int t = 0; t < 4; ++t) {
+      const int r7 = 4 * (s & 1) + t;
+      soff[t] = static_cast<uint32_t>((s >> 1) * 1024 + r7 * 128 + (((lane >> 2) ^ r7) << 4) +
+                                      4 * (lane & 3));
     }
-    float d[4][16];  // d[c][4a + t]: component c of neuron 16a + 4s + t
-#pragma unroll 1
-    for (int g = 0; g < 3; ++g) {
-      warp_wait(bar_dfull(), mlayer & 1u);
-      ++mlayer;
-      tc::fence_after_sync();
-      // GEMM g is complete: its weight slot takes the operand of GEMM g + 2.
-      if (tid == 0) load_weight_slot(g & 1, wsplit, weight_block(g + 2));
-#pragma unroll
-      for (int c = 0; c < 4; ++c)
-#pragma unroll
-        for (int a = 0; a < 4; ++a)
-          tc::ld_x4(tmem_warp + 64u * c + 16u * a + 4u * s,
-                    *reinterpret_cast<float(*)[4]>(&d[c][4 * a]));
-      tc::wait_ld();
-      const float* bias = small + kSmB + 64 * g;
-#pragma unroll
-      for (int i = 0; i < 16; ++i) d[0][i] += bias[16 * (i >> 2) + 4 * s + (i & 3)];
-      if (g < 2) {
-        float* hj = hscratch + g * (4 * 16 * kThreads);  // h_{g+1}
-#pragma unroll
-        for (int a = 0; a < kChunks; ++a) {
-          float h[4][4];
-#pragma unroll
-          for (int t = 0; t < 4; ++t) {
-            const int i = 4 * a + t;
-            tanh_jet_fast(d[0][i], d[1][i], d[2][i], d[3][i], h[0][t], h[1][t], h[2][t],
-                          h[3][t]);
-#pragma unroll
-            for (int c = 0; c < 4; ++c) hj[(c * 16 + i) * kThreads] = h[c][t];
-          }
-          produce_chunk(chunk++, h, tmem_warp, s, cx);
-        }
-      }
-    }
+    const uint32_t ka = static_cast<uint32_t>(q & 1);
+    const int half = q >> 1;
 
-    // ---- output layer, loss seed, layer-3 adjoint (d becomes h3, then zbar3) ----
-    {
-      float pu = 0.0f, pl = 0.0f;
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        tanh_jet_fast(d[0][i], d[1][i], d[2][i], d[3][i], d[0][i], d[1][i], d[2][i], d[3][i]);
-        const float w = small[kSmWout + 16 * (i >> 2) + 4 * s + (i & 3)];
-        pu = fmaf(w, d[0][i], pu);
-        pl = fmaf(w, d[3][i], pl);
-      }
-      red[s * kTile + row] = pu;
-      red[(4 + s) * kTile + row] = pl;
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar_red());
-      warp_wait(bar_red(), tile_count & 1u);
-      float lap = 0.0f;
-#pragma unroll
-      for (int k = 0; k < 4; ++k) lap += red[(4 + k) * kTile + row];
-      float gu, gl;
-      if (kPoisson) {
-        float term;  // this point's loss term
-        if (!btile) {
-          // f = -2 pi^2 sin(pi x) sin(pi y)  (src/fused_hoad/problems/poisson.py:29-39)
-          const float pi = 3.14159265358979323846f;
-          const float f =
-              -2.0f * pi * pi * (sinf(pi * xs[tid]) * sinf(pi * xs[kThreads + tid]));
-          const float r = active ? lap - f : 0.0f;
-          gu = 0.0f;
-          gl = 2.0f * r * ps.inv_total;
-          term = r * r * ps.inv_total;
-          if (s == 0 && active && lap_out != nullptr) lap_out[p] = lap;
-        } else {
-          // boundary term weight * u^2 / boundary_total (src/fused_hoad/training.py:90-92)
-          float u = small[kSmBout];
-#pragma unroll
-          for (int k = 0; k < 4; ++k) u += red[k * kTile + row];
-          u = active ? u : 0.0f;
-          gu = 2.0f * ps.bweight * u * ps.inv_btotal;
-          gl = 0.0f;
-          term = ps.bweight * u * u * ps.inv_btotal;
-        }
-        if (s == 0) {
-          const float l2 = warp_sum(term);
-          const float sg = btile ? warp_sum(gu) : 0.0f;  // b_out gradient (boundary term)
-          if (lane == 0) {
-            part[kPLoss + q] = l2;
-            part[kPBout + q] = sg;
-          }
-        }
-      } else {
-        gu = (active && grad_u != nullptr) ? grad_u[p] : 0.0f;
-        gl = active ? grad_lap[p] : 0.0f;
-        if (s == 0) {
-          const float sg = warp_sum(gu);
-          if (lane == 0) part[kPBout + q] = sg;
-        }
-      }
-      float dwo[16];
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const int o = 16 * (i >> 2) + 4 * s + (i & 3);
-        const float w = small[kSmWout + o];
-        dwo[i] = fmaf(gu, d[0][i], gl * d[3][i]);
-        float gv = gu * w, g0 = 0.0f, g1 = 0.0f, gL = gl * w;
-        adjoint_h(d[0][i], d[1][i], d[2][i], d[3][i], gv, g0, g1, gL);
-        d[0][i] = gv;
-        d[1][i] = g0;
-        d[2][i] = g1;
-        d[3][i] = gL;
-      }
-      store_part16(part, 0, q, s, warp_sum16(dwo));   // w_out
-      store_part16(part, 6, q, s, warp_sum16(d[0]));  // b3
-    }
+    uint32_t chunk = 0, mlayer = 0, tile_count = 0, dw_issued = 0;
+    bool alive = true;
+    float nx0 = 0.0f, nx1 = 0.0f;
+    load_point(ps, blockIdx.x, kTile, row, nx0, nx1);
+    for (int64_t tile = blockIdx.x; alive && tile < tiles; tile += gridDim.x, ++tile_count) {
+      const bool has_next = tile + gridDim.x < tiles;
+      const bool btile = tile >= ps.tiles;  // a tile of the boundary set (PINN step)
+      const int64_t p = (btile ? tile - ps.tiles : tile) * kTile + row;
+      const bool active = p < (btile ? ps.nb : ps.n);
+      // This tile's point, loaded during the previous tile, is kept in shared memory so that
+      // no register holds it through the backward sweep.
+      xs[tid] = nx0;
+      xs[kThreads + tid] = nx1;
 
-    // ---- backward through the hidden layers: d holds zbar_l on entry ----
-#pragma unroll 1
-    for (int l = 3; l >= 1; --l) {
-      const int g = 6 - l;
-      // zbar_l -> ring (input-adjoint GEMM g)
+      // ---- forward recompute: layer 0, then the three hidden GEMMs ----
 #pragma unroll
       for (int a = 0; a < kChunks; ++a) {
-        float z[4][4];
+        float h[4][4];
 #pragma unroll
-        for (int t = 0; t < 4; ++t)
-#pragma unroll
-          for (int c = 0; c < 4; ++c) z[c][t] = d[c][4 * a + t];
-        produce_chunk(chunk++, z, tmem_warp, s, cx);
+        for (int t = 0; t < 4; ++t) {
+          const int o = 16 * a + 4 * s + t;
+          const float w0 = small[kSmW0 + 2 * o], w1 = small[kSmW0 + 2 * o + 1];
+          tanh_jet_fast(fmaf(w0, nx0, fmaf(w1, nx1, small[kSmB0 + o])), w0, w1, 0.0f, h[0][t],
+                        h[1][t], h[2][t], h[3][t]);
+        }
+        produce_chunk(chunk++, h, tmem_warp, s, cx);
       }
-
-      // weight gradient dW_l: per jet component, stage zbar_l and h_{l-1} (hi/lo) for the
-      // tile's 128 points and let one warp issue the MMAs. Unrolled, so that the registers
-      // of component c of zbar_l are free once its round is staged.
-      const float* hsrc = hscratch + (l == 3 ? 4 * 16 * kThreads : 0);  // h_{l-1} (l >= 2)
+      float d[4][16];  // d[c][4a + t]: component c of neuron 16a + 4s + t
+#pragma unroll 1
+      for (int g = 0; g < 3; ++g) {
+        warp_wait(bar_dfull(), mlayer & 1u);
+        ++mlayer;
+        tc::fence_after_sync();
+        // GEMM g is complete: its weight slot takes the operand of GEMM g + 2.
+        if (tid == 0) load_weight_slot(g & 1, wsplit, weight_block(g + 2));
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        float hv[16];
-        if (l > 1) {
+        for (int c = 0; c < 4; ++c)
 #pragma unroll
-          for (int i = 0; i < 16; ++i) hv[i] = hsrc[(c * 16 + i) * kThreads];
-        } else {
-          const float x0 = xs[tid], x1 = xs[kThreads + tid];
+          for (int a = 0; a < 4; ++a)
+            tc::ld_x4(tmem_warp + 64u * c + 16u * a + 4u * s,
+                      *reinterpret_cast<float(*)[4]>(&d[c][4 * a]));
+        tc::wait_ld();
+        const float* bias = small + kSmB + 64 * g;
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int o = 16 * (i >> 2) + 4 * s + (i & 3);
-            const float w0 = small[kSmW0 + 2 * o], w1 = small[kSmW0 + 2 * o + 1];
-            float v, j0, j1, lv;
-            tanh_jet_fast(fmaf(w0, x0, fmaf(w1, x1, small[kSmB0 + o])), w0, w1, 0.0f, v, j0,
-                          j1, lv);
-            hv[i] = c == 0 ? v : c == 1 ? j0 : c == 2 ? j1 : lv;
+        for (int i = 0; i < 16; ++i) d[0][i] += bias[16 * (i >> 2) + 4 * s + (i & 3)];
+        if (g < 2) {
+          float* hj = hscratch + g * (4 * 16 * kThreads);  // h_{g+1}
+#pragma unroll
+          for (int a = 0; a < kChunks; ++a) {
+            float h[4][4];
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+              const int i = 4 * a + t;
+              tanh_jet_fast(d[0][i], d[1][i], d[2][i], d[3][i], h[0][t], h[1][t], h[2][t],
+                            h[3][t]);
+#pragma unroll
+              for (int c = 0; c < 4; ++c) hj[(c * 16 + i) * kThreads] = h[c][t];
+            }
+            produce_chunk(chunk++, h, tmem_warp, s, cx);
           }
         }
-        if (c > 0) warp_wait(bar_dwdone(half), (dw_issued - 1u) & 1u);  // buffer free again
+      }
+
+      // ---- output layer, loss seed, layer-3 adjoint (d becomes h3, then zbar3) ----
+      {
+        float pu = 0.0f, pl = 0.0f;
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const int a = i >> 2, t = i & 3;
-          const float z = c == 0 ? d[0][i] : c == 1 ? d[1][i] : c == 2 ? d[2][i] : d[3][i];
-          uint32_t zh, zl, hh, hl;
-          tc::split_tf32(z, zh, zl);
-          tc::split_tf32(hv[i], hh, hl);
-          const uint32_t o = a * 2048 + soff[t];
-          *reinterpret_cast<uint32_t*>(stage + kStageA + ka * 16384u + o) = zh;
-          *reinterpret_cast<uint32_t*>(stage + kStageA + ka * 16384u + 8192u + o) = zl;
-          *reinterpret_cast<uint32_t*>(stage + kStageB + ka * 16384u + o) = hh;
-          *reinterpret_cast<uint32_t*>(stage + kStageB + ka * 16384u + 8192u + o) = hl;
+          tanh_jet_fast(d[0][i], d[1][i], d[2][i], d[3][i], d[0][i], d[1][i], d[2][i], d[3][i]);
+          const float w = small[kSmWout + 16 * (i >> 2) + 4 * s + (i & 3)];
+          pu = fmaf(w, d[0][i], pu);
+          pl = fmaf(w, d[3][i], pl);
         }
-        tc::fence_proxy_async_smem();
-        half_barrier(half);
-        if (s == 0 && (q & 1) == 0) {  // warp 2 * half issues for its half
-          if (c == 0) {
-            // the input-adjoint GEMM g has finished with the ring columns the weight-gradient
-            // accumulators borrow, and with its weight slot
-            warp_wait(bar_dfull(), mlayer & 1u);
-            tc::fence_after_sync();
-            if (half == 0 && lane == 0 && (g + 2 < kGemmsPerTile || has_next))
-              load_weight_slot(g & 1, wsplit, weight_block((g + 2) % kGemmsPerTile));
+        red[s * kTile + row] = pu;
+        red[(4 + s) * kTile + row] = pl;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar_red());
+        warp_wait(bar_red(), tile_count & 1u);
+        float lap = 0.0f;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) lap += red[(4 + k) * kTile + row];
+        float gu, gl;
+        if (kPoisson) {
+          float term;  // this point's loss term
+          if (!btile) {
+            // f = -2 pi^2 sin(pi x) sin(pi y)  (src/fused_hoad/problems/poisson.py:29-39)
+            const float pi = 3.14159265358979323846f;
+            const float f =
+                -2.0f * pi * pi * (sinf(pi * xs[tid]) * sinf(pi * xs[kThreads + tid]));
+            const float r = active ? lap - f : 0.0f;
+            gu = 0.0f;
+            gl = 2.0f * r * ps.inv_total;
+            term = r * r * ps.inv_total;
+            if (s == 0 && active && lap_out != nullptr) lap_out[p] = lap;
+          } else {
+            // boundary term weight * u^2 / boundary_total (src/fused_hoad/training.py:90-92)
+            float u = small[kSmBout];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) u += red[k * kTile + row];
+            u = active ? u : 0.0f;
+            gu = 2.0f * ps.bweight * u * ps.inv_btotal;
+            gl = 0.0f;
+            term = ps.bweight * u * u * ps.inv_btotal;
           }
-          tc::fence_after_sync();
-          issue_dw_mmas(cx, half, c == 0);
+          if (s == 0) {
+            const float l2 = warp_sum(term);
+            const float sg = btile ? warp_sum(gu) : 0.0f;  // b_out gradient (boundary term)
+            if (lane == 0) {
+              part[kPLoss + q] = l2;
+              part[kPBout + q] = sg;
+            }
+          }
+        } else {
+          gu = (active && grad_u != nullptr) ? grad_u[p] : 0.0f;
+          gl = active ? grad_lap[p] : 0.0f;
+          if (s == 0) {
+            const float sg = warp_sum(gu);
+            if (lane == 0) part[kPBout + q] = sg;
+          }
         }
-        ++dw_issued;
+        float dwo[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int o = 16 * (i >> 2) + 4 * s + (i & 3);
+          const float w = small[kSmWout + o];
+          dwo[i] = fmaf(gu, d[0][i], gl * d[3][i]);
+          float gv = gu * w, g0 = 0.0f, g1 = 0.0f, gL = gl * w;
+          adjoint_h(d[0][i], d[1][i], d[2][i], d[3][i], gv, g0, g1, gL);
+          d[0][i] = gv;
+          d[1][i] = g0;
+          d[2][i] = g1;
+          d[3][i] = gL;
+        }
+        store_part16(part, 0, q, s, warp_sum16(dwo));   // w_out
+        store_part16(part, 6, q, s, warp_sum16(d[0]));  // b3
       }
 
-      // empty the accumulator into this CTA's partial row: hi and lo halves summed in shared
-      // memory (staging buffer 0), one owner thread per entry
-      // Both halves first pass this barrier: each half has then waited for its round-2
-      // commit, so the parity wait below can only mean round 3 (without it, a half that is
-      // two rounds behind would satisfy the wait with its round-1 phase).
-      if (!(alive = barrier_ok())) break;
-      warp_wait(bar_dwdone(0), (dw_issued - 1u) & 1u);
-      warp_wait(bar_dwdone(1), (dw_issued - 1u) & 1u);
-      tc::fence_after_sync();
-      {
-        float* fb = reinterpret_cast<float*>(smem + kStageOff);
-        // columns i (h_hi) and 64 + i (h_lo) of this warp's row, in both halves' accumulators
-        float v[16], w[16];
-        tc::ld_x16(tmem_warp + kDwCol + 16u * s, v);
-        tc::ld_x16(tmem_warp + kDwCol + 64u + 16u * s, w);
-        tc::wait_ld();
-#pragma unroll
-        for (int k = 0; k < 16; ++k) v[k] += w[k];
-        tc::ld_x16(tmem_warp + kDwCol + 128u + 16u * s, w);
-        tc::wait_ld();
-#pragma unroll
-        for (int k = 0; k < 16; ++k) v[k] += w[k];
-        tc::ld_x16(tmem_warp + kDwCol + 192u + 16u * s, w);
-        tc::wait_ld();
-#pragma unroll
-        for (int k = 0; k < 16; ++k) v[k] += w[k];
-#pragma unroll
-        for (int k = 0; k < 16; ++k) fb[row * kFlushStride + 16 * s + k] = v[k];
-        tc::fence_before_sync();
-        if (!(alive = barrier_ok())) break;
-        float* wrow = rowp + kHiddenBase + (l - 1) * kHiddenStride;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const int e = tid + kThreads * j, o = e >> 6, i = e & 63;
-          red_add(wrow + e, fb[o * kFlushStride + i] + fb[(64 + o) * kFlushStride + i]);
-        }
-        if (!(alive = barrier_ok())) break;
-      }
-
-      // input adjoint hbar_{l-1} = zbar_l W_l (GEMM g), then zbar_{l-1}
-      float hn[4][4];  // h_{l-1} of the next neuron group, loaded ahead of use
-      if (l > 1) {
-#pragma unroll
-        for (int t = 0; t < 4; ++t)
-#pragma unroll
-          for (int c = 0; c < 4; ++c) hn[c][t] = hsrc[(c * 16 + t) * kThreads];
-      }
-      warp_wait(bar_dfull(), mlayer & 1u);
-      ++mlayer;
-      tc::fence_after_sync();
-#pragma unroll
-      for (int c = 0; c < 4; ++c)
-#pragma unroll
-        for (int a = 0; a < 4; ++a)
-          tc::ld_x4(tmem_warp + 64u * c + 16u * a + 4u * s,
-                    *reinterpret_cast<float(*)[4]>(&d[c][4 * a]));
-      tc::wait_ld();
-      if (l > 1) {
+      // ---- backward through the hidden layers: d holds zbar_l on entry ----
+#pragma unroll 1
+      for (int l = 3; l >= 1; --l) {
+        const int g = 6 - l;
+        // zbar_l -> ring (input-adjoint GEMM g)
 #pragma unroll
         for (int a = 0; a < kChunks; ++a) {
-          float h[4][4];
+          float z[4][4];
 #pragma unroll
           for (int t = 0; t < 4; ++t)
 #pragma unroll
-            for (int c = 0; c < 4; ++c) h[c][t] = hn[c][t];
-          if (a + 1 < kChunks) {
+            for (int c = 0; c < 4; ++c) z[c][t] = d[c][4 * a + t];
+          produce_chunk(chunk++, z, tmem_warp, s, cx);
+        }
+
+        // weight gradient dW_l: per jet component, stage zbar_l and h_{l-1} (hi/lo) for the
+        // tile's 128 points and let one warp issue the MMAs. Unrolled, so that the registers
+        // of component c of zbar_l are free once its round is staged.
+        const float* hsrc = hscratch + (l == 3 ? 4 * 16 * kThreads : 0);  // h_{l-1} (l >= 2)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          float hv[16];
+          if (l > 1) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i) hv[i] = hsrc[(c * 16 + i) * kThreads];
+          } else {
+            const float x0 = xs[tid], x1 = xs[kThreads + tid];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const int o = 16 * (i >> 2) + 4 * s + (i & 3);
+              const float w0 = small[kSmW0 + 2 * o], w1 = small[kSmW0 + 2 * o + 1];
+              float v, j0, j1, lv;
+              tanh_jet_fast(fmaf(w0, x0, fmaf(w1, x1, small[kSmB0 + o])), w0, w1, 0.0f, v, j0,
+                            j1, lv);
+              hv[i] = c == 0 ? v : c == 1 ? j0 : c == 2 ? j1 : lv;
+            }
+          }
+          if (c > 0) warp_wait(bar_dwdone(half), (dw_issued - 1u) & 1u);  // buffer free again
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int a = i >> 2, t = i & 3;
+            const float z = c == 0 ? d[0][i] : c == 1 ? d[1][i] : c == 2 ? d[2][i] : d[3][i];
+            uint32_t zh, zl, hh, hl;
+            tc::split_tf32(z, zh, zl);
+            tc::split_tf32(hv[i], hh, hl);
+            const uint32_t o = a * 2048 + soff[t];
+            *reinterpret_cast<uint32_t*>(stage + kStageA + ka * 16384u + o) = zh;
+            *reinterpret_cast<uint32_t*>(stage + kStageA + ka * 16384u + 8192u + o) = zl;
+            *reinterpret_cast<uint32_t*>(stage + kStageB + ka * 16384u + o) = hh;
+            *reinterpret_cast<uint32_t*>(stage + kStageB + ka * 16384u + 8192u + o) = hl;
+          }
+          tc::fence_proxy_async_smem();
+          half_barrier(half);
+          if (s == 0 && (q & 1) == 0) {  // warp 2 * half issues for its half
+            if (c == 0) {
+              // the input-adjoint GEMM g has finished with the ring columns the weight-gradient
+              // accumulators borrow, and with its weight slot
+              warp_wait(bar_dfull(), mlayer & 1u);
+              tc::fence_after_sync();
+              if (half == 0 && lane == 0 && (g + 2 < kGemmsPerTile || has_next))
+                load_weight_slot(g & 1, wsplit, weight_block((g + 2) % kGemmsPerTile));
+            }
+            tc::fence_after_sync();
+            issue_dw_mmas(cx, half, c == 0);
+          }
+          ++dw_issued;
+        }
+
+        // empty the accumulator into this CTA's partial row: hi and lo halves summed in shared
+        // memory (staging buffer 0), one owner thread per entry
+        // Both halves first pass this barrier: each half has then waited for its round-2
+        // commit, so the parity wait below can only mean round 3 (without it, a half that is
+        // two rounds behind would satisfy the wait with its round-1 phase).
+        if (!(alive = barrier_ok())) break;
+        warp_wait(bar_dwdone(0), (dw_issued - 1u) & 1u);
+        warp_wait(bar_dwdone(1), (dw_issued - 1u) & 1u);
+        tc::fence_after_sync();
+        {
+          float* fb = reinterpret_cast<float*>(smem + kStageOff);
+          // columns i (h_hi) and 64 + i (h_lo) of this warp's row, in both halves' accumulators
+          float v[16], w[16];
+          tc::ld_x16(tmem_warp + kDwCol + 16u * s, v);
+          tc::ld_x16(tmem_warp + kDwCol + 64u + 16u * s, w);
+          tc::wait_ld();
+#pragma unroll
+          for (int k = 0; k < 16; ++k) v[k] += w[k];
+          tc::ld_x16(tmem_warp + kDwCol + 128u + 16u * s, w);
+          tc::wait_ld();
+#pragma unroll
+          for (int k = 0; k < 16; ++k) v[k] += w[k];
+          tc::ld_x16(tmem_warp + kDwCol + 192u + 16u * s, w);
+          tc::wait_ld();
+#pragma unroll
+          for (int k = 0; k < 16; ++k) v[k] += w[k];
+#pragma unroll
+          for (int k = 0; k < 16; ++k) fb[row * kFlushStride + 16 * s + k] = v[k];
+          tc::fence_before_sync();
+          if (!(alive = barrier_ok())) break;
+          float* wrow = rowp + kHiddenBase + (l - 1) * kHiddenStride;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const int e = tid + kThreads * j, o = e >> 6, i = e & 63;
+            red_add(wrow + e, fb[o * kFlushStride + i] + fb[(64 + o) * kFlushStride + i]);
+          }
+          if (!(alive = barrier_ok())) break;
+        }
+
+        // input adjoint hbar_{l-1} = zbar_l W_l (GEMM g), then zbar_{l-1}
+
+        warp_wait(bar_dfull(), mlayer & 1u);
+        ++mlayer;
+        tc::fence_after_sync();
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+#pragma unroll
+          for (int a = 0; a < 4; ++a)
+            tc::ld_x4(tmem_warp + 64u * c + 16u * a + 4u * s,
+                      *reinterpret_cast<float(*)[4]>(&d[c][4 * a]));
+        tc::wait_ld();
+        if (l > 1) {
+#pragma unroll
+          for (int a = 0; a < kChunks; ++a) {
+            float h[4][4];
 #pragma unroll
             for (int t = 0; t < 4; ++t)
 #pragma unroll
-              for (int c = 0; c < 4; ++c) hn[c][t] = hsrc[(c * 16 + 4 * (a + 1) + t) * kThreads];
-          }
+for (int c = 0; c < 4; ++c) h[c][t] = hsrc[(c * 16 + 4 * a + t) * kThreads];
 #pragma unroll
-          for (int t = 0; t < 4; ++t) {
-            const int i = 4 * a + t;
-            adjoint_h(h[0][t], h[1][t], h[2][t], h[3][t], d[0][i], d[1][i], d[2][i], d[3][i]);
+            for (int t = 0; t < 4; ++t) {
+              const int i = 4 * a + t;
+              adjoint_h(h[0][t], h[1][t], h[2][t], h[3][t], d[0][i], d[1][i], d[2][i], d[3][i]);
+            }
           }
+          store_part16(part, 2 + l, q, s, warp_sum16(d[0]));  // b_{l-1}
         }
-        store_part16(part, 2 + l, q, s, warp_sum16(d[0]));  // b_{l-1}
       }
-    }
-    if (!alive) break;
+      if (!alive) break;
 
-    // The next tile's point: loaded now, used at the next tile's start.
-    load_point(ps, tile + gridDim.x, kTile, row, nx0, nx1);
+      // The next tile's point: loaded now, used at the next tile's start.
+      load_point(ps, tile + gridDim.x, kTile, row, nx0, nx1);
 
-    // ---- layer 0: z_v = W0 x + b0, z_J = W0, z_L = 0; d holds hbar_0 ----
-    {
-      const float x0 = xs[tid], x1 = xs[kThreads + tid];
-      float gx0 = 0.0f, gx1 = 0.0f;
+      // ---- layer 0: z_v = W0 x + b0, z_J = W0, z_L = 0; d holds hbar_0 ----
+      {
+        const float x0 = xs[tid], x1 = xs[kThreads + tid];
+        float gx0 = 0.0f, gx1 = 0.0f;
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const int o = 16 * (i >> 2) + 4 * s + (i & 3);
-        const float w0 = small[kSmW0 + 2 * o], w1 = small[kSmW0 + 2 * o + 1];
-        float a, hj0, hj1, hl;
-        tanh_jet_fast(fmaf(w0, x0, fmaf(w1, x1, small[kSmB0 + o])), w0, w1, 0.0f, a, hj0, hj1,
-                      hl);
-        float gv = d[0][i], g0 = d[1][i], g1 = d[2][i], gL = d[3][i];
-        adjoint_h(a, hj0, hj1, hl, gv, g0, g1, gL);
-        d[0][i] = gv;                  // db0 terms
-        d[1][i] = fmaf(gv, x0, g0);    // dW0[:, 0] terms
-        d[2][i] = fmaf(gv, x1, g1);    // dW0[:, 1] terms
-        gx0 = fmaf(w0, gv, gx0);
-        gx1 = fmaf(w1, gv, gx1);
+        for (int i = 0; i < 16; ++i) {
+          const int o = 16 * (i >> 2) + 4 * s + (i & 3);
+          const float w0 = small[kSmW0 + 2 * o], w1 = small[kSmW0 + 2 * o + 1];
+          float a, hj0, hj1, hl;
+          tanh_jet_fast(fmaf(w0, x0, fmaf(w1, x1, small[kSmB0 + o])), w0, w1, 0.0f, a, hj0, hj1,
+                        hl);
+          float gv = d[0][i], g0 = d[1][i], g1 = d[2][i], gL = d[3][i];
+          adjoint_h(a, hj0, hj1, hl, gv, g0, g1, gL);
+          d[0][i] = gv;                  // db0 terms
+          d[1][i] = fmaf(gv, x0, g0);    // dW0[:, 0] terms
+          d[2][i] = fmaf(gv, x1, g1);    // dW0[:, 1] terms
+          gx0 = fmaf(w0, gv, gx0);
+          gx1 = fmaf(w1, gv, gx1);
+        }
+        store_part16(part, 1, q, s, warp_sum16(d[0]));
+        store_part16(part, 2, q, s, warp_sum16(d[1]));
+        store_part16(part, 3, q, s, warp_sum16(d[2]));
+        red[s * kTile + row] = gx0;
+        red[(4 + s) * kTile + row] = gx1;
       }
-      store_part16(part, 1, q, s, warp_sum16(d[0]));
-      store_part16(part, 2, q, s, warp_sum16(d[1]));
-      store_part16(part, 3, q, s, warp_sum16(d[2]));
-      red[s * kTile + row] = gx0;
-      red[(4 + s) * kTile + row] = gx1;
-    }
-    if (!(alive = barrier_ok())) break;
-    if (s == 0 && active && !btile && grad_coords != nullptr) {
-      float sx = 0.0f, sy = 0.0f;
+      if (!(alive = barrier_ok())) break;
+      if (s == 0 && active && !btile && grad_coords != nullptr) {
+        float sx = 0.0f, sy = 0.0f;
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        sx += red[k * kTile + row];
-        sy += red[(4 + k) * kTile + row];
+        for (int k = 0; k < 4; ++k) {
+          sx += red[k * kTile + row];
+          sy += red[(4 + k) * kTile + row];
+        }
+        grad_coords[2 * p] = sx;
+        grad_coords[2 * p + 1] = sy;
       }
-      grad_coords[2 * p] = sx;
-      grad_coords[2 * p + 1] = sy;
+      // per-quadrant partials -> accumulators, quadrants in index order
+      if (tid < kPartKinds * kWidth) {
+        const int kind = tid >> 6, o = tid & 63;
+        const float* src = part + kind * 256 + o;
+        const float v = ((src[0] + src[64]) + src[128]) + src[192];
+        if (kind == 0) grad[kGWout + o] += v;
+        else if (kind == 1) grad[kGBias + o] += v;
+        else if (kind <= 3) grad[kGW0 + 2 * o + (kind - 2)] += v;
+        else grad[kGBias + (kind - 3) * kWidth + o] += v;
+      } else if (tid == kPartKinds * kWidth) {
+        if (kPoisson)
+          grad[kGLoss] += ((part[kPLoss] + part[kPLoss + 1]) + part[kPLoss + 2]) + part[kPLoss + 3];
+        grad[kGBout] += ((part[kPBout] + part[kPBout + 1]) + part[kPBout + 2]) + part[kPBout + 3];
+      }
+      if (!(alive = barrier_ok())) break;
     }
-    // per-quadrant partials -> accumulators, quadrants in index order
-    if (tid < kPartKinds * kWidth) {
-      const int kind = tid >> 6, o = tid & 63;
-      const float* src = part + kind * 256 + o;
-      const float v = ((src[0] + src[64]) + src[128]) + src[192];
-      if (kind == 0) grad[kGWout + o] += v;
-      else if (kind == 1) grad[kGBias + o] += v;
-      else if (kind <= 3) grad[kGW0 + 2 * o + (kind - 2)] += v;
-      else grad[kGBias + (kind - 3) * kWidth + o] += v;
-    } else if (tid == kPartKinds * kWidth) {
-      if (kPoisson)
-        grad[kGLoss] += ((part[kPLoss] + part[kPLoss + 1]) + part[kPLoss + 2]) + part[kPLoss + 3];
-      grad[kGBout] += ((part[kPBout] + part[kPBout + 1]) + part[kPBout + 2]) + part[kPBout + 3];
-    }
-    if (!(alive = barrier_ok())) break;
+
   }
-
   // ---- teardown: free TMEM (after an abort, let issued MMAs and copies drain first) ----
   const bool aborted = *abort_flag() != 0u;
   tc::fence_before_sync();
@@ -804,15 +850,23 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+template <bool kPoisson>
+cudaError_t set_attributes() {
+  // The setmaxnreg split assumes kLaunchRegs per thread at launch; a build with fewer would
+  // leave the epilogue's register raise waiting forever, so it is refused here.
+  cudaFuncAttributes attr;
+  const cudaError_t e = cudaFuncGetAttributes(&attr, backward_tc_kernel<kPoisson>);
+  if (e != cudaSuccess) return e;
+  if (attr.numRegs != kLaunchRegs) return cudaErrorInvalidKernelImage;
+  return cudaFuncSetAttribute(backward_tc_kernel<kPoisson>,
+                              cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+}
+
 }  // namespace
 
 cudaError_t prepare_backward_tc() {
-  cudaError_t e = cudaFuncSetAttribute(backward_tc_kernel<false>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-  if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(backward_tc_kernel<true>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-  return e;
+  const cudaError_t e = set_attributes<false>();
+  return e == cudaSuccess ? set_attributes<true>() : e;
 }
 
 int backward_tc_grid(int64_t n, int64_t nb, const DeviceInfo& dev) {
@@ -840,11 +894,11 @@ cudaError_t launch_backward_tc(const PointSets& points, const float* params,
   float* scratch = partials + static_cast<size_t>(grid) * kRowStride;
   prep_weights_kernel<<<(kWeightBlocks * 4096 + 255) / 256, 256, 0, stream>>>(params, wsplit);
   if (poisson) {
-    backward_tc_kernel<true><<<grid, kThreads, kSmemBytes, stream>>>(
+    backward_tc_kernel<true><<<grid, kBlockThreads, kSmemBytes, stream>>>(
         ps, params, wsplit, nullptr, nullptr, grad_coords, lap_out, partials, scratch, tiles,
         dev.status);
   } else {
-    backward_tc_kernel<false><<<grid, kThreads, kSmemBytes, stream>>>(
+    backward_tc_kernel<false><<<grid, kBlockThreads, kSmemBytes, stream>>>(
         ps, params, wsplit, grad_u, grad_lap, grad_coords, nullptr, partials, scratch, tiles,
         dev.status);
   }

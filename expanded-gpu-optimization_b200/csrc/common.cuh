@@ -94,18 +94,6 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
-// Atomic +1 on a shared-memory counter with acquire-release semantics, returning the old
-// value: a warp releases its contribution to a pipeline slot and learns whether it was the
-// last contributor.
-__device__ __forceinline__ uint32_t count_contribution(uint32_t* counter) {
-  uint32_t old;
-  asm volatile("atom.acq_rel.cta.shared::cta.add.u32 %0, [%1], 1;"
-               : "=r"(old)
-               : "r"(smem_u32(counter))
-               : "memory");
-  return old;
-}
-
 // One bulk (TMA, non-multicast) copy global -> this CTA's shared memory, completing on bar.
 // Both addresses 16-byte aligned, bytes a multiple of 16.
 __device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32_t bytes,
