@@ -204,10 +204,12 @@ __device__ __forceinline__ float warp_max(float v) {
 // The largest power of 2 <= 2^c / y, y = max(x, 1e-30), clamped to [2^-126, 2^127], from the
 // exponent and mantissa bits alone: for y = m 2^e (m in [1, 2)) the quotient is 2^(c-e) when
 // m = 1 and lies in (2^(c-e-1), 2^(c-e)) otherwise (a correctly rounded division never reaches
-// 2^(c-e) then, so this equals flooring the divided value).
+// 2^(c-e) then, so this equals flooring the divided value; an infinite y divides to 0 and
+// clamps to 2^-126). tests/test_scale_math.py checks the equality over the float32 range.
 __device__ __forceinline__ float pow2_floor_ratio(int c, float x) {
   const uint32_t b = __float_as_uint(fmaxf(x, 1e-30f));
   int k = c - (static_cast<int>(b >> 23) - 127) - ((b & 0x7FFFFFu) != 0u ? 1 : 0);
+  if (b >= 0x7F800000u) k = -126;  // an overflowed (infinite) bound: the quotient is 0
   k = min(max(k, -126), 127);
   return __uint_as_float(static_cast<uint32_t>(k + 127) << 23);
 }

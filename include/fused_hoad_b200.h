@@ -87,7 +87,9 @@ int fhb_prepare_device(int device);
  *               2: 64-point tiles, the default);
  * version 3:    3xFP16 tcgen05/TMEM tensor-core kernel (kind::f16; hi/lo f16 operand pairs
  *               with per-launch power-of-2 scales derived from the weights, so no operand
- *               leaves the f16 range; FP32-level accuracy), the fastest;
+ *               leaves the f16 range; FP32-level accuracy), the fastest. The scales come
+ *               from FP32 upper bounds of the jets, which overflow for weights around
+ *               3e5 times the nn.Linear default init (|W| ~ 4e4); use 4 or 5 beyond that;
  * version 4, 5: 3xTF32 tcgen05/TMEM tensor-core kernel (FP32-level accuracy over the whole
  *               FP32 range).
  * n == 0 is a no-op. The parameter buffer may have any 4-byte alignment.
