@@ -59,21 +59,25 @@ struct AdamArgs {
 };
 
 #ifdef __CUDACC__
-// Sum of column `col` over the partial rows grp, grp + kUpdateGroups, ... in row order, four
-// loads in flight. Adding the kUpdateGroups results in group order gives the column's total;
-// the order is fixed, so every kernel doing this gets the same bits.
+// Sum of column `col` over the partial rows grp, grp + kUpdateGroups, ... in row order, eight
+// loads in flight per batch (the last batch predicated: skipped rows add nothing, so the sum
+// is the plain in-order sum bit for bit). Adding the kUpdateGroups results in group order
+// gives the column's total; the order is fixed, so every kernel doing this gets the same bits.
 __device__ __forceinline__ float column_group_sum(const float* __restrict__ partials, int rows,
                                                   int col, int grp) {
+  constexpr int kBatch = 8;
   float acc = 0.0f;
-  int r = grp;
-  for (; r + 3 * kUpdateGroups < rows; r += 4 * kUpdateGroups) {
-    const float a = partials[static_cast<int64_t>(r) * kRowStride + col];
-    const float b = partials[static_cast<int64_t>(r + kUpdateGroups) * kRowStride + col];
-    const float c = partials[static_cast<int64_t>(r + 2 * kUpdateGroups) * kRowStride + col];
-    const float d = partials[static_cast<int64_t>(r + 3 * kUpdateGroups) * kRowStride + col];
-    acc = (((acc + a) + b) + c) + d;
+  for (int r = grp; r < rows; r += kBatch * kUpdateGroups) {
+    float v[kBatch];
+#pragma unroll
+    for (int k = 0; k < kBatch; ++k) {
+      const int rr = r + k * kUpdateGroups;
+      v[k] = rr < rows ? partials[static_cast<int64_t>(rr) * kRowStride + col] : 0.0f;
+    }
+#pragma unroll
+    for (int k = 0; k < kBatch; ++k)
+      if (r + k * kUpdateGroups < rows) acc += v[k];
   }
-  for (; r < rows; r += kUpdateGroups) acc += partials[static_cast<int64_t>(r) * kRowStride + col];
   return acc;
 }
 
