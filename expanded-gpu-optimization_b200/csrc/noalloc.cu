@@ -1,14 +1,13 @@
 // fhb_backward_noalloc: the backward (vector-Jacobian product) with its scratch memory in a
 // file-scope device array instead of a caller-supplied workspace.
 //
-// Who needs this: callers that cannot allocate device memory at the point where they call
-// the backward. cudaMalloc synchronises the device and is not allowed while a stream is
-// being captured into a CUDA graph, so a host that records its whole training step into a
-// graph it owns cannot call it there; hosts that reach this library through a thin FFI
-// (ctypes, cgo, JNI) often have no handle on a device allocator at all; and deployments
-// that fix their device-memory budget at start-up (per-process limits under MPS, real-time
-// services) forbid allocations later. fhb_backward needs a workspace of
-// fhb_backward_workspace_bytes(n) bytes; this variant needs none.
+// Who needs this: callers that cannot allocate device memory where they call the backward.
+// Hosts that reach this library through a thin FFI (ctypes, cgo, JNI) often have no handle
+// on a device allocator at all; deployments that fix their device-memory budget at start-up
+// (per-process limits under MPS, real-time services) forbid allocations later; and
+// cudaMalloc synchronises the whole device, which a latency-bound caller cannot afford in
+// its step. fhb_backward needs a workspace of fhb_backward_workspace_bytes(n) bytes; this
+// variant needs none.
 //
 // The scratch: one partial-gradient row per CTA of the persistent grid, at most
 // kNoAllocMaxRows rows (148 = one per SM of a B200; 148 x 12,740 floats = 7.5 MB). Every GPU

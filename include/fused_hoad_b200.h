@@ -141,9 +141,9 @@ int fhb_backward_ex(const float* coords, const float* params, const float* grad_
 /*
  * fhb_backward without a workspace argument: no counterpart in the reference (its backward
  * allocates partials and scratch with the ATen allocator on every call).
- * For callers that cannot allocate device memory where they call the backward: inside a
- * CUDA graph they are capturing (cudaMalloc synchronises and is not capturable), behind a
- * thin FFI with no device allocator, or under a device-memory budget fixed at start-up.
+ * For callers that cannot allocate device memory where they call the backward: hosts
+ * behind a thin FFI with no device allocator, processes whose device-memory budget is fixed
+ * at start-up, and callers that cannot afford cudaMalloc's device-wide synchronisation.
  * The scratch is a file-scope device array of 148 partial-gradient rows (7.5 MB, one row per
  * SM of a B200) that every GPU loading this library holds until exit; the call returns
  * FHB_ERR_TOO_LARGE when the persistent grid for n would need more rows (only on a GPU with

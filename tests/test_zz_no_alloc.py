@@ -1,8 +1,8 @@
 """fhb_backward_noalloc: the backward for callers that cannot allocate device memory.
 
-Some callers cannot call cudaMalloc where they run the backward: inside a CUDA graph they
-are capturing, behind an FFI with no device allocator, or under a memory budget fixed at
-start-up. This entry point keeps its scratch in a static device array instead of a
+Some callers cannot call cudaMalloc where they run the backward: hosts behind an FFI with
+no device allocator, processes under a device-memory budget fixed at start-up, or callers
+that cannot afford cudaMalloc's device-wide synchronisation. This entry point keeps its scratch in a static device array instead of a
 caller-supplied workspace. The test calls it through the C ABI twice in a row and checks
 each result against fhb_backward (which takes a workspace) at the parity tolerance used
 for gradients elsewhere (<= 1e-4 x max|expected|). The array keeps the previous call's
