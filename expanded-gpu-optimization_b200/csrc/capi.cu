@@ -109,6 +109,11 @@ int on_device(int device, Body body) {
 
 }  // namespace
 
+namespace fhb {
+int current_device_info(const DeviceInfo** info) { return current_device(info); }
+int record_cuda_error(cudaError_t e) { return record(e); }
+}  // namespace fhb
+
 static_assert(sizeof(cudaIpcMemHandle_t) == FHB_EXCHANGE_HANDLE_BYTES, "IPC handle size");
 static_assert(fhb::kExchangeBytes == FHB_EXCHANGE_BUFFER_BYTES, "exchange ABI drifted");
 

@@ -127,6 +127,14 @@ struct DeviceInfo {
   unsigned int* status = nullptr;  // device address of this device's status word
 };
 
+// ---- capi.cu ----
+// The current device's one-time set-up (kernel attributes, SM count, the address of its
+// status word) and its DeviceInfo: FHB_OK, or the FHB_ERR_* code of the set-up.
+int current_device_info(const DeviceInfo** info);
+// FHB_OK for cudaSuccess; otherwise remembers `e` for fhb_last_cuda_error and returns
+// FHB_ERR_CUDA.
+int record_cuda_error(cudaError_t e);
+
 // ---- forward_fp32.cu ----
 cudaError_t prepare_forward_fp32();
 // tile: 0 -> 32-point tiles, 1 -> 128-point tiles, 2 -> 64-point tiles

@@ -31,26 +31,25 @@ static __device__ __align__(256) float g_noalloc_rows[kNoAllocMaxRows * fhb::kRo
 
 struct NoAllocDevice {
   int code = FHB_OK;
-  fhb::DeviceInfo info;
   float* rows = nullptr;  // device address of g_noalloc_rows on this device
 };
 NoAllocDevice g_state[kMaxDevices];
 std::once_flag g_once[kMaxDevices];
 
-// Once per device, with that device current: the kernels' attributes (fhb_prepare_device),
-// the SM count, and the device address of the scratch array.
+// Once per device, with that device current: the library's shared per-device set-up (kernel
+// attributes, SM count, the status word every entry point reports bounded-wait timeouts
+// into) and the device address of the scratch array.
 void set_up(int device) {
   NoAllocDevice& st = g_state[device];
-  st.code = fhb_prepare_device(device);
+  const fhb::DeviceInfo* info = nullptr;
+  st.code = fhb::current_device_info(&info);
   if (st.code != FHB_OK) return;
-  cudaError_t e = cudaDeviceGetAttribute(&st.info.sms, cudaDevAttrMultiProcessorCount, device);
-  if (e == cudaSuccess) e = cudaGetSymbolAddress(reinterpret_cast<void**>(&st.rows), g_noalloc_rows);
-  if (e != cudaSuccess || st.rows == nullptr) {
-    st.code = FHB_ERR_CUDA;
-    return;
-  }
-  st.info.status = nullptr;  // bounded-wait timeouts of this variant are not recorded
+  st.code = fhb::record_cuda_error(
+      cudaGetSymbolAddress(reinterpret_cast<void**>(&st.rows), g_noalloc_rows));
+  if (st.code == FHB_OK && st.rows == nullptr) st.code = FHB_ERR_CUDA;
 }
+
+bool aligned4(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 3u) == 0; }
 
 }  // namespace
 
@@ -58,26 +57,35 @@ extern "C" int fhb_backward_noalloc(const float* coords, const float* params,
                                     const float* grad_u, const float* grad_lap,
                                     float* grad_params, float* grad_coords, int64_t n,
                                     fhb_stream_t stream) {
+  // Argument checks come before any CUDA call, so a bad argument never reaches the device.
   if (n < 0 || !params || !grad_params) return FHB_ERR_INVALID_ARGUMENT;
+  if (n > 0 && (!coords || !grad_lap)) return FHB_ERR_INVALID_ARGUMENT;
+  if (!aligned4(coords) || !aligned4(params) || !aligned4(grad_u) || !aligned4(grad_lap) ||
+      !aligned4(grad_params) || !aligned4(grad_coords))
+    return FHB_ERR_MISALIGNED;
   int device = 0;
-  cudaError_t e = cudaGetDevice(&device);
-  if (e != cudaSuccess) return FHB_ERR_CUDA;
+  int code = fhb::record_cuda_error(cudaGetDevice(&device));
+  if (code != FHB_OK) return code;
   if (device < 0 || device >= kMaxDevices) return FHB_ERR_INVALID_ARGUMENT;
   std::call_once(g_once[device], [device] { set_up(device); });
   const NoAllocDevice& st = g_state[device];
   if (st.code != FHB_OK) return st.code;
-  if (n == 0) {
-    e = cudaMemsetAsync(grad_params, 0, fhb::kParamCount * sizeof(float), stream);
-    return e == cudaSuccess ? FHB_OK : FHB_ERR_CUDA;
-  }
-  if (!coords || !grad_lap) return FHB_ERR_INVALID_ARGUMENT;
-  const int rows = fhb::backward_grid(n, 0, st.info);
+  const fhb::DeviceInfo* info = nullptr;
+  code = fhb::current_device_info(&info);  // set up already: returns the shared record
+  if (code != FHB_OK) return code;
+  if (n == 0)
+    return fhb::record_cuda_error(
+        cudaMemsetAsync(grad_params, 0, fhb::kParamCount * sizeof(float), stream));
+  const int rows = fhb::backward_grid(n, 0, *info);
   if (rows > kNoAllocMaxRows) return FHB_ERR_TOO_LARGE;  // GPU with more SMs than rows
   fhb::PointSets ps;
   ps.interior = coords;
   ps.n = n;
-  e = fhb::launch_backward_fp32(ps, params, grad_u, grad_lap, grad_coords, nullptr, st.rows,
-                                false, FHB_ACTIVATION_TANH, st.info, stream);
+  // The device's status word goes to the kernel: a CTA whose bounded parameter-staging wait
+  // gives up sets FHB_STATUS_STAGE_TIMEOUT there (read by fhb_read_device_status) before it
+  // returns without writing its row, exactly as in fhb_backward.
+  cudaError_t e = fhb::launch_backward_fp32(ps, params, grad_u, grad_lap, grad_coords, nullptr,
+                                            st.rows, false, FHB_ACTIVATION_TANH, *info, stream);
   if (e == cudaSuccess) e = fhb::launch_reduce_rows(st.rows, rows, grad_params, nullptr, stream);
-  return e == cudaSuccess ? FHB_OK : FHB_ERR_CUDA;
+  return fhb::record_cuda_error(e);
 }

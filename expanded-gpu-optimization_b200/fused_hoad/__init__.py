@@ -13,6 +13,7 @@ from fused_hoad._extension import (
     fused_forward_laplacian_backward,
     fused_forward_laplacian_host,
     load_extension,
+    read_device_status,
 )
 from fused_hoad.backends import BACKENDS, FIXED_CONTRACT_BACKENDS, get_backend
 from fused_hoad.backends.fused import FusedForwardLaplacian, fused_laplacian
@@ -57,6 +58,7 @@ __all__ = [
     "manufactured_solution",
     "manufactured_source",
     "pack_poisson_parameters",
+    "read_device_status",
     "shard_range",
     "uniform_points",
     "unpack_poisson_parameters",

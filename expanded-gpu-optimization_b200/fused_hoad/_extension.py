@@ -97,3 +97,20 @@ def fused_forward_laplacian_host(
         coordinates, parameters, version, output, laplacian, activation
     )
     return u, lap
+
+
+# Bits of the device status word (include/fused_hoad_b200.h FHB_STATUS_*).
+STATUS_STAGE_TIMEOUT = 0x1
+STATUS_MMA_TIMEOUT = 0x2
+STATUS_PEER_TIMEOUT = 0x4
+
+
+def read_device_status(device: int) -> int:
+    """Read and clear device ``device``'s status word (synchronises that device).
+
+    Kernels whose bounded waits give up set bits here instead of hanging or faulting:
+    ``STATUS_STAGE_TIMEOUT`` (parameter staging), ``STATUS_MMA_TIMEOUT`` (tensor-core
+    pipeline), ``STATUS_PEER_TIMEOUT`` (a peer rank's gradient never arrived). Zero means
+    every wait since the last read completed.
+    """
+    return int(load_extension().read_device_status(int(device)))

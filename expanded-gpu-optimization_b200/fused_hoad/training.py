@@ -31,7 +31,7 @@ from collections.abc import Callable
 import torch
 from torch import Tensor, nn
 
-from fused_hoad._extension import load_extension
+from fused_hoad._extension import STATUS_PEER_TIMEOUT, load_extension, read_device_status
 from fused_hoad.distributed import PeerExchange, allreduce_sum_, world
 from fused_hoad.problem import ACTIVATIONS
 from fused_hoad.backends.fused import model_activation
@@ -45,11 +45,15 @@ from fused_hoad.parameters import (
 def cuda_graph_step(
     loss_fn: Callable[[], Tensor], optimizer: torch.optim.Optimizer, *, warmup: int = 3
 ) -> Callable[[], Tensor]:
-    """Capture ``loss_fn() -> backward -> optimizer.step()`` as one CUDA graph.
+    """Record one autograd training iteration and return a function that replays it.
 
-    Warm up on a side stream, drop grads so backward allocates them inside the graph's
-    pool, then capture. The optimizer must be built with ``capturable=True``. Returns a
-    function that replays the step and returns the static loss tensor.
+    The iteration is ``loss = loss_fn(); loss.backward(); optimizer.step()``. It runs
+    ``warmup`` times on a side stream first, so that autograd and the optimizer have set up
+    their state before recording. Gradients are then reset to ``None``: the recorded
+    backward allocates them again from the graph's private memory pool, so replays reuse
+    the same buffers. ``optimizer`` has to be constructed with ``capturable=True`` (its step
+    counter then stays on the device). Calling the returned function replays the recorded
+    kernels and gives back the loss tensor the recording produced, refreshed in place.
     """
     side_stream = torch.cuda.Stream()
     side_stream.wait_stream(torch.cuda.current_stream())
@@ -93,6 +97,13 @@ class PoissonTrainer:
     benchmarks/benchmark_training.py:46-48); passing ``boundary`` points to :meth:`step`
     adds the PINN boundary term ``boundary_weight * mean(u^2)`` of the reference's training
     driver (src/fused_hoad/training.py:68-94), in the same kernel launch.
+
+    A peer wait that gives up (a rank that stopped stepping) leaves the affected parameters
+    and moments of this rank unchanged for that step, so the replicas would drift apart
+    silently; the kernel records it in the device status word instead of hanging.
+    :meth:`check_status` reads that word and raises; :meth:`close` calls it, and
+    ``check_every=K`` calls it after every K-th eager :meth:`step` (each check synchronises
+    the device, so it is skipped inside a stream capture; check after graph replays).
     """
 
     def __init__(
@@ -108,8 +119,13 @@ class PoissonTrainer:
         exchange: str = "peer",
         wait_limit_s: float = 30.0,
         activation: str | None = None,
+        check_every: int = 0,
     ) -> None:
         self._C = load_extension()
+        if check_every < 0:
+            raise ValueError("check_every must be >= 0")
+        self.check_every = int(check_every)
+        self._steps_since_check = 0
         if isinstance(parameters, nn.Module):
             model_act = model_activation(parameters)
             if activation is not None and activation != model_act:
@@ -145,11 +161,40 @@ class PoissonTrainer:
         )
         self._no_boundary = torch.empty((0, 2), dtype=torch.float32, device=flat.device)
 
+    def check_status(self) -> None:
+        """Raise if a bounded wait of this device's kernels gave up since the last read.
+
+        Reads and clears the device status word (synchronises the device). A peer-wait
+        timeout means some parameters of this replica missed an update, so training cannot
+        continue consistently; any other bit means a kernel returned without its work.
+        """
+        self._steps_since_check = 0
+        status = read_device_status(self.params.device.index or 0)
+        if status & STATUS_PEER_TIMEOUT:
+            raise RuntimeError(
+                "a peer rank's gradient never arrived (exchange wait timed out): this "
+                "replica skipped part of an update and no longer matches the others"
+            )
+        if status:
+            raise RuntimeError(f"a kernel's bounded wait gave up (device status {status:#x})")
+
     def close(self) -> None:
-        """Release the peer exchange (collective over the group: call on every rank)."""
-        if self._peer is not None:
+        """Check the device status, then release the peer exchange (collective over the
+        group: call on every rank). The exchange is released even when the check raises."""
+        if self._peer is None:
+            return
+        try:
+            self.check_status()
+        finally:
             self._peer.close()
             self._peer = None
+
+    def _maybe_check(self) -> None:
+        if not self.check_every or torch.cuda.is_current_stream_capturing():
+            return
+        self._steps_since_check += 1
+        if self._steps_since_check >= self.check_every:
+            self.check_status()
 
     def gradients(
         self,
@@ -187,12 +232,14 @@ class PoissonTrainer:
                 boundary, boundary_total = self._no_boundary, 0
             elif boundary_total is None:
                 boundary_total = boundary.shape[0] * world()[1]
-            return self._C.train_step(
+            loss = self._C.train_step(
                 coordinates, boundary, self.params, self.exp_avg, self.exp_avg_sq,
                 self.step_count, self.lr, self.betas[0], self.betas[1], self.eps,
                 total_points, boundary_total, self.boundary_weight, self._peer.handle,
                 self.backward_version, None, self.activation,
             )
+            self._maybe_check()
+            return loss
         out = self.gradients(coordinates, total_points, boundary, boundary_total)
         self._C.adam_step(
             self.params,
@@ -205,6 +252,7 @@ class PoissonTrainer:
             self.betas[1],
             self.eps,
         )
+        self._maybe_check()
         return out[POISSON_PARAMETER_COUNT:]
 
     def capture(

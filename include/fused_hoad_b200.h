@@ -150,7 +150,10 @@ int fhb_backward_ex(const float* coords, const float* params, const float* grad_
  * more than 148 SMs). The first call on a device does the set-up (kernel attributes, the
  * array's device address), so make it before any stream capture. All calls share the array:
  * calls that overlap on the GPU race on it -- order them on one stream. Otherwise as
- * fhb_backward (grad_u may be NULL, grad_coords may be NULL, n == 0 zeroes grad_params).
+ * fhb_backward: grad_u may be NULL, grad_coords may be NULL, n == 0 zeroes grad_params; a
+ * pointer that is not 4-byte aligned returns FHB_ERR_MISALIGNED before anything is
+ * launched; a bounded wait in the kernel that gives up sets its bit in the device status
+ * word (fhb_read_device_status), and fhb_last_cuda_error reports this call's CUDA errors.
  */
 int fhb_backward_noalloc(const float* coords, const float* params, const float* grad_u,
                          const float* grad_lap, float* grad_params, float* grad_coords,

@@ -40,3 +40,26 @@ def test_no_compute_without_gpu_and_clear_status_strings() -> None:
     assert lib.fhb_forward(None, None, None, None, 4, 9, None) == 1  # bad version
     assert lib.fhb_forward(None, None, None, None, -1, 2, None) == 1  # negative size
     assert lib.fhb_forward(None, None, None, None, 0, 2, None) == 0   # empty batch: no-op
+
+
+def test_noalloc_backward_rejects_bad_arguments_before_any_device_work() -> None:
+    """The workspace-free backward checks sizes, missing pointers and 4-byte alignment before
+    it touches the device, so these calls return their codes on a host with no GPU."""
+    lib = _native.library()
+    good = 4096  # an aligned stand-in address: never dereferenced, the checks return first
+    bad = 4098
+    args = dict(coords=good, params=good, grad_u=good, grad_lap=good, grad_params=good,
+                grad_coords=good)
+
+    def call(n: int, **override) -> int:
+        a = {**args, **override}
+        return lib.fhb_backward_noalloc(a["coords"], a["params"], a["grad_u"], a["grad_lap"],
+                                        a["grad_params"], a["grad_coords"], n, None)
+
+    assert call(-1) == 1                      # negative size
+    assert call(8, params=None) == 1          # no parameters
+    assert call(8, grad_params=None) == 1     # nowhere to write the gradient
+    assert call(8, coords=None) == 1          # points missing for a non-empty batch
+    assert call(8, grad_lap=None) == 1        # upstream Laplacian gradient missing
+    for name in args:                         # every pointer's alignment is checked
+        assert call(8, **{name: bad}) == 2, name

@@ -242,3 +242,37 @@ def test_rank_with_no_points_takes_part_with_zeros() -> None:
         assert int(s.item()) == 1
     finally:
         C.exchange_destroy(ex)
+
+
+def test_trainer_raises_when_a_peer_wait_gave_up() -> None:
+    """PoissonTrainer turns a peer-wait timeout into an error instead of drifting silently:
+    its exchange is swapped for a two-rank one whose rank 1 never publishes (2 ms limit)."""
+    C = fused_hoad.load_extension()
+    params = jet.init_parameters(3).cuda()
+    x = uniform_points(2_048, seed=36).cuda()
+    trainer = fused_hoad.PoissonTrainer(params.clone(), exchange="peer", check_every=1)
+    own = trainer._peer.handle
+    ex = C.exchange_create(2, 0, 0.002, 0)
+    peer = torch.zeros(_buffer_words(), dtype=torch.int64, device="cuda")
+    try:
+        C.exchange_connect_local(ex, [0, peer.data_ptr()])
+        trainer._peer.handle = ex
+        with pytest.raises(RuntimeError, match="peer rank"):
+            trainer.step(x)
+        assert torch.equal(trainer.params, params)  # the update was skipped, and reported
+    finally:
+        trainer._peer.handle = own
+        C.exchange_destroy(ex)
+    trainer.step(x)  # the trainer's own exchange still works; nothing left to report
+    trainer.close()
+    assert read_status() == 0
+
+
+def test_trainer_check_status_reports_any_bounded_wait_bit() -> None:
+    lib = _native.library()
+    trainer = fused_hoad.PoissonTrainer(jet.init_parameters(0).cuda())
+    read_status()
+    _native.check(lib.fhb_debug_bounded_wait_selftest(1_000_000, stream_handle()), "selftest")
+    with pytest.raises(RuntimeError, match="bounded wait"):
+        trainer.check_status()
+    trainer.close()  # the status word was cleared by the failed check
