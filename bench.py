@@ -50,6 +50,8 @@ UNIT = "pts/s"
 FLOP_FORWARD = 101_888  # per point: 3 hidden 64x64 jet GEMMs x 4 comps + layer 0/out + tanh jet
 FLOP_STEP = 98_304 * 3 + 256 * 2 + 6_000  # forward + input adjoint + weight gradient + small
 POINTS_PER_GPU = 65_536
+CONFIG3_POINTS = (1_048_576, 4_194_304, 16_777_216)  # global points, split over the ranks
+CONFIG4_POINTS = 16_777_216                          # global points per training step
 WORKLOAD = "config1: residual eval (u, lap) of the 2->64->64->64->64->1 tanh MLP"
 # The reference's only published number for this metric: fused fwd v2 (its default) at
 # 65,536 points, 0.538 ms = 121.9 M pts/s on an RTX A5000 (reference
@@ -83,6 +85,10 @@ def parse_args():
                    help="how the training step sums gradients over ranks")
     p.add_argument("--activation", choices=["tanh", "silu"], default="tanh",
                    help="hidden activation (the BASELINE configs use tanh)")
+    p.add_argument("--config3-steps", type=int, default=20,
+                   help="timed evaluations per config-3 size (0 skips the leg)")
+    p.add_argument("--config4-steps", type=int, default=100,
+                   help="timed training steps of config 4 (0 skips the leg)")
     return p.parse_args()
 
 
@@ -156,41 +162,67 @@ class ClockSampler:
 
 # ---------------------------------------------------------- CPU baseline ----
 
+def _time_cpu_leg(run, budget_s: float, min_runs: int = 3) -> tuple[float, int]:
+    """Median seconds per call of `run` after two warm-up calls, calling until `budget_s`
+    has passed and at least `min_runs` calls were made (benchmarks/timing.py:40-46)."""
+    run()
+    run()
+    times = []
+    deadline = time.perf_counter() + budget_s
+    while len(times) < min_runs or time.perf_counter() < deadline:
+        t0 = time.perf_counter()
+        run()
+        times.append(time.perf_counter() - t0)
+        if len(times) >= 1000:
+            break
+    return statistics.median(times), len(times)
+
+
 def cpu_baseline(points: int, budget_s: float, steps: int | None = None) -> dict:
-    """The oracle port of the reference's PyTorch forward Laplacian on this host's cores."""
+    """The oracle port of the reference's PyTorch paths timed on this host's cores.
+
+    ``value`` is the forward-Laplacian evaluation of the rank's workload (the headline's
+    metric); ``legs`` adds the nested-autograd evaluation, both CPU training steps
+    (benchmarks/benchmark_training.py:39-57: Laplacian, mean squared residual, backward,
+    torch.optim.Adam) at the same size, and both evaluations at config 0's 1,024 points.
+    Each leg is the median of its calls within about budget_s / 6 seconds (3 calls at least,
+    after 2 warm-up calls)."""
     from oracle import jet
 
     cores = os.cpu_count() or 1
     torch.set_num_threads(cores)
     params = jet.init_parameters(0)
+    leg_budget = budget_s / 6.0
+    legs = []
+
+    def add_leg(name: str, n: int, run) -> float:
+        sec, calls = _time_cpu_leg(run, leg_budget)
+        legs.append({"leg": name, "points": n, "value": n / sec, "unit": UNIT,
+                     "ms_per_call": sec * 1e3, "calls": calls})
+        return n / sec
+
     coords = jet.uniform_points(points)
-    jet.forward_laplacian(params, coords)  # warm-up
-    start = time.perf_counter()
-    jet.forward_laplacian(params, coords)
-    one = time.perf_counter() - start
-    sample = points
-    if steps is not None and steps * one > budget_s:
-        sample = max(1024, int(points * budget_s / (steps * one)))
-    coords = coords[:sample].contiguous()
-    times = []
-    deadline = time.perf_counter() + budget_s
-    runs = steps if steps is not None else 10_000
-    for _ in range(runs):
-        t0 = time.perf_counter()
-        jet.forward_laplacian(params, coords)
-        times.append(time.perf_counter() - t0)
-        if steps is None and time.perf_counter() > deadline and len(times) >= 5:
-            break
-    med = statistics.median(times)
+    value = add_leg("forward-Laplacian eval", points, lambda: jet.forward_laplacian(params, coords))
+    add_leg("eager (nested autograd) eval", points, lambda: jet.eager_laplacian(params, coords))
+    source = jet.manufactured_source(coords)
+    for method in ("forward_laplacian", "eager"):
+        flat = params.clone().requires_grad_(True)
+        optimizer = torch.optim.Adam([flat], lr=1e-3, betas=(0.9, 0.999))
+        add_leg(f"{method} train step (loss, backward, Adam)", points,
+                lambda: jet.cpu_train_step(flat, coords, source, optimizer, method))
+    small = jet.uniform_points(1024)
+    add_leg("config0 forward-Laplacian eval", 1024, lambda: jet.forward_laplacian(params, small))
+    add_leg("config0 eager eval", 1024, lambda: jet.eager_laplacian(params, small))
     return {
-        "value": sample / med,
+        "value": value,
         "unit": UNIT,
         "cores": cores,
         "kind": "port",
-        "sample": (f"forward-Laplacian eval of {sample:,} of the config-1 points per call, "
-                   f"median of {len(times)} calls, torch {torch.__version__} on {cores} threads"),
-        "ms_per_call": med * 1e3,
-        "total_s": sum(times),
+        "sample": (f"forward-Laplacian eval of the {points:,} config-1 points per call, median "
+                   f"of {legs[0]['calls']} calls, torch {torch.__version__} on {cores} threads; "
+                   "legs: eager eval, both train steps, config 0 (1,024 points)"),
+        "ms_per_call": legs[0]["ms_per_call"],
+        "legs": legs,
     }
 
 
@@ -336,16 +368,36 @@ def run_ours(args) -> None:
     torch.cuda.synchronize()
     ok = torch.equal(pinned_lap, reference_lap) and staged_ok
 
+    # ---- the 3xTF32 forward (versions 4/5, the operand format north_star names) ----
+    tf32_ms = None
+    if version != 4:
+        tf32_steps = max(1, min(args.steps, 1000))
+        for _ in range(3):
+            C.fused_forward_laplacian(coords, params, 4, act)
+            flush.zero_()
+        events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                  for _ in range(tf32_steps)]
+        barrier()
+        for start, end in events:
+            flush.zero_()
+            start.record(stream)
+            C.fused_forward_laplacian(coords, params, 4, act)
+            end.record(stream)
+        barrier()
+        tf32_ms = max_over_ranks(sum(s.elapsed_time(e) for s, e in events)) / tf32_steps
+
     # ---- training step (config 2) ----
     # One step = weight pre-split, fused forward+loss+backward kernel, update kernel (row
     # reduction + sum over ranks through peer memory + Adam); with --exchange nccl the update
     # is row reduction, [NCCL all-reduce,] Adam. Timed as a CUDA-graph replay (the step's
     # launches replayed without host round trips), and eagerly through PoissonTrainer.step.
-    train_steps = args.train_steps if args.train_steps is not None else max(3, args.steps // 10)
+    train_steps = args.train_steps if args.train_steps is not None else max(50, args.steps // 10)
 
-    def time_train(run) -> float:
+    def time_runs(run, count: int) -> float:
+        """Sum over `count` calls of `run` of the device time between events bracketing each
+        call (L2 flushed before each, outside the events), max over ranks, in ms."""
         events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-                  for _ in range(train_steps)]
+                  for _ in range(count)]
         barrier()
         for start, end in events:
             flush.zero_()
@@ -358,12 +410,12 @@ def run_ours(args) -> None:
     trainer = fused_hoad.PoissonTrainer(params.clone(), exchange=args.exchange, activation=act)
     for _ in range(max(3, args.warmup)):
         trainer.step(coords, n * world)
-    eager_total = time_train(lambda: trainer.step(coords, n * world))
+    eager_total = time_runs(lambda: trainer.step(coords, n * world), train_steps)
     train_mode = "cuda_graph"
     replay = None
     try:
         replay = trainer.capture(coords, n * world, warmup=3)
-        train_total = time_train(replay)
+        train_total = time_runs(replay, train_steps)
     except RuntimeError as exc:  # capture unavailable: report the eager number
         train_mode = f"eager (graph capture failed: {str(exc).splitlines()[0][:120]})"
         train_total = eager_total
@@ -376,6 +428,16 @@ def run_ours(args) -> None:
     train_ms = train_total / train_steps
     train_value = n * world * train_steps / (train_total / 1e3)
     eager_value = n * world * train_steps / (eager_total / 1e3)
+
+    # ---- config 3: evaluation of 1M / 4M / 16M global points split over the ranks ----
+    config3 = None
+    if args.config3_steps > 0:
+        config3 = run_config3(args, C, params, version, act, rank, world, device, time_runs)
+
+    # ---- config 4: 16M global points per training step, 100 graph-replayed steps ----
+    config4 = None
+    if args.config4_steps > 0:
+        config4 = run_config4(args, C, params, act, rank, world, device, time_runs)
 
     peaks, peak_kind = load_peaks()
     clk = clocks.summary()
@@ -445,6 +507,13 @@ def run_ours(args) -> None:
         "gpu_launches": args.steps,
         "roofline": roofline,
         "clocks": clk,
+        "eval_3xtf32": None if tf32_ms is None else {
+            "kernel": "forward_tc_kernel<false> (version 4, 3xTF32)",
+            "value": n * world / (tf32_ms / 1e3), "unit": UNIT, "ms_per_step": tf32_ms,
+            "achieved_tflops": n * FLOP_FORWARD / (tf32_ms / 1e3) / 1e12,
+            "frac_of_split_ceiling": (n * FLOP_FORWARD / (tf32_ms / 1e3) / 1e12)
+                                     / (peaks["bf16_tflops"] / 6.0),
+        },
         "train_step": {
             "workload": "config2: fused forward+loss+backward kernel, " + (
                 "update kernel (row reduction, "
@@ -462,13 +531,118 @@ def run_ours(args) -> None:
             "achieved_tflops": n * FLOP_STEP / (train_ms / 1e3) / 1e12,
             "flop_per_point": FLOP_STEP,
         },
+        "config3": config3,
+        "config4": config4,
     }
     if world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(n, budget_s=15.0)
+        line["cpu_baseline"] = cpu_baseline(n, budget_s=24.0)
     print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def run_config3(args, C, params, version, act, rank, world, device, time_runs) -> dict:
+    """(u, lap) of 1M, 4M and 16M global uniform points, each split evenly
+    by index over the ranks (strong scaling: the global count is fixed as N grows).
+    ``value`` per size = global points / the max-over-ranks device time of one evaluation."""
+    import fused_hoad
+
+    host = fused_hoad.uniform_points(max(CONFIG3_POINTS), seed=1)
+    sizes = []
+    for total in CONFIG3_POINTS:
+        a, b = fused_hoad.shard_range(total, rank, world)
+        shard = host[a:b].to(device)
+        for _ in range(3):
+            C.fused_forward_laplacian(shard, params, version, act)
+        total_ms = time_runs(lambda: C.fused_forward_laplacian(shard, params, version, act),
+                             args.config3_steps)
+        ms = total_ms / args.config3_steps
+        sizes.append({"global_points": total, "points_per_gpu": b - a,
+                      "value": total / (ms / 1e3), "unit": UNIT, "ms_per_step": ms,
+                      "steps": args.config3_steps})
+        del shard
+    return {"workload": "config3: residual eval (u, lap) at 1M/4M/16M global points, split "
+                        "evenly by point index over the ranks",
+            "forward_version": version, "scaling": "strong", "sizes": sizes,
+            "points": "the first 1M/4M/16M rows of one 16,777,216-point uniform draw (seed 1)"}
+
+
+def run_config4(args, C, params, act, rank, world, device, time_runs) -> dict:
+    """data-parallel Poisson training at 16,777,216 global points per step
+    (16M / N per rank), graph-replayed steps (gradient kernel, then the update kernel that
+    sums over the ranks and applies Adam), then a bitwise cross-rank check of the replicas.
+
+    ``gradients_only_ms`` times the same gradient kernel plus a local fixed-order row
+    reduction without the exchange and Adam; ``update_overhead_ms`` = step - that, the cost
+    of the cross-rank sum (including the wait for the slowest rank) and Adam."""
+    import torch.distributed as dist
+
+    import fused_hoad
+
+    total = CONFIG4_POINTS
+    a, b = fused_hoad.shard_range(total, rank, world)
+    coords = fused_hoad.uniform_points(total, seed=1)[a:b].to(device)
+    trainer = fused_hoad.PoissonTrainer(params.clone(), exchange=args.exchange, activation=act)
+    replay = trainer.capture(coords, total, warmup=3)
+    step_total = time_runs(replay, args.config4_steps)
+    steps_done = int(trainer.step_count.item())
+    loss = float(replay().item())
+    del replay.graph
+    replay = None
+    trainer.check_status()
+
+    def gathered_equal(t: torch.Tensor) -> bool:
+        if world == 1:
+            return True
+        parts = [torch.empty_like(t) for _ in range(world)]
+        dist.all_gather(parts, t.contiguous())
+        return all(torch.equal(q, parts[0]) for q in parts)
+
+    replicas_equal = all(gathered_equal(t) for t in
+                         (trainer.params, trainer.exp_avg, trainer.exp_avg_sq,
+                          trainer.step_count))
+    trainer.close()
+
+    # gradient kernel + local row reduction alone (no exchange, no Adam), same shard
+    for _ in range(3):
+        C.poisson_step_gradients(coords, params, total)
+    grad_total = time_runs(lambda: C.poisson_step_gradients(coords, params, total),
+                           args.config4_steps)
+
+    # the in-kernel peer exchange against the NCCL all-reduce composition, from one start
+    peer = fused_hoad.PoissonTrainer(params.clone(), exchange="peer", activation=act)
+    nccl = fused_hoad.PoissonTrainer(params.clone(), exchange="nccl", activation=act)
+    for _ in range(3):
+        peer.step(coords, total)
+        nccl.step(coords, total)
+    torch.cuda.synchronize()
+    equal_to_nccl = bool(torch.equal(peer.params, nccl.params))
+    max_diff = float((peer.params - nccl.params).abs().max().item())
+    scale = float(nccl.params.abs().max().item())
+    peer.close()
+
+    ms = step_total / args.config4_steps
+    grad_ms = grad_total / args.config4_steps
+    return {
+        "workload": "config4: Poisson training step at 16,777,216 global points (fused "
+                    "forward+loss+backward kernel, update kernel: row sums, the sum over "
+                    "ranks, Adam), CUDA-graph replay",
+        "exchange": args.exchange, "scaling": "strong", "global_points": total,
+        "points_per_gpu": b - a, "steps": args.config4_steps,
+        "value": total / (ms / 1e3), "unit": UNIT, "ms_per_step": ms,
+        "achieved_tflops_per_gpu": (b - a) * FLOP_STEP / (ms / 1e3) / 1e12,
+        "gradients_only_ms": grad_ms, "update_overhead_ms": ms - grad_ms,
+        "update_overhead_share": (ms - grad_ms) / ms,
+        "loss_after": loss, "steps_applied": steps_done,
+        "replicas_equal": replicas_equal,
+        "replicas_check": "all_gather of params, exp_avg, exp_avg_sq and the step counter "
+                          "after the timed steps; torch.equal against rank 0's (bitwise)",
+        "peer_vs_nccl": {"steps": 3, "equal": equal_to_nccl, "max_abs_diff": max_diff,
+                         "param_scale": scale,
+                         "note": "bitwise equal expected at N <= 2 (a sum of two values does "
+                                 "not depend on order); NCCL's order differs beyond"},
+    }
 
 
 def main() -> None:

@@ -125,11 +125,9 @@ def forward_laplacian(
     return forward_laplacian_from_linears(unpack(params.to(coords.dtype)), coords, activation)
 
 
-def eager_laplacian(
-    params: Tensor, coords: Tensor, activation: str = "tanh"
-) -> tuple[Tensor, Tensor]:
-    """Nested-autograd Laplacian; src/fused_hoad/autodiff.py:16-40, reference.py:9-20."""
-    linears = unpack(params.to(coords.dtype))
+def _eager_laplacian_graph(linears, coords: Tensor, activation: str = "tanh"):
+    """(u, lap) by nested autograd, keeping the graph (so lap can be differentiated again
+    with respect to the weights); src/fused_hoad/autodiff.py:16-40, reference.py:9-20."""
     x = coords.detach().clone().requires_grad_(True)
     with torch.enable_grad():
         h = x
@@ -142,7 +140,41 @@ def eager_laplacian(
         for d in range(x.shape[1]):
             (second,) = torch.autograd.grad(first[:, d].sum(), x, create_graph=True)
             lap = lap + second[:, d : d + 1]
+    return h, lap
+
+
+def eager_laplacian(
+    params: Tensor, coords: Tensor, activation: str = "tanh"
+) -> tuple[Tensor, Tensor]:
+    """Nested-autograd Laplacian; src/fused_hoad/autodiff.py:16-40, reference.py:9-20."""
+    h, lap = _eager_laplacian_graph(unpack(params.to(coords.dtype)), coords, activation)
     return h.detach(), lap.detach()
+
+
+def cpu_train_step(
+    flat: Tensor, coords: Tensor, source: Tensor, optimizer, method: str = "forward_laplacian"
+) -> Tensor:
+    """One training step of benchmarks/benchmark_training.py:39-57 on the CPU: the Laplacian
+    by the forward-Laplacian jet (``method="forward_laplacian"``) or by nested autograd
+    (``"eager"``), ``loss = mean((lap - f)^2)``, ``loss.backward()``, ``optimizer.step()``.
+
+    ``flat`` is the packed parameter buffer with ``requires_grad``; the layers are views of
+    it, so one backward fills ``flat.grad`` and ``optimizer`` (torch.optim.Adam over
+    ``[flat]``) updates all of them. Returns the loss before the update.
+    """
+    optimizer.zero_grad(set_to_none=True)
+    with torch.enable_grad():
+        linears = unpack(flat)
+        if method == "forward_laplacian":
+            _, lap = forward_laplacian_from_linears(linears, coords)
+        elif method == "eager":
+            _, lap = _eager_laplacian_graph(linears, coords)
+        else:
+            raise ValueError(f"unknown method {method!r}")
+        loss = (lap - source).pow(2).mean()
+        loss.backward()
+    optimizer.step()
+    return loss.detach()
 
 
 def recompute_backward(
