@@ -130,7 +130,7 @@ struct Layout {
   static constexpr int kBarOff = kRedOff + 8 * kTile * 4;
   static constexpr int kMiscOff = kBarOff + 16 * 8;        // TMEM base, abort flag
   static constexpr int kScaleOff = kMiscOff + 16;          // f16: F16Consts
-  static constexpr int kParamOff = kScaleOff + 256 * 4;    // staged parameter buffer
+  static constexpr int kParamOff = kScaleOff + (F16 ? 4096 : 1024);  // staged parameters
   static constexpr int kSmemUsed = kParamOff + kParamSmemFloats * 4;
   // Padded so two CTAs never share an SM (each allocates all 512 TMEM columns).
   static constexpr int kSmemBytes = kSmemUsed > 120 * 1024 ? (kSmemUsed + 1023) / 1024 * 1024
@@ -154,24 +154,35 @@ struct Ctx {
   const float* f16c;          // f16: the F16Consts words
 };
 
-// f16 scale constants in shared memory (floats at Layout::kScaleOff). GEMM l's A operand,
+// f16 constants in shared memory (floats at Layout::kScaleOff). GEMM l's A operand,
 // component c, is the true activation times sigma[l][c] (a power of 2; sigma_x = sigma_y),
-// its weights are times tau[l], so its accumulators are the true products times
-// sigma tau. The epilogue of GEMM l (l = 0, 1) turns accumulators D straight into the next
-// GEMM's scaled operand: with us = 1 / (sigma_l tau_l) and s' = sigma_{l+1},
-//   z_v = D_v us_v + b,  a = tanh z_v = 1 - 2r,  s = 1 - a^2,
-//   v' = s'_v a,  J' = s (s'_J us_J) D_J,  L' = s (s'_L us_L D_L - 2 s'_L us_J^2 a |D_J|^2).
+// its weights are times tau[l], so its accumulators D are the true products times
+// sigma tau. With us = 1 / (sigma_l tau_l), s' = sigma_{l+1} and k = 2 / ln 2, the epilogue
+// of GEMM l (l = 0, 1) turns D straight into the next GEMM's scaled operand:
+//   z' = k z = D_v (k us_v) + k b,  r = 1 / (2^z' + 1),  a = tanh z = 1 - 2r,
+//   t = r (1 - r) = (1 - a^2) / 4,
+//   v' = s'_v a = s'_v - 2 s'_v r,   J' = 4 t E1 D_J,
+//   L' = 4 t (E2 D_L + E3 a |D_J|^2) = t (4 E2 D_L + (4 E3 - 8 E3 r) |D_J|^2),
+// with E1 = s'_J us_J, E2 = s'_L us_L, E3 = -2 s'_L us_J^2 -- every constant a product of
+// powers of 2 (exact) except k. The output stage (after GEMM 2) forms
+//   u = sum_o w_o a_o + b_out,   lap = sum_o w_o t_o (4 us_L D_L - 8 us_J^2 a_o |D_J|^2),
+// and layer 0 (2 inputs, z_L = 0, z_J = the row of W0) writes
+//   v' = sigma_v a,  J'_d = 4 t sigma_J W0[o][d],  L' = t (4 C0 - 8 C0 r),
+//   C0 = -2 sigma_L |W0[o]|^2.
 struct F16Consts {
-  static constexpr int kUnscale = 0;   // [3][4] 1 / (sigma tau) of GEMM l's accumulators
-  static constexpr int kTau = 12;      // [3]
-  static constexpr int kEpi = 16;      // [2][4]: s'_v, s'_J us_J, s'_L us_L, -2 s'_L us_J^2
-  static constexpr int kSigma0 = 24;   // s_v of GEMM 0 (layer-0 jets)
-  static constexpr int kW0 = 32;       // [64] sigma_J0 W0[o][0]
-  static constexpr int kW1 = 96;       // [64] sigma_J0 W0[o][1]
-  static constexpr int kC0 = 160;      // [64] -2 sigma_L0 (W0[o][0]^2 + W0[o][1]^2)
-  static constexpr int kWords = 224;
+  static constexpr int kTau = 0;       // [3] tau_l (one pad word)
+  static constexpr int kHid = 4;       // [2][8] GEMM l = 0, 1: k us_v, s'_v, -2 s'_v, 4 E1,
+                                       //        4 E2, 4 E3, -8 E3, 0
+  static constexpr int kOut = 20;      // k us_v, 4 us_L, -8 us_J^2 of GEMM 2; sigma_v and
+                                       // -2 sigma_v of GEMM 0's operand (layer 0); pad
+  static constexpr int kBias = 32;     // [3][64] k b of hidden layers 1..3
+  static constexpr int kL0 = 224;      // [7][64] per layer-0 neuron: k W0[o][0], k W0[o][1],
+                                       // k b0[o], 4 sigma_J W0[o][0], 4 sigma_J W0[o][1],
+                                       // 4 C0, -8 C0
+  static constexpr int kWords = 672;
 };
-static_assert(F16Consts::kWords <= 256, "the F16Consts words fit the scale region");
+constexpr int kScaleFloats = 1024;
+static_assert(F16Consts::kWords <= kScaleFloats, "the F16Consts words fit the scale region");
 
 // Bounded wait that also gives up when another warp has aborted the CTA.
 __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, const Ctx& cx) {
@@ -226,13 +237,52 @@ __device__ __forceinline__ void split_f16_pair(float a, float b, uint32_t& hi, u
   lo = *reinterpret_cast<const uint32_t*>(&l);
 }
 
-// tanh through 1 - 2r, r = 1 / (exp(2x) + 1) on the special-function unit (tanh_fast's
-// formula, which returns 1 - 2r): the f16 epilogue folds its operand scale into 1 - 2r.
-__device__ __forceinline__ float tanh_fast_r(float x) {
+// The epilogue's f16 pairs: hi = x rounded to f16 (11 significant bits), lo = x - hi
+// rounded to f16, element a (even K) in the low halves. x - hi is exact in FP32 and comes
+// from one mixed-precision fma (f16 hi times -1 plus the FP32 x), so a pair costs four
+// instructions: two packs and two fmas. Inside the scaled range (|x| <= 2^14) hi is a normal
+// f16; values below 2^-14 lose precision, at most 2^-25 absolute in scaled units.
+__device__ __forceinline__ void split_f16_pair_fast(float a, float b, uint32_t& hi,
+                                                    uint32_t& lo) {
+  asm("{\n\t.reg .b16 h0, h1, m;\n\t.reg .f32 la, lb;\n\t"
+      "cvt.rn.f16x2.f32 %0, %3, %2;\n\t"
+      "mov.b32 {h0, h1}, %0;\n\t"
+      "mov.b16 m, 0xBC00;\n\t"
+      "fma.rn.f32.f16 la, h0, m, %2;\n\t"
+      "fma.rn.f32.f16 lb, h1, m, %3;\n\t"
+      "cvt.rn.f16x2.f32 %1, lb, la;\n\t}"
+      : "=r"(hi), "=r"(lo)
+      : "f"(a), "f"(b));
+}
+
+// r = 1 / (2^zp + 1) on the special-function unit (ex2.approx, rcp.approx), zp = 2 z / ln 2
+// already scaled by the caller's constants: tanh z = 1 - 2r (tanh_fast's formula, <= 5e-7
+// from tanhf). 2^zp overflows to +inf for large z (r = 0, tanh = 1) and underflows to 0 for
+// very negative z (r = 1, tanh = -1): never NaN.
+__device__ __forceinline__ float tanh_r_scaled(float zp) {
   float e, r;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(x * 2.8853900817779268f));
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(zp));
   asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(e + 1.0f));
   return r;
+}
+
+constexpr float kTwoOverLn2 = 2.8853900817779268f;  // 2 / ln 2 = 2 log2(e)
+
+// B row (accumulator column within a component) k = 16s + 4a + t holds output neuron
+// 16a + 4s + t, so the 16 neurons an epilogue warp of block s owns (chunks a = 0..3, four
+// neurons each) sit in 16 consecutive columns: one tcgen05.ld.x16 per component. The map is
+// its own inverse.
+__host__ __device__ constexpr int neuron_of_column(int k) {
+  return (k & 3) | (((k >> 4) & 3) << 2) | (((k >> 2) & 3) << 4);
+}
+static_assert(neuron_of_column(neuron_of_column(37)) == 37 && neuron_of_column(16) == 4,
+              "column permutation");
+
+__device__ __forceinline__ float4 ld_f4(const float* p) {
+  return *reinterpret_cast<const float4*>(p);
+}
+__device__ __forceinline__ float at(const float4& v, int t) {
+  return t == 0 ? v.x : t == 1 ? v.y : t == 2 ? v.z : v.w;
 }
 
 // The MMAs of chunk j (input neurons 16j..16j+15) of hidden GEMM `layer`, A from ring slot
@@ -306,8 +356,8 @@ __device__ __forceinline__ bool produce_chunk(uint32_t n, const float (&h)[4][4]
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
       uint32_t hi0, lo0, hi1, lo1;
-      split_f16_pair(h[c][0], h[c][1], hi0, lo0);
-      split_f16_pair(h[c][2], h[c][3], hi1, lo1);
+      split_f16_pair_fast(h[c][0], h[c][1], hi0, lo0);
+      split_f16_pair_fast(h[c][2], h[c][3], hi1, lo1);
       tc::st_x2(base + 16u * c, hi0, hi1);
       tc::st_x2(base + 16u * c + 8u, lo0, lo1);
     }
@@ -372,7 +422,7 @@ __device__ __forceinline__ void stage_tf32(const float* __restrict__ params, uin
     const int layer = idx >> 12, e = idx & 4095;
     const int row = ((e >> 9) << 3) | ((e >> 2) & 7);
     const int k = (((e >> 5) & 15) << 2) | (e & 3);
-    w[r] = params[kHiddenBase + layer * kHiddenStride + row * kWidth + k];
+    w[r] = params[kHiddenBase + layer * kHiddenStride + neuron_of_column(row) * kWidth + k];
   }
 #pragma unroll
   for (int r = 0; r < kPerThread; ++r) {
@@ -422,7 +472,8 @@ __device__ __forceinline__ void stage_f16(const float* __restrict__ params, uint
       const int layer = idx >> 11, e = (idx & 2047) * 2;
       const int row = ((e >> 9) << 3) | ((e >> 3) & 7);
       const int kk = (((e >> 6) & 7) << 3) | (e & 7);
-      const float* wr = params + kHiddenBase + layer * kHiddenStride + row * kWidth + kk;
+      const float* wr =
+          params + kHiddenBase + layer * kHiddenStride + neuron_of_column(row) * kWidth + kk;
       wp[k][0] = wr[0];
       wp[k][1] = wr[1];
     }
@@ -461,22 +512,31 @@ __device__ __forceinline__ void stage_f16(const float* __restrict__ params, uint
         bl = fmaf(nrm[l], bl, 2.0f * nj * nj);
         bj = nj;
       }
-      for (int l = 0; l < 3; ++l) {
-        const float us[3] = {1.0f / (sig[l][0] * tau[l]), 1.0f / (sig[l][1] * tau[l]),
-                             1.0f / (sig[l][2] * tau[l])};
-        cst[C::kUnscale + 4 * l + 0] = us[0];
-        cst[C::kUnscale + 4 * l + 1] = us[1];
-        cst[C::kUnscale + 4 * l + 2] = us[1];
-        cst[C::kUnscale + 4 * l + 3] = us[2];
-        cst[C::kTau + l] = tau[l];
-        if (l < 2) {
-          cst[C::kEpi + 4 * l + 0] = sig[l + 1][0];
-          cst[C::kEpi + 4 * l + 1] = sig[l + 1][1] * us[1];
-          cst[C::kEpi + 4 * l + 2] = sig[l + 1][2] * us[2];
-          cst[C::kEpi + 4 * l + 3] = -2.0f * sig[l + 1][2] * us[1] * us[1];
-        }
+      float us[3][3];  // 1 / (sigma tau) of GEMM l's accumulators, per component
+      for (int l = 0; l < 3; ++l)
+        for (int c = 0; c < 3; ++c) us[l][c] = 1.0f / (sig[l][c] * tau[l]);
+      for (int l = 0; l < 3; ++l) cst[C::kTau + l] = tau[l];
+      for (int l = 0; l < 2; ++l) {  // hidden epilogues: GEMM l's accumulators -> GEMM l+1
+        const float e1 = sig[l + 1][1] * us[l][1];
+        const float e2 = sig[l + 1][2] * us[l][2];
+        const float e3 = -2.0f * sig[l + 1][2] * us[l][1] * us[l][1];
+        float* k = cst + C::kHid + 8 * l;
+        k[0] = kTwoOverLn2 * us[l][0];
+        k[1] = sig[l + 1][0];
+        k[2] = -2.0f * sig[l + 1][0];
+        k[3] = 4.0f * e1;
+        k[4] = 4.0f * e2;
+        k[5] = 4.0f * e3;
+        k[6] = -8.0f * e3;
+        k[7] = 0.0f;
       }
-      cst[C::kSigma0] = sig[0][0];
+      float* k = cst + C::kOut;  // the output stage, and layer 0's value scale
+      k[0] = kTwoOverLn2 * us[2][0];
+      k[1] = 4.0f * us[2][2];
+      k[2] = -8.0f * us[2][1] * us[2][1];
+      k[3] = 0.0f;
+      k[4] = sig[0][0];
+      k[5] = -2.0f * sig[0][0];
       sigma[0] = sig[0][1];
       sigma[1] = sig[0][2];
     }
@@ -485,10 +545,18 @@ __device__ __forceinline__ void stage_f16(const float* __restrict__ params, uint
   if (threadIdx.x < kWidth) {  // layer-0 jets: J = W0 columns, L = -2 a s |W0 row|^2
     const int o = threadIdx.x;
     const float w0 = small[kSmW0 + 2 * o], w1 = small[kSmW0 + 2 * o + 1];
-    cst[C::kW0 + o] = sigma[0] * w0;
-    cst[C::kW1 + o] = sigma[0] * w1;
-    cst[C::kC0 + o] = -2.0f * sigma[1] * fmaf(w0, w0, w1 * w1);
+    const float c0 = -2.0f * sigma[1] * fmaf(w0, w0, w1 * w1);
+    float* l0 = cst + C::kL0;
+    l0[0 * kWidth + o] = kTwoOverLn2 * w0;
+    l0[1 * kWidth + o] = kTwoOverLn2 * w1;
+    l0[2 * kWidth + o] = kTwoOverLn2 * small[kSmB0 + o];
+    l0[3 * kWidth + o] = 4.0f * sigma[0] * w0;
+    l0[4 * kWidth + o] = 4.0f * sigma[0] * w1;
+    l0[5 * kWidth + o] = 4.0f * c0;
+    l0[6 * kWidth + o] = -8.0f * c0;
   }
+  if (threadIdx.x < 3 * kWidth)  // hidden biases in the scaled tanh argument
+    cst[C::kBias + threadIdx.x] = kTwoOverLn2 * small[kSmB + threadIdx.x];
   // The split: pairs of adjacent K elements, enumerated (row group, K chunk of 8, row in
   // group, K pair) so consecutive threads store consecutive words of the canonical layout.
 #pragma unroll
@@ -631,81 +699,118 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
       }
 
       // layer 0: z = W0 x + b0, z_J = W0 columns, z_L = 0 (f16: the scaled operand directly)
+      if constexpr (F16) {
+        using C = F16Consts;
+        const float sv = cx.f16c[C::kOut + 4], sv2 = cx.f16c[C::kOut + 5];
+        const float* l0 = cx.f16c + C::kL0 + 4 * s;
 #pragma unroll
-      for (int j = 0; j < kChunks; ++j) {
-        float h[4][4];
+        for (int j = 0; j < kChunks; ++j) {
+          const float* c0 = l0 + 16 * j;  // neurons 16j + 4s + t, t = 0..3
+          const float4 wx = ld_f4(c0), wy = ld_f4(c0 + kWidth), bz = ld_f4(c0 + 2 * kWidth);
+          const float4 kj0 = ld_f4(c0 + 3 * kWidth), kj1 = ld_f4(c0 + 4 * kWidth);
+          const float4 kl = ld_f4(c0 + 5 * kWidth), kl2 = ld_f4(c0 + 6 * kWidth);
+          float h[4][4];
 #pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          const int o = 16 * j + 4 * s + t;
-          const float w0 = small[kSmW0 + 2 * o], w1 = small[kSmW0 + 2 * o + 1];
-          const float z = fmaf(w0, x0, fmaf(w1, x1, small[kSmB0 + o]));
-          if constexpr (F16) {
-            using C = F16Consts;
-            const float r = tanh_fast_r(z), sv = cx.f16c[C::kSigma0];
-            const float a = fmaf(-2.0f, r, 1.0f), sd = fmaf(-a, a, 1.0f);
-            h[0][t] = fmaf(-2.0f * sv, r, sv);
-            h[1][t] = sd * cx.f16c[C::kW0 + o];
-            h[2][t] = sd * cx.f16c[C::kW1 + o];
-            h[3][t] = cx.f16c[C::kC0 + o] * (a * sd);
-          } else {
+          for (int t = 0; t < 4; ++t) {
+            const float r = tanh_r_scaled(fmaf(at(wx, t), x0, fmaf(at(wy, t), x1, at(bz, t))));
+            const float tt = fmaf(-r, r, r);  // (1 - tanh^2) / 4
+            h[0][t] = fmaf(sv2, r, sv);
+            h[1][t] = tt * at(kj0, t);
+            h[2][t] = tt * at(kj1, t);
+            h[3][t] = tt * fmaf(at(kl2, t), r, at(kl, t));
+          }
+          if (!(ok = produce_chunk<F16>(chunk++, h, tmem_warp, s, cx))) break;
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < kChunks; ++j) {
+          float h[4][4];
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            const int o = 16 * j + 4 * s + t;
+            const float w0 = small[kSmW0 + 2 * o], w1 = small[kSmW0 + 2 * o + 1];
+            const float z = fmaf(w0, x0, fmaf(w1, x1, small[kSmB0 + o]));
             Act::jet_fast(z, w0, w1, 0.0f, h[0][t], h[1][t], h[2][t], h[3][t]);
           }
+          if (!(ok = produce_chunk<F16>(chunk++, h, tmem_warp, s, cx))) break;
         }
-        if (!(ok = produce_chunk<F16>(chunk++, h, tmem_warp, s, cx))) break;
       }
 
       for (int l = 0; ok && l < kHiddenGemms; ++l, ++mlayer) {
         if (!(ok = warp_wait(cx.dfull, mlayer & 1u, cx))) break;
         tc::fence_after_sync();
-        // d[c][4a + t] = component c of neuron 16a + 4s + t
+        // d[c][4a + t] = component c of neuron 16a + 4s + t: 16 consecutive accumulator
+        // columns (the B rows are permuted, neuron_of_column)
         float d[4][16];
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
-#pragma unroll
-          for (int a = 0; a < 4; ++a)
-            tc::ld_x4(tmem_warp + 64u * c + 16u * a + 4u * s,
-                      *reinterpret_cast<float(*)[4]>(&d[c][4 * a]));
+        for (int c = 0; c < 4; ++c) tc::ld_x16(tmem_warp + 64u * c + 16u * s, d[c]);
         tc::wait_ld();
-        const float* bias = small + kSmB + 64 * l;
-        if (l + 1 < kHiddenGemms) {
+        float pu = 0.0f, pl = 0.0f;  // output stage: this warp's share of u and lap
+        if constexpr (F16) {
+          using C = F16Consts;
+          const float* bias = cx.f16c + C::kBias + 64 * l + 4 * s;  // k b, layer l + 1
+          if (l + 1 < kHiddenGemms) {  // accumulators -> the next GEMM's scaled operand
+            const float4 ka = ld_f4(cx.f16c + C::kHid + 8 * l);
+            const float4 kb = ld_f4(cx.f16c + C::kHid + 8 * l + 4);
+#pragma unroll
+            for (int j = 0; j < kChunks; ++j) {
+              const float4 bb = ld_f4(bias + 16 * j);
+              float h[4][4];
+#pragma unroll
+              for (int t = 0; t < 4; ++t) {
+                const int i = 4 * j + t;
+                const float r = tanh_r_scaled(fmaf(d[0][i], ka.x, at(bb, t)));
+                const float tt = fmaf(-r, r, r);  // (1 - tanh^2) / 4
+                const float sk = tt * ka.w;
+                const float q = fmaf(d[1][i], d[1][i], d[2][i] * d[2][i]);
+                const float g = fmaf(kb.z, r, kb.y);
+                h[0][t] = fmaf(ka.z, r, ka.y);
+                h[1][t] = sk * d[1][i];
+                h[2][t] = sk * d[2][i];
+                h[3][t] = tt * fmaf(g, q, kb.x * d[3][i]);
+              }
+              if (!(ok = produce_chunk<F16>(chunk++, h, tmem_warp, s, cx))) break;
+            }
+            continue;
+          }
+          // output layer: u = w.a + b, lap = w.L, over this warp's 16 neurons
+          const float4 ko = ld_f4(cx.f16c + C::kOut);
+          const float* wout = small + kSmWout + 4 * s;
 #pragma unroll
           for (int j = 0; j < kChunks; ++j) {
-            float h[4][4];
+            const float4 bb = ld_f4(bias + 16 * j), ww = ld_f4(wout + 16 * j);
 #pragma unroll
             for (int t = 0; t < 4; ++t) {
               const int i = 4 * j + t;
-              const float b = bias[16 * j + 4 * s + t];
-              if constexpr (F16) {  // accumulators -> the next GEMM's scaled operand
-                using C = F16Consts;
-                const float* e = cx.f16c + C::kEpi + 4 * l;
-                const float r = tanh_fast_r(fmaf(d[0][i], cx.f16c[C::kUnscale + 4 * l], b));
-                const float a = fmaf(-2.0f, r, 1.0f), sd = fmaf(-a, a, 1.0f);
-                const float sk = sd * e[1];
-                const float q = fmaf(d[1][i], d[1][i], d[2][i] * d[2][i]);
-                h[0][t] = fmaf(-2.0f * e[0], r, e[0]);
-                h[1][t] = sk * d[1][i];
-                h[2][t] = sk * d[2][i];
-                h[3][t] = sd * fmaf(e[3] * a, q, e[2] * d[3][i]);
-              } else {
+              const float r = tanh_r_scaled(fmaf(d[0][i], ko.x, at(bb, t)));
+              const float tt = fmaf(-r, r, r);
+              const float a = fmaf(-2.0f, r, 1.0f);
+              const float q = fmaf(d[1][i], d[1][i], d[2][i] * d[2][i]);
+              const float inner = fmaf(ko.z * a, q, ko.y * d[3][i]);
+              pu = fmaf(at(ww, t), a, pu);
+              pl = fmaf(at(ww, t) * tt, inner, pl);
+            }
+          }
+        } else {
+          const float* bias = small + kSmB + 64 * l;
+          if (l + 1 < kHiddenGemms) {
+#pragma unroll
+            for (int j = 0; j < kChunks; ++j) {
+              float h[4][4];
+#pragma unroll
+              for (int t = 0; t < 4; ++t) {
+                const int i = 4 * j + t;
+                const float b = bias[16 * j + 4 * s + t];
                 Act::jet_fast(d[0][i] + b, d[1][i], d[2][i], d[3][i], h[0][t], h[1][t],
                               h[2][t], h[3][t]);
               }
+              if (!(ok = produce_chunk<F16>(chunk++, h, tmem_warp, s, cx))) break;
             }
-            if (!(ok = produce_chunk<F16>(chunk++, h, tmem_warp, s, cx))) break;
-          }
-        } else {
-          if constexpr (F16) {  // remove the operand scales: exact powers of 2
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-              const float us = cx.f16c[F16Consts::kUnscale + 4 * l + c];
-#pragma unroll
-              for (int i = 0; i < 16; ++i) d[c][i] *= us;
-            }
+            continue;
           }
 #pragma unroll
           for (int i = 0; i < 16; ++i) d[0][i] += bias[16 * (i >> 2) + 4 * s + (i & 3)];
           // output layer: u = w.v + b, lap = w.L, over this warp's 16 neurons
-          float pu = 0.0f, pl = 0.0f;
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
             float v, j0, j1, lv;
@@ -714,6 +819,8 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
             pu = fmaf(w, v, pu);
             pl = fmaf(w, lv, pl);
           }
+        }
+        {
           red[s * kTile + row] = pu;
           red[(4 + s) * kTile + row] = pl;
           __syncwarp();
