@@ -333,10 +333,12 @@ __device__ __forceinline__ void issue_chunk_mmas(const Ctx& cx, int layer, int j
 // the scaled operand) into ring slot n % kRing; the warp completing the chunk last issues its
 // MMAs. False if aborted.
 template <bool F16>
-__device__ __forceinline__ bool produce_chunk(uint32_t n, const float (&h)[4][4],
+__device__ __forceinline__ bool produce_chunk(uint32_t n, int j, const float (&h)[4][4],
                                               uint32_t tmem_warp, int s, const Ctx& cx) {
   using F = Format<F16>;
-  const uint32_t slot = n % F::kRing;
+  // n = 12 tile + 4 layer + j, and the ring size divides 4: the slot is j % kRing, known at
+  // compile time in the unrolled chunk loops (so are the TMEM store addresses).
+  const uint32_t slot = static_cast<uint32_t>(j) % F::kRing;
   // A slot is free once the MMAs of the chunk that used it before have completed. Chunks 0
   // and 1 of a GEMM (and every f16 chunk: the f16 ring holds a whole layer) reuse a slot of
   // the previous GEMM, whose MMAs the "D complete" commit that this warp waited on before
@@ -345,7 +347,7 @@ __device__ __forceinline__ bool produce_chunk(uint32_t n, const float (&h)[4][4]
   // measured ~300 cycles per chunk). The commits still come once per chunk, so the parity of
   // the waits that remain counts every chunk of the slot.
   if constexpr (!F16) {
-    if (n % kChunks >= static_cast<uint32_t>(F::kRing)) {
+    if (j >= F::kRing) {  // n % kChunks == j
       if (!warp_wait(&cx.empty[slot], ((n / F::kRing) & 1u) ^ 1u, cx)) return false;
       tc::fence_after_sync();
     }
@@ -719,7 +721,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
             h[2][t] = tt * at(kj1, t);
             h[3][t] = tt * fmaf(at(kl2, t), r, at(kl, t));
           }
-          if (!(ok = produce_chunk<F16>(chunk++, h, tmem_warp, s, cx))) break;
+          if (!(ok = produce_chunk<F16>(chunk++, j, h, tmem_warp, s, cx))) break;
         }
       } else {
 #pragma unroll
@@ -732,7 +734,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
             const float z = fmaf(w0, x0, fmaf(w1, x1, small[kSmB0 + o]));
             Act::jet_fast(z, w0, w1, 0.0f, h[0][t], h[1][t], h[2][t], h[3][t]);
           }
-          if (!(ok = produce_chunk<F16>(chunk++, h, tmem_warp, s, cx))) break;
+          if (!(ok = produce_chunk<F16>(chunk++, j, h, tmem_warp, s, cx))) break;
         }
       }
 
@@ -769,7 +771,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
                 h[2][t] = sk * d[2][i];
                 h[3][t] = tt * fmaf(g, q, kb.x * d[3][i]);
               }
-              if (!(ok = produce_chunk<F16>(chunk++, h, tmem_warp, s, cx))) break;
+              if (!(ok = produce_chunk<F16>(chunk++, j, h, tmem_warp, s, cx))) break;
             }
             continue;
           }
@@ -804,7 +806,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
                 Act::jet_fast(d[0][i] + b, d[1][i], d[2][i], d[3][i], h[0][t], h[1][t],
                               h[2][t], h[3][t]);
               }
-              if (!(ok = produce_chunk<F16>(chunk++, h, tmem_warp, s, cx))) break;
+              if (!(ok = produce_chunk<F16>(chunk++, j, h, tmem_warp, s, cx))) break;
             }
             continue;
           }

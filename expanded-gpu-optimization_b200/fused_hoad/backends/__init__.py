@@ -3,9 +3,11 @@
 The reference registers ``fused_cuda*`` backends in ``BACKENDS`` only when its extension
 is built (``src/fused_hoad/backends/__init__.py:37-67``). This package holds only the
 fused hot path, so the registry holds only those names, each mapped onto the sm_100a
-kernels: forward versions 0-2 are the FP32 CUDA-core kernel, 3-5 the 3xTF32 tensor-core
-kernel; every ``bwd`` name uses the fused adjoint kernel. The reference's PyTorch backends
-(eager, forward_laplacian, func, compiled) are not part of this package.
+kernels: forward versions 0-2 are the FP32 CUDA-core kernel, 3 the 3xFP16 tensor-core
+kernel and 4-5 the 3xTF32 one; ``fused_cuda`` and every ``bwd`` name use the fused adjoint
+kernels (backward 6, the default, on the tensor cores; 1-5 on the FP32 CUDA cores). The
+reference's PyTorch backends (eager, forward_laplacian, func, compiled) are not part of this
+package.
 """
 
 from __future__ import annotations

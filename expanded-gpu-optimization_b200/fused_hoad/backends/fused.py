@@ -1,10 +1,10 @@
 """Fused CUDA backend: ``model -> (u, Laplacian u)`` in one sm_100a kernel launch.
 
-Mirrors the reference's ``src/fused_hoad/backends/fused.py:1-138``: the autograd function
-``FusedForwardLaplacian``, the weakref-keyed pack cache ``_packed_parameters`` and
-``fused_laplacian(model, x, version=2, backward="cuda")``. The backward is always the fused
-adjoint-jet kernel; the reference's PyTorch "recompute" backward is an oracle and lives in
-the test suite's ``oracle`` package, not here.
+The reference's public surface (``src/fused_hoad/backends/fused.py``): the autograd function
+``FusedForwardLaplacian``, the pack cache ``_packed_parameters`` and
+``fused_laplacian(model, x, version=2, backward="cuda")`` with its backward-mode names. The
+backward is always one of the fused adjoint kernels; the reference's PyTorch "recompute"
+backward is an oracle and lives in the test suite's ``oracle`` package, not here.
 """
 
 from __future__ import annotations
@@ -15,83 +15,76 @@ import torch
 from torch import Tensor, nn
 
 from fused_hoad._extension import fused_forward_laplacian, fused_forward_laplacian_backward
-from fused_hoad.parameters import pack_poisson_parameters
+from fused_hoad.parameters import flat_buffer_of, pack_poisson_parameters
 from fused_hoad.problem import ACTIVATIONS
 
-_cache: dict[str, object] = {}
-
-# Backward modes kept for drop-in compatibility with the reference's names
-# (backends/fused.py:24-32); every one runs the single fused adjoint kernel.
-_CUDA_BACKWARD_VERSIONS = {
-    "cuda": 6,
-    "cuda_v1": 1,
-    "cuda_v2": 2,
-    "cuda_v3": 3,
-    "cuda_v4": 4,
-    "cuda_v5": 5,
-}
+# Backward-mode names callers pass (the reference's), and the backward kernel version each
+# selects: "cuda" is version 6 (tensor cores), "cuda_vN" is version N (FP32 CUDA cores).
+_CUDA_BACKWARD_VERSIONS = {"cuda": 6, **{f"cuda_v{k}": k for k in range(1, 6)}}
 BACKWARD_MODES = tuple(_CUDA_BACKWARD_VERSIONS)
 
 
 class FusedForwardLaplacian(torch.autograd.Function):
-    """Fused-kernel forward ``(u, lap)``; fused-kernel backward to ``(coords, params)``."""
+    """``(u, lap)`` from the fused forward kernel; gradients for the coordinates and the
+    flat parameters from one fused backward kernel. Autograd hands the backward zero tensors
+    for an output that received no gradient (materialised gradients, the default)."""
 
     @staticmethod
-    def forward(
-        ctx,
-        coordinates: Tensor,
-        parameters: Tensor,
-        version: int,
-        backward: str,
-        activation: str = "tanh",
-    ):
+    def forward(ctx, coordinates: Tensor, parameters: Tensor, version: int, backward: str,
+                activation: str = "tanh"):
+        ctx.kernel = (_CUDA_BACKWARD_VERSIONS[backward], activation)
         ctx.save_for_backward(coordinates, parameters)
-        ctx.backward_mode = backward
-        ctx.activation = activation
         return fused_forward_laplacian(coordinates, parameters, version, activation)
 
     @staticmethod
-    def backward(ctx, grad_output: Tensor | None, grad_laplacian: Tensor | None):
+    def backward(ctx, grad_output: Tensor, grad_laplacian: Tensor):
         coordinates, parameters = ctx.saved_tensors
-        needs_coordinates, needs_parameters = ctx.needs_input_grad[:2]
-        if grad_output is None:
-            grad_output = torch.zeros_like(coordinates[:, :1])
-        if grad_laplacian is None:
-            grad_laplacian = torch.zeros_like(coordinates[:, :1])
-        grad_parameters, grad_coordinates = fused_forward_laplacian_backward(
-            coordinates,
-            parameters,
-            grad_output,
-            grad_laplacian,
-            _CUDA_BACKWARD_VERSIONS[ctx.backward_mode],
-            ctx.activation,
+        want_x, want_p = ctx.needs_input_grad[:2]
+        if not (want_x or want_p):
+            return None, None, None, None, None
+        bwd_version, activation = ctx.kernel
+        grad_p, grad_x = fused_forward_laplacian_backward(
+            coordinates, parameters, grad_output, grad_laplacian, bwd_version, activation
         )
-        return (
-            grad_coordinates if needs_coordinates else None,
-            grad_parameters if needs_parameters else None,
-            None,
-            None,
-            None,
-        )
+        return (grad_x if want_x else None), (grad_p if want_p else None), None, None, None
+
+
+class _PackEntry:
+    """What the pack cache holds for one model."""
+
+    __slots__ = ("tensors", "versions", "packed")
+
+    def __init__(self, tensors: list[Tensor]) -> None:
+        self.tensors = tensors
+        self.versions: tuple[int, ...] | None = None
+        self.packed: Tensor | None = None
+
+
+# One entry per live model, dropped with the model (no id() reuse hazard).
+_pack_cache: "weakref.WeakKeyDictionary[nn.Module, _PackEntry]" = weakref.WeakKeyDictionary()
 
 
 def _packed_parameters(model: nn.Module) -> Tensor:
-    """Differentiable pack when training; otherwise pack once per in-place weight update.
+    """The model's flat ABI buffer for a kernel call.
 
-    The parameter list is cached per model through a weakref, and the packed buffer is
-    rebuilt only when a parameter's version counter moved (reference fused.py:104-121).
+    While autograd records (grad enabled and a parameter requires grad) this is a fresh
+    differentiable pack, so gradients reach the model's parameters. Otherwise it is reused
+    until a parameter's version counter moves (an in-place update such as an optimizer step)
+    and re-packed then; a model whose parameters are already views of one flat buffer
+    (``bind_model_to_flat``) hands out that buffer itself and never copies.
     """
-    model_ref = _cache.get("model")
-    if model_ref is None or model_ref() is not model:
-        _cache.clear()
-        _cache.update(model=weakref.ref(model), parameters=list(model.parameters()))
-    parameters = _cache["parameters"]
-    if torch.is_grad_enabled() and any(p.requires_grad for p in parameters):
+    entry = _pack_cache.get(model)
+    if entry is None:
+        entry = _PackEntry(list(model.parameters()))
+        _pack_cache[model] = entry
+    if torch.is_grad_enabled() and any(t.requires_grad for t in entry.tensors):
         return pack_poisson_parameters(model, differentiable=True)
-    versions = [p._version for p in parameters]
-    if versions != _cache.get("versions"):
-        _cache.update(versions=versions, packed=pack_poisson_parameters(model))
-    return _cache["packed"]
+    versions = tuple(t._version for t in entry.tensors)
+    if entry.packed is None or versions != entry.versions:
+        bound = flat_buffer_of(model)
+        entry.packed = bound if bound is not None else pack_poisson_parameters(model)
+        entry.versions = versions
+    return entry.packed
 
 
 def model_activation(model: nn.Module) -> str:
@@ -109,15 +102,14 @@ def fused_laplacian(
     """Evaluate the fixed Poisson MLP and its input Laplacian with one CUDA kernel.
 
     ``backward`` names the gradient path when autograd is active (``"cuda"`` or
-    ``"cuda_vN"``; all run the fused adjoint kernel). The hidden activation (tanh or SiLU)
+    ``"cuda_vN"``; all run a fused adjoint kernel). The hidden activation (tanh or SiLU)
     is read from the model.
     """
     if backward not in BACKWARD_MODES:
         raise ValueError(f"backward must be one of {BACKWARD_MODES}")
     activation = model_activation(model)
     parameters = _packed_parameters(model)
+    coordinates = coordinates.contiguous()
     if parameters.requires_grad or coordinates.requires_grad:
-        return FusedForwardLaplacian.apply(
-            coordinates.contiguous(), parameters, version, backward, activation
-        )
-    return fused_forward_laplacian(coordinates.contiguous(), parameters, version, activation)
+        return FusedForwardLaplacian.apply(coordinates, parameters, version, backward, activation)
+    return fused_forward_laplacian(coordinates, parameters, version, activation)

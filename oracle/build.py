@@ -24,7 +24,11 @@ from pathlib import Path
 ORACLE = Path(__file__).resolve().parent
 BUILD = ORACLE / "_build"
 REF_OUT = ORACLE / "_ref"
-REFERENCE_ROOT = Path(os.environ.get("FUSED_HOAD_REFERENCE", "/root/reference"))
+# The reference checkout: FUSED_HOAD_REFERENCE, else a "reference" directory beside this
+# repository. Absent (as on a GPU box), the prebuilt oracle/_ref library is used as is.
+REFERENCE_ROOT = Path(
+    os.environ.get("FUSED_HOAD_REFERENCE", str(ORACLE.parent.parent / "reference"))
+)
 REF_MODULE = "fused_hoad_ref_C"
 
 

@@ -53,9 +53,12 @@ def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__)
     parser.add_argument(
         "--reference-src",
-        default=os.environ.get("FUSED_HOAD_REFERENCE_SRC", "/root/reference/src"),
+        default=os.environ.get("FUSED_HOAD_REFERENCE_SRC"),
+        help="the reference checkout's src/ directory (or FUSED_HOAD_REFERENCE_SRC)",
     )
     args = parser.parse_args()
+    if not args.reference_src:
+        parser.error("give --reference-src or set FUSED_HOAD_REFERENCE_SRC")
     sys.path.insert(0, args.reference_src)
 
     import torch

@@ -123,3 +123,48 @@ def test_missing_extension_message_is_actionable() -> None:
 def test_trainer_rejects_cpu_parameters() -> None:
     with pytest.raises(ValueError, match="CUDA"):
         fused_hoad.PoissonTrainer(torch.zeros(POISSON_PARAMETER_COUNT))
+
+
+def test_pack_cache_tracks_model_identity_and_in_place_updates() -> None:
+    """The reference's pack-cache contract (tests/test_backends.py:137-148): cached per
+    model, re-packed after an in-place update, and never another model's buffer."""
+    from fused_hoad.backends.fused import _packed_parameters
+
+    with torch.no_grad():
+        first = build_mlp(DEFAULT_POISSON_MLP)
+        packed = _packed_parameters(first)
+        assert _packed_parameters(first) is packed
+        first[0].weight.mul_(2.0)
+        torch.testing.assert_close(_packed_parameters(first), pack_poisson_parameters(first))
+        second = build_mlp(DEFAULT_POISSON_MLP)
+        torch.testing.assert_close(_packed_parameters(second), pack_poisson_parameters(second))
+        torch.testing.assert_close(_packed_parameters(first), pack_poisson_parameters(first))
+
+
+def test_pack_cache_hands_out_a_bound_flat_buffer_without_copying() -> None:
+    from fused_hoad.backends.fused import _packed_parameters
+
+    torch.manual_seed(4)
+    model = build_mlp()
+    flat = pack_poisson_parameters(model).clone()
+    bind_model_to_flat(model, flat)
+    with torch.no_grad():
+        packed = _packed_parameters(model)
+        assert packed.data_ptr() == flat.data_ptr() and torch.equal(packed, flat)
+        flat.mul_(0.5)  # an update of the buffer is the model's update
+        assert torch.equal(_packed_parameters(model), flat)
+    # while autograd records, the pack is differentiable and reaches the module parameters
+    differentiable = _packed_parameters(model)
+    assert differentiable.requires_grad
+    differentiable.sum().backward()
+    assert all(torch.all(p.grad == 1) for p in model.parameters())
+
+
+def test_layout_table_is_contiguous_and_ordered() -> None:
+    offset = 0
+    for spec in POISSON_PARAMETER_LAYOUT:
+        assert spec.weight_offset == offset
+        assert spec.bias_offset == offset + spec.out_features * spec.in_features
+        assert spec.weight_elements == spec.out_features * spec.in_features
+        offset = spec.end_offset
+    assert offset == POISSON_PARAMETER_COUNT
