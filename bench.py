@@ -49,6 +49,9 @@ METRIC = "collocation pts/sec for (u,Δu) eval and fwd+bwd step at 64K–16M pts
 UNIT = "pts/s"
 FLOP_FORWARD = 101_888  # per point: 3 hidden 64x64 jet GEMMs x 4 comps + layer 0/out + tanh jet
 FLOP_STEP = 98_304 * 3 + 256 * 2 + 6_000  # forward + input adjoint + weight gradient + small
+# per point: 3 hidden 64x64 GEMMs x 9 jet components, layer 0 and the 3-output layer, and
+# about 45 flops of the nine-component tanh map per neuron (256 neurons)
+FLOP_BIHARMONIC = 3 * 64 * 64 * 9 * 2 + 640 + 256 * 45
 POINTS_PER_GPU = 65_536
 CONFIG3_POINTS = (1_048_576, 4_194_304, 16_777_216)  # global points, split over the ranks
 CONFIG4_POINTS = 16_777_216                          # global points per training step
@@ -386,6 +389,22 @@ def run_ours(args) -> None:
         barrier()
         tf32_ms = max_over_ranks(sum(s.elapsed_time(e) for s, e in events)) / tf32_steps
 
+    # ---- the biharmonic (u, lap, bilap) on the FP32 CUDA cores, same points ----
+    bih_steps = max(1, min(args.steps, 500))
+    for _ in range(3):
+        C.fused_forward_biharmonic(coords, params)
+        flush.zero_()
+    events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(bih_steps)]
+    barrier()
+    for start, end in events:
+        flush.zero_()
+        start.record(stream)
+        C.fused_forward_biharmonic(coords, params)
+        end.record(stream)
+    barrier()
+    bih_ms = max_over_ranks(sum(s.elapsed_time(e) for s, e in events)) / bih_steps
+
     # ---- training step (config 2) ----
     # One step = weight pre-split, fused forward+loss+backward kernel, update kernel (row
     # reduction + sum over ranks through peer memory + Adam); with --exchange nccl the update
@@ -513,6 +532,14 @@ def run_ours(args) -> None:
             "achieved_tflops": n * FLOP_FORWARD / (tf32_ms / 1e3) / 1e12,
             "frac_of_split_ceiling": (n * FLOP_FORWARD / (tf32_ms / 1e3) / 1e12)
                                      / (peaks["bf16_tflops"] / 6.0),
+        },
+        "eval_biharmonic": {
+            "kernel": "forward_biharmonic_kernel (FP32 CUDA cores, nine-component jet)",
+            "outputs": "u, Laplacian, biharmonic", "points_per_gpu": n,
+            "value": n * world / (bih_ms / 1e3), "unit": UNIT, "ms_per_step": bih_ms,
+            "steps": bih_steps, "flop_per_point": FLOP_BIHARMONIC,
+            "achieved_tflops": n * FLOP_BIHARMONIC / (bih_ms / 1e3) / 1e12,
+            "frac_of_fp32_peak": (n * FLOP_BIHARMONIC / (bih_ms / 1e3) / 1e12) / fp32_peak,
         },
         "train_step": {
             "workload": "config2: fused forward+loss+backward kernel, " + (

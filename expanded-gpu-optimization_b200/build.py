@@ -41,7 +41,7 @@ NVCC_FLAGS = [
 ]
 CU_SOURCES = [
     "forward_fp32.cu", "forward_tc.cu", "backward_fp32.cu", "backward_tc.cu", "adam.cu",
-    "collective.cu", "capi.cu", "noalloc.cu",
+    "collective.cu", "capi.cu", "noalloc.cu", "biharmonic.cu",
 ]
 
 

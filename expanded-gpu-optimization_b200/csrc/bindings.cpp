@@ -85,6 +85,24 @@ std::vector<torch::Tensor> fused_forward_laplacian(torch::Tensor coordinates,
   return {output, laplacian};
 }
 
+// (u, lap, bilap) [N,1] each: the biharmonic of the tanh MLP (fhb_forward_biharmonic).
+std::vector<torch::Tensor> fused_forward_biharmonic(torch::Tensor coordinates,
+                                                    torch::Tensor parameters) {
+  check_inputs(coordinates, parameters);
+  const c10::cuda::CUDAGuard device_guard(coordinates.device());
+  const int64_t batch = coordinates.size(0);
+  auto output = torch::empty({batch, 1}, coordinates.options());
+  auto laplacian = torch::empty({batch, 1}, coordinates.options());
+  auto biharmonic = torch::empty({batch, 1}, coordinates.options());
+  if (batch == 0) return {output, laplacian, biharmonic};
+  check_status(fhb_forward_biharmonic(coordinates.data_ptr<float>(),
+                                      parameters.data_ptr<float>(), output.data_ptr<float>(),
+                                      laplacian.data_ptr<float>(), biharmonic.data_ptr<float>(),
+                                      batch, at::cuda::getCurrentCUDAStream()),
+               "fused_forward_biharmonic");
+  return {output, laplacian, biharmonic};
+}
+
 std::vector<torch::Tensor> fused_forward_laplacian_backward(torch::Tensor coordinates,
                                                             torch::Tensor parameters,
                                                             torch::Tensor grad_output,
@@ -359,6 +377,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, module) {
              "Fixed MLP forward pass and input Laplacian (CUDA, sm_100a)",
              pybind11::arg("coordinates"), pybind11::arg("parameters"),
              pybind11::arg("version") = 2, pybind11::arg("activation") = "tanh");
+  module.def("fused_forward_biharmonic", &fused_forward_biharmonic,
+             "Fixed tanh MLP forward pass, its input Laplacian and biharmonic (CUDA, sm_100a)",
+             pybind11::arg("coordinates"), pybind11::arg("parameters"));
   module.def("fused_forward_laplacian_backward", &fused_forward_laplacian_backward,
              "Gradients of the fused forward Laplacian w.r.t. parameters and coordinates "
              "(CUDA, sm_100a)",

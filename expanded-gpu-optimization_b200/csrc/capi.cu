@@ -49,7 +49,8 @@ int prepare_locked(int device) {
         (e = fhb::prepare_forward_fp32()) != cudaSuccess ||
         (e = fhb::prepare_forward_tc()) != cudaSuccess ||
         (e = fhb::prepare_backward_fp32()) != cudaSuccess ||
-        (e = fhb::prepare_backward_tc()) != cudaSuccess) {
+        (e = fhb::prepare_backward_tc()) != cudaSuccess ||
+        (e = fhb::prepare_biharmonic()) != cudaSuccess) {
       code = record(e);
       break;
     }
@@ -198,6 +199,20 @@ int fhb_forward_ex(const float* coords, const float* params, float* u, float* la
 int fhb_forward(const float* coords, const float* params, float* u, float* lap, int64_t n,
                 int version, fhb_stream_t stream) {
   return fhb_forward_ex(coords, params, u, lap, n, version, FHB_ACTIVATION_TANH, stream);
+}
+
+int fhb_forward_biharmonic(const float* coords, const float* params, float* u, float* lap,
+                           float* bilap, int64_t n, fhb_stream_t stream) {
+  if (n < 0) return FHB_ERR_INVALID_ARGUMENT;
+  if (n == 0) return FHB_OK;
+  if (!coords || !params || !u || !lap || !bilap) return FHB_ERR_INVALID_ARGUMENT;
+  if (!aligned(coords, 4) || !aligned(params, 4) || !aligned(u, 4) || !aligned(lap, 4) ||
+      !aligned(bilap, 4))
+    return FHB_ERR_MISALIGNED;
+  const fhb::DeviceInfo* dev = nullptr;
+  int code = current_device(&dev);
+  if (code != FHB_OK) return code;
+  return record(fhb::launch_forward_biharmonic(coords, params, u, lap, bilap, n, *dev, stream));
 }
 
 size_t fhb_backward_workspace_bytes(int64_t n) {

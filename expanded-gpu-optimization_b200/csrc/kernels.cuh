@@ -152,6 +152,13 @@ cudaError_t launch_forward_tc(const float* coords, const float* params, float* u
                               int64_t n, bool f16, int activation, const DeviceInfo& dev,
                               cudaStream_t stream);
 
+// ---- biharmonic.cu ----
+cudaError_t prepare_biharmonic();
+// (u, Laplacian, biharmonic) of the tanh MLP, FP32 CUDA cores.
+cudaError_t launch_forward_biharmonic(const float* coords, const float* params, float* u,
+                                      float* lap, float* bilap, int64_t n,
+                                      const DeviceInfo& dev, cudaStream_t stream);
+
 // ---- backward_fp32.cu ----
 cudaError_t prepare_backward_fp32();
 int backward_grid(int64_t n, int64_t nb, const DeviceInfo& dev);

@@ -9,6 +9,7 @@ CPU or PyTorch fallback: calls raise if the extension is missing.
 
 from fused_hoad._extension import (
     extension_available,
+    fused_forward_biharmonic,
     fused_forward_laplacian,
     fused_forward_laplacian_backward,
     fused_forward_laplacian_host,
@@ -49,6 +50,7 @@ __all__ = [
     "build_mlp",
     "cuda_graph_step",
     "extension_available",
+    "fused_forward_biharmonic",
     "fused_forward_laplacian",
     "fused_forward_laplacian_backward",
     "fused_forward_laplacian_host",

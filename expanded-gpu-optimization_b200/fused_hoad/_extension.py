@@ -54,6 +54,17 @@ def fused_forward_laplacian(
     return output, laplacian
 
 
+def fused_forward_biharmonic(
+    coordinates: Tensor, parameters: Tensor
+) -> tuple[Tensor, Tensor, Tensor]:
+    """``(u, lap, bilap)``, each ``[N, 1]``: the tanh MLP, its input Laplacian and its
+    biharmonic (the Laplacian of the Laplacian), from one FP32 CUDA-core kernel that carries
+    a nine-component jet per neuron. Not part of the reference's extension (it computes the
+    biharmonic only by nested autograd)."""
+    u, lap, bilap = load_extension().fused_forward_biharmonic(coordinates, parameters)
+    return u, lap, bilap
+
+
 def fused_forward_laplacian_backward(
     coordinates: Tensor,
     parameters: Tensor,

@@ -22,6 +22,7 @@ _SIGNATURES: dict[str, tuple[object, list]] = {
     "fhb_prepare_device": (ctypes.c_int, [ctypes.c_int]),
     "fhb_forward": (ctypes.c_int, [_p, _p, _p, _p, _i64, ctypes.c_int, _p]),
     "fhb_forward_ex": (ctypes.c_int, [_p, _p, _p, _p, _i64, ctypes.c_int, ctypes.c_int, _p]),
+    "fhb_forward_biharmonic": (ctypes.c_int, [_p, _p, _p, _p, _p, _i64, _p]),
     "fhb_backward_workspace_bytes": (ctypes.c_size_t, [_i64]),
     "fhb_backward": (
         ctypes.c_int,

@@ -107,6 +107,18 @@ int fhb_forward_ex(const float* coords, const float* params, float* u, float* la
                    int version, int activation, fhb_stream_t stream);
 
 /*
+ * The biharmonic of the tanh MLP: u[n], lap[n] (the Laplacian) and bilap[n] (the Laplacian
+ * of the Laplacian, u_xxxx + 2 u_xxyy + u_yyyy) at coords[n][2], on the FP32 CUDA cores by a
+ * nine-component jet (value, gradient, Hessian, gradient of the Laplacian, biharmonic per
+ * neuron). No counterpart entry in the reference, which names the biharmonic as the next
+ * operator for its kernel design and computes it only by nested autograd
+ * (src/fused_hoad/autodiff.py:39-41 applied twice). Tolerance against that FP64 autograd:
+ * that of the FP32 forward (atol 1e-5, rtol 1e-4). n == 0 is a no-op.
+ */
+int fhb_forward_biharmonic(const float* coords, const float* params, float* u, float* lap,
+                           float* bilap, int64_t n, fhb_stream_t stream);
+
+/*
  * Workspace the backward needs for n points on the current device, in bytes (0 for n==0),
  * enough for every backward version: one partial-gradient row per CTA of the persistent
  * grid, and for the tensor-core kernel also the pre-split weights (192 KB) and 512 KB of

@@ -294,3 +294,96 @@ def adam_update(
     bias2 = 1.0 - beta2**step
     denom = exp_avg_sq.sqrt() / math.sqrt(bias2) + eps
     params.addcdiv_(exp_avg, denom, value=-lr / bias1)
+
+
+# ---- the biharmonic (fourth-order) jet ---------------------------------------------------
+#
+# Not in the reference, which names the biharmonic as the next operator to test its kernel
+# design on (README.md, "Directions to try next"). Its own higher-order tool is nested
+# autograd (src/fused_hoad/autodiff.py:39-41, ``laplacian``); ``eager_biharmonic`` applies
+# that construction twice and the golden vectors come from the reference's ``laplacian``
+# applied twice. The jet carries, per neuron, the nine components
+#     [v, g_x, g_y, H_xx, H_xy, H_yy, T_x, T_y, B]
+# (value, gradient, Hessian, T = grad(Laplacian), B = biharmonic). A linear layer maps every
+# component linearly (the bias only the value); phi = tanh maps them by the chain rule
+# (d1..d4 the first to fourth derivatives of tanh at z):
+#     H'_ij = d2 g_i g_j + d1 H_ij
+#     T'_k  = d3 g_k |g|^2 + 2 d2 (H g)_k + d2 g_k tr H + d1 T_k
+#     B'    = d4 |g|^4 + d3 (2 tr H |g|^2 + 4 g.H.g) + d2 (2 |H|_F^2 + 4 g.T + (tr H)^2)
+#             + d1 B
+# with d1 = 1 - a^2, d2 = -2 a d1, d3 = -2 d1 (1 - 3a^2), d4 = 8 a d1 (2 - 3a^2), a = tanh z.
+BIHARMONIC_COMPONENTS = 9
+
+
+def _tanh_biharmonic_jet(jet: Tensor) -> Tensor:
+    """The tanh map of a ``[n, 9, width]`` biharmonic jet (formulas above)."""
+    z, gx, gy, hxx, hxy, hyy, tx, ty, b = jet.unbind(1)
+    a = torch.tanh(z)
+    d1 = 1 - a * a
+    d2 = -2 * a * d1
+    d3 = -2 * d1 * (1 - 3 * a * a)
+    d4 = 8 * a * d1 * (2 - 3 * a * a)
+    g2 = gx * gx + gy * gy
+    lap = hxx + hyy
+    hgx = hxx * gx + hxy * gy
+    hgy = hxy * gx + hyy * gy
+    ghg = gx * hgx + gy * hgy
+    hf2 = hxx * hxx + 2 * hxy * hxy + hyy * hyy
+    gt = gx * tx + gy * ty
+    return torch.stack(
+        (
+            a,
+            d1 * gx,
+            d1 * gy,
+            d2 * gx * gx + d1 * hxx,
+            d2 * gx * gy + d1 * hxy,
+            d2 * gy * gy + d1 * hyy,
+            d3 * gx * g2 + 2 * d2 * hgx + d2 * gx * lap + d1 * tx,
+            d3 * gy * g2 + 2 * d2 * hgy + d2 * gy * lap + d1 * ty,
+            d4 * g2 * g2 + d3 * (2 * lap * g2 + 4 * ghg) + d2 * (2 * hf2 + 4 * gt + lap * lap)
+            + d1 * b,
+        ),
+        dim=1,
+    )
+
+
+def forward_biharmonic(params: Tensor, coords: Tensor) -> tuple[Tensor, Tensor, Tensor]:
+    """``(u, lap, bilap)`` each ``[n, 1]`` of the packed tanh MLP by the biharmonic jet, in
+    the dtype of ``coords``."""
+    linears = unpack(params.to(coords.dtype))
+    n = coords.shape[0]
+    jet = coords.new_zeros(n, BIHARMONIC_COMPONENTS, 2)
+    jet[:, 0] = coords
+    jet[:, 1, 0] = 1.0  # d/dx of (x, y)
+    jet[:, 2, 1] = 1.0  # d/dy
+    for index, (weight, bias) in enumerate(linears):
+        jet = jet @ weight.T
+        jet[:, 0].add_(bias)
+        if index < len(linears) - 1:
+            jet = _tanh_biharmonic_jet(jet)
+    return jet[:, 0], jet[:, 3] + jet[:, 5], jet[:, 8]
+
+
+def eager_biharmonic(params: Tensor, coords: Tensor) -> tuple[Tensor, Tensor, Tensor]:
+    """``(u, lap, bilap)`` by nested autograd: the Laplacian of the Laplacian, each by the
+    construction of src/fused_hoad/autodiff.py:24-41 (the Hessian diagonal, summed)."""
+    linears = unpack(params.to(coords.dtype))
+    x = coords.detach().clone().requires_grad_(True)
+
+    def laplacian_of(f: Tensor) -> Tensor:
+        (first,) = torch.autograd.grad(f.sum(), x, create_graph=True)
+        total = torch.zeros_like(f)
+        for d in range(x.shape[1]):
+            (second,) = torch.autograd.grad(first[:, d].sum(), x, create_graph=True)
+            total = total + second[:, d : d + 1]
+        return total
+
+    with torch.enable_grad():
+        h = x
+        for index, (weight, bias) in enumerate(linears):
+            h = h @ weight.T + bias
+            if index < len(linears) - 1:
+                h = torch.tanh(h)
+        lap = laplacian_of(h)
+        bilap = laplacian_of(lap)
+    return h.detach(), lap.detach(), bilap.detach()

@@ -17,6 +17,9 @@ Imports ``fused_hoad`` from the reference checkout's ``src/`` (default: the path
 * the full PINN loss of ``poisson_loss_fn`` (``src/fused_hoad/training.py:68-94``: interior
   residual + 100 * mean(u^2) on ``boundary_points``, ``:45-53``) through the FL backend, and
   its parameter gradients;
+* the biharmonic: the reference's ``autodiff.laplacian`` (``src/fused_hoad/autodiff.py:39-41``)
+  applied to its own output, on the seed-0 MLP in FP32 and FP64 and on the x3 seed-1 MLP in
+  FP64 (u, Laplacian, biharmonic);
 * for the SiLU MLP (``MLPConfig(activation="silu")``, ``src/fused_hoad/models.py:9-12``): FL
   forwards in FP32/FP64 and the FP64 eager Laplacian, an x3-scaled FP64 forward, FP64
   gradients by autograd through FL (the reference's fused backward is tanh-only), and the
@@ -47,6 +50,8 @@ PINN_INTERIOR = 256
 PINN_BOUNDARY = 64
 SILU_FORWARD_BATCHES = (1, 33, 129, 1000)
 SILU_BACKWARD_BATCHES = (33, 1000)
+BIHARMONIC_BATCHES = (1, 33, 129, 1000)
+BIHARMONIC_SATURATED_BATCH = 1024
 
 
 def main() -> None:
@@ -233,6 +238,36 @@ def main() -> None:
         losses.append(loss.item())
     out["siluadam_losses"] = np.array(losses, dtype=np.float64)
     out["siluadam_params_final"] = pack_poisson_parameters(train).detach().numpy()
+
+    # The biharmonic: the reference's own higher-order operator, autodiff.laplacian
+    # (src/fused_hoad/autodiff.py:39-41), applied to its own output, on the seed-0 MLP
+    # (FP32 and FP64) and on the x3 seed-1 MLP (FP64).
+    from fused_hoad.autodiff import differentiable_coordinates, laplacian
+
+    def reference_biharmonic(m, x):
+        with torch.enable_grad():
+            xd = differentiable_coordinates(x)
+            u = m(xd)
+            lap = laplacian(u, xd)
+            bilap = laplacian(lap, xd)
+        return u.detach(), lap.detach(), bilap.detach()
+
+    for n in BIHARMONIC_BATCHES:
+        x = points(n)
+        out[f"bih{n}_x"] = x.numpy()
+        for tag in ("32", "64"):  # nn.Module.float()/.double() convert in place
+            m = m0.float() if tag == "32" else m0.double()
+            u, lap, bilap = reference_biharmonic(m, x if tag == "32" else x.double())
+            out[f"bih{n}_u{tag}"] = u.numpy()
+            out[f"bih{n}_lap{tag}"] = lap.numpy()
+            out[f"bih{n}_bilap{tag}"] = bilap.numpy()
+        m0.float()
+    xs = points(BIHARMONIC_SATURATED_BATCH)
+    u, lap, bilap = reference_biharmonic(m1.double(), xs.double())
+    m1.float()
+    out["bihsat_x"] = xs.numpy()
+    out["bihsat_u64"], out["bihsat_lap64"], out["bihsat_bilap64"] = (
+        u.numpy(), lap.numpy(), bilap.numpy())
 
     np.savez_compressed(OUT, **out)
     print(f"wrote {OUT} ({OUT.stat().st_size / 1024:.0f} KiB, {len(out)} arrays)")

@@ -63,3 +63,12 @@ def test_noalloc_backward_rejects_bad_arguments_before_any_device_work() -> None
     assert call(8, grad_lap=None) == 1        # upstream Laplacian gradient missing
     for name in args:                         # every pointer's alignment is checked
         assert call(8, **{name: bad}) == 2, name
+
+
+def test_biharmonic_entry_validates_before_device_work() -> None:
+    lib = _native.library()
+    good, bad = 4096, 4098  # stand-in addresses, never dereferenced
+    assert lib.fhb_forward_biharmonic(good, good, good, good, good, -1, None) == 1
+    assert lib.fhb_forward_biharmonic(None, None, None, None, None, 0, None) == 0
+    assert lib.fhb_forward_biharmonic(good, good, good, None, good, 8, None) == 1
+    assert lib.fhb_forward_biharmonic(good, good, good, good, bad, 8, None) == 2

@@ -196,3 +196,41 @@ def test_oracle_silu_adam_trajectory_matches_reference(golden) -> None:
     np.testing.assert_allclose(losses, golden["siluadam_losses"], rtol=1e-5)
     diff = np.abs(p.numpy() - golden["siluadam_params_final"])
     assert np.mean(diff > 1e-6) < 1e-3, float(diff.max())
+
+
+BIHARMONIC_BATCHES = (1, 33, 129, 1000)
+
+
+@pytest.mark.parametrize("n", BIHARMONIC_BATCHES)
+def test_biharmonic_jet_fp64_matches_reference_autograd(golden, n: int) -> None:
+    """The nine-component jet against the reference's laplacian(laplacian(u)) in FP64."""
+    params = torch.from_numpy(golden["params_seed0"]).double()
+    x = torch.from_numpy(golden[f"bih{n}_x"]).double()
+    u, lap, bilap = jet.forward_biharmonic(params, x)
+    np.testing.assert_allclose(u.numpy(), golden[f"bih{n}_u64"], rtol=1e-12, atol=1e-14)
+    np.testing.assert_allclose(lap.numpy(), golden[f"bih{n}_lap64"], rtol=1e-11, atol=1e-13)
+    np.testing.assert_allclose(bilap.numpy(), golden[f"bih{n}_bilap64"], rtol=1e-10, atol=1e-12)
+
+
+@pytest.mark.parametrize("n", BIHARMONIC_BATCHES)
+def test_biharmonic_jet_fp32_within_fp32_tolerance_of_reference(golden, n: int) -> None:
+    params = torch.from_numpy(golden["params_seed0"])
+    x = torch.from_numpy(golden[f"bih{n}_x"])
+    u, lap, bilap = jet.forward_biharmonic(params, x)
+    for got, key in ((u, "u"), (lap, "lap"), (bilap, "bilap")):
+        np.testing.assert_allclose(got.numpy(), golden[f"bih{n}_{key}32"], rtol=1e-4, atol=1e-5)
+
+
+def test_biharmonic_eager_oracle_matches_reference(golden) -> None:
+    params = torch.from_numpy(golden["params_seed0"]).double()
+    x = torch.from_numpy(golden["bih33_x"]).double()
+    _, _, bilap = jet.eager_biharmonic(params, x)
+    np.testing.assert_allclose(bilap.numpy(), golden["bih33_bilap64"], rtol=1e-10, atol=1e-12)
+
+
+def test_biharmonic_jet_saturated_weights(golden) -> None:
+    params = torch.from_numpy(golden["params_seed1_x3"]).double()
+    x = torch.from_numpy(golden["bihsat_x"]).double()
+    u, lap, bilap = jet.forward_biharmonic(params, x)
+    assert_scaled_close(bilap.numpy(), golden["bihsat_bilap64"], 1e-10, "bilap x3")
+    assert_scaled_close(lap.numpy(), golden["bihsat_lap64"], 1e-10, "lap x3")
