@@ -574,6 +574,52 @@ __device__ __forceinline__ void stage_f16(const float* __restrict__ params, uint
   }
 }
 
+// Layer 0 of one tile, for the point (x0, x1) of this thread: z = W0 x + b0, z_J = the row of
+// W0, z_L = 0, through the activation into the four chunks of GEMM 0's A operand (f16: the
+// scaled operand directly). Advances the chunk counter; false if a wait gave up.
+template <bool F16, class Act>
+__device__ __forceinline__ bool produce_layer0(float x0, float x1, uint32_t& chunk,
+                                               uint32_t tmem_warp, int s, const Ctx& cx,
+                                               const float* small) {
+  if constexpr (F16) {
+    using C = F16Consts;
+    const float sv = cx.f16c[C::kOut + 4], sv2 = cx.f16c[C::kOut + 5];
+    const float* l0 = cx.f16c + C::kL0 + 4 * s;
+#pragma unroll
+    for (int j = 0; j < kChunks; ++j) {
+      const float* c0 = l0 + 16 * j;  // neurons 16j + 4s + t, t = 0..3
+      const float4 wx = ld_f4(c0), wy = ld_f4(c0 + kWidth), bz = ld_f4(c0 + 2 * kWidth);
+      const float4 kj0 = ld_f4(c0 + 3 * kWidth), kj1 = ld_f4(c0 + 4 * kWidth);
+      const float4 kl = ld_f4(c0 + 5 * kWidth), kl2 = ld_f4(c0 + 6 * kWidth);
+      float h[4][4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const float r = tanh_r_scaled(fmaf(at(wx, t), x0, fmaf(at(wy, t), x1, at(bz, t))));
+        const float tt = fmaf(-r, r, r);  // (1 - tanh^2) / 4
+        h[0][t] = fmaf(sv2, r, sv);
+        h[1][t] = tt * at(kj0, t);
+        h[2][t] = tt * at(kj1, t);
+        h[3][t] = tt * fmaf(at(kl2, t), r, at(kl, t));
+      }
+      if (!produce_chunk<F16>(chunk++, j, h, tmem_warp, s, cx)) return false;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < kChunks; ++j) {
+      float h[4][4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        const int o = 16 * j + 4 * s + t;
+        const float w0 = small[kSmW0 + 2 * o], w1 = small[kSmW0 + 2 * o + 1];
+        const float z = fmaf(w0, x0, fmaf(w1, x1, small[kSmB0 + o]));
+        Act::jet_fast(z, w0, w1, 0.0f, h[0][t], h[1][t], h[2][t], h[3][t]);
+      }
+      if (!produce_chunk<F16>(chunk++, j, h, tmem_warp, s, cx)) return false;
+    }
+  }
+  return true;
+}
+
 template <bool F16, class Act>
 __global__ void __launch_bounds__(kBlockThreads, 1)
     forward_tc_kernel(const float* __restrict__ coords, const float* __restrict__ params,
@@ -686,56 +732,21 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
     const int row = 32 * q + lane;
     uint32_t chunk = 0, mlayer = 0, tile_count = 0;
     bool ok = run;
-    // Points of the next tile are loaded one tile ahead, so the load latency (long when the
+    // Layer 0 of a tile runs at the end of the previous tile (right after GEMM 2's
+    // accumulators are loaded, before that tile's output stage), so GEMM 0 of the next tile
+    // runs on the tensor core while the warps finish the output stage. The first tile's
+    // layer 0 runs here. Points are loaded one tile ahead, so the load latency (long when the
     // points sit in pinned host memory read over the host link) overlaps a tile of work.
+    if (ok && static_cast<int64_t>(blockIdx.x) < tiles)
+      ok = produce_layer0<F16, Act>(nx0, nx1, chunk, tmem_warp, s, cx, small);
     for (int64_t tile = blockIdx.x; ok && tile < tiles; tile += gridDim.x, ++tile_count) {
       const int64_t p = tile * kTile + row;
       const bool active = p < n;
-      const float x0 = nx0, x1 = nx1;
+      const bool has_next = tile + gridDim.x < tiles;
       {
         const int64_t pn = p + static_cast<int64_t>(gridDim.x) * kTile;
-        if (pn < n) {
-          nx0 = coords[2 * pn];
-          nx1 = coords[2 * pn + 1];
-        }
-      }
-
-      // layer 0: z = W0 x + b0, z_J = W0 columns, z_L = 0 (f16: the scaled operand directly)
-      if constexpr (F16) {
-        using C = F16Consts;
-        const float sv = cx.f16c[C::kOut + 4], sv2 = cx.f16c[C::kOut + 5];
-        const float* l0 = cx.f16c + C::kL0 + 4 * s;
-#pragma unroll
-        for (int j = 0; j < kChunks; ++j) {
-          const float* c0 = l0 + 16 * j;  // neurons 16j + 4s + t, t = 0..3
-          const float4 wx = ld_f4(c0), wy = ld_f4(c0 + kWidth), bz = ld_f4(c0 + 2 * kWidth);
-          const float4 kj0 = ld_f4(c0 + 3 * kWidth), kj1 = ld_f4(c0 + 4 * kWidth);
-          const float4 kl = ld_f4(c0 + 5 * kWidth), kl2 = ld_f4(c0 + 6 * kWidth);
-          float h[4][4];
-#pragma unroll
-          for (int t = 0; t < 4; ++t) {
-            const float r = tanh_r_scaled(fmaf(at(wx, t), x0, fmaf(at(wy, t), x1, at(bz, t))));
-            const float tt = fmaf(-r, r, r);  // (1 - tanh^2) / 4
-            h[0][t] = fmaf(sv2, r, sv);
-            h[1][t] = tt * at(kj0, t);
-            h[2][t] = tt * at(kj1, t);
-            h[3][t] = tt * fmaf(at(kl2, t), r, at(kl, t));
-          }
-          if (!(ok = produce_chunk<F16>(chunk++, j, h, tmem_warp, s, cx))) break;
-        }
-      } else {
-#pragma unroll
-        for (int j = 0; j < kChunks; ++j) {
-          float h[4][4];
-#pragma unroll
-          for (int t = 0; t < 4; ++t) {
-            const int o = 16 * j + 4 * s + t;
-            const float w0 = small[kSmW0 + 2 * o], w1 = small[kSmW0 + 2 * o + 1];
-            const float z = fmaf(w0, x0, fmaf(w1, x1, small[kSmB0 + o]));
-            Act::jet_fast(z, w0, w1, 0.0f, h[0][t], h[1][t], h[2][t], h[3][t]);
-          }
-          if (!(ok = produce_chunk<F16>(chunk++, j, h, tmem_warp, s, cx))) break;
-        }
+        nx0 = pn < n ? coords[2 * pn] : 0.0f;
+        nx1 = pn < n ? coords[2 * pn + 1] : 0.0f;
       }
 
       for (int l = 0; ok && l < kHiddenGemms; ++l, ++mlayer) {
@@ -775,6 +786,9 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
             }
             continue;
           }
+          if (has_next && !(ok = produce_layer0<F16, Act>(nx0, nx1, chunk, tmem_warp, s, cx,
+                                                          small)))
+            break;
           // output layer: u = w.a + b, lap = w.L, over this warp's 16 neurons
           const float4 ko = ld_f4(cx.f16c + C::kOut);
           const float* wout = small + kSmWout + 4 * s;
@@ -810,6 +824,9 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
             }
             continue;
           }
+          if (has_next && !(ok = produce_layer0<F16, Act>(nx0, nx1, chunk, tmem_warp, s, cx,
+                                                          small)))
+            break;
 #pragma unroll
           for (int i = 0; i < 16; ++i) d[0][i] += bias[16 * (i >> 2) + 4 * s + (i & 3)];
           // output layer: u = w.v + b, lap = w.L, over this warp's 16 neurons
