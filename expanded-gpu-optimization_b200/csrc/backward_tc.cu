@@ -111,7 +111,8 @@ constexpr int kPartKinds = 7;
 constexpr int kPLoss = kPartKinds * 256, kPBout = kPLoss + 4;
 constexpr int kPartFloats = kPBout + 4;
 constexpr int kXsOff = kPartOff + kPartFloats * 4;            // the tile's points x[512], y[512]
-constexpr int kBarOff = kXsOff + 2 * kThreads * 4;            // mbarriers
+constexpr int kXnOff = kXsOff + 2 * kThreads * 4;             // the next tile's, same layout
+constexpr int kBarOff = kXnOff + 2 * kThreads * 4;            // mbarriers
 constexpr int kNumBars = 10;   // empty[2] dfull red wfull[2] dwdone[2] full[2]
 constexpr int kMiscOff = kBarOff + kNumBars * 8;              // TMEM base, abort flag, status
 constexpr int kSmemBytes = kMiscOff + 16;
@@ -267,6 +268,48 @@ __device__ __forceinline__ bool produce_chunk(uint32_t n, const float (&h)[4][4]
   return true;
 }
 
+// Layer 0 of the forward recompute for the point (x0, x1): z = W0 x + b0, z_J = the row of
+// W0, z_L = 0, through the tanh jet into the four chunks of GEMM 0's A operand.
+__device__ __forceinline__ void produce_layer0(float x0, float x1, const float* small,
+                                               uint32_t& chunk, uint32_t tmem_warp, int s,
+                                               const Ctx& cx) {
+#pragma unroll
+  for (int a = 0; a < kChunks; ++a) {
+    float h[4][4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const int o = 16 * a + 4 * s + t;
+      const float w0 = small[kSmW0 + 2 * o], w1 = small[kSmW0 + 2 * o + 1];
+      tanh_jet_fast(fmaf(w0, x0, fmaf(w1, x1, small[kSmB0 + o])), w0, w1, 0.0f, h[0][t],
+                    h[1][t], h[2][t], h[3][t]);
+    }
+    produce_chunk(chunk++, h, tmem_warp, s, cx);
+  }
+}
+
+// Asynchronous copy of point `row` of tile `tile` into shared memory (x at dst[0], y at
+// dst[kThreads]): cp.async with a zero source size past the end of the point set, which
+// writes zeros. No register holds the point while the copy is in flight.
+__device__ __forceinline__ void prefetch_point(const PointSets& ps, int64_t tile, int row,
+                                               float* dst) {
+  const bool b = tile >= ps.tiles;
+  const int64_t p = (b ? tile - ps.tiles : tile) * kTile + row;
+  const float* set = b ? ps.boundary : ps.interior;
+  const bool in = p < (b ? ps.nb : ps.n);
+  const float* src = in ? set + 2 * p : set;  // a valid address even when nothing is read
+  const uint32_t bytes = in ? 4u : 0u;
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_u32(dst)), "l"(src),
+               "r"(bytes)
+               : "memory");
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(smem_u32(dst + kThreads)),
+               "l"(src + (in ? 1 : 0)), "r"(bytes)
+               : "memory");
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+__device__ __forceinline__ void prefetch_wait() {
+  asm volatile("cp.async.wait_all;" ::: "memory");
+}
+
 // Adjoint of the tanh jet in terms of the activation it produced. With h = (a, h_J0, h_J1,
 // h_L), s = 1 - a^2 and the upstream adjoint (gv, g0, g1, gl) of h, the pre-activation
 // adjoint is (tanh_jet_adjoint's formulas after substituting h_J = s z_J and
@@ -359,6 +402,38 @@ __device__ __forceinline__ float warp_sum16(const float (&v)[16]) {
   return r + __shfl_xor_sync(0xffffffffu, r, 1);
 }
 
+// Sums v[k] over the 32 lanes for every k < 8 with the same halving butterfly as
+// warp_sum16; lane l returns the total for k = (l >> 2) & 7.
+__device__ __forceinline__ float warp_sum8(const float (&v)[8]) {
+  const int lane = threadIdx.x & 31;
+  float u4[4], u2[2];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const bool hi = (lane & 16) != 0;
+    const float keep = hi ? v[4 + j] : v[j], send = hi ? v[j] : v[4 + j];
+    u4[j] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+  }
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const bool hi = (lane & 8) != 0;
+    const float keep = hi ? u4[2 + j] : u4[j], send = hi ? u4[j] : u4[2 + j];
+    u2[j] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+  }
+  const bool hi = (lane & 4) != 0;
+  float r = (hi ? u2[1] : u2[0]) + __shfl_xor_sync(0xffffffffu, hi ? u2[0] : u2[1], 4);
+  r += __shfl_xor_sync(0xffffffffu, r, 2);
+  return r + __shfl_xor_sync(0xffffffffu, r, 1);
+}
+
+// Writes half `h` (neuron slots 8h..8h+7) of a warp_sum8 result to the per-quadrant partials.
+__device__ __forceinline__ void store_part8(float* part, int kind, int q, int s, int h, float r) {
+  const int lane = threadIdx.x & 31;
+  if ((lane & 3) == 0) {
+    const int i = 8 * h + (lane >> 2);
+    part[kind * 256 + q * 64 + 16 * (i >> 2) + 4 * s + (i & 3)] = r;
+  }
+}
+
 // Writes this warp's per-neuron sums (warp_sum16 output) to the per-quadrant partials.
 __device__ __forceinline__ void store_part16(float* part, int kind, int q, int s, float r) {
   const int lane = threadIdx.x & 31;
@@ -382,7 +457,7 @@ __global__ void __launch_bounds__(256) prep_weights_kernel(const float* __restri
   if (idx >= kWeightBlocks * 4096) return;
   const int blk = idx >> 12, e = idx & 4095;
   const int layer = blk % 3;
-  const int row = ((e >> 9) << 3) | ((e >> 2) & 7);
+  const int row = neuron_of_column(((e >> 9) << 3) | ((e >> 2) & 7));  // epilogue column order
   const int k = (((e >> 5) & 15) << 2) | (e & 3);
   const float* W = params + kHiddenBase + layer * kHiddenStride;
   const float w = blk >= 3 ? W[k * kWidth + row] : W[row * kWidth + k];
@@ -489,31 +564,27 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
 
     uint32_t chunk = 0, mlayer = 0, tile_count = 0, dw_issued = 0;
     bool alive = true;
-    float nx0 = 0.0f, nx1 = 0.0f;
-    load_point(ps, blockIdx.x, kTile, row, nx0, nx1);
+    // The tile's point lives in shared memory (xs), so no register holds it through the
+    // backward sweep. Layer 0 of a tile is produced at the end of the previous tile (right
+    // after the last input-adjoint GEMM's accumulators are read, before that tile's layer-0
+    // adjoint), so GEMM 0 of the next tile runs under it; the first tile's layer 0 runs here.
+    {
+      float x0 = 0.0f, x1 = 0.0f;
+      load_point(ps, blockIdx.x, kTile, row, x0, x1);
+      xs[tid] = x0;
+      xs[kThreads + tid] = x1;
+      if (static_cast<int64_t>(blockIdx.x) < tiles)
+        produce_layer0(x0, x1, small, chunk, tmem_warp, s, cx);
+    }
+    float* const xn = reinterpret_cast<float*>(smem + kXnOff);  // the next tile's points
     for (int64_t tile = blockIdx.x; alive && tile < tiles; tile += gridDim.x, ++tile_count) {
       const bool has_next = tile + gridDim.x < tiles;
       const bool btile = tile >= ps.tiles;  // a tile of the boundary set (PINN step)
       const int64_t p = (btile ? tile - ps.tiles : tile) * kTile + row;
       const bool active = p < (btile ? ps.nb : ps.n);
-      // This tile's point, loaded during the previous tile, is kept in shared memory so that
-      // no register holds it through the backward sweep.
-      xs[tid] = nx0;
-      xs[kThreads + tid] = nx1;
+      if (has_next) prefetch_point(ps, tile + gridDim.x, row, xn + tid);
 
-      // ---- forward recompute: layer 0, then the three hidden GEMMs ----
-#pragma unroll
-      for (int a = 0; a < kChunks; ++a) {
-        float h[4][4];
-#pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          const int o = 16 * a + 4 * s + t;
-          const float w0 = small[kSmW0 + 2 * o], w1 = small[kSmW0 + 2 * o + 1];
-          tanh_jet_fast(fmaf(w0, nx0, fmaf(w1, nx1, small[kSmB0 + o])), w0, w1, 0.0f, h[0][t],
-                        h[1][t], h[2][t], h[3][t]);
-        }
-        produce_chunk(chunk++, h, tmem_warp, s, cx);
-      }
+      // ---- forward recompute: the three hidden GEMMs (layer 0 is already in the ring) ----
       float d[4][16];  // d[c][4a + t]: component c of neuron 16a + 4s + t
 #pragma unroll 1
       for (int g = 0; g < 3; ++g) {
@@ -523,11 +594,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
         // GEMM g is complete: its weight slot takes the operand of GEMM g + 2.
         if (tid == 0) load_weight_slot(g & 1, wsplit, weight_block(g + 2));
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
-#pragma unroll
-          for (int a = 0; a < 4; ++a)
-            tc::ld_x4(tmem_warp + 64u * c + 16u * a + 4u * s,
-                      *reinterpret_cast<float(*)[4]>(&d[c][4 * a]));
+        for (int c = 0; c < 4; ++c) tc::ld_x16(tmem_warp + 64u * c + 16u * s, d[c]);
         tc::wait_ld();
         const float* bias = small + kSmB + 64 * g;
 #pragma unroll
@@ -607,12 +674,19 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
             if (lane == 0) part[kPBout + q] = sg;
           }
         }
-        float dwo[16];
+        // w_out gradient terms, reduced eight neurons at a time (fewer live registers)
+#pragma unroll
+        for (int half8 = 0; half8 < 2; ++half8) {
+          float dwo[8];
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+            dwo[k] = fmaf(gu, d[0][8 * half8 + k], gl * d[3][8 * half8 + k]);
+          store_part8(part, 0, q, s, half8, warp_sum8(dwo));
+        }
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           const int o = 16 * (i >> 2) + 4 * s + (i & 3);
           const float w = small[kSmWout + o];
-          dwo[i] = fmaf(gu, d[0][i], gl * d[3][i]);
           float gv = gu * w, g0 = 0.0f, g1 = 0.0f, gL = gl * w;
           adjoint_h(d[0][i], d[1][i], d[2][i], d[3][i], gv, g0, g1, gL);
           d[0][i] = gv;
@@ -620,7 +694,6 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
           d[2][i] = g1;
           d[3][i] = gL;
         }
-        store_part16(part, 0, q, s, warp_sum16(dwo));   // w_out
         store_part16(part, 6, q, s, warp_sum16(d[0]));  // b3
       }
 
@@ -737,12 +810,12 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
         ++mlayer;
         tc::fence_after_sync();
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
-#pragma unroll
-          for (int a = 0; a < 4; ++a)
-            tc::ld_x4(tmem_warp + 64u * c + 16u * a + 4u * s,
-                      *reinterpret_cast<float(*)[4]>(&d[c][4 * a]));
+        for (int c = 0; c < 4; ++c) tc::ld_x16(tmem_warp + 64u * c + 16u * s, d[c]);
         tc::wait_ld();
+        if (l == 1 && has_next) {  // GEMM 0 of the next tile may now overwrite D
+          prefetch_wait();
+          produce_layer0(xn[tid], xn[kThreads + tid], small, chunk, tmem_warp, s, cx);
+        }
         if (l > 1) {
 #pragma unroll
           for (int a = 0; a < kChunks; ++a) {
@@ -762,8 +835,6 @@ for (int c = 0; c < 4; ++c) h[c][t] = hsrc[(c * 16 + 4 * a + t) * kThreads];
       }
       if (!alive) break;
 
-      // The next tile's point: loaded now, used at the next tile's start.
-      load_point(ps, tile + gridDim.x, kTile, row, nx0, nx1);
 
       // ---- layer 0: z_v = W0 x + b0, z_J = W0, z_L = 0; d holds hbar_0 ----
       {
@@ -816,6 +887,10 @@ for (int c = 0; c < 4; ++c) h[c][t] = hsrc[(c * 16 + 4 * a + t) * kThreads];
         grad[kGBout] += ((part[kPBout] + part[kPBout + 1]) + part[kPBout + 2]) + part[kPBout + 3];
       }
       if (!(alive = barrier_ok())) break;
+      if (has_next) {  // this thread's own entries: no other thread reads them
+        xs[tid] = xn[tid];
+        xs[kThreads + tid] = xn[kThreads + tid];
+      }
     }
 
   }

@@ -268,16 +268,6 @@ __device__ __forceinline__ float tanh_r_scaled(float zp) {
 
 constexpr float kTwoOverLn2 = 2.8853900817779268f;  // 2 / ln 2 = 2 log2(e)
 
-// B row (accumulator column within a component) k = 16s + 4a + t holds output neuron
-// 16a + 4s + t, so the 16 neurons an epilogue warp of block s owns (chunks a = 0..3, four
-// neurons each) sit in 16 consecutive columns: one tcgen05.ld.x16 per component. The map is
-// its own inverse.
-__host__ __device__ constexpr int neuron_of_column(int k) {
-  return (k & 3) | (((k >> 4) & 3) << 2) | (((k >> 2) & 3) << 4);
-}
-static_assert(neuron_of_column(neuron_of_column(37)) == 37 && neuron_of_column(16) == 4,
-              "column permutation");
-
 __device__ __forceinline__ float4 ld_f4(const float* p) {
   return *reinterpret_cast<const float4*>(p);
 }

@@ -212,4 +212,15 @@ __host__ __device__ constexpr uint32_t idesc_f16(int m, int n) {
 }
 
 }  // namespace tc
+
+// The epilogues' accumulator-column order: the B operand's row (accumulator column within a
+// component) k = 16s + 4a + t holds neuron 16a + 4s + t, so the 16 neurons an epilogue warp
+// of block s owns (chunks a = 0..3, four neurons each) sit in 16 consecutive columns -- one
+// tcgen05.ld.x16 per component. The map is its own inverse.
+__host__ __device__ constexpr int neuron_of_column(int k) {
+  return (k & 3) | (((k >> 4) & 3) << 2) | (((k >> 2) & 3) << 4);
+}
+static_assert(neuron_of_column(neuron_of_column(37)) == 37 && neuron_of_column(16) == 4,
+              "column permutation");
+
 }  // namespace fhb
