@@ -21,11 +21,23 @@ Also reported in the same line:
   exchange, Adam) at 65,536 points per GPU; ``--exchange nccl`` times the composition of
   separate launches (row reduction, NCCL all-reduce, Adam) instead;
 * ``roofline`` of the forward kernel against the measured peaks in MEASURED_PEAKS.json;
-* ``cpu_baseline``: the CPU oracle port of the reference's PyTorch forward Laplacian timed
-  on this host (rank 0, N=1 only), a reported baseline.
+* ``eval_3xtf32``: the same evaluation with forward version 4 (3xTF32, the operand format
+  the north star names); ``eval_biharmonic``: (u, lap, bilap) of the same points by the
+  biharmonic kernel;
+* ``config3``: BASELINE config 3, the evaluation of 1M, 4M and 16M global points split
+  evenly over the ranks (strong scaling), per size;
+* ``config4``: BASELINE config 4, the training step at 16,777,216 global points (2,097,152 per
+  GPU at N=8), graph replay, 100 timed steps by default, with the gradient kernel alone timed
+  beside it (the difference is the exchange + Adam), a bitwise all-gather check that every
+  rank holds the same parameters and Adam moments, and a 3-step comparison of the in-kernel
+  peer exchange with the NCCL all-reduce composition;
+* ``cpu_baseline``: the CPU oracle port of the reference's PyTorch paths timed on this host
+  (rank 0, N=1 only), a reported baseline: the forward-Laplacian evaluation (``value``), the
+  nested-autograd evaluation, both CPU training steps, and both evaluations at 1,024 points.
 
-``--impl reference`` times only that CPU port (the reference's own algorithm; the reference
-package itself does not exist on the GPU box) on the same metric and prints its line.
+``--impl reference`` times only the CPU port of the forward-Laplacian evaluation (the
+reference's own algorithm; the reference package itself does not exist on the GPU box) on
+the same metric and prints its line.
 """
 
 from __future__ import annotations
@@ -63,7 +75,8 @@ WORKLOAD = "config1: residual eval (u, lap) of the 2->64->64->64->64->1 tanh MLP
 PUBLISHED_PTS_S = 121.9e6
 PUBLISHED_NOTE = ("value / 121.9 M pts/s, the reference's published fused fwd v2 at 65,536 "
                   "points on an RTX A5000 (its only published hardware)")
-F16_TRAFFIC = 643_328  # DRAM bytes of one version-3 launch at 65,536 points (ncu)
+F16_TRAFFIC = 643_072  # DRAM bytes of one version-3 launch at 65,536 points (ncu)
+TF32_TRAFFIC = 641_536  # the same for version 4 (3xTF32)
 FLUSH_BYTES = 192 << 20
 PEAKS_FILE = ROOT / "MEASURED_PEAKS.json"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
@@ -467,11 +480,11 @@ def run_ours(args) -> None:
         return
 
     # DRAM read + write bytes of one forward launch at 65,536 points, from one ncu capture of
-    # the same command per kernel family (0-2: FP32 kernel, 3: 3xFP16, 4-5: 3xTF32; the
-    # 3xTF32 figure predates the bulk-copied parameter staging, which reads the same bytes).
+    # the same command per kernel family (0-2: FP32 kernel, 3: 3xFP16, 4-5: 3xTF32).
     traffic = None
     if n == POINTS_PER_GPU and act == "tanh":
-        traffic = {0: 611_840, 1: 611_840, 2: 611_840, 3: F16_TRAFFIC, 4: 646_400, 5: 646_400}[version]
+        traffic = {0: 611_840, 1: 611_840, 2: 611_840, 3: F16_TRAFFIC, 4: TF32_TRAFFIC,
+                   5: TF32_TRAFFIC}[version]
     per_launch_s = ms_per_step / 1e3
     achieved_tflops = n * FLOP_FORWARD / per_launch_s / 1e12
     fp32_peak = SM_COUNT * 128 * 2 * peaks.get("sm_max_mhz", 1965.0) * 1e6 / 1e12
