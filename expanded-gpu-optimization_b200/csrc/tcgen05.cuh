@@ -154,11 +154,14 @@ __device__ __forceinline__ void wait_st() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
 
-// Round to TF32 (nearest, ties away): the 32-bit pattern with the low 13 mantissa bits zero.
+// Round to TF32 (nearest, ties away from zero): the 32-bit pattern with the low 13 mantissa
+// bits zero. Done on the bit pattern -- add half a TF32 ulp (bit 12; a carry moves into the
+// exponent, as rounding up to the next binade requires), then clear bits 0..12 -- in two
+// integer instructions; the same result as cvt.rna.tf32.f32 for every finite input and for
+// infinities (tests/test_scale_math.py checks the rounding on the CPU). The kernels never
+// split a NaN.
 __device__ __forceinline__ uint32_t to_tf32(float x) {
-  uint32_t r;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-  return r;
+  return (__float_as_uint(x) + 0x1000u) & 0xFFFFE000u;
 }
 
 // 3xTF32 split: hi = x rounded to TF32; lo = x - hi (exact in FP32), fed as is: the tensor

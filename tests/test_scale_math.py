@@ -60,3 +60,47 @@ def test_scales_are_powers_of_two_in_range() -> None:
     bits = got.view(np.uint32)
     assert np.all((bits & 0x7FFFFF) == 0)  # no mantissa bits: exact powers of 2
     assert np.all(got >= np.float32(2.0**-126)) and np.all(got <= np.float32(2.0**127))
+
+
+def _tf32_bits(x: np.ndarray) -> np.ndarray:
+    """The kernels' TF32 rounding (tcgen05.cuh: to_tf32) on the float32 bit pattern."""
+    b = x.astype(np.float32).view(np.uint32)
+    return ((b.astype(np.uint64) + 0x1000) & 0xFFFFE000).astype(np.uint32)
+
+
+def _tf32_nearest_ties_away(x: np.ndarray) -> np.ndarray:
+    """Round float32 values to 10 explicit mantissa bits, nearest with ties away from zero,
+    in float64 arithmetic (exact for these magnitudes): the definition of cvt.rna.tf32."""
+    x = x.astype(np.float64)
+    out = np.zeros_like(x)
+    nz = (x != 0) & np.isfinite(x)
+    a = np.abs(x[nz])
+    e = np.floor(np.log2(a))
+    e = np.where(2.0**e > a, e - 1, e)           # guard log2 rounding at powers of two
+    e = np.where(2.0 ** (e + 1) <= a, e + 1, e)
+    ulp = 2.0 ** (np.maximum(e, -126) - 10)     # subnormals keep the 2^-136 step
+    out[nz] = np.sign(x[nz]) * np.floor(a / ulp + 0.5) * ulp
+    keep = ~np.isfinite(x) | (x == 0)  # infinities, and zeros with their sign
+    out[keep] = x[keep]
+    return out.astype(np.float32).view(np.uint32)
+
+
+def test_tf32_bit_rounding_is_nearest_ties_away() -> None:
+    rng = np.random.default_rng(3)
+    bits = rng.integers(0, 2**32, size=400_000, dtype=np.uint64).astype(np.uint32)
+    x = bits.view(np.float32)
+    x = x[np.isfinite(x)]
+    # exact ties and their neighbours, around 1 and in the subnormal range
+    base = np.array([1.0, 1.5, -3.25, 1e-40, -7e-39, 65504.0, 3.0e38], np.float32)
+    tie = (base.view(np.uint32) | 0x1000).view(np.float32)
+    extra = np.concatenate([base, tie, np.nextafter(tie, np.float32(0)),
+                            np.nextafter(tie, np.float32(np.inf)),
+                            np.array([np.inf, -np.inf, 0.0, -0.0], np.float32)])
+    for v in (x, extra):
+        got = _tf32_bits(v)
+        want = _tf32_nearest_ties_away(v)
+        finite = np.isfinite(v)
+        np.testing.assert_array_equal(got[finite], want[finite])
+    # infinities stay infinite; the largest finite values round up to infinity
+    assert _tf32_bits(np.array([np.inf], np.float32))[0] == 0x7F800000
+    assert _tf32_bits(np.array([np.float32(3.4028235e38)]))[0] == 0x7F800000
