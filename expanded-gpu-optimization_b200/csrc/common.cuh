@@ -74,6 +74,24 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t phase) {
   return done != 0;
 }
 
+// try_wait with a suspend-time hint: the thread may stay suspended until the phase
+// completes or about hint_ns nanoseconds pass, instead of the shorter system-dependent
+// limit of the plain form, so a warp that has to wait re-polls -- and issues the loop's
+// instructions -- rarely. Completion still wakes it at once.
+constexpr uint32_t kSuspendHintNs = 20000;
+__device__ __forceinline__ bool mbar_try_wait_for(uint64_t* bar, uint32_t phase,
+                                                  uint32_t hint_ns) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(phase), "r"(hint_ns)
+      : "memory");
+  return done != 0;
+}
+
 // Wait for `phase` of `bar` to complete, giving up after kWaitLimitNs. Returns false on
 // timeout (and records `bits` in *status).
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t phase,
@@ -81,7 +99,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t phase,
   if (mbar_try_wait(bar, phase)) return true;
   const uint64_t start = global_timer_ns();
   while (true) {
-    if (mbar_try_wait(bar, phase)) return true;
+    if (mbar_try_wait_for(bar, phase, kSuspendHintNs)) return true;
     if (global_timer_ns() - start > kWaitLimitNs) {
       report_status(status, bits);
       return false;

@@ -189,7 +189,7 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, co
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t start = global_timer_ns();
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_for(bar, parity, kSuspendHintNs)) return true;
     if (*cx.abort_flag) return false;
     if (global_timer_ns() - start > kWaitLimitNs) {
       *cx.abort_flag = 1u;
