@@ -89,10 +89,14 @@ constexpr int kWeightSlots = 2;
 constexpr int kScratchFloats = 2 * 4 * 16 * kThreads;
 
 // Weight-gradient staging buffer (one per point half): A = [zbar_hi; zbar_lo] and
-// B = [h_hi; h_lo] (128 rows x 64 points each), 128-byte-swizzled K-major: a K atom is 32
-// points, rows in 8-row groups of 1024 bytes, the lo rows 8192 bytes after the hi rows.
-constexpr int kStageA = 0, kStageB = 32768;
-constexpr int kStageBytes = 65536;
+// B = [h_hi; h_lo] as f16, 128 rows x 64 points each, MN-major without swizzle: element
+// (row r, point k) at byte (r % 8) * 2 + (k % 8) * 16 + (r / 8) * kDwSbo + (k / 8) * kDwLbo,
+// so the 8 rows of a 16-byte group are one thread's 8 neurons of one point. Rows 0..63 are
+// the hi parts and 64..127 the lo parts of the neurons in accumulator-column order
+// (neuron_of_column): row 16s + i is neuron slot i of the warps of block s.
+constexpr uint32_t kDwLbo = 128, kDwSbo = 1024;
+constexpr int kStageA = 0, kStageB = 16384;
+constexpr int kStageBytes = 32768;
 constexpr int kFlushStride = 65;                 // [128 rows][65] floats when emptying TMEM
 
 // Shared memory (bytes).
@@ -112,14 +116,19 @@ constexpr int kPLoss = kPartKinds * 256, kPBout = kPLoss + 4;
 constexpr int kPartFloats = kPBout + 4;
 constexpr int kXsOff = kPartOff + kPartFloats * 4;            // the tile's points x[512], y[512]
 constexpr int kXnOff = kXsOff + 2 * kThreads * 4;             // the next tile's, same layout
-constexpr int kBarOff = kXnOff + 2 * kThreads * 4;            // mbarriers
+// weight-gradient scales: per epilogue warp its copy of the h scales sigma[3][4] and their
+// inverses (h_0, h_1, h_2; v, d/dx, d/dy, L), then the per-warp maxima of the scaled zbar
+constexpr int kDwScaleOff = kXnOff + 2 * kThreads * 4;
+constexpr int kSigFloats = 24;
+constexpr int kZmaxOff = kDwScaleOff + kWarps * kSigFloats * 4;
+constexpr int kBarOff = kZmaxOff + kWarps * 4;                // mbarriers
 constexpr int kNumBars = 10;   // empty[2] dfull red wfull[2] dwdone[2] full[2]
 constexpr int kMiscOff = kBarOff + kNumBars * 8;              // TMEM base, abort flag, status
 constexpr int kSmemBytes = kMiscOff + 16;
 static_assert(kSmemBytes <= 227 * 1024, "shared memory layout overflow");
 static_assert(kStageOff % 1024 == 0 && kBarOff % 8 == 0 && (kMiscOff + 8) % 8 == 0,
               "alignment");
-static_assert(kTile * kFlushStride * 4 <= kStageBytes, "flush buffer fits a staging buffer");
+static_assert(kTile * kFlushStride * 4 <= 2 * kStageBytes, "flush buffer fits the staging buffers");
 
 // Shared-memory objects are addressed as constant offsets of the dynamic shared-memory base
 // (no pointers kept in registers across the tile loop).
@@ -331,21 +340,45 @@ __device__ __forceinline__ void adjoint_h(float a, float hj0, float hj1, float h
   g1 = z1;
 }
 
-// The 8 weight-gradient MMAs of one jet component for one point half (M = 128, N = 128,
-// K = 8 points each) into that half's accumulator. Issued by one converged warp of the
-// half, then committed to the half's barrier.
+// The 4 weight-gradient MMAs of one jet component for one point half (M = 128, N = 128,
+// K = 16 points each, f16, both operands MN-major) into that half's accumulator. Issued by
+// one converged warp of the half, then committed to the half's barrier.
 __device__ __forceinline__ void issue_dw_mmas(const Ctx& cx, int half, bool first) {
-  constexpr uint32_t kIdescDw = tc::idesc_tf32(128, 128);
+  constexpr uint32_t kIdescDw =
+      tc::idesc_f16(128, 128) | tc::kIdescAMnMajor | tc::kIdescBMnMajor;
   const uint32_t base = smem_u32(dsmem() + kStageOff + half * kStageBytes);
   const uint32_t d = cx.tmem + kDwCol + 128u * static_cast<uint32_t>(half);
 #pragma unroll
-  for (int ks = 0; ks < 8; ++ks) {
-    const uint32_t ka = static_cast<uint32_t>(ks >> 2), ko = static_cast<uint32_t>(ks & 3) * 32u;
-    const uint64_t a = tc::smem_desc_kmajor_sw128(base + kStageA + ka * 16384u + ko, 1024);
-    const uint64_t bb = tc::smem_desc_kmajor_sw128(base + kStageB + ka * 16384u + ko, 1024);
-    tc::mma_tf32_ss_warp(d, a, bb, kIdescDw, (first && ks == 0) ? 0u : 1u);
+  for (int ks = 0; ks < 4; ++ks) {  // points 16 ks .. 16 ks + 15: two 8-point K groups
+    const uint32_t k0 = static_cast<uint32_t>(ks) * 2u * kDwLbo;
+    const uint64_t a = tc::smem_desc_kmajor(base + kStageA + k0, kDwLbo, kDwSbo);
+    const uint64_t bb = tc::smem_desc_kmajor(base + kStageB + k0, kDwLbo, kDwSbo);
+    tc::mma_f16_ss_warp(d, a, bb, kIdescDw, (first && ks == 0) ? 0u : 1u);
   }
   tc::commit_warp(bar_dwdone(half));
+}
+
+// 16-byte shared-memory store.
+__device__ __forceinline__ void st_shared_v4(uint8_t* p, uint32_t a, uint32_t b, uint32_t c,
+                                             uint32_t d) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(smem_u32(p)), "r"(a), "r"(b),
+               "r"(c), "r"(d)
+               : "memory");
+}
+
+// Stages one operand's 16 values of this thread (neuron slots i = 0..15, times `scale`) as f16
+// hi/lo pairs: slots 8g..8g+7 are one 16-byte group, hi at row group 2s + g, lo 8 groups on.
+__device__ __forceinline__ void stage_f16_rows(uint8_t* at, int s, const float (&v)[16],
+                                               float scale) {
+  uint32_t hi[8], lo[8];
+#pragma unroll
+  for (int p = 0; p < 8; ++p) split_f16_pair_fast(v[2 * p] * scale, v[2 * p + 1] * scale, hi[p], lo[p]);
+#pragma unroll
+  for (int g = 0; g < 2; ++g) {
+    st_shared_v4(at + (2 * s + g) * kDwSbo, hi[4 * g], hi[4 * g + 1], hi[4 * g + 2], hi[4 * g + 3]);
+    st_shared_v4(at + (8 + 2 * s + g) * kDwSbo, lo[4 * g], lo[4 * g + 1], lo[4 * g + 2],
+                 lo[4 * g + 3]);
+  }
 }
 
 // Barrier over the 8 warps (256 threads) of one point half; ids 1 and 2 (0 is __syncthreads,
@@ -371,6 +404,12 @@ __device__ __forceinline__ void mma_warp(const Ctx& cx, int64_t tiles) {
       }
     }
   }
+}
+
+__device__ __forceinline__ float warp_max_f(float v) {
+#pragma unroll
+  for (int m = 16; m >= 1; m >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, m));
+  return v;
 }
 
 // Sums v[i] over the 32 lanes of the warp for every i < 16 with a fixed butterfly that
@@ -529,6 +568,23 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
     tc::tmem_alloc(tmem_base_slot, kTmemCols);
     tc::tmem_relinquish();
   }
+  if (warp < kWarps) {
+    // Absolute row sums of W1 and W2 (rows warp + 16 i), fixed-order warp sums: the norms
+    // that bound the activations h_1, h_2 for the weight gradient's f16 operand scales.
+    float rs[8][2];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int r = warp + kWarps * i;
+      const float* wr = params + kHiddenBase + (r >> 6) * kHiddenStride + (r & 63) * kWidth;
+      rs[i][0] = wr[lane];
+      rs[i][1] = wr[lane + 32];
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float sum = warp_sum(fabsf(rs[i][0]) + fabsf(rs[i][1]));
+      if (lane == 0) red[warp + kWarps * i] = sum;
+    }
+  }
   tc::fence_before_sync();
   __syncthreads();
   tc::fence_after_sync();
@@ -548,19 +604,42 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
     const uint32_t tmem_warp = cx.tmem + (static_cast<uint32_t>(32 * q) << 16);
     const int row = 32 * q + lane;
     float* const hscratch = scratch + static_cast<int64_t>(blockIdx.x) * kScratchFloats + tid;
-    // Weight-gradient staging: this thread's point is K index `lane` of K atom q & 1 of
-    // staging buffer q >> 1; neuron row 16a + 4s + t sits at byte a * 2048 + soff[t] of an
-    // operand (plus 8192 for the zbar_lo rows 64.. of A).
-    uint8_t* const stage = smem + kStageOff + (q >> 1) * kStageBytes;
-    uint32_t soff[4];
-#pragma unroll
-    for (int t = 0; t < 4; ++t) {
-      const int r7 = 4 * (s & 1) + t;
-      soff[t] = static_cast<uint32_t>((s >> 1) * 1024 + r7 * 128 + (((lane >> 2) ^ r7) << 4) +
-                                      4 * (lane & 3));
-    }
-    const uint32_t ka = static_cast<uint32_t>(q & 1);
+    // Weight-gradient staging: this thread's point is K index kpt = 32 (q & 1) + lane of the
+    // staging buffer of its point half q >> 1.
     const int half = q >> 1;
+    const int kpt = 32 * (q & 1) + lane;
+    uint8_t* const stage_at =
+        smem + kStageOff + half * kStageBytes + (kpt % 8) * 16 + (kpt / 8) * kDwLbo;
+    float* const zmax = reinterpret_cast<float*>(smem + kZmaxOff);
+    float* const sigw = reinterpret_cast<float*>(smem + kDwScaleOff) + warp * kSigFloats;
+    {
+      // The f16 scales of the weight gradient's h operands, this warp's own copy: the bounds
+      // of the 3xFP16 forward (|v| <= 1; |d/dx|, |d/dy| <= B_J grow by the norm N_l of W_l,
+      // |L| <= B_L becomes N_l B_L + 2 (N_l B_J)^2), each mapped to <= 2^14 by a power of 2.
+      const float n1 = warp_max_f(fmaxf(red[lane], red[lane + 32]));
+      const float n2 = warp_max_f(fmaxf(red[64 + lane], red[96 + lane]));
+      const float w0x = small[kSmW0 + 2 * lane], w0y = small[kSmW0 + 2 * lane + 1];
+      const float w1x = small[kSmW0 + 2 * (lane + 32)], w1y = small[kSmW0 + 2 * (lane + 32) + 1];
+      float bj = warp_max_f(fmaxf(fmaxf(fabsf(w0x), fabsf(w1x)), fmaxf(fabsf(w0y), fabsf(w1y))));
+      float bl = warp_max_f(fmaxf(fmaf(w0x, w0x, w0y * w0y), fmaf(w1x, w1x, w1y * w1y)));
+      if (lane == 0) {
+        const float nrm[2] = {n1, n2};
+        for (int l = 0; l < 3; ++l) {  // h_l
+          const float sig[4] = {16384.0f, pow2_floor_ratio(14, bj), pow2_floor_ratio(14, bj),
+                                pow2_floor_ratio(14, bl)};
+          for (int c = 0; c < 4; ++c) {
+            sigw[4 * l + c] = sig[c];
+            sigw[12 + 4 * l + c] = 1.0f / sig[c];  // exact: a power of 2
+          }
+          if (l < 2) {
+            const float nj = nrm[l] * bj;
+            bl = fmaf(nrm[l], bl, 2.0f * nj * nj);
+            bj = nj;
+          }
+        }
+      }
+      __syncwarp();
+    }
 
     uint32_t chunk = 0, mlayer = 0, tile_count = 0, dw_issued = 0;
     bool alive = true;
@@ -701,6 +780,23 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
 #pragma unroll 1
       for (int l = 3; l >= 1; --l) {
         const int g = 6 - l;
+        // The f16 scale of zbar_l for this tile and point half: z~_c = zbar_c S / sigma_c pairs
+        // with h~_c = h_c sigma_c, so every component's product carries the same factor S,
+        // chosen so that max |z~| <= 2^14. This warp's maximum of |zbar_c| / sigma_c first.
+        const float* sg = sigw + 4 * (l - 1);         // sigma of h_{l-1}: v, d/dx, d/dy, L
+        const float* isg = sigw + 12 + 4 * (l - 1);  // 1 / sigma
+        {
+          float zm = 0.0f;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            float mc = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) mc = fmaxf(mc, fabsf(d[c][i]));
+            zm = fmaxf(zm, mc * isg[c]);
+          }
+          const uint32_t wm = __reduce_max_sync(0xffffffffu, __float_as_uint(zm));
+          if (lane == 0) zmax[warp] = __uint_as_float(wm);
+        }
         // zbar_l -> ring (input-adjoint GEMM g)
 #pragma unroll
         for (int a = 0; a < kChunks; ++a) {
@@ -712,9 +808,19 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
           produce_chunk(chunk++, z, tmem_warp, s, cx);
         }
 
-        // weight gradient dW_l: per jet component, stage zbar_l and h_{l-1} (hi/lo) for the
-        // tile's 128 points and let one warp issue the MMAs. Unrolled, so that the registers
-        // of component c of zbar_l are free once its round is staged.
+        // The half's scale from its 8 warps' maxima (written before the chunks above).
+        half_barrier(half);
+        float zs;
+        {
+          float hm = 0.0f;
+#pragma unroll
+          for (int w4 = 0; w4 < 4; ++w4)
+            hm = fmaxf(hm, fmaxf(zmax[2 * half + 4 * w4], zmax[2 * half + 1 + 4 * w4]));
+          zs = pow2_floor_ratio(14, hm);
+        }
+        // weight gradient dW_l: per jet component, stage zbar_l and h_{l-1} (f16 hi/lo, scaled)
+        // for the tile's 128 points and let one warp issue the MMAs. Unrolled, so that the
+        // registers of component c of zbar_l are free once its round is staged.
         const float* hsrc = hscratch + (l == 3 ? 4 * 16 * kThreads : 0);  // h_{l-1} (l >= 2)
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
@@ -735,19 +841,8 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
             }
           }
           if (c > 0) warp_wait(bar_dwdone(half), (dw_issued - 1u) & 1u);  // buffer free again
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int a = i >> 2, t = i & 3;
-            const float z = c == 0 ? d[0][i] : c == 1 ? d[1][i] : c == 2 ? d[2][i] : d[3][i];
-            uint32_t zh, zl, hh, hl;
-            tc::split_tf32(z, zh, zl);
-            tc::split_tf32(hv[i], hh, hl);
-            const uint32_t o = a * 2048 + soff[t];
-            *reinterpret_cast<uint32_t*>(stage + kStageA + ka * 16384u + o) = zh;
-            *reinterpret_cast<uint32_t*>(stage + kStageA + ka * 16384u + 8192u + o) = zl;
-            *reinterpret_cast<uint32_t*>(stage + kStageB + ka * 16384u + o) = hh;
-            *reinterpret_cast<uint32_t*>(stage + kStageB + ka * 16384u + 8192u + o) = hl;
-          }
+          stage_f16_rows(stage_at + kStageA, s, d[c], zs * isg[c]);
+          stage_f16_rows(stage_at + kStageB, s, hv, sg[c]);
           tc::fence_proxy_async_smem();
           half_barrier(half);
           if (s == 0 && (q & 1) == 0) {  // warp 2 * half issues for its half
@@ -776,30 +871,42 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
         tc::fence_after_sync();
         {
           float* fb = reinterpret_cast<float*>(smem + kStageOff);
-          // columns i (h_hi) and 64 + i (h_lo) of this warp's row, in both halves' accumulators
+          // columns i (h_hi) and 64 + i (h_lo) of this warp's row, in both halves' accumulators,
+          // each half divided by its scale (exact powers of 2)
+          float inv[2];
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {
+            float hm = 0.0f;
+#pragma unroll
+            for (int w4 = 0; w4 < 4; ++w4)
+              hm = fmaxf(hm, fmaxf(zmax[2 * hh + 4 * w4], zmax[2 * hh + 1 + 4 * w4]));
+            inv[hh] = 1.0f / pow2_floor_ratio(14, hm);
+          }
           float v[16], w[16];
           tc::ld_x16(tmem_warp + kDwCol + 16u * s, v);
           tc::ld_x16(tmem_warp + kDwCol + 64u + 16u * s, w);
           tc::wait_ld();
 #pragma unroll
-          for (int k = 0; k < 16; ++k) v[k] += w[k];
+          for (int k = 0; k < 16; ++k) v[k] = (v[k] + w[k]) * inv[0];
           tc::ld_x16(tmem_warp + kDwCol + 128u + 16u * s, w);
           tc::wait_ld();
 #pragma unroll
-          for (int k = 0; k < 16; ++k) v[k] += w[k];
+          for (int k = 0; k < 16; ++k) v[k] = fmaf(w[k], inv[1], v[k]);
           tc::ld_x16(tmem_warp + kDwCol + 192u + 16u * s, w);
           tc::wait_ld();
 #pragma unroll
-          for (int k = 0; k < 16; ++k) v[k] += w[k];
+          for (int k = 0; k < 16; ++k) v[k] = fmaf(w[k], inv[1], v[k]);
 #pragma unroll
           for (int k = 0; k < 16; ++k) fb[row * kFlushStride + 16 * s + k] = v[k];
           tc::fence_before_sync();
           if (!(alive = barrier_ok())) break;
           float* wrow = rowp + kHiddenBase + (l - 1) * kHiddenStride;
+          // accumulator row r / column n hold neuron neuron_of_column(r % 64) / (n % 64)
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
-            const int e = tid + kThreads * j, o = e >> 6, i = e & 63;
-            red_add(wrow + e, fb[o * kFlushStride + i] + fb[(64 + o) * kFlushStride + i]);
+            const int e = tid + kThreads * j;
+            const int ro = neuron_of_column(e >> 6), ci = neuron_of_column(e & 63);
+            red_add(wrow + e, fb[ro * kFlushStride + ci] + fb[(64 + ro) * kFlushStride + ci]);
           }
           if (!(alive = barrier_ok())) break;
         }

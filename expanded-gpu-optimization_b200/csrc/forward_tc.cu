@@ -212,19 +212,6 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
-// The largest power of 2 <= 2^c / y, y = max(x, 1e-30), clamped to [2^-126, 2^127], from the
-// exponent and mantissa bits alone: for y = m 2^e (m in [1, 2)) the quotient is 2^(c-e) when
-// m = 1 and lies in (2^(c-e-1), 2^(c-e)) otherwise (a correctly rounded division never reaches
-// 2^(c-e) then, so this equals flooring the divided value; an infinite y divides to 0 and
-// clamps to 2^-126). tests/test_scale_math.py checks the equality over the float32 range.
-__device__ __forceinline__ float pow2_floor_ratio(int c, float x) {
-  const uint32_t b = __float_as_uint(fmaxf(x, 1e-30f));
-  int k = c - (static_cast<int>(b >> 23) - 127) - ((b & 0x7FFFFFu) != 0u ? 1 : 0);
-  if (b >= 0x7F800000u) k = -126;  // an overflowed (infinite) bound: the quotient is 0
-  k = min(max(k, -126), 127);
-  return __uint_as_float(static_cast<uint32_t>(k + 127) << 23);
-}
-
 // f16 pairs of a split: hi = x rounded to 11 significant bits (tf32 rounding; exact in f16
 // inside the scaled range), lo = x - hi (exact in FP32, rounded to f16); element a (even K)
 // in the low halves. Values below f16's normal range (2^-14, 2^28 below a scaled bound) lose
@@ -235,24 +222,6 @@ __device__ __forceinline__ void split_f16_pair(float a, float b, uint32_t& hi, u
   const __half2 l = __floats2half2_rn(a - ha, b - hb);
   hi = *reinterpret_cast<const uint32_t*>(&h);
   lo = *reinterpret_cast<const uint32_t*>(&l);
-}
-
-// The epilogue's f16 pairs: hi = x rounded to f16 (11 significant bits), lo = x - hi
-// rounded to f16, element a (even K) in the low halves. x - hi is exact in FP32 and comes
-// from one mixed-precision fma (f16 hi times -1 plus the FP32 x), so a pair costs four
-// instructions: two packs and two fmas. Inside the scaled range (|x| <= 2^14) hi is a normal
-// f16; values below 2^-14 lose precision, at most 2^-25 absolute in scaled units.
-__device__ __forceinline__ void split_f16_pair_fast(float a, float b, uint32_t& hi,
-                                                    uint32_t& lo) {
-  asm("{\n\t.reg .b16 h0, h1, m;\n\t.reg .f32 la, lb;\n\t"
-      "cvt.rn.f16x2.f32 %0, %3, %2;\n\t"
-      "mov.b32 {h0, h1}, %0;\n\t"
-      "mov.b16 m, 0xBC00;\n\t"
-      "fma.rn.f32.f16 la, h0, m, %2;\n\t"
-      "fma.rn.f32.f16 lb, h1, m, %3;\n\t"
-      "cvt.rn.f16x2.f32 %1, lb, la;\n\t}"
-      : "=r"(hi), "=r"(lo)
-      : "f"(a), "f"(b));
 }
 
 // r = 1 / (2^zp + 1) on the special-function unit (ex2.approx, rcp.approx), zp = 2 z / ln 2

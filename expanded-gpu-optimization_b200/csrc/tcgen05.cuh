@@ -96,6 +96,18 @@ __device__ __forceinline__ void mma_tf32_ss_warp(uint32_t d_tmem, uint64_t a_des
       "r"(0u), "r"(0u)
       : "memory");
 }
+// D[tmem] (+)= A[smem] * B[smem]^T, kind::f16 (both f16, D f32), issued by a converged warp;
+// the operand majors (K or MN) are in the instruction descriptor.
+__device__ __forceinline__ void mma_f16_ss_warp(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                                uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "elect.sync _|e, 0xffffffff;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+      ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 // tcgen05.commit from one elected lane of a converged warp.
 __device__ __forceinline__ void commit_warp(uint64_t* bar) {
   asm volatile(
@@ -203,6 +215,9 @@ __host__ __device__ constexpr uint32_t idesc_tf32(int m, int n) {
          | (static_cast<uint32_t>(n >> 3) << 17)    // N / 8
          | (static_cast<uint32_t>(m >> 4) << 24);   // M / 16
 }
+
+// Instruction-descriptor bits selecting MN-major A (bit 15) and B (bit 16) operands.
+constexpr uint32_t kIdescAMnMajor = 1u << 15, kIdescBMnMajor = 1u << 16;
 
 // Instruction descriptor for kind::f16 with f16 A and B (format 0), D f32, both K-major.
 __host__ __device__ constexpr uint32_t idesc_f16(int m, int n) {
