@@ -363,6 +363,23 @@ def test_backward_is_bitwise_reproducible(kernel: int) -> None:
     assert torch.equal(a[0], b[0]) and torch.equal(a[1], b[1])
 
 
+@pytest.mark.parametrize("kernel", BACKWARD_KERNELS)
+@pytest.mark.parametrize("k", [-60, -30, 30, 60])
+def test_backward_scales_exactly_with_power_of_two_upstream_gradients(kernel: int, k: int) -> None:
+    """The backward is linear in (grad_u, grad_lap), and every operand scale the kernels
+    choose (the f16 weight-gradient scales, the tf32 splits) is a power of 2 that follows the
+    data: multiplying the upstream gradients by 2^k multiplies every gradient by exactly
+    2^k, bit for bit, far outside the default magnitudes."""
+    params = _params()
+    coords = uniform_points(20_000, seed=15).cuda()
+    gu, gl = (t.cuda() for t in _upstream(20_000, seed=6))
+    f = 2.0**k
+    p1, x1 = fused_forward_laplacian_backward(coords, params, gu, gl, kernel)
+    p2, x2 = fused_forward_laplacian_backward(coords, params, gu * f, gl * f, kernel)
+    assert torch.equal(p2, p1 * f)
+    assert torch.equal(x2, x1 * f)
+
+
 @pytest.mark.parametrize("batch", [129, 65_536, 300_000])
 def test_backward_kernels_agree(batch: int) -> None:
     """The tensor-core and FP32 kernels agree far inside the oracle tolerance; 300,000
