@@ -243,6 +243,11 @@ def cpu_baseline(points: int, budget_s: float, steps: int | None = None) -> dict
 
 
 def run_reference(args) -> None:
+    """The reference's CPU residual evaluation on all host threads: both of its CPU paths for
+    (u, Laplacian u) -- the PyTorch forward-Laplacian jet (backends/forward_laplacian.py) and
+    nested eager autograd (autodiff.py) -- each timed over the same bounded sample; the line's
+    value is the faster of the two, so the ratio against this arm is against the reference's
+    best CPU path on this host."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
@@ -252,36 +257,48 @@ def run_reference(args) -> None:
     points = args.points
     params = jet.init_parameters(0)
     coords_full = jet.uniform_points(points)
-    jet.forward_laplacian(params, coords_full)
-    t0 = time.perf_counter()
-    jet.forward_laplacian(params, coords_full)
-    one = time.perf_counter() - t0
-    budget = 120.0
-    sample = points if args.steps * one <= budget else max(1024, int(points * budget / (args.steps * one)))
-    coords = coords_full[:sample].contiguous()
-    for _ in range(args.warmup):
-        jet.forward_laplacian(params, coords)
-    times = []
-    for _ in range(args.steps):
-        t = time.perf_counter()
-        jet.forward_laplacian(params, coords)
-        times.append(time.perf_counter() - t)
-    total = sum(times)
-    value = sample * args.steps / total
+    paths = {"forward_laplacian": jet.forward_laplacian, "eager_autograd": jet.eager_laplacian}
+    budget = 60.0  # seconds of timed work per path
+    legs = {}
+    for name, fn in paths.items():
+        probe = coords_full[: min(points, 65536)].contiguous()
+        fn(params, probe)
+        t0 = time.perf_counter()
+        fn(params, probe)
+        per_point = (time.perf_counter() - t0) / probe.shape[0]
+        sample = points if args.steps * points * per_point <= budget else max(
+            1024, int(budget / (args.steps * per_point)))
+        coords = coords_full[:sample].contiguous()
+        for _ in range(args.warmup):
+            fn(params, coords)
+        total = 0.0
+        for _ in range(args.steps):
+            t = time.perf_counter()
+            fn(params, coords)
+            total += time.perf_counter() - t
+        legs[name] = {"value": sample * args.steps / total, "points_per_step": sample,
+                      "ms_per_step": total / args.steps * 1e3}
+    best = max(legs, key=lambda k: legs[k]["value"])
+    value = legs[best]["value"]
+    sample = legs[best]["points_per_step"]
     cores = os.cpu_count() or 1
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": total / args.steps * 1e3,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": legs[best]["ms_per_step"],
         "higher_is_better": True, "scaling": "weak", "vs_baseline": value / PUBLISHED_PTS_S,
         "vs_baseline_note": PUBLISHED_NOTE, "dtype": "f32",
         "data": "synthetic (uniform points in [-1,1]^2, CPU generator seed 1; seed-0 nn.Linear init)",
         "config": {"workload": WORKLOAD, "points_per_gpu": points, "global_points": points,
                    "points_per_step": sample, "parallelism": "rank 0 only (CPU)"},
         "impl": "reference",
+        "paths": legs,
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
                          "sample": f"{sample:,} points per step of the {points:,}-point "
-                                   f"workload; PyTorch forward Laplacian (oracle port of "
-                                   f"src/fused_hoad/backends/forward_laplacian.py) on {cores} threads"},
+                                   f"workload; the faster ({best}) of the reference's two CPU "
+                                   f"paths, PyTorch forward Laplacian (oracle port of "
+                                   f"src/fused_hoad/backends/forward_laplacian.py) and nested "
+                                   f"eager autograd (src/fused_hoad/autodiff.py), on {cores} "
+                                   f"threads"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)

@@ -50,6 +50,11 @@ def test_reference_arm_prints_one_contract_line() -> None:
     e2e = line["e2e"]
     assert e2e["value"] == line["value"] and e2e["unit"] == bench.UNIT
     assert e2e["h2d_bytes_per_step"] == 0 and e2e["d2h_bytes_per_step"] == 0
+    # both of the reference's CPU evaluation paths are timed; the line reports the faster
+    paths = line["paths"]
+    assert set(paths) == {"forward_laplacian", "eager_autograd"}
+    assert line["value"] == max(leg["value"] for leg in paths.values())
+    assert all(leg["points_per_step"] >= 1024 for leg in paths.values())
 
 
 def test_warmup_below_three_is_rejected() -> None:
