@@ -528,6 +528,9 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
   float* const rowp = partials + static_cast<int64_t>(blockIdx.x) * kRowStride;
 
   // ---- set-up ----
+  // The first tile's point, requested first: its latency overlaps the set-up below.
+  float x0 = 0.0f, x1 = 0.0f;
+  if (warp < kWarps) load_point(ps, blockIdx.x, kTile, 32 * (warp & 3) + lane, x0, x1);
   for (int i = tid; i < kGradFloats; i += kThreads) grad[i] = 0.0f;
   for (int i = tid; i < kSmallFloats; i += kThreads) {
     float v = 0.0f;
@@ -579,11 +582,11 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
       rs[i][0] = wr[lane];
       rs[i][1] = wr[lane + 32];
     }
+    float v[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float sum = warp_sum(fabsf(rs[i][0]) + fabsf(rs[i][1]));
-      if (lane == 0) red[warp + kWarps * i] = sum;
-    }
+    for (int i = 0; i < 8; ++i) v[i] = fabsf(rs[i][0]) + fabsf(rs[i][1]);
+    const float sum = warp_sum8(v);  // lane l: the sum of row warp + 16 ((l >> 2) & 7)
+    if ((lane & 3) == 0) red[warp + kWarps * ((lane >> 2) & 7)] = sum;
   }
   tc::fence_before_sync();
   __syncthreads();
@@ -616,27 +619,33 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
       // The f16 scales of the weight gradient's h operands, this warp's own copy: the bounds
       // of the 3xFP16 forward (|v| <= 1; |d/dx|, |d/dy| <= B_J grow by the norm N_l of W_l,
       // |L| <= B_L becomes N_l B_L + 2 (N_l B_J)^2), each mapped to <= 2^14 by a power of 2.
-      const float n1 = warp_max_f(fmaxf(red[lane], red[lane + 32]));
-      const float n2 = warp_max_f(fmaxf(red[64 + lane], red[96 + lane]));
+      const float n1 = warp_max_nonneg(fmaxf(red[lane], red[lane + 32]));
+      const float n2 = warp_max_nonneg(fmaxf(red[64 + lane], red[96 + lane]));
       const float w0x = small[kSmW0 + 2 * lane], w0y = small[kSmW0 + 2 * lane + 1];
       const float w1x = small[kSmW0 + 2 * (lane + 32)], w1y = small[kSmW0 + 2 * (lane + 32) + 1];
-      float bj = warp_max_f(fmaxf(fmaxf(fabsf(w0x), fabsf(w1x)), fmaxf(fabsf(w0y), fabsf(w1y))));
-      float bl = warp_max_f(fmaxf(fmaf(w0x, w0x, w0y * w0y), fmaf(w1x, w1x, w1y * w1y)));
-      if (lane == 0) {
-        const float nrm[2] = {n1, n2};
-        for (int l = 0; l < 3; ++l) {  // h_l
-          const float sig[4] = {16384.0f, pow2_floor_ratio(14, bj), pow2_floor_ratio(14, bj),
-                                pow2_floor_ratio(14, bl)};
-          for (int c = 0; c < 4; ++c) {
-            sigw[4 * l + c] = sig[c];
-            sigw[12 + 4 * l + c] = 1.0f / sig[c];  // exact: a power of 2
-          }
-          if (l < 2) {
-            const float nj = nrm[l] * bj;
-            bl = fmaf(nrm[l], bl, 2.0f * nj * nj);
-            bj = nj;
-          }
+      float bj = warp_max_nonneg(
+          fmaxf(fmaxf(fabsf(w0x), fabsf(w1x)), fmaxf(fabsf(w0y), fabsf(w1y))));
+      float bl = warp_max_nonneg(fmaxf(fmaf(w0x, w0x, w0y * w0y), fmaf(w1x, w1x, w1y * w1y)));
+      // lane 4l + c writes sigma of component c of h_l and its inverse (exact: a power of 2)
+      const float nrm[2] = {n1, n2};
+      float sl[3][2];  // h_l: sigma of d/dx and d/dy, of L
+#pragma unroll
+      for (int l = 0; l < 3; ++l) {
+        sl[l][0] = pow2_floor_ratio(14, bj);
+        sl[l][1] = pow2_floor_ratio(14, bl);
+        if (l < 2) {
+          const float nj = nrm[l] * bj;
+          bl = fmaf(nrm[l], bl, 2.0f * nj * nj);
+          bj = nj;
         }
+      }
+      if (lane < 12) {
+        const int l = lane >> 2, c = lane & 3;
+        const float j = l == 0 ? sl[0][0] : l == 1 ? sl[1][0] : sl[2][0];
+        const float lv = l == 0 ? sl[0][1] : l == 1 ? sl[1][1] : sl[2][1];
+        const float sg = c == 0 ? 16384.0f : c == 3 ? lv : j;
+        sigw[lane] = sg;
+        sigw[12 + lane] = inv_pow2(sg);
       }
       __syncwarp();
     }
@@ -648,8 +657,6 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
     // after the last input-adjoint GEMM's accumulators are read, before that tile's layer-0
     // adjoint), so GEMM 0 of the next tile runs under it; the first tile's layer 0 runs here.
     {
-      float x0 = 0.0f, x1 = 0.0f;
-      load_point(ps, blockIdx.x, kTile, row, x0, x1);
       xs[tid] = x0;
       xs[kThreads + tid] = x1;
       if (static_cast<int64_t>(blockIdx.x) < tiles)
@@ -880,7 +887,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
 #pragma unroll
             for (int w4 = 0; w4 < 4; ++w4)
               hm = fmaxf(hm, fmaxf(zmax[2 * hh + 4 * w4], zmax[2 * hh + 1 + 4 * w4]));
-            inv[hh] = 1.0f / pow2_floor_ratio(14, hm);
+            inv[hh] = inv_pow2(pow2_floor_ratio(14, hm));
           }
           float v[16], w[16];
           tc::ld_x16(tmem_warp + kDwCol + 16u * s, v);

@@ -161,6 +161,19 @@ __device__ __forceinline__ float pow2_floor_ratio(int c, float x) {
   return __uint_as_float(static_cast<uint32_t>(k + 127) << 23);
 }
 
+// Maximum over the warp of a non-negative float (non-negative floats order as their bit
+// patterns): one redux instruction.
+__device__ __forceinline__ float warp_max_nonneg(float v) {
+  return __uint_as_float(__reduce_max_sync(0xffffffffu, __float_as_uint(v)));
+}
+
+// 1 / x for a positive power of 2 x: exact, from the exponent field, when the result is a
+// normal float; otherwise the division (1 / inf = 0, 1 / 2^127 is subnormal).
+__device__ __forceinline__ float inv_pow2(float x) {
+  const uint32_t e = __float_as_uint(x) >> 23;
+  return (e >= 1u && e <= 253u) ? __uint_as_float((254u - e) << 23) : 1.0f / x;
+}
+
 // f16 operand pairs: hi = x rounded to f16 (11 significant bits), lo = x - hi
 // rounded to f16, element a (even K) in the low halves. x - hi is exact in FP32 and comes
 // from one mixed-precision fma (f16 hi times -1 plus the FP32 x), so a pair costs four

@@ -367,130 +367,150 @@ __device__ __forceinline__ float small_param(const float* __restrict__ params, i
   return 0.0f;
 }
 
-// tf32 set-up: the small parameters and the hi/lo split of the hidden weights. Element e of
-// an operand, enumerated as (row group, K chunk, row in group, K in chunk), sits at byte 4e of
-// the canonical layout: consecutive threads store consecutive words. All 25 loads of a thread
-// (24 weights, one small parameter) are issued before any is used.
+// tf32 set-up: the small parameters and the hi/lo split of the hidden weights. Element
+// (row, k) of a layer's operand sits at word (row / 8) 512 + (k / 4) 32 + (row % 8) 4 + k % 4
+// of the canonical K-major layout. Pass j of warp w covers row group g = j % 8 of layer j / 8
+// with the K chunks rotated by w: lane (r = lane / 4, t = lane % 4) takes row 8g + r and
+// k = 4 ((r + w) % 16) + t, so the row-major read (bank k % 32) and the canonical store
+// (bank 4r + t) each touch 32 distinct banks. All 25 loads of a thread (24 weights, one
+// small parameter) are issued before any is used.
 __device__ __forceinline__ void stage_tf32(const float* __restrict__ params, uint8_t* smem,
-                                           float* small) {
+                                           float* small, int warp, int lane) {
   using F = Format<false>;
   const float sv = small_param(params, threadIdx.x);
-  constexpr int kPerThread = kHiddenGemms * kWidth * kWidth / kThreads;  // 24
-  float w[kPerThread];
+  constexpr int kPasses = kHiddenGemms * kWidth * kWidth / kThreads;  // 24
+  const int r = lane >> 2, t = lane & 3;
+  const int kc = (r + warp) & 15;  // this lane's K chunk of 4
+  const int k = 4 * kc + t;
+  float w[kPasses];
 #pragma unroll
-  for (int r = 0; r < kPerThread; ++r) {
-    const int idx = threadIdx.x + r * kThreads;
-    const int layer = idx >> 12, e = idx & 4095;
-    const int row = ((e >> 9) << 3) | ((e >> 2) & 7);
-    const int k = (((e >> 5) & 15) << 2) | (e & 3);
-    w[r] = params[kHiddenBase + layer * kHiddenStride + neuron_of_column(row) * kWidth + k];
+  for (int j = 0; j < kPasses; ++j) {
+    const int layer = j >> 3, row = 8 * (j & 7) + r;
+    w[j] = params[kHiddenBase + layer * kHiddenStride + neuron_of_column(row) * kWidth + k];
   }
 #pragma unroll
-  for (int r = 0; r < kPerThread; ++r) {
-    const int idx = threadIdx.x + r * kThreads;
-    const int layer = idx >> 12, e = idx & 4095;
-    const uint32_t hi = tc::to_tf32(w[r]);
-    const uint32_t lo = tc::to_tf32(w[r] - __uint_as_float(hi));
-    reinterpret_cast<uint32_t*>(smem + (2 * layer) * F::kOperandBytes)[e] = hi;
-    reinterpret_cast<uint32_t*>(smem + (2 * layer + 1) * F::kOperandBytes)[e] = lo;
+  for (int j = 0; j < kPasses; ++j) {
+    const int layer = j >> 3, g = j & 7;
+    const uint32_t hi = tc::to_tf32(w[j]);
+    const uint32_t lo = tc::to_tf32(w[j] - __uint_as_float(hi));
+    const int word = g * 512 + kc * 32 + 4 * r + t;
+    reinterpret_cast<uint32_t*>(smem + (2 * layer) * F::kOperandBytes)[word] = hi;
+    reinterpret_cast<uint32_t*>(smem + (2 * layer + 1) * F::kOperandBytes)[word] = lo;
   }
   small[threadIdx.x] = sv;
 }
 
 // f16 set-up: the small parameters, the operand scales and the epilogue constants
-// (F16Consts), then the split of the tau-scaled hidden weights into W_hi and W_lo. Every load
-// is issued before any is used (one memory round trip): the small parameter, 24 values for the
-// weight-row statistics and 12 pairs for the split. Power-of-2 scales keep every f16 operand
-// in range: tau_l maps max|W_l| to <= 16; sigma_{l,c} maps a bound of component c of GEMM l's
-// A operand to <= 2^14 (one sigma for d/dx and d/dy, from the larger bound). Bounds: |v| <= 1;
-// |d/dx|, |d/dy| grow by N_l (max row-abs-sum of W_l) per layer; |L| becomes
-// N_l |L| + (N_l Bx)^2 + (N_l By)^2 (tanh' <= 1, 2 |tanh tanh'| <= 1). Row statistics are
-// fixed-order warp reductions, so every CTA derives the same scales. Contains two block-wide
+// (F16Consts), then the split of the tau-scaled hidden weights into W_hi and W_lo. Power-of-2
+// scales keep every f16 operand in range: tau_l maps max|W_l| to <= 16; sigma_{l,c} maps a
+// bound of component c of GEMM l's A operand to <= 2^14 (one sigma for d/dx and d/dy, from
+// the larger bound). Bounds: |v| <= 1; |d/dx|, |d/dy| grow by N_l (max row-abs-sum of W_l)
+// per layer; |L| becomes N_l |L| + (N_l Bx)^2 + (N_l By)^2 (tanh' <= 1, 2 |tanh tanh'| <= 1).
+// Statistics: threads 0..383 take half a hidden-weight row each (row tid / 2, 32 elements
+// read in a rotated order, so a warp's 32 reads touch 32 banks), threads 384..447 one row of
+// W0; per-warp maxima by redux (non-negative floats order as their bit patterns). All sums
+// run in a fixed order, so every CTA derives the same scales. Contains two block-wide
 // barriers.
 __device__ __forceinline__ void stage_f16(const float* __restrict__ params, uint8_t* smem,
                                           float* small, float* red, float* cst, int warp,
                                           int lane) {
   using F = Format<true>;
-  constexpr int kStatRows = 3 * kWidth / kWarps;                   // 12 rows per warp
   constexpr int kPairs = kHiddenGemms * kWidth * kWidth / 2;       // 6144
   constexpr int kPairsPerThread = kPairs / kThreads;               // 12
   static_assert(kPairs % kThreads == 0, "whole pairs per thread");
+  constexpr int kStatThreads = 2 * kHiddenGemms * kWidth;          // 384
   using C = F16Consts;
   float wp[kPairsPerThread][2];
   {
     const float sv = small_param(params, threadIdx.x);
-    float rs[kStatRows][2];
 #pragma unroll
-    for (int i = 0; i < kStatRows; ++i) {  // row warp + 16 i of the 192 hidden-weight rows
-      const int r = warp + kWarps * i;
-      const float* wr = params + kHiddenBase + (r >> 6) * kHiddenStride + (r & 63) * kWidth;
-      rs[i][0] = wr[lane];
-      rs[i][1] = wr[lane + 32];
+    for (int j = 0; j < kPairsPerThread; ++j) {
+      const int it = warp + kWarps * j;  // layer it / 64, row group (it / 8) % 8, rotation it % 8
+      const int layer = it >> 6, row = 8 * ((it >> 3) & 7) + (lane >> 2);
+      const int kk = 8 * (((lane >> 2) + it) & 7) + 2 * (lane & 3);
+      const float2 v = *reinterpret_cast<const float2*>(
+          params + kHiddenBase + layer * kHiddenStride + neuron_of_column(row) * kWidth + kk);
+      wp[j][0] = v.x;
+      wp[j][1] = v.y;
     }
+    float m0 = 0.0f, m1 = 0.0f;  // hidden rows: abs-sum, max |w|; W0 rows: max |w|, |w|^2
+    if (threadIdx.x < kStatThreads) {
+      const int r = threadIdx.x >> 1, h = threadIdx.x & 1;
+      const float* wr = params + kHiddenBase + (r >> 6) * kHiddenStride + (r & 63) * kWidth +
+                        32 * h;
+      float a[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-    for (int k = 0; k < kPairsPerThread; ++k) {
-      const int idx = threadIdx.x + k * kThreads;
-      const int layer = idx >> 11, e = (idx & 2047) * 2;
-      const int row = ((e >> 9) << 3) | ((e >> 3) & 7);
-      const int kk = (((e >> 6) & 7) << 3) | (e & 7);
-      const float* wr =
-          params + kHiddenBase + layer * kHiddenStride + neuron_of_column(row) * kWidth + kk;
-      wp[k][0] = wr[0];
-      wp[k][1] = wr[1];
-    }
-#pragma unroll
-    for (int i = 0; i < kStatRows; ++i) {
-      const float a = fabsf(rs[i][0]), b = fabsf(rs[i][1]);
-      const float sum = warp_sum(a + b), mx = warp_max(fmaxf(a, b));
-      if (lane == 0) {
-        red[warp + kWarps * i] = sum;  // the output-layer buffer is free during set-up
-        red[256 + warp + kWarps * i] = mx;
+      for (int j = 0; j < 32; ++j) {
+        const float x = fabsf(wr[(j + threadIdx.x) & 31]);
+        a[j & 3] += x;
+        m1 = fmaxf(m1, x);
       }
+      m0 = (a[0] + a[1]) + (a[2] + a[3]);
+      m0 += __shfl_xor_sync(0xffffffffu, m0, 1);  // the row's two halves
+    } else if (threadIdx.x < kStatThreads + kWidth) {
+      const int o = threadIdx.x - kStatThreads;
+      const float wx = params[2 * o], wy = params[2 * o + 1];
+      m0 = fmaxf(fabsf(wx), fabsf(wy));
+      m1 = fmaf(wx, wx, wy * wy);
+    }
+    const uint32_t r0 = __reduce_max_sync(0xffffffffu, __float_as_uint(m0));
+    const uint32_t r1 = __reduce_max_sync(0xffffffffu, __float_as_uint(m1));
+    if (lane == 0) {  // warps 4l..4l+3: layer l's rows; warps 12, 13: W0
+      red[warp] = __uint_as_float(r0);
+      red[16 + warp] = __uint_as_float(r1);
     }
     small[threadIdx.x] = sv;
   }
   epi_sync();
   float* sigma = red + 512;  // [3][4] scratch for the layer-0 constants below
   if (warp == 0) {
-    float nrm[3], wmax[3];
+    // lane l < 3 derives tau_l; the bound recursion over the layers runs in every lane
+    float nrm[3];
+#pragma unroll
+    for (int l = 0; l < 3; ++l)
+      nrm[l] = fmaxf(fmaxf(red[4 * l], red[4 * l + 1]), fmaxf(red[4 * l + 2], red[4 * l + 3]));
+    const int lt = lane < 3 ? lane : 0;
+    const float wmax = fmaxf(fmaxf(red[16 + 4 * lt], red[17 + 4 * lt]),
+                             fmaxf(red[18 + 4 * lt], red[19 + 4 * lt]));
+    const float tau_mine = pow2_floor_ratio(4, wmax);
+    float tau[3];
+#pragma unroll
+    for (int l = 0; l < 3; ++l) tau[l] = __shfl_sync(0xffffffffu, tau_mine, l);
+    float bj = fmaxf(red[12], red[13]);
+    float bl = fmaxf(red[28], red[29]);
+    float sig[3][3];  // sig[l]: v, J, L
 #pragma unroll
     for (int l = 0; l < 3; ++l) {
-      nrm[l] = warp_max(fmaxf(red[64 * l + lane], red[64 * l + lane + 32]));
-      wmax[l] = warp_max(fmaxf(red[256 + 64 * l + lane], red[256 + 64 * l + lane + 32]));
+      sig[l][0] = 16384.0f;
+      sig[l][1] = pow2_floor_ratio(14, bj);
+      sig[l][2] = pow2_floor_ratio(14, bl);
+      const float nj = nrm[l] * bj;
+      bl = fmaf(nrm[l], bl, 2.0f * nj * nj);
+      bj = nj;
     }
-    const float w0x = small[kSmW0 + 2 * lane], w0y = small[kSmW0 + 2 * lane + 1];
-    const float w0x2 = small[kSmW0 + 2 * (lane + 32)], w0y2 = small[kSmW0 + 2 * (lane + 32) + 1];
-    float bj = warp_max(fmaxf(fmaxf(fabsf(w0x), fabsf(w0x2)), fmaxf(fabsf(w0y), fabsf(w0y2))));
-    float bl = warp_max(fmaxf(fmaf(w0x, w0x, w0y * w0y), fmaf(w0x2, w0x2, w0y2 * w0y2)));
-    if (lane == 0) {
-      float tau[3], sig[3][3];  // sig[l]: v, J, L
-      for (int l = 0; l < 3; ++l) {
-        tau[l] = pow2_floor_ratio(4, wmax[l]);
-        sig[l][0] = 16384.0f;
-        sig[l][1] = pow2_floor_ratio(14, bj);
-        sig[l][2] = pow2_floor_ratio(14, bl);
-        const float nj = nrm[l] * bj;
-        bl = fmaf(nrm[l], bl, 2.0f * nj * nj);
-        bj = nj;
-      }
-      float us[3][3];  // 1 / (sigma tau) of GEMM l's accumulators, per component
-      for (int l = 0; l < 3; ++l)
-        for (int c = 0; c < 3; ++c) us[l][c] = 1.0f / (sig[l][c] * tau[l]);
-      for (int l = 0; l < 3; ++l) cst[C::kTau + l] = tau[l];
-      for (int l = 0; l < 2; ++l) {  // hidden epilogues: GEMM l's accumulators -> GEMM l+1
-        const float e1 = sig[l + 1][1] * us[l][1];
-        const float e2 = sig[l + 1][2] * us[l][2];
-        const float e3 = -2.0f * sig[l + 1][2] * us[l][1] * us[l][1];
-        float* k = cst + C::kHid + 8 * l;
-        k[0] = kTwoOverLn2 * us[l][0];
-        k[1] = sig[l + 1][0];
-        k[2] = -2.0f * sig[l + 1][0];
-        k[3] = 4.0f * e1;
-        k[4] = 4.0f * e2;
-        k[5] = 4.0f * e3;
-        k[6] = -8.0f * e3;
-        k[7] = 0.0f;
-      }
+    float us[3][3];  // 1 / (sigma tau) of GEMM l's accumulators, per component (exact)
+#pragma unroll
+    for (int l = 0; l < 3; ++l)
+#pragma unroll
+      for (int c = 0; c < 3; ++c) us[l][c] = inv_pow2(sig[l][c] * tau[l]);
+    if (lane < 3) cst[C::kTau + lane] = tau_mine;
+    if (lane < 2) {  // hidden epilogues: GEMM l's accumulators -> GEMM l+1
+      const int l = lane;
+      const float u1 = l == 0 ? us[0][1] : us[1][1], u2 = l == 0 ? us[0][2] : us[1][2];
+      const float u0 = l == 0 ? us[0][0] : us[1][0];
+      const float s0 = l == 0 ? sig[1][0] : sig[2][0], s1 = l == 0 ? sig[1][1] : sig[2][1];
+      const float s2 = l == 0 ? sig[1][2] : sig[2][2];
+      const float e1 = s1 * u1, e2 = s2 * u2, e3 = -2.0f * s2 * u1 * u1;
+      float* k = cst + C::kHid + 8 * l;
+      k[0] = kTwoOverLn2 * u0;
+      k[1] = s0;
+      k[2] = -2.0f * s0;
+      k[3] = 4.0f * e1;
+      k[4] = 4.0f * e2;
+      k[5] = 4.0f * e3;
+      k[6] = -8.0f * e3;
+      k[7] = 0.0f;
+    } else if (lane == 2) {
       float* k = cst + C::kOut;  // the output stage, and layer 0's value scale
       k[0] = kTwoOverLn2 * us[2][0];
       k[1] = 4.0f * us[2][2];
@@ -498,6 +518,7 @@ __device__ __forceinline__ void stage_f16(const float* __restrict__ params, uint
       k[3] = 0.0f;
       k[4] = sig[0][0];
       k[5] = -2.0f * sig[0][0];
+    } else if (lane == 3) {
       sigma[0] = sig[0][1];
       sigma[1] = sig[0][2];
     }
@@ -518,18 +539,23 @@ __device__ __forceinline__ void stage_f16(const float* __restrict__ params, uint
   }
   if (threadIdx.x < 3 * kWidth)  // hidden biases in the scaled tanh argument
     cst[C::kBias + threadIdx.x] = kTwoOverLn2 * small[kSmB + threadIdx.x];
-  // The split: pairs of adjacent K elements, enumerated (row group, K chunk of 8, row in
-  // group, K pair) so consecutive threads store consecutive words of the canonical layout.
+  // The split: pair (row, kk..kk+1) of a layer's operand is word
+  // (row / 8) 256 + (kk / 8) 32 + (row % 8) 4 + (kk % 8) / 2 of the canonical K-major layout.
+  // Pass j of warp w is iteration it = w + 16 j: row group (it / 8) % 8 of layer it / 64, with
+  // the K chunks of 8 rotated by it % 8. Lane (r = lane / 4, p = lane % 4) takes row
+  // 8 ((it / 8) % 8) + r and the pair at kk = 8 ((r + it) % 8) + 2p: the row-major float2 read
+  // touches 16 distinct bank pairs per half warp and the canonical store banks 4r + p.
 #pragma unroll
-  for (int k = 0; k < kPairsPerThread; ++k) {
-    const int idx = threadIdx.x + k * kThreads;
-    const int layer = idx >> 11, e = (idx & 2047) * 2;
+  for (int j = 0; j < kPairsPerThread; ++j) {
+    const int it = warp + kWarps * j;
+    const int layer = it >> 6;
     const float tau = cst[C::kTau + layer];
     uint32_t hi, lo;
-    split_f16_pair(wp[k][0] * tau, wp[k][1] * tau, hi, lo);
-    uint8_t* base = smem + (2 * layer) * F::kOperandBytes + 2 * e;
-    *reinterpret_cast<uint32_t*>(base) = hi;
-    *reinterpret_cast<uint32_t*>(base + F::kOperandBytes) = lo;
+    split_f16_pair(wp[j][0] * tau, wp[j][1] * tau, hi, lo);
+    const int word = ((it >> 3) & 7) * 256 + (((lane >> 2) + it) & 7) * 32 + lane;
+    uint32_t* base = reinterpret_cast<uint32_t*>(smem + (2 * layer) * F::kOperandBytes);
+    base[word] = hi;
+    base[word + F::kOperandBytes / 4] = lo;
   }
 }
 
@@ -656,7 +682,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
     if constexpr (F16) {
       stage_f16(sp, smem, small, red, reinterpret_cast<float*>(smem + L::kScaleOff), warp, lane);
     } else {
-      stage_tf32(sp, smem, small);
+      stage_tf32(sp, smem, small, warp, lane);
     }
   }
   tc::fence_proxy_async_smem();  // weight operands visible to the tensor core
