@@ -406,12 +406,6 @@ __device__ __forceinline__ void mma_warp(const Ctx& cx, int64_t tiles) {
   }
 }
 
-__device__ __forceinline__ float warp_max_f(float v) {
-#pragma unroll
-  for (int m = 16; m >= 1; m >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, m));
-  return v;
-}
-
 // Sums v[i] over the 32 lanes of the warp for every i < 16 with a fixed butterfly that
 // halves the values held per lane at each step (16 shuffles instead of 80); lane l returns
 // the total for i = l >> 1.

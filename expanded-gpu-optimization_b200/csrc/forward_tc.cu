@@ -206,12 +206,6 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, const 
   return __all_sync(0xffffffffu, wait_or_abort(bar, parity, cx) ? 1 : 0) != 0;
 }
 
-__device__ __forceinline__ float warp_max(float v) {
-#pragma unroll
-  for (int m = 16; m >= 1; m >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, m));
-  return v;
-}
-
 // f16 pairs of a split: hi = x rounded to 11 significant bits (tf32 rounding; exact in f16
 // inside the scaled range), lo = x - hi (exact in FP32, rounded to f16); element a (even K)
 // in the low halves. Values below f16's normal range (2^-14, 2^28 below a scaled bound) lose
@@ -409,8 +403,8 @@ __device__ __forceinline__ void stage_tf32(const float* __restrict__ params, uin
 // Statistics: threads 0..383 take half a hidden-weight row each (row tid / 2, 32 elements
 // read in a rotated order, so a warp's 32 reads touch 32 banks), threads 384..447 one row of
 // W0; per-warp maxima by redux (non-negative floats order as their bit patterns). All sums
-// run in a fixed order, so every CTA derives the same scales. Contains two block-wide
-// barriers.
+// run in a fixed order, so every CTA derives the same scales. Contains one barrier of the
+// epilogue warps.
 __device__ __forceinline__ void stage_f16(const float* __restrict__ params, uint8_t* smem,
                                           float* small, float* red, float* cst, int warp,
                                           int lane) {
@@ -462,23 +456,23 @@ __device__ __forceinline__ void stage_f16(const float* __restrict__ params, uint
     small[threadIdx.x] = sv;
   }
   epi_sync();
-  float* sigma = red + 512;  // [3][4] scratch for the layer-0 constants below
-  if (warp == 0) {
-    // lane l < 3 derives tau_l; the bound recursion over the layers runs in every lane
-    float nrm[3];
+  // Every warp derives the scales itself (no second barrier); warp 0 stores the constants.
+  // Lane l < 3 derives tau_l; the bound recursion over the layers runs in every lane.
+  float nrm[3];
 #pragma unroll
-    for (int l = 0; l < 3; ++l)
-      nrm[l] = fmaxf(fmaxf(red[4 * l], red[4 * l + 1]), fmaxf(red[4 * l + 2], red[4 * l + 3]));
-    const int lt = lane < 3 ? lane : 0;
-    const float wmax = fmaxf(fmaxf(red[16 + 4 * lt], red[17 + 4 * lt]),
-                             fmaxf(red[18 + 4 * lt], red[19 + 4 * lt]));
-    const float tau_mine = pow2_floor_ratio(4, wmax);
-    float tau[3];
+  for (int l = 0; l < 3; ++l)
+    nrm[l] = fmaxf(fmaxf(red[4 * l], red[4 * l + 1]), fmaxf(red[4 * l + 2], red[4 * l + 3]));
+  const int lt = lane < 3 ? lane : 0;
+  const float wmax = fmaxf(fmaxf(red[16 + 4 * lt], red[17 + 4 * lt]),
+                           fmaxf(red[18 + 4 * lt], red[19 + 4 * lt]));
+  const float tau_mine = pow2_floor_ratio(4, wmax);
+  float tau[3];
 #pragma unroll
-    for (int l = 0; l < 3; ++l) tau[l] = __shfl_sync(0xffffffffu, tau_mine, l);
+  for (int l = 0; l < 3; ++l) tau[l] = __shfl_sync(0xffffffffu, tau_mine, l);
+  float sig[3][3];  // sig[l]: v, J, L
+  {
     float bj = fmaxf(red[12], red[13]);
     float bl = fmaxf(red[28], red[29]);
-    float sig[3][3];  // sig[l]: v, J, L
 #pragma unroll
     for (int l = 0; l < 3; ++l) {
       sig[l][0] = 16384.0f;
@@ -488,6 +482,8 @@ __device__ __forceinline__ void stage_f16(const float* __restrict__ params, uint
       bl = fmaf(nrm[l], bl, 2.0f * nj * nj);
       bj = nj;
     }
+  }
+  if (warp == 0) {
     float us[3][3];  // 1 / (sigma tau) of GEMM l's accumulators, per component (exact)
 #pragma unroll
     for (int l = 0; l < 3; ++l)
@@ -518,22 +514,18 @@ __device__ __forceinline__ void stage_f16(const float* __restrict__ params, uint
       k[3] = 0.0f;
       k[4] = sig[0][0];
       k[5] = -2.0f * sig[0][0];
-    } else if (lane == 3) {
-      sigma[0] = sig[0][1];
-      sigma[1] = sig[0][2];
     }
   }
-  epi_sync();
   if (threadIdx.x < kWidth) {  // layer-0 jets: J = W0 columns, L = -2 a s |W0 row|^2
     const int o = threadIdx.x;
     const float w0 = small[kSmW0 + 2 * o], w1 = small[kSmW0 + 2 * o + 1];
-    const float c0 = -2.0f * sigma[1] * fmaf(w0, w0, w1 * w1);
+    const float c0 = -2.0f * sig[0][2] * fmaf(w0, w0, w1 * w1);
     float* l0 = cst + C::kL0;
     l0[0 * kWidth + o] = kTwoOverLn2 * w0;
     l0[1 * kWidth + o] = kTwoOverLn2 * w1;
     l0[2 * kWidth + o] = kTwoOverLn2 * small[kSmB0 + o];
-    l0[3 * kWidth + o] = 4.0f * sigma[0] * w0;
-    l0[4 * kWidth + o] = 4.0f * sigma[0] * w1;
+    l0[3 * kWidth + o] = 4.0f * sig[0][1] * w0;
+    l0[4 * kWidth + o] = 4.0f * sig[0][1] * w1;
     l0[5 * kWidth + o] = 4.0f * c0;
     l0[6 * kWidth + o] = -8.0f * c0;
   }
@@ -548,10 +540,10 @@ __device__ __forceinline__ void stage_f16(const float* __restrict__ params, uint
 #pragma unroll
   for (int j = 0; j < kPairsPerThread; ++j) {
     const int it = warp + kWarps * j;
-    const int layer = it >> 6;
-    const float tau = cst[C::kTau + layer];
+    const int layer = it >> 6;  // = j / 4
+    const float t = tau[j >> 2];
     uint32_t hi, lo;
-    split_f16_pair(wp[j][0] * tau, wp[j][1] * tau, hi, lo);
+    split_f16_pair(wp[j][0] * t, wp[j][1] * t, hi, lo);
     const int word = ((it >> 3) & 7) * 256 + (((lane >> 2) + it) & 7) * 32 + lane;
     uint32_t* base = reinterpret_cast<uint32_t*>(smem + (2 * layer) * F::kOperandBytes);
     base[word] = hi;
