@@ -71,15 +71,17 @@ static_assert((kLaunchRegs - kMmaRegs) * 128 >= (kEpiRegs - kLaunchRegs) * kThre
               "register split exceeds the launch's registers");
 constexpr int kChunks = 4;                       // 16-neuron chunks per 64-wide GEMM
 constexpr int kGemmsPerTile = 6;                 // forward W1..W3, backward W3^T, W2^T, W1^T
-constexpr int kRing = 2;
-constexpr uint32_t kSlotCols = 128;
+// The ring holds the four chunks of a GEMM's A operand (f16 hi/lo pairs): every chunk's slot
+// was last read by the previous GEMM, whose completion the producing warp has waited for.
+constexpr int kRing = 4;
+constexpr uint32_t kSlotCols = 64;               // 4 components x {hi, lo} x 8 columns of pairs
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kRingCol = 256;
 constexpr uint32_t kDwCol = kRingCol;            // weight-gradient accumulators (borrowed)
-constexpr uint32_t kIdesc = tc::idesc_tf32(128, 64);
-constexpr uint32_t kLbo = 128, kSbo = 2048;      // K-major no-swizzle canonical operand
+constexpr uint32_t kIdesc = tc::idesc_f16(128, 64);
+constexpr uint32_t kLbo = 128, kSbo = 1024;      // K-major no-swizzle canonical f16 operand
 
-constexpr int kOperandBytes = kWidth * kWidth * 4;   // 16 KB
+constexpr int kOperandBytes = kWidth * kWidth * 2;   // 8 KB
 constexpr int kLayerBytes = 2 * kOperandBytes;       // hi + lo
 constexpr int kWeightBlocks = 6;                     // W1, W2, W3, W1^T, W2^T, W3^T
 constexpr int kWeightSlots = 2;
@@ -116,13 +118,20 @@ constexpr int kPLoss = kPartKinds * 256, kPBout = kPLoss + 4;
 constexpr int kPartFloats = kPBout + 4;
 constexpr int kXsOff = kPartOff + kPartFloats * 4;            // the tile's points x[512], y[512]
 constexpr int kXnOff = kXsOff + 2 * kThreads * 4;             // the next tile's, same layout
-// weight-gradient scales: per epilogue warp its copy of the h scales sigma[3][4] and their
-// inverses (h_0, h_1, h_2; v, d/dx, d/dy, L), then the per-warp maxima of the scaled zbar
+// f16 operand scales: per epilogue warp its copy of the h scales sigma[3][4] (h_0, h_1, h_2;
+// v, d/dx, d/dy, L) at kSig, their inverses at kInvSig, the weight scales tau[3] (W1..W3)
+// at kTau and their inverses at kInvTau; then per warp the maxima of its zbar components
+// (kZmaxFloats: |zbar_c| for c = 0..3, and max_c |zbar_c| / sigma_c for the weight gradient)
 constexpr int kDwScaleOff = kXnOff + 2 * kThreads * 4;
-constexpr int kSigFloats = 24;
+constexpr int kSig = 0, kInvSig = 12, kTau = 24, kInvTau = 28;
+// per layer of a tile: the weight-gradient staging scales zs / (sigma_c S_c) of the zbar_c
+// already multiplied by S_c, and 1 / (S_c tau) for the input adjoint's accumulators
+constexpr int kStg = 32, kIsc = 36;
+constexpr int kSigFloats = 40;
 constexpr int kZmaxOff = kDwScaleOff + kWarps * kSigFloats * 4;
-constexpr int kBarOff = kZmaxOff + kWarps * 4;                // mbarriers
-constexpr int kNumBars = 10;   // empty[2] dfull red wfull[2] dwdone[2] full[2]
+constexpr int kZmaxFloats = 8;
+constexpr int kBarOff = kZmaxOff + kWarps * kZmaxFloats * 4;  // mbarriers
+constexpr int kNumBars = 10;   // dfull red wfull[2] dwdone[2] full[4]
 constexpr int kMiscOff = kBarOff + kNumBars * 8;              // TMEM base, abort flag, status
 constexpr int kSmemBytes = kMiscOff + 16;
 static_assert(kSmemBytes <= 227 * 1024, "shared memory layout overflow");
@@ -139,14 +148,13 @@ __device__ __forceinline__ uint8_t* dsmem() {
 __device__ __forceinline__ uint64_t* bar_at(int k) {
   return reinterpret_cast<uint64_t*>(dsmem() + kBarOff) + k;
 }
-__device__ __forceinline__ uint64_t* bar_empty(uint32_t r) { return bar_at(static_cast<int>(r)); }
-__device__ __forceinline__ uint64_t* bar_dfull() { return bar_at(kRing); }
-__device__ __forceinline__ uint64_t* bar_red() { return bar_at(kRing + 1); }
-__device__ __forceinline__ uint64_t* bar_wfull(int k) { return bar_at(kRing + 2 + k); }
-__device__ __forceinline__ uint64_t* bar_dwdone(int half) { return bar_at(kRing + 4 + half); }
+__device__ __forceinline__ uint64_t* bar_dfull() { return bar_at(0); }
+__device__ __forceinline__ uint64_t* bar_red() { return bar_at(1); }
+__device__ __forceinline__ uint64_t* bar_wfull(int k) { return bar_at(2 + k); }
+__device__ __forceinline__ uint64_t* bar_dwdone(int half) { return bar_at(4 + half); }
 // A ring slot written by the 16 epilogue warps.
 __device__ __forceinline__ uint64_t* bar_full(uint32_t r) {
-  return bar_at(kRing + 6 + static_cast<int>(r));
+  return bar_at(6 + static_cast<int>(r));
 }
 __device__ __forceinline__ volatile uint32_t* abort_flag() {
   return reinterpret_cast<volatile uint32_t*>(dsmem() + kMiscOff + 4);
@@ -218,70 +226,61 @@ __device__ __forceinline__ void load_weight_slot(int slot, const float* wsplit, 
                 kLayerBytes, bar_wfull(slot));
 }
 
-// The 24 MMAs of chunk j of GEMM g (A from ring slot `slot`); the first chunk of a GEMM
-// first waits for its weight slot. False if that wait gave up (nothing is issued). Not
-// inlined: one copy instead of twelve keeps the kernel small enough for the instruction
-// cache (measured faster than the inlined form here).
+// The 12 MMAs of chunk j of GEMM g (A from ring slot `slot`: 4 components x (A_hi B_hi +
+// A_lo B_hi + A_hi B_lo), K = 16, the component's hi block at column 16c of the slot and its
+// lo block 8 columns on); the first chunk of a GEMM first waits for its weight slot. False if
+// that wait gave up (nothing is issued). Not inlined: one copy instead of twenty-four keeps
+// the kernel small enough for the instruction cache.
 __device__ __noinline__ bool issue_chunk_mmas(const Ctx& cx, uint32_t tile_index, int g,
                                                  int j, uint32_t slot) {
   const int ws = g & 1;
   if (j == 0 && !warp_wait(bar_wfull(ws), weight_parity(tile_index, g))) return false;
   tc::fence_after_sync();
+  const uint32_t w_hi = smem_u32(dsmem() + kWOff + ws * kLayerBytes + 256 * j);
+  const uint64_t bhi = tc::smem_desc_kmajor(w_hi, kLbo, kSbo);
+  const uint64_t blo = tc::smem_desc_kmajor(w_hi + kOperandBytes, kLbo, kSbo);
 #pragma unroll
-  for (int kk = 0; kk < 2; ++kk) {
-    const uint32_t w_hi = smem_u32(dsmem() + kWOff + ws * kLayerBytes + 256 * (2 * j + kk));
-    const uint64_t bhi = tc::smem_desc_kmajor(w_hi, kLbo, kSbo);
-    const uint64_t blo = tc::smem_desc_kmajor(w_hi + kOperandBytes, kLbo, kSbo);
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      const uint32_t d = cx.tmem + 64u * c;
-      const uint32_t a_hi = cx.tmem + kRingCol + kSlotCols * slot + 32u * c + 8u * kk;
-      const uint32_t a_lo = a_hi + 16u;
-      tc::mma_tf32_ts_warp(d, a_hi, bhi, kIdesc, (j > 0 || kk > 0) ? 1u : 0u);
-      tc::mma_tf32_ts_warp(d, a_lo, bhi, kIdesc, 1u);
-      tc::mma_tf32_ts_warp(d, a_hi, blo, kIdesc, 1u);
-    }
+  for (int c = 0; c < 4; ++c) {
+    const uint32_t d = cx.tmem + 64u * c;
+    const uint32_t a_hi = cx.tmem + kRingCol + kSlotCols * slot + 16u * c;
+    const uint32_t a_lo = a_hi + 8u;
+    tc::mma_f16_ts_warp(d, a_hi, bhi, kIdesc, j > 0 ? 1u : 0u);
+    tc::mma_f16_ts_warp(d, a_lo, bhi, kIdesc, 1u);
+    tc::mma_f16_ts_warp(d, a_hi, blo, kIdesc, 1u);
   }
-  tc::commit_warp(bar_empty(slot));
   if (j == kChunks - 1) tc::commit_warp(bar_dfull());
   return true;
 }
 
-// Write chunk `n` (this warp's 4 neurons x 4 components, hi and lo) into ring slot n % 2;
-// the warp completing the chunk last issues its MMAs. False if a wait gave up.
-__device__ __forceinline__ bool produce_chunk(uint32_t n, const float (&h)[4][4],
-                                              uint32_t tmem_warp, int s, const Ctx& cx) {
+// Write chunk `n` (this warp's 4 neurons x 4 components, already multiplied by their f16
+// scales) into ring slot n % 4 as f16 hi/lo pairs: neuron 4s + t of the chunk is K index
+// 4s + t, so the thread's pairs (t = 0, 1) and (t = 2, 3) are columns 2s and 2s + 1 of the
+// component's hi block (16c) and lo block (16c + 8).
+__device__ __forceinline__ void produce_chunk(uint32_t n, const float (&h)[4][4],
+                                              uint32_t tmem_warp, int s) {
   const uint32_t slot = n % kRing;
-  // Chunks 0 and 1 of a GEMM reuse the slots of chunks 2 and 3 of the previous GEMM (or the
-  // weight-gradient accumulators borrowed in between), which this warp's wait for that GEMM's
-  // "D complete" commit (and the block barrier after emptying the accumulators) already
-  // covers; only chunks 2 and 3 wait for the commit of chunk n - 2. A phase still completes
-  // per chunk, so the parity below counts every chunk of the slot.
-  if (n % kChunks >= static_cast<uint32_t>(kRing)) {
-    if (!warp_wait(bar_empty(slot), ((n / kRing) & 1u) ^ 1u)) return false;
-    tc::fence_after_sync();
-  }
-  const uint32_t base = tmem_warp + kRingCol + kSlotCols * slot + 4u * s;
+  const uint32_t base = tmem_warp + kRingCol + kSlotCols * slot + 2u * s;
 #pragma unroll
   for (int c = 0; c < 4; ++c) {
-    uint32_t hi[4], lo[4];
-#pragma unroll
-    for (int t = 0; t < 4; ++t) tc::split_tf32(h[c][t], hi[t], lo[t]);
-    tc::st_x4(base + 32u * c, hi[0], hi[1], hi[2], hi[3]);
-    tc::st_x4(base + 32u * c + 16u, lo[0], lo[1], lo[2], lo[3]);
+    uint32_t hi0, lo0, hi1, lo1;
+    split_f16_pair_fast(h[c][0], h[c][1], hi0, lo0);
+    split_f16_pair_fast(h[c][2], h[c][3], hi1, lo1);
+    tc::st_x2(base + 16u * c, hi0, hi1);
+    tc::st_x2(base + 16u * c + 8u, lo0, lo1);
   }
   tc::wait_st();
   tc::fence_before_sync();
   __syncwarp();
   if ((threadIdx.x & 31) == 0) mbar_arrive(bar_full(slot));
-  return true;
 }
 
 // Layer 0 of the forward recompute for the point (x0, x1): z = W0 x + b0, z_J = the row of
-// W0, z_L = 0, through the tanh jet into the four chunks of GEMM 0's A operand.
+// W0, z_L = 0, through the tanh jet, times the f16 scales sg[c] of h_0, into the four chunks
+// of GEMM 0's A operand.
 __device__ __forceinline__ void produce_layer0(float x0, float x1, const float* small,
-                                               uint32_t& chunk, uint32_t tmem_warp, int s,
-                                               const Ctx& cx) {
+                                               const float* sg, uint32_t& chunk,
+                                               uint32_t tmem_warp, int s) {
+  const float s0 = sg[0], s1 = sg[1], s3 = sg[3];
 #pragma unroll
   for (int a = 0; a < kChunks; ++a) {
     float h[4][4];
@@ -291,8 +290,12 @@ __device__ __forceinline__ void produce_layer0(float x0, float x1, const float* 
       const float w0 = small[kSmW0 + 2 * o], w1 = small[kSmW0 + 2 * o + 1];
       tanh_jet_fast(fmaf(w0, x0, fmaf(w1, x1, small[kSmB0 + o])), w0, w1, 0.0f, h[0][t],
                     h[1][t], h[2][t], h[3][t]);
+      h[0][t] *= s0;
+      h[1][t] *= s1;
+      h[2][t] *= s1;
+      h[3][t] *= s3;
     }
-    produce_chunk(chunk++, h, tmem_warp, s, cx);
+    produce_chunk(chunk++, h, tmem_warp, s);
   }
 }
 
@@ -480,24 +483,40 @@ __device__ __forceinline__ void red_add(float* addr, float v) {
   asm volatile("red.global.add.f32 [%0], %1;" ::"l"(addr), "f"(v) : "memory");
 }
 
-// Pre-split weights for the tensor-core backward: six K-major canonical tf32 operands, hi
-// then lo, of W1, W2, W3 ([out][in], forward GEMMs) and W1^T, W2^T, W3^T ([in][out], input
-// adjoint GEMMs). Element e of an operand sits at word e (row = ((e>>9)<<3)|((e>>2)&7),
-// K = (((e>>5)&15)<<2)|(e&3)), the layout of the forward kernel's shared-memory operands.
-__global__ void __launch_bounds__(256) prep_weights_kernel(const float* __restrict__ params,
+// Pre-split weights for the tensor-core backward: six K-major canonical f16 operands, hi then
+// lo, of W1, W2, W3 ([out][in], forward GEMMs) and W1^T, W2^T, W3^T ([in][out], input-adjoint
+// GEMMs), each times tau_l (the power of 2 that maps max |W_l| to <= 16; the step kernel
+// derives the same tau from the same maximum). One block per operand; pair (row, kk..kk+1)
+// of an operand is word (row / 8) 256 + (kk / 8) 32 + (row % 8) 4 + (kk % 8) / 2, the layout
+// of the forward kernel's f16 weight operands, and row r holds neuron neuron_of_column(r).
+__global__ void __launch_bounds__(512) prep_weights_kernel(const float* __restrict__ params,
                                                            float* __restrict__ wsplit) {
-  const int idx = blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx >= kWeightBlocks * 4096) return;
-  const int blk = idx >> 12, e = idx & 4095;
-  const int layer = blk % 3;
-  const int row = neuron_of_column(((e >> 9) << 3) | ((e >> 2) & 7));  // epilogue column order
-  const int k = (((e >> 5) & 15) << 2) | (e & 3);
-  const float* W = params + kHiddenBase + layer * kHiddenStride;
-  const float w = blk >= 3 ? W[k * kWidth + row] : W[row * kWidth + k];
-  const uint32_t hi = tc::to_tf32(w);
-  const uint32_t lo = tc::to_tf32(w - __uint_as_float(hi));
-  wsplit[blk * 8192 + e] = __uint_as_float(hi);
-  wsplit[blk * 8192 + 4096 + e] = __uint_as_float(lo);
+  __shared__ float wmax[16];
+  const int blk = blockIdx.x, tid = threadIdx.x;
+  const float* W = params + kHiddenBase + (blk % 3) * kHiddenStride;
+  float m = 0.0f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) m = fmaxf(m, fabsf(W[tid + 512 * j]));
+  m = warp_max_nonneg(m);
+  if ((tid & 31) == 0) wmax[tid >> 5] = m;
+  __syncthreads();
+  float mx = 0.0f;
+#pragma unroll
+  for (int w = 0; w < 16; ++w) mx = fmaxf(mx, wmax[w]);
+  const float tau = pow2_floor_ratio(4, mx);
+  uint32_t* out = reinterpret_cast<uint32_t*>(wsplit) + blk * (kLayerBytes / 4);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int w = tid + 512 * k;
+    const int n = neuron_of_column(((w >> 8) << 3) | ((w >> 2) & 7));
+    const int kk = (((w >> 5) & 7) << 3) | ((w & 3) << 1);
+    const float a = blk >= 3 ? W[kk * kWidth + n] : W[n * kWidth + kk];
+    const float b = blk >= 3 ? W[(kk + 1) * kWidth + n] : W[n * kWidth + kk + 1];
+    uint32_t hi, lo;
+    split_f16_pair_fast(a * tau, b * tau, hi, lo);
+    out[w] = hi;
+    out[kOperandBytes / 4 + w] = lo;
+  }
 }
 
 template <bool kPoisson>
@@ -547,10 +566,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
         rowp[kHiddenBase + l * kHiddenStride + tid + kThreads * j] = 0.0f;
   }
   if (tid == 0) {
-    for (uint32_t r = 0; r < kRing; ++r) {
-      mbar_init(bar_empty(r), 1);
-      mbar_init(bar_full(r), kWarps);
-    }
+    for (uint32_t r = 0; r < kRing; ++r) mbar_init(bar_full(r), kWarps);
 
     mbar_init(bar_dfull(), 1);
     mbar_init(bar_red(), kWarps);
@@ -566,11 +582,12 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
     tc::tmem_relinquish();
   }
   if (warp < kWarps) {
-    // Absolute row sums of W1 and W2 (rows warp + 16 i), fixed-order warp sums: the norms
-    // that bound the activations h_1, h_2 for the weight gradient's f16 operand scales.
-    float rs[8][2];
+    // Rows warp + 16 i of W1, W2, W3: the absolute row sums of W1 and W2 (fixed-order warp
+    // sums), the norms that bound the activations h_1, h_2 and so their f16 scales, and this
+    // warp's maximum |w| of each layer (its weight scale tau).
+    float rs[12][2];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
+    for (int i = 0; i < 12; ++i) {
       const int r = warp + kWarps * i;
       const float* wr = params + kHiddenBase + (r >> 6) * kHiddenStride + (r & 63) * kWidth;
       rs[i][0] = wr[lane];
@@ -581,6 +598,14 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
     for (int i = 0; i < 8; ++i) v[i] = fabsf(rs[i][0]) + fabsf(rs[i][1]);
     const float sum = warp_sum8(v);  // lane l: the sum of row warp + 16 ((l >> 2) & 7)
     if ((lane & 3) == 0) red[warp + kWarps * ((lane >> 2) & 7)] = sum;
+#pragma unroll
+    for (int l = 0; l < 3; ++l) {
+      float m = 0.0f;
+#pragma unroll
+      for (int i = 4 * l; i < 4 * l + 4; ++i) m = fmaxf(m, fmaxf(fabsf(rs[i][0]), fabsf(rs[i][1])));
+      m = warp_max_nonneg(m);
+      if (lane == 0) red[128 + kWarps * l + warp] = m;
+    }
   }
   tc::fence_before_sync();
   __syncthreads();
@@ -638,8 +663,18 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
         const float j = l == 0 ? sl[0][0] : l == 1 ? sl[1][0] : sl[2][0];
         const float lv = l == 0 ? sl[0][1] : l == 1 ? sl[1][1] : sl[2][1];
         const float sg = c == 0 ? 16384.0f : c == 3 ? lv : j;
-        sigw[lane] = sg;
-        sigw[12 + lane] = inv_pow2(sg);
+        sigw[kSig + lane] = sg;
+        sigw[kInvSig + lane] = inv_pow2(sg);
+      }
+      // tau_l maps max |W_l| to <= 16 (the same scale the pre-split weights carry)
+      float tl[3];
+#pragma unroll
+      for (int l = 0; l < 3; ++l)
+        tl[l] = pow2_floor_ratio(4, warp_max_nonneg(red[128 + kWarps * l + (lane & 15)]));
+      if (lane < 3) {
+        const float t = lane == 0 ? tl[0] : lane == 1 ? tl[1] : tl[2];
+        sigw[kTau + lane] = t;
+        sigw[kInvTau + lane] = inv_pow2(t);
       }
       __syncwarp();
     }
@@ -654,7 +689,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
       xs[tid] = x0;
       xs[kThreads + tid] = x1;
       if (static_cast<int64_t>(blockIdx.x) < tiles)
-        produce_layer0(x0, x1, small, chunk, tmem_warp, s, cx);
+        produce_layer0(x0, x1, small, sigw + kSig, chunk, tmem_warp, s);
     }
     float* const xn = reinterpret_cast<float*>(smem + kXnOff);  // the next tile's points
     for (int64_t tile = blockIdx.x; alive && tile < tiles; tile += gridDim.x, ++tile_count) {
@@ -676,11 +711,23 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
 #pragma unroll
         for (int c = 0; c < 4; ++c) tc::ld_x16(tmem_warp + 64u * c + 16u * s, d[c]);
         tc::wait_ld();
-        const float* bias = small + kSmB + 64 * g;
+        {
+          // D carries sigma_c of h_g times tau_g of W_{g+1}: both powers of 2, undone exactly
+          const float* bias = small + kSmB + 64 * g;
+          const float it = sigw[kInvTau + g];
+          const float uv = sigw[kInvSig + 4 * g] * it, uj = sigw[kInvSig + 4 * g + 1] * it;
+          const float ul = sigw[kInvSig + 4 * g + 3] * it;
 #pragma unroll
-        for (int i = 0; i < 16; ++i) d[0][i] += bias[16 * (i >> 2) + 4 * s + (i & 3)];
+          for (int i = 0; i < 16; ++i) {
+            d[0][i] = fmaf(d[0][i], uv, bias[16 * (i >> 2) + 4 * s + (i & 3)]);
+            d[1][i] *= uj;
+            d[2][i] *= uj;
+            d[3][i] *= ul;
+          }
+        }
         if (g < 2) {
           float* hj = hscratch + g * (4 * 16 * kThreads);  // h_{g+1}
+          const float* sg = sigw + kSig + 4 * (g + 1);     // its f16 scales
 #pragma unroll
           for (int a = 0; a < kChunks; ++a) {
             float h[4][4];
@@ -690,9 +737,12 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
               tanh_jet_fast(d[0][i], d[1][i], d[2][i], d[3][i], h[0][t], h[1][t], h[2][t],
                             h[3][t]);
 #pragma unroll
-              for (int c = 0; c < 4; ++c) hj[(c * 16 + i) * kThreads] = h[c][t];
+              for (int c = 0; c < 4; ++c) {
+                hj[(c * 16 + i) * kThreads] = h[c][t];
+                h[c][t] *= sg[c];
+              }
             }
-            produce_chunk(chunk++, h, tmem_warp, s, cx);
+            produce_chunk(chunk++, h, tmem_warp, s);
           }
         }
       }
@@ -781,43 +831,59 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
 #pragma unroll 1
       for (int l = 3; l >= 1; --l) {
         const int g = 6 - l;
-        // The f16 scale of zbar_l for this tile and point half: z~_c = zbar_c S / sigma_c pairs
-        // with h~_c = h_c sigma_c, so every component's product carries the same factor S,
-        // chosen so that max |z~| <= 2^14. This warp's maximum of |zbar_c| / sigma_c first.
-        const float* sg = sigw + 4 * (l - 1);         // sigma of h_{l-1}: v, d/dx, d/dy, L
-        const float* isg = sigw + 12 + 4 * (l - 1);  // 1 / sigma
+        // f16 scales of zbar_l, per tile and point half (a point's row of either GEMM stays in
+        // its half): S_c maps the half's max |zbar_c| to <= 2^14 for the input adjoint (one
+        // GEMM per component), and zs maps max_c |zbar_c| / sigma_c to <= 2^14 for the weight
+        // gradient, whose operands z~_c = zbar_c zs / sigma_c pair with h~_c = h_c sigma_c, so
+        // that every component's product carries the same factor zs. This warp's maxima first.
+        const float* sg = sigw + kSig + 4 * (l - 1);      // sigma of h_{l-1}: v, d/dx, d/dy, L
+        const float* isg = sigw + kInvSig + 4 * (l - 1);  // 1 / sigma
         {
+          float* zw = zmax + kZmaxFloats * warp;
           float zm = 0.0f;
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
             float mc = 0.0f;
 #pragma unroll
             for (int i = 0; i < 16; ++i) mc = fmaxf(mc, fabsf(d[c][i]));
+            mc = warp_max_nonneg(mc);
             zm = fmaxf(zm, mc * isg[c]);
+            if (lane == 0) zw[c] = mc;
           }
-          const uint32_t wm = __reduce_max_sync(0xffffffffu, __float_as_uint(zm));
-          if (lane == 0) zmax[warp] = __uint_as_float(wm);
+          if (lane == 0) zw[4] = zm;
         }
-        // zbar_l -> ring (input-adjoint GEMM g)
-#pragma unroll
-        for (int a = 0; a < kChunks; ++a) {
-          float z[4][4];
-#pragma unroll
-          for (int t = 0; t < 4; ++t)
-#pragma unroll
-            for (int c = 0; c < 4; ++c) z[c][t] = d[c][4 * a + t];
-          produce_chunk(chunk++, z, tmem_warp, s, cx);
-        }
-
-        // The half's scale from its 8 warps' maxima (written before the chunks above).
         half_barrier(half);
-        float zs;
         {
-          float hm = 0.0f;
+          float hm[5] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-          for (int w4 = 0; w4 < 4; ++w4)
-            hm = fmaxf(hm, fmaxf(zmax[2 * half + 4 * w4], zmax[2 * half + 1 + 4 * w4]));
-          zs = pow2_floor_ratio(14, hm);
+          for (int w8 = 0; w8 < 8; ++w8) {
+            const float* zw = zmax + kZmaxFloats * (2 * half + (w8 & 1) + 4 * (w8 >> 1));
+#pragma unroll
+            for (int k = 0; k < 5; ++k) hm[k] = fmaxf(hm[k], zw[k]);
+          }
+          const float zs = pow2_floor_ratio(14, hm[4]);
+          const float itau = sigw[kInvTau + (l - 1)];
+          // d becomes zbar_l times S_c (exact: powers of 2) -> ring (input-adjoint GEMM g)
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const float sc = pow2_floor_ratio(14, hm[c]), isc = inv_pow2(sc);
+            if (lane == 0) {
+              sigw[kStg + c] = zs * isg[c] * isc;
+              sigw[kIsc + c] = isc * itau;
+            }
+#pragma unroll
+            for (int i = 0; i < 16; ++i) d[c][i] *= sc;
+          }
+          __syncwarp();
+#pragma unroll
+          for (int a = 0; a < kChunks; ++a) {
+            float z[4][4];
+#pragma unroll
+            for (int t = 0; t < 4; ++t)
+#pragma unroll
+              for (int c = 0; c < 4; ++c) z[c][t] = d[c][4 * a + t];
+            produce_chunk(chunk++, z, tmem_warp, s);
+          }
         }
         // weight gradient dW_l: per jet component, stage zbar_l and h_{l-1} (f16 hi/lo, scaled)
         // for the tile's 128 points and let one warp issue the MMAs. Unrolled, so that the
@@ -842,7 +908,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
             }
           }
           if (c > 0) warp_wait(bar_dwdone(half), (dw_issued - 1u) & 1u);  // buffer free again
-          stage_f16_rows(stage_at + kStageA, s, d[c], zs * isg[c]);
+          stage_f16_rows(stage_at + kStageA, s, d[c], sigw[kStg + c]);
           stage_f16_rows(stage_at + kStageB, s, hv, sg[c]);
           tc::fence_proxy_async_smem();
           half_barrier(half);
@@ -879,10 +945,11 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
           for (int hh = 0; hh < 2; ++hh) {
             float hm = 0.0f;
 #pragma unroll
-            for (int w4 = 0; w4 < 4; ++w4)
-              hm = fmaxf(hm, fmaxf(zmax[2 * hh + 4 * w4], zmax[2 * hh + 1 + 4 * w4]));
+            for (int w8 = 0; w8 < 8; ++w8)
+              hm = fmaxf(hm, zmax[kZmaxFloats * (2 * hh + (w8 & 1) + 4 * (w8 >> 1)) + 4]);
             inv[hh] = inv_pow2(pow2_floor_ratio(14, hm));
           }
+
           float v[16], w[16];
           tc::ld_x16(tmem_warp + kDwCol + 16u * s, v);
           tc::ld_x16(tmem_warp + kDwCol + 64u + 16u * s, w);
@@ -912,17 +979,22 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
           if (!(alive = barrier_ok())) break;
         }
 
-        // input adjoint hbar_{l-1} = zbar_l W_l (GEMM g), then zbar_{l-1}
-
+        // input adjoint hbar_{l-1} = zbar_l W_l (GEMM g; D carries S_c tau), then zbar_{l-1}
         warp_wait(bar_dfull(), mlayer & 1u);
         ++mlayer;
         tc::fence_after_sync();
 #pragma unroll
         for (int c = 0; c < 4; ++c) tc::ld_x16(tmem_warp + 64u * c + 16u * s, d[c]);
         tc::wait_ld();
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const float isc = sigw[kIsc + c];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) d[c][i] *= isc;
+        }
         if (l == 1 && has_next) {  // GEMM 0 of the next tile may now overwrite D
           prefetch_wait();
-          produce_layer0(xn[tid], xn[kThreads + tid], small, chunk, tmem_warp, s, cx);
+          produce_layer0(xn[tid], xn[kThreads + tid], small, sigw + kSig, chunk, tmem_warp, s);
         }
         if (l > 1) {
 #pragma unroll
@@ -1075,7 +1147,7 @@ cudaError_t launch_backward_tc(const PointSets& points, const float* params,
   float* wsplit = workspace;
   float* partials = wsplit + kWeightBlocks * (kLayerBytes / 4);
   float* scratch = partials + static_cast<size_t>(grid) * kRowStride;
-  prep_weights_kernel<<<(kWeightBlocks * 4096 + 255) / 256, 256, 0, stream>>>(params, wsplit);
+  prep_weights_kernel<<<kWeightBlocks, 512, 0, stream>>>(params, wsplit);
   if (poisson) {
     backward_tc_kernel<true><<<grid, kBlockThreads, kSmemBytes, stream>>>(
         ps, params, wsplit, nullptr, nullptr, grad_coords, lap_out, partials, scratch, tiles,
