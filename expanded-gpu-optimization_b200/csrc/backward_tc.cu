@@ -343,6 +343,27 @@ __device__ __forceinline__ void adjoint_h(float a, float hj0, float hj1, float h
   g1 = z1;
 }
 
+// Component c of h_{l-1} for this thread's 16 neuron slots: from the scratch (l >= 2) or,
+// for h_0, recomputed from the point.
+__device__ __forceinline__ void h_component(float (&hv)[16], int l, int c, const float* hsrc,
+                                            const float* small, const float* xs, int tid,
+                                            int s) {
+  if (l > 1) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) hv[i] = hsrc[(c * 16 + i) * kThreads];
+  } else {
+    const float x0 = xs[tid], x1 = xs[kThreads + tid];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int o = 16 * (i >> 2) + 4 * s + (i & 3);
+      const float w0 = small[kSmW0 + 2 * o], w1 = small[kSmW0 + 2 * o + 1];
+      float v, j0, j1, lv;
+      tanh_jet_fast(fmaf(w0, x0, fmaf(w1, x1, small[kSmB0 + o])), w0, w1, 0.0f, v, j0, j1, lv);
+      hv[i] = c == 0 ? v : c == 1 ? j0 : c == 2 ? j1 : lv;
+    }
+  }
+}
+
 // The 4 weight-gradient MMAs of one jet component for one point half (M = 128, N = 128,
 // K = 16 points each, f16, both operands MN-major) into that half's accumulator. Issued by
 // one converged warp of the half, then committed to the half's barrier.
@@ -838,6 +859,7 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
         // that every component's product carries the same factor zs. This warp's maxima first.
         const float* sg = sigw + kSig + 4 * (l - 1);      // sigma of h_{l-1}: v, d/dx, d/dy, L
         const float* isg = sigw + kInvSig + 4 * (l - 1);  // 1 / sigma
+        const float* hsrc = hscratch + (l == 3 ? 4 * 16 * kThreads : 0);  // h_{l-1} (l >= 2)
         {
           float* zw = zmax + kZmaxFloats * warp;
           float zm = 0.0f;
@@ -854,12 +876,13 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
         }
         half_barrier(half);
         {
-          float hm[5] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+          // lane k < 8 reads warp k of the half; the maxima over the lanes by redux
+          float hm[5];
+          {
+            const float* zw =
+                zmax + kZmaxFloats * (2 * half + (lane & 1) + 4 * ((lane >> 1) & 3));
 #pragma unroll
-          for (int w8 = 0; w8 < 8; ++w8) {
-            const float* zw = zmax + kZmaxFloats * (2 * half + (w8 & 1) + 4 * (w8 >> 1));
-#pragma unroll
-            for (int k = 0; k < 5; ++k) hm[k] = fmaxf(hm[k], zw[k]);
+            for (int k = 0; k < 5; ++k) hm[k] = warp_max_nonneg(lane < 8 ? zw[k] : 0.0f);
           }
           const float zs = pow2_floor_ratio(14, hm[4]);
           const float itau = sigw[kInvTau + (l - 1)];
@@ -887,29 +910,17 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
         }
         // weight gradient dW_l: per jet component, stage zbar_l and h_{l-1} (f16 hi/lo, scaled)
         // for the tile's 128 points and let one warp issue the MMAs. Unrolled, so that the
-        // registers of component c of zbar_l are free once its round is staged.
-        const float* hsrc = hscratch + (l == 3 ? 4 * 16 * kThreads : 0);  // h_{l-1} (l >= 2)
+        // registers of component c of zbar_l are free once its round is staged; component
+        // c + 1 of h_{l-1} is read right after component c is staged, so its latency overlaps
+        // the round's barrier, issue and commit wait.
+        float hv[16];
+        h_component(hv, l, 0, hsrc, small, xs, tid, s);
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-          float hv[16];
-          if (l > 1) {
-#pragma unroll
-            for (int i = 0; i < 16; ++i) hv[i] = hsrc[(c * 16 + i) * kThreads];
-          } else {
-            const float x0 = xs[tid], x1 = xs[kThreads + tid];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const int o = 16 * (i >> 2) + 4 * s + (i & 3);
-              const float w0 = small[kSmW0 + 2 * o], w1 = small[kSmW0 + 2 * o + 1];
-              float v, j0, j1, lv;
-              tanh_jet_fast(fmaf(w0, x0, fmaf(w1, x1, small[kSmB0 + o])), w0, w1, 0.0f, v, j0,
-                            j1, lv);
-              hv[i] = c == 0 ? v : c == 1 ? j0 : c == 2 ? j1 : lv;
-            }
-          }
           if (c > 0) warp_wait(bar_dwdone(half), (dw_issued - 1u) & 1u);  // buffer free again
           stage_f16_rows(stage_at + kStageA, s, d[c], sigw[kStg + c]);
           stage_f16_rows(stage_at + kStageB, s, hv, sg[c]);
+          if (c < 3) h_component(hv, l, c + 1, hsrc, small, xs, tid, s);
           tc::fence_proxy_async_smem();
           half_barrier(half);
           if (s == 0 && (q & 1) == 0) {  // warp 2 * half issues for its half
@@ -940,14 +951,13 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
           float* fb = reinterpret_cast<float*>(smem + kStageOff);
           // columns i (h_hi) and 64 + i (h_lo) of this warp's row, in both halves' accumulators,
           // each half divided by its scale (exact powers of 2)
-          float inv[2];
+          float inv[2];  // lane k < 16 reads warp k's maximum
+          {
+            const float m = lane < 16 ? zmax[kZmaxFloats * lane + 4] : 0.0f;
+            const bool h1 = (lane & 2) != 0;  // warp k is in half (k & 3) >> 1
 #pragma unroll
-          for (int hh = 0; hh < 2; ++hh) {
-            float hm = 0.0f;
-#pragma unroll
-            for (int w8 = 0; w8 < 8; ++w8)
-              hm = fmaxf(hm, zmax[kZmaxFloats * (2 * hh + (w8 & 1) + 4 * (w8 >> 1)) + 4]);
-            inv[hh] = inv_pow2(pow2_floor_ratio(14, hm));
+            for (int hh = 0; hh < 2; ++hh)
+              inv[hh] = inv_pow2(pow2_floor_ratio(14, warp_max_nonneg(h1 == (hh == 1) ? m : 0.0f)));
           }
 
           float v[16], w[16];
