@@ -60,6 +60,9 @@ namespace fhb {
 namespace {
 
 constexpr int kTile = 128;
+// CTAs per cluster: the partial-gradient rows are summed over a cluster through distributed
+// shared memory before they reach global memory (one row per cluster).
+constexpr int kCluster = 2;
 constexpr int kWarps = 16;
 constexpr int kThreads = kWarps * 32;          // epilogue threads
 constexpr int kMmaWarp = kWarps;                 // warp 16: first warp of the MMA warpgroup
@@ -130,7 +133,11 @@ constexpr int kStg = 32, kIsc = 36;
 constexpr int kSigFloats = 40;
 constexpr int kZmaxOff = kDwScaleOff + kWarps * kSigFloats * 4;
 constexpr int kZmaxFloats = 8;
-constexpr int kBarOff = kZmaxOff + kWarps * kZmaxFloats * 4;  // mbarriers
+// This CTA's hidden-layer weight gradients (3 x 4096, accumulator order e = 64 r + n of
+// layer l at 4096 l + e), summed over its tiles; reduced over the cluster at the end.
+constexpr int kHiddenGrads = 3 * kWidth * kWidth;
+constexpr int kRowsOff = kZmaxOff + kWarps * kZmaxFloats * 4;
+constexpr int kBarOff = kRowsOff + kHiddenGrads * 4;         // mbarriers
 constexpr int kNumBars = 10;   // dfull red wfull[2] dwdone[2] full[4]
 constexpr int kMiscOff = kBarOff + kNumBars * 8;              // TMEM base, abort flag, status
 constexpr int kSmemBytes = kMiscOff + 16;
@@ -500,8 +507,27 @@ __device__ __forceinline__ void store_part16(float* part, int kind, int q, int s
   }
 }
 
-__device__ __forceinline__ void red_add(float* addr, float v) {
-  asm volatile("red.global.add.f32 [%0], %1;" ::"l"(addr), "f"(v) : "memory");
+// Cluster helpers: this CTA's rank, a barrier over every thread of the cluster (release /
+// acquire: shared-memory writes before it are visible to the cluster's reads after it), the
+// shared::cluster address of a shared::cta address in CTA `rank`, and a load through it.
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;"
+               ::: "memory");
+}
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float ld_dsmem_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
 }
 
 // Pre-split weights for the tensor-core backward: six K-major canonical f16 operands, hi then
@@ -541,7 +567,7 @@ __global__ void __launch_bounds__(512) prep_weights_kernel(const float* __restri
 }
 
 template <bool kPoisson>
-__global__ void __launch_bounds__(kBlockThreads, 1)
+__global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kBlockThreads, 1)
     backward_tc_kernel(const PointSets ps, const float* __restrict__ params,
                        const float* __restrict__ wsplit, const float* __restrict__ grad_u,
                        const float* __restrict__ grad_lap, float* __restrict__ grad_coords,
@@ -559,7 +585,6 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
-  float* const rowp = partials + static_cast<int64_t>(blockIdx.x) * kRowStride;
 
   // ---- set-up ----
   // The first tile's point, requested first: its latency overlaps the set-up below.
@@ -577,15 +602,10 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
     else if (i == kSmBout) v = params[kOutBase + kWidth];               // b_out
     small[i] = v;
   }
-  // The hidden-layer weight gradients are accumulated in place in this CTA's partial row
-  // (red.global.add by the thread that owns the entry, so the order is fixed).
-  if (tid < kThreads) {
-#pragma unroll
-    for (int l = 0; l < 3; ++l)
-#pragma unroll
-      for (int j = 0; j < 8; ++j)
-        rowp[kHiddenBase + l * kHiddenStride + tid + kThreads * j] = 0.0f;
-  }
+  // The hidden-layer weight gradients are accumulated in shared memory, each entry by the
+  // one thread that owns it, so the order is fixed.
+  float* const hgrad = reinterpret_cast<float*>(smem + kRowsOff);
+  for (int i = tid; i < kHiddenGrads; i += kBlockThreads) hgrad[i] = 0.0f;
   if (tid == 0) {
     for (uint32_t r = 0; r < kRing; ++r) mbar_init(bar_full(r), kWarps);
 
@@ -978,13 +998,13 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
           for (int k = 0; k < 16; ++k) fb[row * kFlushStride + 16 * s + k] = v[k];
           tc::fence_before_sync();
           if (!(alive = barrier_ok())) break;
-          float* wrow = rowp + kHiddenBase + (l - 1) * kHiddenStride;
+          float* wrow = hgrad + (l - 1) * (kWidth * kWidth);
           // accumulator row r / column n hold neuron neuron_of_column(r % 64) / (n % 64)
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
             const int e = tid + kThreads * j;
             const int ro = neuron_of_column(e >> 6), ci = neuron_of_column(e & 63);
-            red_add(wrow + e, fb[ro * kFlushStride + ci] + fb[(64 + ro) * kFlushStride + ci]);
+            wrow[e] += fb[ro * kFlushStride + ci] + fb[(64 + ro) * kFlushStride + ci];
           }
           if (!(alive = barrier_ok())) break;
         }
@@ -1097,22 +1117,59 @@ for (int c = 0; c < 4; ++c) h[c][t] = hsrc[(c * 16 + 4 * a + t) * kThreads];
     tc::fence_after_sync();
     tc::tmem_dealloc(cx.tmem, kTmemCols);
   }
-  if (aborted) return;
-
-  // ---- the rest of this CTA's partial-gradient row (hidden weights are already there) ----
-  for (int k = tid; k < 2 * kWidth; k += kThreads) rowp[k] = grad[kGW0 + k];
-  if (tid < kWidth) {
-    rowp[kB0 + tid] = grad[kGBias + tid];
+  // ---- the cluster's partial-gradient row ----
+  // Every CTA of the cluster takes both cluster barriers, aborted or not (a peer's abort
+  // shows in the status word). CTA rank k writes its share of the columns, each the sum over
+  // the cluster's CTAs in rank order, read through distributed shared memory.
+  cluster_sync();  // the cluster's gradients are complete and visible
+  if (!aborted) {
+    const uint32_t rank = cluster_ctarank();
+    float* const crow = partials + static_cast<int64_t>(blockIdx.x / kCluster) * kRowStride;
+    uint32_t hg[kCluster], gr[kCluster];
 #pragma unroll
-    for (int l = 1; l < 4; ++l)
-      rowp[kHiddenBase + (l - 1) * kHiddenStride + kWidth * kWidth + tid] =
-          grad[kGBias + l * kWidth + tid];
-    rowp[kOutBase + tid] = grad[kGWout + tid];
+    for (int r = 0; r < kCluster; ++r) {
+      hg[r] = mapa_shared(smem_u32(hgrad), static_cast<uint32_t>(r));
+      gr[r] = mapa_shared(smem_u32(grad), static_cast<uint32_t>(r));
+    }
+    constexpr int kShare = kHiddenGrads / kCluster;
+    for (int i = tid; i < kShare; i += kBlockThreads) {
+      const int e = static_cast<int>(rank) * kShare + i;
+      float v = ld_dsmem_f32(hg[0] + 4u * e);
+#pragma unroll
+      for (int r = 1; r < kCluster; ++r) v += ld_dsmem_f32(hg[r] + 4u * e);
+      crow[kHiddenBase + (e >> 12) * kHiddenStride + (e & 4095)] = v;
+    }
+    if (rank == 0) {  // W0, b0, b1..b3, w_out, b_out and the loss
+      int gi = -1, col = 0;
+      if (tid < 2 * kWidth) {
+        gi = kGW0 + tid;
+        col = tid;
+      } else if (tid < 3 * kWidth) {
+        gi = kGBias + (tid - 2 * kWidth);
+        col = kB0 + (tid - 2 * kWidth);
+      } else if (tid < 6 * kWidth) {
+        const int l = (tid - 3 * kWidth) >> 6, o = (tid - 3 * kWidth) & 63;
+        gi = kGBias + (l + 1) * kWidth + o;
+        col = kHiddenBase + l * kHiddenStride + kWidth * kWidth + o;
+      } else if (tid < 7 * kWidth) {
+        gi = kGWout + (tid - 6 * kWidth);
+        col = kOutBase + (tid - 6 * kWidth);
+      } else if (tid == 7 * kWidth) {
+        gi = kGBout;
+        col = kOutBase + kWidth;
+      } else if (tid == 7 * kWidth + 1) {
+        gi = kGLoss;
+        col = kLossColumn;
+      }
+      if (gi >= 0) {
+        float v = ld_dsmem_f32(gr[0] + 4u * gi);
+#pragma unroll
+        for (int r = 1; r < kCluster; ++r) v += ld_dsmem_f32(gr[r] + 4u * gi);
+        crow[col] = v;
+      }
+    }
   }
-  if (tid == 0) {
-    rowp[kOutBase + kWidth] = grad[kGBout];
-    rowp[kLossColumn] = grad[kGLoss];
-  }
+  cluster_sync();  // no CTA leaves while a peer still reads its shared memory
 }
 
 template <bool kPoisson>
@@ -1136,7 +1193,12 @@ cudaError_t prepare_backward_tc() {
 
 int backward_tc_grid(int64_t n, int64_t nb, const DeviceInfo& dev) {
   const int64_t tiles = (n + kTile - 1) / kTile + (nb + kTile - 1) / kTile;
-  return static_cast<int>(std::min<int64_t>(tiles, dev.sms));
+  const int64_t whole = (tiles + kCluster - 1) / kCluster * kCluster;  // whole clusters
+  return static_cast<int>(std::min<int64_t>(whole, dev.sms / kCluster * kCluster));
+}
+
+int backward_tc_rows(int64_t n, int64_t nb, const DeviceInfo& dev) {
+  return backward_tc_grid(n, nb, dev) / kCluster;
 }
 
 size_t backward_tc_workspace_bytes(int64_t n, int64_t nb, const DeviceInfo& dev) {

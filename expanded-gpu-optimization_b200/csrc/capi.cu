@@ -233,7 +233,7 @@ static cudaError_t launch_gradient_kernel(const fhb::PointSets& ps, const float*
   // (tanh's derivatives are functions of tanh); other activations run the FP32 kernel.
   if (tensor_core && activation == FHB_ACTIVATION_TANH) {
     *partials = fhb::backward_tc_partials(ws);
-    *rows = fhb::backward_tc_grid(ps.n, ps.nb, dev);
+    *rows = fhb::backward_tc_rows(ps.n, ps.nb, dev);
     return fhb::launch_backward_tc(ps, params, grad_u, grad_lap, grad_coords, lap_out, ws,
                                    poisson, dev, stream);
   }

@@ -175,6 +175,8 @@ cudaError_t launch_reduce_rows(const float* partials, int rows, float* grad_para
 // ---- backward_tc.cu ----
 cudaError_t prepare_backward_tc();
 int backward_tc_grid(int64_t n, int64_t nb, const DeviceInfo& dev);
+// Partial-gradient rows the tensor-core backward leaves (one per cluster of CTAs).
+int backward_tc_rows(int64_t n, int64_t nb, const DeviceInfo& dev);
 // Workspace: pre-split weights, one partial-gradient row per CTA, per-CTA L2 scratch.
 size_t backward_tc_workspace_bytes(int64_t n, int64_t nb, const DeviceInfo& dev);
 float* backward_tc_partials(float* workspace);
