@@ -257,9 +257,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           float lap = 0.0f;
 #pragma unroll
           for (int w = 0; w < kWarps; ++w) lap += red[w * kTile + lane];
-          // f = -2 pi^2 sin(pi x) sin(pi y)  (src/fused_hoad/problems/poisson.py:29-39)
+          // f = -2 pi^2 sin(pi x) sin(pi y)  (src/fused_hoad/problems/poisson.py:29-39); sinpif
+          // needs no large-argument reduction (no local-memory path)
           const float pi = 3.14159265358979323846f;
-          const float f = -2.0f * pi * pi * (sinf(pi * x0) * sinf(pi * x1));
+          const float f = -2.0f * pi * pi * (sinpif(x0) * sinpif(x1));
           const float r = active ? lap - f : 0.0f;
           gu = 0.0f;
           gl = 2.0f * r * ps.inv_total;

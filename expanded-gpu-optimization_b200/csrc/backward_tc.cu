@@ -541,9 +541,22 @@ __global__ void __launch_bounds__(512) prep_weights_kernel(const float* __restri
   __shared__ float wmax[16];
   const int blk = blockIdx.x, tid = threadIdx.x;
   const float* W = params + kHiddenBase + (blk % 3) * kHiddenStride;
+  // The block's 2048 pairs cover every element of W_l once: their maximum is tau's input,
+  // so all loads are issued at once (one memory round trip).
+  float a[4], b[4];
+  int word[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int w = tid + 512 * k;
+    const int n = neuron_of_column(((w >> 8) << 3) | ((w >> 2) & 7));
+    const int kk = (((w >> 5) & 7) << 3) | ((w & 3) << 1);
+    a[k] = blk >= 3 ? W[kk * kWidth + n] : W[n * kWidth + kk];
+    b[k] = blk >= 3 ? W[(kk + 1) * kWidth + n] : W[n * kWidth + kk + 1];
+    word[k] = w;
+  }
   float m = 0.0f;
 #pragma unroll
-  for (int j = 0; j < 8; ++j) m = fmaxf(m, fabsf(W[tid + 512 * j]));
+  for (int k = 0; k < 4; ++k) m = fmaxf(m, fmaxf(fabsf(a[k]), fabsf(b[k])));
   m = warp_max_nonneg(m);
   if ((tid & 31) == 0) wmax[tid >> 5] = m;
   __syncthreads();
@@ -554,15 +567,10 @@ __global__ void __launch_bounds__(512) prep_weights_kernel(const float* __restri
   uint32_t* out = reinterpret_cast<uint32_t*>(wsplit) + blk * (kLayerBytes / 4);
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
-    const int w = tid + 512 * k;
-    const int n = neuron_of_column(((w >> 8) << 3) | ((w >> 2) & 7));
-    const int kk = (((w >> 5) & 7) << 3) | ((w & 3) << 1);
-    const float a = blk >= 3 ? W[kk * kWidth + n] : W[n * kWidth + kk];
-    const float b = blk >= 3 ? W[(kk + 1) * kWidth + n] : W[n * kWidth + kk + 1];
     uint32_t hi, lo;
-    split_f16_pair_fast(a * tau, b * tau, hi, lo);
-    out[w] = hi;
-    out[kOperandBytes / 4 + w] = lo;
+    split_f16_pair_fast(a[k] * tau, b[k] * tau, hi, lo);
+    out[word[k]] = hi;
+    out[kOperandBytes / 4 + word[k]] = lo;
   }
 }
 
@@ -810,10 +818,11 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kBlockThreads
         if (kPoisson) {
           float term;  // this point's loss term
           if (!btile) {
-            // f = -2 pi^2 sin(pi x) sin(pi y)  (src/fused_hoad/problems/poisson.py:29-39)
+            // f = -2 pi^2 sin(pi x) sin(pi y)  (src/fused_hoad/problems/poisson.py:29-39); sinpif
+            // needs no large-argument reduction (no local-memory path)
             const float pi = 3.14159265358979323846f;
             const float f =
-                -2.0f * pi * pi * (sinf(pi * xs[tid]) * sinf(pi * xs[kThreads + tid]));
+                -2.0f * pi * pi * (sinpif(xs[tid]) * sinpif(xs[kThreads + tid]));
             const float r = active ? lap - f : 0.0f;
             gu = 0.0f;
             gl = 2.0f * r * ps.inv_total;
