@@ -102,7 +102,7 @@ constexpr int kScratchFloats = 2 * 4 * 16 * kThreads;
 constexpr uint32_t kDwLbo = 128, kDwSbo = 1024;
 constexpr int kStageA = 0, kStageB = 16384;
 constexpr int kStageBytes = 32768;
-constexpr int kFlushStride = 65;                 // [128 rows][65] floats when emptying TMEM
+constexpr int kFlushStride = 65;                 // [64 rows][65] floats: the z_hi rows when emptying TMEM
 
 // Shared memory (bytes).
 constexpr int kWOff = 0;                                      // 2 weight slots
@@ -133,8 +133,9 @@ constexpr int kStg = 32, kIsc = 36;
 constexpr int kSigFloats = 40;
 constexpr int kZmaxOff = kDwScaleOff + kWarps * kSigFloats * 4;
 constexpr int kZmaxFloats = 8;
-// This CTA's hidden-layer weight gradients (3 x 4096, accumulator order e = 64 r + n of
-// layer l at 4096 l + e), summed over its tiles; reduced over the cluster at the end.
+// This CTA's hidden-layer weight gradients (3 x 4096; layer l's entry for accumulator
+// column c and row r at 4096 l + 64 c + r), summed over its tiles; reduced over the cluster
+// at the end.
 constexpr int kHiddenGrads = 3 * kWidth * kWidth;
 constexpr int kRowsOff = kZmaxOff + kWarps * kZmaxFloats * 4;
 constexpr int kBarOff = kRowsOff + kHiddenGrads * 4;         // mbarriers
@@ -144,7 +145,7 @@ constexpr int kSmemBytes = kMiscOff + 16;
 static_assert(kSmemBytes <= 227 * 1024, "shared memory layout overflow");
 static_assert(kStageOff % 1024 == 0 && kBarOff % 8 == 0 && (kMiscOff + 8) % 8 == 0,
               "alignment");
-static_assert(kTile * kFlushStride * 4 <= 2 * kStageBytes, "flush buffer fits the staging buffers");
+static_assert(64 * kFlushStride * 4 <= kStageBytes, "flush buffer fits a staging buffer");
 
 // Shared-memory objects are addressed as constant offsets of the dynamic shared-memory base
 // (no pointers kept in registers across the tile loop).
@@ -967,8 +968,13 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kBlockThreads
           ++dw_issued;
         }
 
-        // empty the accumulator into this CTA's partial row: hi and lo halves summed in shared
-        // memory (staging buffer 0), one owner thread per entry
+        // Empty the accumulators into the gradient block. A thread holds row r of the
+        // accumulator, columns 16s..16s+15, each the sum over the h_hi and h_lo columns of both
+        // halves' accumulators, each half divided by its scale (exact powers of 2). Row r < 64
+        // is z_hi times h; row r + 64 is z_lo times h of the same neuron. The rows < 64 go
+        // through shared memory (half 1's staging buffer) to the thread of row r + 64, which adds
+        // hi + lo into the entry it owns: column-major in accumulator order,
+        // hgrad[4096 (l - 1) + 64 c + r] for column c and row r.
         // Both halves first pass this barrier: each half has then waited for its round-2
         // commit, so the parity wait below can only mean round 3 (without it, a half that is
         // two rounds behind would satisfy the wait with its round-1 phase).
@@ -977,9 +983,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kBlockThreads
         warp_wait(bar_dwdone(1), (dw_issued - 1u) & 1u);
         tc::fence_after_sync();
         {
-          float* fb = reinterpret_cast<float*>(smem + kStageOff);
-          // columns i (h_hi) and 64 + i (h_lo) of this warp's row, in both halves' accumulators,
-          // each half divided by its scale (exact powers of 2)
+          float* fb = reinterpret_cast<float*>(smem + kStageOff + kStageBytes);  // [64][65]
           float inv[2];  // lane k < 16 reads warp k's maximum
           {
             const float m = lane < 16 ? zmax[kZmaxFloats * lane + 4] : 0.0f;
@@ -1003,19 +1007,21 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kBlockThreads
           tc::wait_ld();
 #pragma unroll
           for (int k = 0; k < 16; ++k) v[k] = fmaf(w[k], inv[1], v[k]);
+          if (row < 64) {
 #pragma unroll
-          for (int k = 0; k < 16; ++k) fb[row * kFlushStride + 16 * s + k] = v[k];
+            for (int k = 0; k < 16; ++k) fb[row * kFlushStride + 16 * s + k] = v[k];
+          }
+          // Every warp's accumulator loads are complete past this barrier (the ring's columns
+          // take chunks again afterwards); half 1 reads its staging buffer before its next
+          // half barrier, after which it stages there again.
           tc::fence_before_sync();
           if (!(alive = barrier_ok())) break;
-          float* wrow = hgrad + (l - 1) * (kWidth * kWidth);
-          // accumulator row r / column n hold neuron neuron_of_column(r % 64) / (n % 64)
+          if (row >= 64) {
+            float* wcol = hgrad + (l - 1) * (kWidth * kWidth) + (row - 64);
+            const float* src = fb + (row - 64) * kFlushStride + 16 * s;
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const int e = tid + kThreads * j;
-            const int ro = neuron_of_column(e >> 6), ci = neuron_of_column(e & 63);
-            wrow[e] += fb[ro * kFlushStride + ci] + fb[(64 + ro) * kFlushStride + ci];
+            for (int k = 0; k < 16; ++k) wcol[(16 * s + k) * kWidth] += src[k] + v[k];
           }
-          if (!(alive = barrier_ok())) break;
         }
 
         // input adjoint hbar_{l-1} = zbar_l W_l (GEMM g; D carries S_c tau), then zbar_{l-1}
@@ -1140,13 +1146,16 @@ for (int c = 0; c < 4; ++c) h[c][t] = hsrc[(c * 16 + 4 * a + t) * kThreads];
       hg[r] = mapa_shared(smem_u32(hgrad), static_cast<uint32_t>(r));
       gr[r] = mapa_shared(smem_u32(grad), static_cast<uint32_t>(r));
     }
+    // gradient-block entry e = 4096 l + 64 c + r: accumulator column c (input neuron
+    // neuron_of_column(c)) and row r (output neuron neuron_of_column(r)) of layer l + 1
     constexpr int kShare = kHiddenGrads / kCluster;
     for (int i = tid; i < kShare; i += kBlockThreads) {
       const int e = static_cast<int>(rank) * kShare + i;
       float v = ld_dsmem_f32(hg[0] + 4u * e);
 #pragma unroll
       for (int r = 1; r < kCluster; ++r) v += ld_dsmem_f32(hg[r] + 4u * e);
-      crow[kHiddenBase + (e >> 12) * kHiddenStride + (e & 4095)] = v;
+      const int o = neuron_of_column(e & 63), n = neuron_of_column((e >> 6) & 63);
+      crow[kHiddenBase + (e >> 12) * kHiddenStride + o * kWidth + n] = v;
     }
     if (rank == 0) {  // W0, b0, b1..b3, w_out, b_out and the loss
       int gi = -1, col = 0;
