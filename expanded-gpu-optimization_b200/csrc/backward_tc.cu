@@ -1111,7 +1111,9 @@ for (int c = 0; c < 4; ++c) h[c][t] = hsrc[(c * 16 + 4 * a + t) * kThreads];
           grad[kGLoss] += ((part[kPLoss] + part[kPLoss + 1]) + part[kPLoss + 2]) + part[kPLoss + 3];
         grad[kGBout] += ((part[kPBout] + part[kPBout + 1]) + part[kPBout + 2]) + part[kPBout + 3];
       }
-      if (!(alive = barrier_ok())) break;
+      // No barrier before the next tile: its first writes of `part`, `red` and `grad` come
+      // after its GEMM 2, whose chunks every warp produces only after finishing the reads
+      // above; xs is this thread's own.
       if (has_next) {  // this thread's own entries: no other thread reads them
         xs[tid] = xn[tid];
         xs[kThreads + tid] = xn[kThreads + tid];
