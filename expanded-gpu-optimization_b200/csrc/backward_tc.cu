@@ -2,30 +2,35 @@
 //
 // Math: the reverse pass of the reference backward (csrc/fused_backward.cu:15-33 adjoint
 // formulas, :208-233 output seed, :262-321 weight gradient and input adjoint, :324-359 layer
-// 0), on 128-point tiles with all three per-layer contractions on the tensor cores, each in
-// 3xTF32 split precision (x = hi + lo, error ~2^-21 |x|):
-//   * forward recompute  Z_l[128 x 64] = H_{l-1} W_l^T   (as the forward kernel: A = H in
-//     TMEM, B = W_l in shared memory, M = 128 points, N = 64, K = 64 per component);
-//   * input adjoint      Hbar_{l-1} = Zbar_l W_l           (A = Zbar in TMEM, B = W_l^T);
+// 0), on 128-point tiles with all three per-layer contractions on the tensor cores, as f16
+// hi/lo operand pairs (x = hi + lo with power-of-2 range scales; the products keep ~22
+// significant bits):
+//   * forward recompute  Z_l[128 x 64] = H_{l-1} W_l^T   (3xFP16 as the forward kernel's
+//     version 3: A = sigma-scaled H in TMEM, B = tau-scaled W_l in shared memory, M = 128
+//     points, N = 64, K = 64 per component in chunks of 16);
+//   * input adjoint      Hbar_{l-1} = Zbar_l W_l           (3xFP16: A = Zbar scaled per point
+//     half and component, in TMEM; B = tau-scaled W_l^T);
 //   * weight gradient    dW_l[64 x 64] = sum over points and components of zbar h^T, as
 //     M = 128 rows (zbar_hi rows 0..63, zbar_lo rows 64..127) x N = 128 columns (h_hi,
-//     h_lo) x K = points: one MMA per K step gives all four hi/lo products in four
-//     quadrants of the accumulator, summed when it is emptied. A and B are
-//     written by the threads straight from registers into two shared-memory staging
-//     buffers (128-byte-swizzled K-major: a warp writes 32 consecutive points of one row,
-//     conflict-free), one per point half, one jet component at a time. The halves run
-//     independently (named barriers, one commit barrier each), so one half stages its next
-//     component while the tensor core works through the other half's MMAs.
+//     h_lo) x K = points: one f16 MMA per 16 points gives all four hi/lo products in four
+//     quadrants of the accumulator, summed when it is emptied. A and B are written by the
+//     threads straight from registers into two shared-memory staging buffers (MN-major: a
+//     thread's 8 neuron rows of one point are one 16-byte store), one per point half, one jet
+//     component at a time. The halves run independently (named barriers, one commit barrier
+//     each), so one half stages its next component while the tensor core works through the
+//     other half's MMAs.
 //
-// Where the data lives (one CTA per SM, persistent over tiles):
-//   * TMEM: accumulators D_c at columns 64c..64c+63 and a ring of two A-operand chunks at
-//     [256, 512), as in the forward kernel. The two weight-gradient accumulators (one per
+// Where the data lives (one CTA per SM, persistent over tiles, clusters of 2 CTAs):
+//   * TMEM: accumulators D_c at columns 64c..64c+63 and a ring of four A-operand chunks at
+//     [256, 512) (a GEMM's whole A operand). The two weight-gradient accumulators (one per
 //     point half) borrow the ring while it is idle (after the input-adjoint GEMM of the
 //     layer has completed, before the next layer's chunks) and are emptied every layer;
-//   * shared memory: two weight slots (hi + lo, 32 KB each), the six operands of a tile's
-//     GEMMs (W1, W2, W3, then W3^T, W2^T, W1^T; all K-major) taking turns: a one-thread bulk
-//     copy reloads a slot from a pre-split global copy as soon as the GEMM that used it has
-//     completed, two GEMMs before the slot is needed again;
+//   * shared memory: two weight slots (f16 hi + lo, 16 KB each), the six operands of a
+//     tile's GEMMs (W1, W2, W3, then W3^T, W2^T, W1^T; all K-major) taking turns: a one-thread
+//     bulk copy reloads a slot from a pre-split global copy as soon as the GEMM that used it
+//     has completed, two GEMMs before the slot is needed again; the staging buffers; the
+//     CTA's hidden-layer weight gradients (48 KB), summed over the cluster at the end through
+//     distributed shared memory into one partial row per cluster;
 //   * per-CTA scratch in global memory, 256 KB per CTA so it stays in L2: h_1 and h_2 of the
 //     tile, written during the forward recompute in a thread-private coalesced layout and
 //     read back by the same thread for the adjoint and the weight-gradient staging (h_0 is
@@ -33,23 +38,20 @@
 //   * registers: per thread one point (TMEM lane) and the 16 neurons 16a+4s+t.
 // Warps: 16 epilogue warps (all of the elementwise work above; warp w serves TMEM lane
 // quadrant w%4 and, with s = w/4, neurons 16a+4s+t) and an MMA warpgroup (warps 16-19) whose
-// warp 16 issues the 24 MMAs of every chunk in order once the chunk's 16 arrivals are in --
-// the warp that completed a chunk used to issue it and, blocked for the MMAs' execution
-// (~1,000 cycles), completed the next chunk last as well. The weight-gradient rounds stay
-// with one epilogue warp per point half, which issues right after its half's barrier (handing
-// them to the MMA warpgroup serialised them behind two mbarrier wake-ups per round). The MMA
-// warpgroup gives its registers to the epilogue with setmaxnreg (launch 640 x 96, MMA
-// warpgroup 32, epilogue 112), and the adjoint reads h_{l-1} without a group-ahead prefetch,
-// which frees 16 registers and was itself slower: 281 -> 268 us at 64K points, 3.41 -> 3.23
-// ms at 1M, bitwise unchanged. The host refuses a build whose launch register count is not
-// the 96 the split assumes.
+// warp 16 issues the 12 MMAs of every chunk in order once the chunk's 16 arrivals are in.
+// The weight-gradient rounds stay with one epilogue warp per point half, which issues right
+// after its half's barrier (handing them to the MMA warpgroup serialised them behind two
+// mbarrier wake-ups per round). The MMA warpgroup gives its registers to the epilogue with
+// setmaxnreg (launch 640 x 96, MMA warpgroup 32, epilogue 112); the host refuses a build
+// whose launch register count is not the 96 the split assumes.
 // The adjoint is written in terms of the stored activation h = (a, s z_J, s z_L - 2as|z_J|^2)
 // with s = 1 - a^2, the quantities the forward produced, so no pre-activation is stored.
 // Gradients are accumulated in a fixed order (warp butterflies, quadrants and tiles in
-// index order, the tensor core's own order for the weight gradient, one partial row per CTA
-// summed in row order), so results are bitwise reproducible for a given grid. Every wait
-// is bounded; a wait that gives up sets the CTA abort flag, the epilogue warps leave
-// together at their next barrier, the MMA warp at its next wait, and TMEM is freed.
+// index order, the tensor core's own order for the weight gradient, the cluster's CTAs in
+// rank order, one partial row per cluster summed in row order), so results are bitwise
+// reproducible for a given grid. Every wait is bounded; a wait that gives up sets the CTA
+// abort flag, the epilogue warps leave together at their next barrier, the MMA warp at its
+// next wait, TMEM is freed and every CTA still takes the cluster barriers.
 #include <algorithm>
 
 #include "common.cuh"

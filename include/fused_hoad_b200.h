@@ -55,8 +55,8 @@ typedef struct CUstream_st* fhb_stream_t;
 #define FHB_BACKWARD_VERSION_MIN 1
 #define FHB_BACKWARD_VERSION_MAX 6
 /* Backward versions 1..5 run the FP32 CUDA-core adjoint kernel; 6 (the reference's default)
- * runs the tensor-core one (forward recompute, input adjoint and weight gradient on tcgen05
- * in 3xTF32). Both reduce in a fixed order. */
+ * runs the tensor-core one (forward recompute and input adjoint in 3xFP16, weight gradient
+ * as scaled f16 hi/lo pairs, all on tcgen05). Both reduce in a fixed order. */
 #define FHB_BACKWARD_VERSION_TENSOR_CORE 6
 
 /* Hidden-layer activations (reference src/fused_hoad/specs.py:17, models.py:9-12). The
@@ -121,8 +121,9 @@ int fhb_forward_biharmonic(const float* coords, const float* params, float* u, f
 /*
  * Workspace the backward needs for n points on the current device, in bytes (0 for n==0),
  * enough for every backward version: one partial-gradient row per CTA of the persistent
- * grid, and for the tensor-core kernel also the pre-split weights (192 KB) and 512 KB of
- * per-CTA scratch that stays in L2 (about 84 MB on a 148-SM B200 from 18,944 points up).
+ * grid (the tensor-core kernel fills one per cluster of two CTAs), and for the tensor-core
+ * kernel also the f16 pre-split weights (96 KB) and 256 KB of per-CTA scratch that stays in
+ * L2 (about 45 MB on a 148-SM B200 from 18,944 points up).
  */
 size_t fhb_backward_workspace_bytes(int64_t n);
 
