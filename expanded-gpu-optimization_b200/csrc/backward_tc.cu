@@ -238,9 +238,9 @@ __device__ __forceinline__ void load_weight_slot(int slot, const float* wsplit, 
 
 // The 12 MMAs of chunk j of GEMM g (A from ring slot `slot`: 4 components x (A_hi B_hi +
 // A_lo B_hi + A_hi B_lo), K = 16, the component's hi block at column 16c of the slot and its
-// lo block 8 columns on); the first chunk of a GEMM first waits for its weight slot. False if
-// that wait gave up (nothing is issued). Not inlined: one copy instead of twenty-four keeps
-// the kernel small enough for the instruction cache.
+// lo block 8 columns on), issued by one elected lane in one block; the first chunk of a GEMM
+// first waits for its weight slot. False if that wait gave up (nothing is issued). Not
+// inlined: one copy instead of twenty-four keeps the kernel small for the instruction cache.
 __device__ __noinline__ bool issue_chunk_mmas(const Ctx& cx, uint32_t tile_index, int g,
                                                  int j, uint32_t slot) {
   const int ws = g & 1;
@@ -249,15 +249,8 @@ __device__ __noinline__ bool issue_chunk_mmas(const Ctx& cx, uint32_t tile_index
   const uint32_t w_hi = smem_u32(dsmem() + kWOff + ws * kLayerBytes + 256 * j);
   const uint64_t bhi = tc::smem_desc_kmajor(w_hi, kLbo, kSbo);
   const uint64_t blo = tc::smem_desc_kmajor(w_hi + kOperandBytes, kLbo, kSbo);
-#pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    const uint32_t d = cx.tmem + 64u * c;
-    const uint32_t a_hi = cx.tmem + kRingCol + kSlotCols * slot + 16u * c;
-    const uint32_t a_lo = a_hi + 8u;
-    tc::mma_f16_ts_warp(d, a_hi, bhi, kIdesc, j > 0 ? 1u : 0u);
-    tc::mma_f16_ts_warp(d, a_lo, bhi, kIdesc, 1u);
-    tc::mma_f16_ts_warp(d, a_hi, blo, kIdesc, 1u);
-  }
+  tc::mma_f16_ts_chunk_warp(cx.tmem, cx.tmem + kRingCol + kSlotCols * slot, bhi, blo, kIdesc,
+                            j > 0 ? 1u : 0u);
   if (j == kChunks - 1) tc::commit_warp(bar_dfull());
   return true;
 }

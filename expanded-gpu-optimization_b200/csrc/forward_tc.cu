@@ -242,7 +242,9 @@ __device__ __forceinline__ float at(const float4& v, int t) {
 // `slot`, then (tf32) a commit that frees the slot, and after the 4th chunk one that marks D
 // complete. tf32: 2 K steps x 4 components x (H_hi W_hi + H_lo W_hi + H_hi W_lo), A block
 // (component c, hi/lo sp, K step kk) at columns 32c + 16sp + 8kk of the slot. f16: 4
-// components x (H_hi W_hi + H_lo W_hi + H_hi W_lo), A block (c, sp) at 16c + 8sp.
+// components x (H_hi W_hi + H_lo W_hi + H_hi W_lo), A block (c, sp) at 16c + 8sp. One elected
+// lane issues a chunk's MMAs in one block (issued one call each, with their own election and
+// predicate set-up, the chunk's MMAs took ~80 issue cycles apiece).
 template <bool F16>
 __device__ __forceinline__ void issue_chunk_mmas(const Ctx& cx, int layer, int j, uint32_t slot) {
   using F = Format<F16>;
@@ -251,32 +253,15 @@ __device__ __forceinline__ void issue_chunk_mmas(const Ctx& cx, int layer, int j
     const uint32_t w0 = smem_u32(cx.smem + (2 * layer) * F::kOperandBytes + 256 * j);
     const uint64_t b_hi = tc::smem_desc_kmajor(w0, kLbo, F::kSbo);
     const uint64_t b_lo = tc::smem_desc_kmajor(w0 + F::kOperandBytes, kLbo, F::kSbo);
-#pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      const uint32_t d = cx.tmem + 64u * c;
-      const uint32_t a_hi = slot_col + 16u * c;
-      const uint32_t a_lo = a_hi + 8u;
-      tc::mma_f16_ts_warp(d, a_hi, b_hi, F::kIdesc, j > 0 ? 1u : 0u);
-      tc::mma_f16_ts_warp(d, a_lo, b_hi, F::kIdesc, 1u);
-      tc::mma_f16_ts_warp(d, a_hi, b_lo, F::kIdesc, 1u);
-    }
+    tc::mma_f16_ts_chunk_warp(cx.tmem, slot_col, b_hi, b_lo, F::kIdesc, j > 0 ? 1u : 0u);
   } else {
-#pragma unroll
-    for (int kk = 0; kk < 2; ++kk) {
-      const uint32_t w_hi =
-          smem_u32(cx.smem + (2 * layer) * F::kOperandBytes + 256 * (2 * j + kk));
-      const uint64_t bhi = tc::smem_desc_kmajor(w_hi, kLbo, F::kSbo);
-      const uint64_t blo = tc::smem_desc_kmajor(w_hi + F::kOperandBytes, kLbo, F::kSbo);
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const uint32_t d = cx.tmem + 64u * c;
-        const uint32_t a_hi = slot_col + 32u * c + 8u * kk;
-        const uint32_t a_lo = a_hi + 16u;
-        tc::mma_tf32_ts_warp(d, a_hi, bhi, F::kIdesc, (j > 0 || kk > 0) ? 1u : 0u);
-        tc::mma_tf32_ts_warp(d, a_lo, bhi, F::kIdesc, 1u);
-        tc::mma_tf32_ts_warp(d, a_hi, blo, F::kIdesc, 1u);
-      }
-    }
+    const uint32_t w0 = smem_u32(cx.smem + (2 * layer) * F::kOperandBytes + 512 * j);
+    const uint64_t bh0 = tc::smem_desc_kmajor(w0, kLbo, F::kSbo);
+    const uint64_t bl0 = tc::smem_desc_kmajor(w0 + F::kOperandBytes, kLbo, F::kSbo);
+    const uint64_t bh1 = tc::smem_desc_kmajor(w0 + 256, kLbo, F::kSbo);
+    const uint64_t bl1 = tc::smem_desc_kmajor(w0 + 256 + F::kOperandBytes, kLbo, F::kSbo);
+    tc::mma_tf32_ts_chunk_warp(cx.tmem, slot_col, bh0, bl0, bh1, bl1, F::kIdesc,
+                               j > 0 ? 1u : 0u);
   }
   if constexpr (!F16) tc::commit_warp(&cx.empty[slot]);  // f16: see produce_chunk
   if (j == kChunks - 1) tc::commit_warp(cx.dfull);

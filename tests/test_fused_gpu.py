@@ -311,6 +311,16 @@ def test_backward_matches_oracle(batch: int, route: str, kernel: int) -> None:
     assert_scaled(gx.cpu(), ex, 1e-4, "grad coords")
 
 
+@pytest.mark.parametrize("tiles", [3, 5, 147, 149, 150, 297])
+def test_tensor_core_backward_cluster_grid(tiles: int) -> None:
+    """The tensor-core backward launches whole clusters of 2 CTAs and one partial row per
+    cluster: odd tile counts leave the last cluster's second CTA without a tile (its rows
+    are zeros), and counts just past one round of 148 CTAs give some CTAs a second tile."""
+    (gp, gx), (ep, ex) = _backward_pair(128 * tiles - 5, "capi", version=6)
+    assert_scaled(gp.cpu(), ep, 1e-4, "grad params")
+    assert_scaled(gx.cpu(), ex, 1e-4, "grad coords")
+
+
 @pytest.mark.parametrize("version", [1, 2, 3, 4, 5, 6])
 def test_backward_every_version_number_is_accepted(version: int) -> None:
     (gp, gx), (ep, ex) = _backward_pair(257, "torch", version=version)
