@@ -1,6 +1,6 @@
 // Thin inline-PTX wrappers for the sm_100a tensor-core path: TMEM allocation, tcgen05.mma
-// (kind::tf32, A from tensor memory, B from shared memory), commits, TMEM loads/stores,
-// fences and the shared-memory matrix / instruction descriptors.
+// issue (kind::f16 and kind::tf32, A from tensor or shared memory, B from shared memory),
+// commits, TMEM loads/stores, fences and the shared-memory matrix / instruction descriptors.
 //
 // Descriptor encodings follow the PTX ISA's tcgen05 "shared memory descriptor" and
 // "instruction descriptor" tables (the same bit positions CUTLASS's
@@ -41,47 +41,7 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-// ---- MMA: D[tmem] (+)= A[tmem] * B[smem]^T, kind::tf32, one CTA ----
-__device__ __forceinline__ void mma_tf32_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
-                                            uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}"
-      ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u),
-      "r"(0u), "r"(0u)
-      : "memory");
-}
-
-// The same MMA issued by a converged warp: every lane evaluates the operands (so they stay
-// warp-uniform) and elect.sync picks the one lane that issues. Issuing from a lane-divergent
-// branch instead costs ~4x the MMA's own execution time per instruction for these shapes.
-__device__ __forceinline__ void mma_tf32_ts_warp(uint32_t d_tmem, uint32_t a_tmem,
-                                                 uint64_t b_desc, uint32_t idesc,
-                                                 uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p, e;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "elect.sync _|e, 0xffffffff;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}"
-      ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u),
-      "r"(0u), "r"(0u)
-      : "memory");
-}
-// D[tmem] (+)= A[tmem] * B[smem]^T, kind::f16 (A and B both f16, D f32), issued by a converged
-// warp (elect.sync picks the lane). A holds two f16 K elements per 32-bit TMEM column.
-__device__ __forceinline__ void mma_f16_ts_warp(uint32_t d_tmem, uint32_t a_tmem,
-                                                uint64_t b_desc, uint32_t idesc,
-                                                uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p, e;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "elect.sync _|e, 0xffffffff;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}"
-      ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u),
-      "r"(0u), "r"(0u)
-      : "memory");
-}
+// ---- MMA issue: one elected lane of a converged warp issues the MMAs ----
 // The 12 MMAs of one 3xFP16 chunk (K = 16), issued by one elected lane of a converged warp in
 // one block: for each jet component c, D_c (+)= A_hi B_hi, then += A_lo B_hi and A_hi B_lo,
 // with D_c at TMEM column d0 + 64c, A_hi at a0 + 16c and A_lo 8 columns on. The first MMA of
@@ -163,20 +123,6 @@ __device__ __forceinline__ void mma_tf32_ts_chunk_warp(uint32_t d0, uint32_t a0,
       : "memory");
 }
 
-// D[tmem] (+)= A[smem] * B[smem]^T, kind::tf32, both operands from shared memory, issued by
-// a converged warp (elect.sync picks the lane).
-__device__ __forceinline__ void mma_tf32_ss_warp(uint32_t d_tmem, uint64_t a_desc,
-                                                 uint64_t b_desc, uint32_t idesc,
-                                                 uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p, e;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "elect.sync _|e, 0xffffffff;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
-      ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u),
-      "r"(0u), "r"(0u)
-      : "memory");
-}
 // D[tmem] (+)= A[smem] * B[smem]^T, kind::f16 (both f16, D f32), issued by a converged warp;
 // the operand majors (K or MN) are in the instruction descriptor.
 __device__ __forceinline__ void mma_f16_ss_warp(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
@@ -198,13 +144,6 @@ __device__ __forceinline__ void commit_warp(uint64_t* bar) {
       : "memory");
 }
 
-// Arrive once on `bar` when every tcgen05.mma issued so far by this thread has completed.
-__device__ __forceinline__ void commit(uint64_t* bar) {
-  asm volatile(
-      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-          smem_u32(bar))
-      : "memory");
-}
 
 // ---- TMEM <-> registers (32 lanes x 32-bit, one lane per thread of the warp) ----
 __device__ __forceinline__ void ld_x16(uint32_t taddr, float (&v)[16]) {
@@ -279,13 +218,6 @@ __device__ __forceinline__ uint64_t smem_desc_kmajor(uint32_t smem_addr, uint32_
   return d;
 }
 
-// Shared-memory matrix descriptor, K-major, 128-byte swizzle: atoms of 8 rows x 128 bytes
-// (1024-byte aligned) whose 16-byte chunks are XOR-permuted by row % 8; `sbo` = byte distance
-// between consecutive 8-row atoms. Moving the start address by 32 bytes inside an atom
-// selects the next K step of 8 tf32 elements.
-__device__ __forceinline__ uint64_t smem_desc_kmajor_sw128(uint32_t smem_addr, uint32_t sbo) {
-  return smem_desc_kmajor(smem_addr, 16, sbo) | (2ull << 61);  // layout type 2: 128B swizzle
-}
 
 // Instruction descriptor for kind::tf32: D f32, A/B tf32, both K-major, shape M x N.
 __host__ __device__ constexpr uint32_t idesc_tf32(int m, int n) {
