@@ -161,6 +161,19 @@ __device__ __forceinline__ float pow2_floor_ratio(int c, float x) {
   return __uint_as_float(static_cast<uint32_t>(k + 127) << 23);
 }
 
+// Two FP32 fmas in one instruction (fma.rn.f32x2, sm_100a): d0 = a0 b0 + d0, d1 = a1 b1 + d1,
+// each rounded exactly as fmaf. The FP32 pipe's rate is the same as two scalar fmas; the
+// packed form halves the issue slots they take.
+__device__ __forceinline__ void fma2(float& d0, float& d1, float a0, float a1, float b0,
+                                     float b1) {
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rd, {%0, %1};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rd;\n\t"
+      "mov.b64 {%0, %1}, rd;\n\t}"
+      : "+f"(d0), "+f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+
 // Maximum over the warp of a non-negative float (non-negative floats order as their bit
 // patterns): one redux instruction.
 __device__ __forceinline__ float warp_max_nonneg(float v) {

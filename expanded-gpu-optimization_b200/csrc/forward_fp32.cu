@@ -184,13 +184,25 @@ __global__ void __launch_bounds__(Cfg<PPL>::kBlock, 1)
           const float* src = jet + (i + j) * C::kTile + col;
 #pragma unroll
           for (int c = 0; c < 4; ++c) ld_pts<PPL>(src + c * C::kPlane, h[c]);
+          // packed fmas: pairs of points, or pairs of neurons with one point per lane
+          if constexpr (PPL % 2 == 0) {
 #pragma unroll
-          for (int k = 0; k < kNeuronsPerWarp; ++k) {
-            const float wk = lane_of(w[k], j);
+            for (int k = 0; k < kNeuronsPerWarp; ++k) {
+              const float wk = lane_of(w[k], j);
 #pragma unroll
-            for (int c = 0; c < 4; ++c)
+              for (int c = 0; c < 4; ++c)
 #pragma unroll
-              for (int q = 0; q < PPL; ++q) acc[c][k][q] = fmaf(wk, h[c][q], acc[c][k][q]);
+                for (int q = 0; q < PPL; q += 2)
+                  fma2(acc[c][k][q], acc[c][k][q + 1], wk, wk, h[c][q], h[c][q + 1]);
+            }
+          } else {
+#pragma unroll
+            for (int k = 0; k < kNeuronsPerWarp; k += 2) {
+              const float wa = lane_of(w[k], j), wb = lane_of(w[k + 1], j);
+#pragma unroll
+              for (int c = 0; c < 4; ++c)
+                fma2(acc[c][k][0], acc[c][k + 1][0], wa, wb, h[c][0], h[c][0]);
+            }
           }
         }
       }
