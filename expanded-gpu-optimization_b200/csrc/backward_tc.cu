@@ -293,10 +293,13 @@ __device__ __forceinline__ void produce_layer0(float x0, float x1, const float* 
       const float w0 = small[kSmW0 + 2 * o], w1 = small[kSmW0 + 2 * o + 1];
       tanh_jet_fast(fmaf(w0, x0, fmaf(w1, x1, small[kSmB0 + o])), w0, w1, 0.0f, h[0][t],
                     h[1][t], h[2][t], h[3][t]);
-      h[0][t] *= s0;
-      h[1][t] *= s1;
-      h[2][t] *= s1;
-      h[3][t] *= s3;
+    }
+#pragma unroll
+    for (int t = 0; t < 4; t += 2) {
+      mul2(h[0][t], h[0][t + 1], s0, s0);
+      mul2(h[1][t], h[1][t + 1], s1, s1);
+      mul2(h[2][t], h[2][t + 1], s1, s1);
+      mul2(h[3][t], h[3][t + 1], s3, s3);
     }
     produce_chunk(chunk++, h, tmem_warp, s);
   }
@@ -399,7 +402,11 @@ __device__ __forceinline__ void stage_f16_rows(uint8_t* at, int s, const float (
                                                float scale) {
   uint32_t hi[8], lo[8];
 #pragma unroll
-  for (int p = 0; p < 8; ++p) split_f16_pair_fast(v[2 * p] * scale, v[2 * p + 1] * scale, hi[p], lo[p]);
+  for (int p = 0; p < 8; ++p) {
+    float a = v[2 * p], b = v[2 * p + 1];
+    mul2(a, b, scale, scale);
+    split_f16_pair_fast(a, b, hi[p], lo[p]);
+  }
 #pragma unroll
   for (int g = 0; g < 2; ++g) {
     st_shared_v4(at + (2 * s + g) * kDwSbo, hi[4 * g], hi[4 * g + 1], hi[4 * g + 2], hi[4 * g + 3]);
@@ -765,9 +772,12 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kBlockThreads
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
             d[0][i] = fmaf(d[0][i], uv, bias[16 * (i >> 2) + 4 * s + (i & 3)]);
-            d[1][i] *= uj;
-            d[2][i] *= uj;
-            d[3][i] *= ul;
+          }
+#pragma unroll
+          for (int i = 0; i < 16; i += 2) {
+            mul2(d[1][i], d[1][i + 1], uj, uj);
+            mul2(d[2][i], d[2][i + 1], uj, uj);
+            mul2(d[3][i], d[3][i + 1], ul, ul);
           }
         }
         if (g < 2) {
@@ -782,10 +792,13 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kBlockThreads
               tanh_jet_fast(d[0][i], d[1][i], d[2][i], d[3][i], h[0][t], h[1][t], h[2][t],
                             h[3][t]);
 #pragma unroll
-              for (int c = 0; c < 4; ++c) {
-                hj[(c * 16 + i) * kThreads] = h[c][t];
-                h[c][t] *= sg[c];
-              }
+              for (int c = 0; c < 4; ++c) hj[(c * 16 + i) * kThreads] = h[c][t];
+            }
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              const float g2 = sg[c];
+              mul2(h[c][0], h[c][1], g2, g2);
+              mul2(h[c][2], h[c][3], g2, g2);
             }
             produce_chunk(chunk++, h, tmem_warp, s);
           }
@@ -920,7 +933,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kBlockThreads
               sigw[kIsc + c] = isc * itau;
             }
 #pragma unroll
-            for (int i = 0; i < 16; ++i) d[c][i] *= sc;
+            for (int i = 0; i < 16; i += 2) mul2(d[c][i], d[c][i + 1], sc, sc);
           }
           __syncwarp();
 #pragma unroll
@@ -1030,7 +1043,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kBlockThreads
         for (int c = 0; c < 4; ++c) {
           const float isc = sigw[kIsc + c];
 #pragma unroll
-          for (int i = 0; i < 16; ++i) d[c][i] *= isc;
+          for (int i = 0; i < 16; i += 2) mul2(d[c][i], d[c][i + 1], isc, isc);
         }
         if (l == 1 && has_next) {  // GEMM 0 of the next tile may now overwrite D
           prefetch_wait();

@@ -174,6 +174,17 @@ __device__ __forceinline__ void fma2(float& d0, float& d1, float a0, float a1, f
       : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
 }
 
+// Two FP32 products in one instruction (mul.rn.f32x2): d0 *= a0, d1 *= a1, rounded as a
+// scalar multiply.
+__device__ __forceinline__ void mul2(float& d0, float& d1, float a0, float a1) {
+  asm("{\n\t.reg .b64 ra, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rd, {%0, %1};\n\t"
+      "mul.rn.f32x2 rd, rd, ra;\n\t"
+      "mov.b64 {%0, %1}, rd;\n\t}"
+      : "+f"(d0), "+f"(d1)
+      : "f"(a0), "f"(a1));
+}
+
 // Maximum over the warp of a non-negative float (non-negative floats order as their bit
 // patterns): one redux instruction.
 __device__ __forceinline__ float warp_max_nonneg(float v) {
