@@ -288,11 +288,15 @@ __device__ __forceinline__ void produce_layer0(float x0, float x1, const float* 
   for (int a = 0; a < kChunks; ++a) {
     float h[4][4];
 #pragma unroll
-    for (int t = 0; t < 4; ++t) {
+    for (int t = 0; t < 4; t += 2) {
       const int o = 16 * a + 4 * s + t;
-      const float w0 = small[kSmW0 + 2 * o], w1 = small[kSmW0 + 2 * o + 1];
-      tanh_jet_fast(fmaf(w0, x0, fmaf(w1, x1, small[kSmB0 + o])), w0, w1, 0.0f, h[0][t],
-                    h[1][t], h[2][t], h[3][t]);
+      const float w0a = small[kSmW0 + 2 * o], w1a = small[kSmW0 + 2 * o + 1];
+      const float w0b = small[kSmW0 + 2 * o + 2], w1b = small[kSmW0 + 2 * o + 3];
+      float za, zb;
+      fma2o(za, zb, w1a, w1b, x1, x1, small[kSmB0 + o], small[kSmB0 + o + 1]);
+      fma2o(za, zb, w0a, w0b, x0, x0, za, zb);
+      tanh_jet_fast2(za, zb, w0a, w0b, w1a, w1b, 0.0f, 0.0f, h[0][t], h[0][t + 1], h[1][t],
+                     h[1][t + 1], h[2][t], h[2][t + 1], h[3][t], h[3][t + 1]);
     }
 #pragma unroll
     for (int t = 0; t < 4; t += 2) {
@@ -347,6 +351,33 @@ __device__ __forceinline__ void adjoint_h(float a, float hj0, float hj1, float h
   gv = zv;
   g0 = z0;
   g1 = z1;
+}
+
+// adjoint_h of two neurons in packed pair arithmetic: bitwise the results of two adjoint_h
+// calls (the same roundings in the same order; the negated products -2 (.) and -f h_Jd are
+// formed as (-2) (.) and (-4 a) gl h_Jd, which round to the same magnitudes).
+__device__ __forceinline__ void adjoint_h2(float a0, float a1, float hj00, float hj01,
+                                           float hj10, float hj11, float hl0, float hl1,
+                                           float& gv0, float& gv1, float& g00, float& g01,
+                                           float& g10, float& g11, float& gl0, float& gl1) {
+  float s0, s1, u0, u1, gj0, gj1, t0, t1, w0, w1, f0, f1, m0, m1;
+  fma2o(s0, s1, -a0, -a1, a0, a1, 1.0f, 1.0f);
+  mul2o(u0, u1, g10, g11, hj10, hj11);
+  fma2o(gj0, gj1, g00, g01, hj00, hj01, u0, u1);
+  mul2o(u0, u1, hj10, hj11, hj10, hj11);
+  fma2o(u0, u1, hj00, hj01, hj00, hj01, u0, u1);
+  fma2o(t0, t1, a0, a1, hl0, hl1, u0, u1);
+  mul2o(w0, w1, gl0, gl1, t0, t1);
+  fma2o(w0, w1, a0, a1, gj0, gj1, w0, w1);
+  mul2o(w0, w1, -2.0f, -2.0f, w0, w1);
+  fma2o(gv0, gv1, gv0, gv1, s0, s1, w0, w1);
+  mul2o(f0, f1, -4.0f, -4.0f, a0, a1);
+  mul2o(f0, f1, f0, f1, gl0, gl1);
+  mul2o(m0, m1, f0, f1, hj00, hj01);
+  fma2o(g00, g01, g00, g01, s0, s1, m0, m1);
+  mul2o(m0, m1, f0, f1, hj10, hj11);
+  fma2o(g10, g11, g10, g11, s0, s1, m0, m1);
+  mul2o(gl0, gl1, gl0, gl1, s0, s1);
 }
 
 // Component c of h_{l-1} for this thread's 16 neuron slots: from the scratch (l >= 2) or,
@@ -787,12 +818,16 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kBlockThreads
           for (int a = 0; a < kChunks; ++a) {
             float h[4][4];
 #pragma unroll
-            for (int t = 0; t < 4; ++t) {
+            for (int t = 0; t < 4; t += 2) {
               const int i = 4 * a + t;
-              tanh_jet_fast(d[0][i], d[1][i], d[2][i], d[3][i], h[0][t], h[1][t], h[2][t],
-                            h[3][t]);
+              tanh_jet_fast2(d[0][i], d[0][i + 1], d[1][i], d[1][i + 1], d[2][i], d[2][i + 1],
+                             d[3][i], d[3][i + 1], h[0][t], h[0][t + 1], h[1][t], h[1][t + 1],
+                             h[2][t], h[2][t + 1], h[3][t], h[3][t + 1]);
 #pragma unroll
-              for (int c = 0; c < 4; ++c) hj[(c * 16 + i) * kThreads] = h[c][t];
+              for (int c = 0; c < 4; ++c) {
+                hj[(c * 16 + i) * kThreads] = h[c][t];
+                hj[(c * 16 + i + 1) * kThreads] = h[c][t + 1];
+              }
             }
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
@@ -809,11 +844,16 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kBlockThreads
       {
         float pu = 0.0f, pl = 0.0f;
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          tanh_jet_fast(d[0][i], d[1][i], d[2][i], d[3][i], d[0][i], d[1][i], d[2][i], d[3][i]);
-          const float w = small[kSmWout + 16 * (i >> 2) + 4 * s + (i & 3)];
-          pu = fmaf(w, d[0][i], pu);
-          pl = fmaf(w, d[3][i], pl);
+        for (int i = 0; i < 16; i += 2) {
+          tanh_jet_fast2(d[0][i], d[0][i + 1], d[1][i], d[1][i + 1], d[2][i], d[2][i + 1],
+                         d[3][i], d[3][i + 1], d[0][i], d[0][i + 1], d[1][i], d[1][i + 1],
+                         d[2][i], d[2][i + 1], d[3][i], d[3][i + 1]);
+#pragma unroll
+          for (int k = 0; k < 2; ++k) {
+            const float w = small[kSmWout + 16 * ((i + k) >> 2) + 4 * s + ((i + k) & 3)];
+            pu = fmaf(w, d[0][i + k], pu);
+            pl = fmaf(w, d[3][i + k], pl);
+          }
         }
         red[s * kTile + row] = pu;
         red[(4 + s) * kTile + row] = pl;
@@ -873,15 +913,22 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kBlockThreads
           store_part8(part, 0, q, s, half8, warp_sum8(dwo));
         }
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int o = 16 * (i >> 2) + 4 * s + (i & 3);
-          const float w = small[kSmWout + o];
-          float gv = gu * w, g0 = 0.0f, g1 = 0.0f, gL = gl * w;
-          adjoint_h(d[0][i], d[1][i], d[2][i], d[3][i], gv, g0, g1, gL);
-          d[0][i] = gv;
-          d[1][i] = g0;
-          d[2][i] = g1;
-          d[3][i] = gL;
+        for (int i = 0; i < 16; i += 2) {
+          const int o = 16 * (i >> 2) + 4 * s + (i & 3);  // o + 1 is neuron slot i + 1
+          const float wa = small[kSmWout + o], wb = small[kSmWout + o + 1];
+          float gva, gvb, g0a = 0.0f, g0b = 0.0f, g1a = 0.0f, g1b = 0.0f, gLa, gLb;
+          mul2o(gva, gvb, gu, gu, wa, wb);
+          mul2o(gLa, gLb, gl, gl, wa, wb);
+          adjoint_h2(d[0][i], d[0][i + 1], d[1][i], d[1][i + 1], d[2][i], d[2][i + 1], d[3][i],
+                     d[3][i + 1], gva, gvb, g0a, g0b, g1a, g1b, gLa, gLb);
+          d[0][i] = gva;
+          d[0][i + 1] = gvb;
+          d[1][i] = g0a;
+          d[1][i + 1] = g0b;
+          d[2][i] = g1a;
+          d[2][i + 1] = g1b;
+          d[3][i] = gLa;
+          d[3][i + 1] = gLb;
         }
         store_part16(part, 6, q, s, warp_sum16(d[0]));  // b3
       }
@@ -1058,9 +1105,11 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kBlockThreads
 #pragma unroll
 for (int c = 0; c < 4; ++c) h[c][t] = hsrc[(c * 16 + 4 * a + t) * kThreads];
 #pragma unroll
-            for (int t = 0; t < 4; ++t) {
+            for (int t = 0; t < 4; t += 2) {
               const int i = 4 * a + t;
-              adjoint_h(h[0][t], h[1][t], h[2][t], h[3][t], d[0][i], d[1][i], d[2][i], d[3][i]);
+              adjoint_h2(h[0][t], h[0][t + 1], h[1][t], h[1][t + 1], h[2][t], h[2][t + 1],
+                         h[3][t], h[3][t + 1], d[0][i], d[0][i + 1], d[1][i], d[1][i + 1],
+                         d[2][i], d[2][i + 1], d[3][i], d[3][i + 1]);
             }
           }
           store_part16(part, 2 + l, q, s, warp_sum16(d[0]));  // b_{l-1}
@@ -1074,19 +1123,24 @@ for (int c = 0; c < 4; ++c) h[c][t] = hsrc[(c * 16 + 4 * a + t) * kThreads];
         const float x0 = xs[tid], x1 = xs[kThreads + tid];
         float gx0 = 0.0f, gx1 = 0.0f;
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int o = 16 * (i >> 2) + 4 * s + (i & 3);
-          const float w0 = small[kSmW0 + 2 * o], w1 = small[kSmW0 + 2 * o + 1];
-          float a, hj0, hj1, hl;
-          tanh_jet_fast(fmaf(w0, x0, fmaf(w1, x1, small[kSmB0 + o])), w0, w1, 0.0f, a, hj0, hj1,
-                        hl);
-          float gv = d[0][i], g0 = d[1][i], g1 = d[2][i], gL = d[3][i];
-          adjoint_h(a, hj0, hj1, hl, gv, g0, g1, gL);
-          d[0][i] = gv;                  // db0 terms
-          d[1][i] = fmaf(gv, x0, g0);    // dW0[:, 0] terms
-          d[2][i] = fmaf(gv, x1, g1);    // dW0[:, 1] terms
-          gx0 = fmaf(w0, gv, gx0);
-          gx1 = fmaf(w1, gv, gx1);
+        for (int i = 0; i < 16; i += 2) {
+          const int o = 16 * (i >> 2) + 4 * s + (i & 3);  // o + 1 is neuron slot i + 1
+          const float w0a = small[kSmW0 + 2 * o], w1a = small[kSmW0 + 2 * o + 1];
+          const float w0b = small[kSmW0 + 2 * o + 2], w1b = small[kSmW0 + 2 * o + 3];
+          float za, zb, aa, ab, j0a, j0b, j1a, j1b, la, lb;
+          fma2o(za, zb, w1a, w1b, x1, x1, small[kSmB0 + o], small[kSmB0 + o + 1]);
+          fma2o(za, zb, w0a, w0b, x0, x0, za, zb);
+          tanh_jet_fast2(za, zb, w0a, w0b, w1a, w1b, 0.0f, 0.0f, aa, ab, j0a, j0b, j1a, j1b, la,
+                         lb);
+          adjoint_h2(aa, ab, j0a, j0b, j1a, j1b, la, lb, d[0][i], d[0][i + 1], d[1][i],
+                     d[1][i + 1], d[2][i], d[2][i + 1], d[3][i], d[3][i + 1]);
+          fma2o(d[1][i], d[1][i + 1], d[0][i], d[0][i + 1], x0, x0, d[1][i], d[1][i + 1]);
+          fma2o(d[2][i], d[2][i + 1], d[0][i], d[0][i + 1], x1, x1, d[2][i], d[2][i + 1]);
+          // d[0] holds the db0 terms, d[1] and d[2] the dW0[:, 0] and dW0[:, 1] terms
+          gx0 = fmaf(w0a, d[0][i], gx0);
+          gx1 = fmaf(w1a, d[0][i], gx1);
+          gx0 = fmaf(w0b, d[0][i + 1], gx0);
+          gx1 = fmaf(w1b, d[0][i + 1], gx1);
         }
         store_part16(part, 1, q, s, warp_sum16(d[0]));
         store_part16(part, 2, q, s, warp_sum16(d[1]));

@@ -278,6 +278,67 @@ __device__ __forceinline__ void tanh_jet_fast(float zv, float zj0, float zj1, fl
   l = fmaf(s, zl, -2.0f * a * s * q);
 }
 
+// ---- packed FP32 pair arithmetic (sm_100a .f32x2): each lane rounded as the scalar op ----
+// r = a * b
+__device__ __forceinline__ void mul2o(float& r0, float& r1, float a0, float a1, float b0,
+                                      float b1) {
+  asm("{\n\t.reg .b64 ra, rb, rr;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mul.rn.f32x2 rr, ra, rb;\n\t"
+      "mov.b64 {%0, %1}, rr;\n\t}"
+      : "=f"(r0), "=f"(r1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+// r = a + b
+__device__ __forceinline__ void add2o(float& r0, float& r1, float a0, float a1, float b0,
+                                      float b1) {
+  asm("{\n\t.reg .b64 ra, rb, rr;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rr, ra, rb;\n\t"
+      "mov.b64 {%0, %1}, rr;\n\t}"
+      : "=f"(r0), "=f"(r1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+// r = a * b + c
+__device__ __forceinline__ void fma2o(float& r0, float& r1, float a0, float a1, float b0,
+                                      float b1, float c0, float c1) {
+  asm("{\n\t.reg .b64 ra, rb, rc, rr;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rr, ra, rb, rc;\n\t"
+      "mov.b64 {%0, %1}, rr;\n\t}"
+      : "=f"(r0), "=f"(r1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+}
+
+// tanh_jet_fast of two neurons in packed pair arithmetic: bitwise the results of two
+// tanh_jet_fast calls (the same operations in the same order; -a from 2r - 1, exact).
+__device__ __forceinline__ void tanh_jet_fast2(float zv0, float zv1, float zj00, float zj01,
+                                               float zj10, float zj11, float zl0, float zl1,
+                                               float& v0, float& v1, float& j00, float& j01,
+                                               float& j10, float& j11, float& l0, float& l1) {
+  constexpr float k = 2.8853900817779268f;
+  float x0, x1, e0, e1, p0, p1, r0, r1, a0, a1, n0, n1, s0, s1, t0, t1, q0, q1, m0, m1;
+  mul2o(x0, x1, zv0, zv1, k, k);
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e0) : "f"(x0));
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e1) : "f"(x1));
+  add2o(p0, p1, e0, e1, 1.0f, 1.0f);
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r0) : "f"(p0));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r1) : "f"(p1));
+  fma2o(a0, a1, -2.0f, -2.0f, r0, r1, 1.0f, 1.0f);    // a = 1 - 2r
+  fma2o(n0, n1, 2.0f, 2.0f, r0, r1, -1.0f, -1.0f);    // -a
+  fma2o(s0, s1, n0, n1, a0, a1, 1.0f, 1.0f);          // s = 1 - a^2
+  mul2o(t0, t1, zj10, zj11, zj10, zj11);
+  fma2o(q0, q1, zj00, zj01, zj00, zj01, t0, t1);      // |z_J|^2
+  v0 = a0;
+  v1 = a1;
+  mul2o(j00, j01, s0, s1, zj00, zj01);
+  mul2o(j10, j11, s0, s1, zj10, zj11);
+  mul2o(m0, m1, -2.0f, -2.0f, a0, a1);
+  mul2o(m0, m1, m0, m1, s0, s1);
+  mul2o(m0, m1, m0, m1, q0, q1);
+  fma2o(l0, l1, s0, s1, zl0, zl1, m0, m1);
+}
+
 // ---- the SiLU jet and its adjoint ----
 //
 // Reference src/fused_hoad/backends/forward_laplacian.py:34-38 (_silu_jet) with :60-67: for
@@ -352,6 +413,15 @@ struct TanhAct {
                                                   float& v, float& j0, float& j1, float& l) {
     tanh_jet_fast(zv, zj0, zj1, zl, v, j0, j1, l);
   }
+  // jet_fast of two neurons (packed pair arithmetic, bitwise two jet_fast calls)
+  static __device__ __forceinline__ void jet_fast2(float zv0, float zv1, float zj00, float zj01,
+                                                   float zj10, float zj11, float zl0, float zl1,
+                                                   float& v0, float& v1, float& j00,
+                                                   float& j01, float& j10, float& j11,
+                                                   float& l0, float& l1) {
+    tanh_jet_fast2(zv0, zv1, zj00, zj01, zj10, zj11, zl0, zl1, v0, v1, j00, j01, j10, j11, l0,
+                   l1);
+  }
   static __device__ __forceinline__ void adjoint(float zv, float zj0, float zj1, float zl,
                                                  float& av, float& aj0, float& aj1, float& al) {
     tanh_jet_adjoint(zv, zj0, zj1, zl, av, aj0, aj1, al);
@@ -366,6 +436,14 @@ struct SiluAct {
   static __device__ __forceinline__ void jet_fast(float zv, float zj0, float zj1, float zl,
                                                   float& v, float& j0, float& j1, float& l) {
     silu_jet_fast(zv, zj0, zj1, zl, v, j0, j1, l);
+  }
+  static __device__ __forceinline__ void jet_fast2(float zv0, float zv1, float zj00, float zj01,
+                                                   float zj10, float zj11, float zl0, float zl1,
+                                                   float& v0, float& v1, float& j00,
+                                                   float& j01, float& j10, float& j11,
+                                                   float& l0, float& l1) {
+    silu_jet_fast(zv0, zj00, zj10, zl0, v0, j00, j10, l0);
+    silu_jet_fast(zv1, zj01, zj11, zl1, v1, j01, j11, l1);
   }
   static __device__ __forceinline__ void adjoint(float zv, float zj0, float zj1, float zl,
                                                  float& av, float& aj0, float& aj1, float& al) {

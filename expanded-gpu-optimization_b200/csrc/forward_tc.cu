@@ -231,6 +231,18 @@ __device__ __forceinline__ float tanh_r_scaled(float zp) {
 
 constexpr float kTwoOverLn2 = 2.8853900817779268f;  // 2 / ln 2 = 2 log2(e)
 
+// tanh_r_scaled of two values, the sum 2^zp + 1 as one packed add (rounded as the scalar
+// add): bitwise the results of two tanh_r_scaled calls.
+__device__ __forceinline__ void tanh_r_scaled2(float zp0, float zp1, float& r0, float& r1) {
+  float e0, e1, p0, p1;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e0) : "f"(zp0));
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e1) : "f"(zp1));
+  add2o(p0, p1, e0, e1, 1.0f, 1.0f);
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r0) : "f"(p0));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r1) : "f"(p1));
+}
+
+
 __device__ __forceinline__ float4 ld_f4(const float* p) {
   return *reinterpret_cast<const float4*>(p);
 }
@@ -554,14 +566,19 @@ __device__ __forceinline__ bool produce_layer0(float x0, float x1, uint32_t& chu
       const float4 kj0 = ld_f4(c0 + 3 * kWidth), kj1 = ld_f4(c0 + 4 * kWidth);
       const float4 kl = ld_f4(c0 + 5 * kWidth), kl2 = ld_f4(c0 + 6 * kWidth);
       float h[4][4];
+      // neuron pairs (t, t + 1) in packed FP32 arithmetic, each lane rounded as the scalar op
 #pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        const float r = tanh_r_scaled(fmaf(at(wx, t), x0, fmaf(at(wy, t), x1, at(bz, t))));
-        const float tt = fmaf(-r, r, r);  // (1 - tanh^2) / 4
-        h[0][t] = fmaf(sv2, r, sv);
-        h[1][t] = tt * at(kj0, t);
-        h[2][t] = tt * at(kj1, t);
-        h[3][t] = tt * fmaf(at(kl2, t), r, at(kl, t));
+      for (int t = 0; t < 4; t += 2) {
+        float z0, z1, r0, r1, tt0, tt1, m0, m1;
+        fma2o(z0, z1, at(wy, t), at(wy, t + 1), x1, x1, at(bz, t), at(bz, t + 1));
+        fma2o(z0, z1, at(wx, t), at(wx, t + 1), x0, x0, z0, z1);
+        tanh_r_scaled2(z0, z1, r0, r1);
+        fma2o(tt0, tt1, -r0, -r1, r0, r1, r0, r1);  // (1 - tanh^2) / 4
+        fma2o(h[0][t], h[0][t + 1], sv2, sv2, r0, r1, sv, sv);
+        mul2o(h[1][t], h[1][t + 1], tt0, tt1, at(kj0, t), at(kj0, t + 1));
+        mul2o(h[2][t], h[2][t + 1], tt0, tt1, at(kj1, t), at(kj1, t + 1));
+        fma2o(m0, m1, at(kl2, t), at(kl2, t + 1), r0, r1, at(kl, t), at(kl, t + 1));
+        mul2o(h[3][t], h[3][t + 1], tt0, tt1, m0, m1);
       }
       if (!produce_chunk<F16>(chunk++, j, h, tmem_warp, s, cx)) return false;
     }
@@ -731,18 +748,24 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
             for (int j = 0; j < kChunks; ++j) {
               const float4 bb = ld_f4(bias + 16 * j);
               float h[4][4];
+              // neuron pairs (t, t + 1) in packed FP32 arithmetic, rounded as the scalar ops
 #pragma unroll
-              for (int t = 0; t < 4; ++t) {
+              for (int t = 0; t < 4; t += 2) {
                 const int i = 4 * j + t;
-                const float r = tanh_r_scaled(fmaf(d[0][i], ka.x, at(bb, t)));
-                const float tt = fmaf(-r, r, r);  // (1 - tanh^2) / 4
-                const float sk = tt * ka.w;
-                const float q = fmaf(d[1][i], d[1][i], d[2][i] * d[2][i]);
-                const float g = fmaf(kb.z, r, kb.y);
-                h[0][t] = fmaf(ka.z, r, ka.y);
-                h[1][t] = sk * d[1][i];
-                h[2][t] = sk * d[2][i];
-                h[3][t] = tt * fmaf(g, q, kb.x * d[3][i]);
+                float z0, z1, r0, r1, tt0, tt1, sk0, sk1, q0, q1, g0, g1, m0, m1;
+                fma2o(z0, z1, d[0][i], d[0][i + 1], ka.x, ka.x, at(bb, t), at(bb, t + 1));
+                tanh_r_scaled2(z0, z1, r0, r1);
+                fma2o(tt0, tt1, -r0, -r1, r0, r1, r0, r1);  // (1 - tanh^2) / 4
+                mul2o(sk0, sk1, tt0, tt1, ka.w, ka.w);
+                mul2o(q0, q1, d[2][i], d[2][i + 1], d[2][i], d[2][i + 1]);
+                fma2o(q0, q1, d[1][i], d[1][i + 1], d[1][i], d[1][i + 1], q0, q1);
+                fma2o(g0, g1, kb.z, kb.z, r0, r1, kb.y, kb.y);
+                fma2o(h[0][t], h[0][t + 1], ka.z, ka.z, r0, r1, ka.y, ka.y);
+                mul2o(h[1][t], h[1][t + 1], sk0, sk1, d[1][i], d[1][i + 1]);
+                mul2o(h[2][t], h[2][t + 1], sk0, sk1, d[2][i], d[2][i + 1]);
+                mul2o(m0, m1, kb.x, kb.x, d[3][i], d[3][i + 1]);
+                fma2o(m0, m1, g0, g1, q0, q1, m0, m1);
+                mul2o(h[3][t], h[3][t + 1], tt0, tt1, m0, m1);
               }
               if (!(ok = produce_chunk<F16>(chunk++, j, h, tmem_warp, s, cx))) break;
             }
@@ -758,15 +781,24 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
           for (int j = 0; j < kChunks; ++j) {
             const float4 bb = ld_f4(bias + 16 * j), ww = ld_f4(wout + 16 * j);
 #pragma unroll
-            for (int t = 0; t < 4; ++t) {
+            for (int t = 0; t < 4; t += 2) {
               const int i = 4 * j + t;
-              const float r = tanh_r_scaled(fmaf(d[0][i], ko.x, at(bb, t)));
-              const float tt = fmaf(-r, r, r);
-              const float a = fmaf(-2.0f, r, 1.0f);
-              const float q = fmaf(d[1][i], d[1][i], d[2][i] * d[2][i]);
-              const float inner = fmaf(ko.z * a, q, ko.y * d[3][i]);
-              pu = fmaf(at(ww, t), a, pu);
-              pl = fmaf(at(ww, t) * tt, inner, pl);
+              float z0, z1, r0, r1, tt0, tt1, a0, a1, q0, q1, m0, m1, n0, n1, w0, w1;
+              fma2o(z0, z1, d[0][i], d[0][i + 1], ko.x, ko.x, at(bb, t), at(bb, t + 1));
+              tanh_r_scaled2(z0, z1, r0, r1);
+              fma2o(tt0, tt1, -r0, -r1, r0, r1, r0, r1);
+              fma2o(a0, a1, -2.0f, -2.0f, r0, r1, 1.0f, 1.0f);
+              mul2o(q0, q1, d[2][i], d[2][i + 1], d[2][i], d[2][i + 1]);
+              fma2o(q0, q1, d[1][i], d[1][i + 1], d[1][i], d[1][i + 1], q0, q1);
+              mul2o(m0, m1, ko.z, ko.z, a0, a1);
+              mul2o(n0, n1, ko.y, ko.y, d[3][i], d[3][i + 1]);
+              fma2o(m0, m1, m0, m1, q0, q1, n0, n1);  // inner
+              mul2o(w0, w1, at(ww, t), at(ww, t + 1), tt0, tt1);
+              // the sums in neuron order, as scalar fmas
+              pu = fmaf(at(ww, t), a0, pu);
+              pl = fmaf(w0, m0, pl);
+              pu = fmaf(at(ww, t + 1), a1, pu);
+              pl = fmaf(w1, m1, pl);
             }
           }
         } else {
@@ -776,11 +808,14 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
             for (int j = 0; j < kChunks; ++j) {
               float h[4][4];
 #pragma unroll
-              for (int t = 0; t < 4; ++t) {
+              for (int t = 0; t < 4; t += 2) {
                 const int i = 4 * j + t;
-                const float b = bias[16 * j + 4 * s + t];
-                Act::jet_fast(d[0][i] + b, d[1][i], d[2][i], d[3][i], h[0][t], h[1][t],
-                              h[2][t], h[3][t]);
+                float z0, z1;
+                add2o(z0, z1, d[0][i], d[0][i + 1], bias[16 * j + 4 * s + t],
+                      bias[16 * j + 4 * s + t + 1]);
+                Act::jet_fast2(z0, z1, d[1][i], d[1][i + 1], d[2][i], d[2][i + 1], d[3][i],
+                               d[3][i + 1], h[0][t], h[0][t + 1], h[1][t], h[1][t + 1], h[2][t],
+                               h[2][t + 1], h[3][t], h[3][t + 1]);
               }
               if (!(ok = produce_chunk<F16>(chunk++, j, h, tmem_warp, s, cx))) break;
             }
