@@ -391,12 +391,17 @@ __device__ __forceinline__ void h_component(float (&hv)[16], int l, int c, const
   } else {
     const float x0 = xs[tid], x1 = xs[kThreads + tid];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
+    for (int i = 0; i < 16; i += 2) {  // neuron pairs, packed pair arithmetic
       const int o = 16 * (i >> 2) + 4 * s + (i & 3);
-      const float w0 = small[kSmW0 + 2 * o], w1 = small[kSmW0 + 2 * o + 1];
-      float v, j0, j1, lv;
-      tanh_jet_fast(fmaf(w0, x0, fmaf(w1, x1, small[kSmB0 + o])), w0, w1, 0.0f, v, j0, j1, lv);
-      hv[i] = c == 0 ? v : c == 1 ? j0 : c == 2 ? j1 : lv;
+      const float w0a = small[kSmW0 + 2 * o], w1a = small[kSmW0 + 2 * o + 1];
+      const float w0b = small[kSmW0 + 2 * o + 2], w1b = small[kSmW0 + 2 * o + 3];
+      float za, zb, va, vb, j0a, j0b, j1a, j1b, la, lb;
+      fma2o(za, zb, w1a, w1b, x1, x1, small[kSmB0 + o], small[kSmB0 + o + 1]);
+      fma2o(za, zb, w0a, w0b, x0, x0, za, zb);
+      tanh_jet_fast2(za, zb, w0a, w0b, w1a, w1b, 0.0f, 0.0f, va, vb, j0a, j0b, j1a, j1b, la,
+                     lb);
+      hv[i] = c == 0 ? va : c == 1 ? j0a : c == 2 ? j1a : la;
+      hv[i + 1] = c == 0 ? vb : c == 1 ? j0b : c == 2 ? j1b : lb;
     }
   }
 }
@@ -908,8 +913,11 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kBlockThreads
         for (int half8 = 0; half8 < 2; ++half8) {
           float dwo[8];
 #pragma unroll
-          for (int k = 0; k < 8; ++k)
-            dwo[k] = fmaf(gu, d[0][8 * half8 + k], gl * d[3][8 * half8 + k]);
+          for (int k = 0; k < 8; k += 2) {
+            const int i = 8 * half8 + k;
+            mul2o(dwo[k], dwo[k + 1], gl, gl, d[3][i], d[3][i + 1]);
+            fma2o(dwo[k], dwo[k + 1], gu, gu, d[0][i], d[0][i + 1], dwo[k], dwo[k + 1]);
+          }
           store_part8(part, 0, q, s, half8, warp_sum8(dwo));
         }
 #pragma unroll

@@ -587,11 +587,15 @@ __device__ __forceinline__ bool produce_layer0(float x0, float x1, uint32_t& chu
     for (int j = 0; j < kChunks; ++j) {
       float h[4][4];
 #pragma unroll
-      for (int t = 0; t < 4; ++t) {
+      for (int t = 0; t < 4; t += 2) {  // neuron pairs o, o + 1
         const int o = 16 * j + 4 * s + t;
-        const float w0 = small[kSmW0 + 2 * o], w1 = small[kSmW0 + 2 * o + 1];
-        const float z = fmaf(w0, x0, fmaf(w1, x1, small[kSmB0 + o]));
-        Act::jet_fast(z, w0, w1, 0.0f, h[0][t], h[1][t], h[2][t], h[3][t]);
+        const float w0a = small[kSmW0 + 2 * o], w1a = small[kSmW0 + 2 * o + 1];
+        const float w0b = small[kSmW0 + 2 * o + 2], w1b = small[kSmW0 + 2 * o + 3];
+        float za, zb;
+        fma2o(za, zb, w1a, w1b, x1, x1, small[kSmB0 + o], small[kSmB0 + o + 1]);
+        fma2o(za, zb, w0a, w0b, x0, x0, za, zb);
+        Act::jet_fast2(za, zb, w0a, w0b, w1a, w1b, 0.0f, 0.0f, h[0][t], h[0][t + 1], h[1][t],
+                       h[1][t + 1], h[2][t], h[2][t + 1], h[3][t], h[3][t + 1]);
       }
       if (!produce_chunk<F16>(chunk++, j, h, tmem_warp, s, cx)) return false;
     }
@@ -824,16 +828,20 @@ __global__ void __launch_bounds__(kBlockThreads, 1)
           if (has_next && !(ok = produce_layer0<F16, Act>(nx0, nx1, chunk, tmem_warp, s, cx,
                                                           small)))
             break;
+          // output layer: u = w.v + b, lap = w.L, over this warp's 16 neurons (pairs of
+          // neuron slots i, i + 1 = neurons o, o + 1; the sums in neuron order)
 #pragma unroll
-          for (int i = 0; i < 16; ++i) d[0][i] += bias[16 * (i >> 2) + 4 * s + (i & 3)];
-          // output layer: u = w.v + b, lap = w.L, over this warp's 16 neurons
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            float v, j0, j1, lv;
-            Act::jet_fast(d[0][i], d[1][i], d[2][i], d[3][i], v, j0, j1, lv);
-            const float w = small[kSmWout + 16 * (i >> 2) + 4 * s + (i & 3)];
-            pu = fmaf(w, v, pu);
-            pl = fmaf(w, lv, pl);
+          for (int i = 0; i < 16; i += 2) {
+            const int o = 16 * (i >> 2) + 4 * s + (i & 3);
+            float za, zb, va, vb, j0a, j0b, j1a, j1b, la, lb;
+            add2o(za, zb, d[0][i], d[0][i + 1], bias[o], bias[o + 1]);
+            Act::jet_fast2(za, zb, d[1][i], d[1][i + 1], d[2][i], d[2][i + 1], d[3][i],
+                           d[3][i + 1], va, vb, j0a, j0b, j1a, j1b, la, lb);
+            const float wa = small[kSmWout + o], wb = small[kSmWout + o + 1];
+            pu = fmaf(wa, va, pu);
+            pl = fmaf(wa, la, pl);
+            pu = fmaf(wb, vb, pu);
+            pl = fmaf(wb, lb, pl);
           }
         }
         {
