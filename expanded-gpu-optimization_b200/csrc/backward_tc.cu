@@ -806,8 +806,9 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kBlockThreads
           const float uv = sigw[kInvSig + 4 * g] * it, uj = sigw[kInvSig + 4 * g + 1] * it;
           const float ul = sigw[kInvSig + 4 * g + 3] * it;
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            d[0][i] = fmaf(d[0][i], uv, bias[16 * (i >> 2) + 4 * s + (i & 3)]);
+          for (int i = 0; i < 16; i += 2) {
+            const int o = 16 * (i >> 2) + 4 * s + (i & 3);  // neuron slots i, i + 1: o, o + 1
+            fma2o(d[0][i], d[0][i + 1], d[0][i], d[0][i + 1], uv, uv, bias[o], bias[o + 1]);
           }
 #pragma unroll
           for (int i = 0; i < 16; i += 2) {
@@ -960,7 +961,7 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kBlockThreads
           for (int c = 0; c < 4; ++c) {
             float mc = 0.0f;
 #pragma unroll
-            for (int i = 0; i < 16; ++i) mc = fmaxf(mc, fabsf(d[c][i]));
+            for (int i = 0; i < 16; i += 2) mc = fmax3(mc, fabsf(d[c][i]), fabsf(d[c][i + 1]));
             mc = warp_max_nonneg(mc);
             zm = fmaxf(zm, mc * isg[c]);
             if (lane == 0) zw[c] = mc;

@@ -185,6 +185,14 @@ __device__ __forceinline__ void mul2(float& d0, float& d1, float a0, float a1) {
       : "f"(a0), "f"(a1));
 }
 
+// max(a, b, c) in one instruction (the three-input form of max.f32 on sm_100a); as fmaxf, a
+// NaN input is ignored when another input is a number.
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
 // Maximum over the warp of a non-negative float (non-negative floats order as their bit
 // patterns): one redux instruction.
 __device__ __forceinline__ float warp_max_nonneg(float v) {
