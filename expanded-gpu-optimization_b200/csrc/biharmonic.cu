@@ -18,9 +18,11 @@
 // SM with two independent 256-thread tile groups; the parameter buffer staged once per CTA
 // by one bulk copy; a tile is 32 points, warp w of a group owns neurons 8w..8w+7 and lane l
 // point l, so a layer is a register-tiled GEMM with 9 x 8 accumulators per thread, weights
-// read as broadcast float4 and the jet as [component][neuron][point] in shared memory (72 KB
+// read as broadcast float2 and the jet as [component][neuron][point] in shared memory (72 KB
 // per group); the last hidden layer folds in the output layer with a fixed-order sum of the
-// 8 warps' partials. Bound: FP32 FMA issue, ~2.25x the Laplacian kernel's FLOPs per point.
+// 8 warps' partials. Bound: FP32 FMA issue, ~2.25x the Laplacian kernel's FLOPs per point;
+// the GEMM's fmas run as packed pairs over the components of one neuron (fma.rn.f32x2), with
+// the weights read two K at a time (float2) to leave the registers for them.
 #include <algorithm>
 
 #include "common.cuh"
@@ -78,10 +80,6 @@ __device__ __forceinline__ void tanh_biharmonic(float (&c)[kComps]) {
   c[8] = b;
 }
 
-__device__ __forceinline__ float lane_of(const float4& w, int j) {
-  return j == 0 ? w.x : j == 1 ? w.y : j == 2 ? w.z : w.w;
-}
-
 __global__ void __launch_bounds__(kBlock, 1)
     forward_biharmonic_kernel(const float* __restrict__ coords, const float* __restrict__ params,
                               float* __restrict__ u_out, float* __restrict__ lap_out,
@@ -135,22 +133,26 @@ __global__ void __launch_bounds__(kBlock, 1)
         for (int m = 1; m < kComps; ++m) acc[m][k] = 0.0f;
       }
 #pragma unroll 1
-      for (int i = 0; i < kWidth; i += 4) {
-        float4 w[kNeuronsPerWarp];
+      for (int i = 0; i < kWidth; i += 2) {
+        float2 w[kNeuronsPerWarp];
 #pragma unroll
         for (int k = 0; k < kNeuronsPerWarp; ++k)
-          w[k] = *reinterpret_cast<const float4*>(W + (o0 + k) * kWidth + i);
+          w[k] = *reinterpret_cast<const float2*>(W + (o0 + k) * kWidth + i);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
+        for (int j = 0; j < 2; ++j) {
           float h[kComps];
           const float* src = jet + (i + j) * kTile + lane;
 #pragma unroll
           for (int m = 0; m < kComps; ++m) h[m] = src[m * kPlane];
+          // component pairs (m, m + 1) of one neuron in packed fmas (fma.rn.f32x2, each lane
+          // rounded as fmaf: bitwise the scalar loop); the ninth component alone
 #pragma unroll
           for (int k = 0; k < kNeuronsPerWarp; ++k) {
-            const float wk = lane_of(w[k], j);
+            const float wk = j == 0 ? w[k].x : w[k].y;
 #pragma unroll
-            for (int m = 0; m < kComps; ++m) acc[m][k] = fmaf(wk, h[m], acc[m][k]);
+            for (int m = 0; m + 1 < kComps; m += 2)
+              fma2(acc[m][k], acc[m + 1][k], wk, wk, h[m], h[m + 1]);
+            acc[kComps - 1][k] = fmaf(wk, h[kComps - 1], acc[kComps - 1][k]);
           }
         }
       }
