@@ -45,7 +45,10 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
 // The 12 MMAs of one 3xFP16 chunk (K = 16), issued by one elected lane of a converged warp in
 // one block: for each jet component c, D_c (+)= A_hi B_hi, then += A_lo B_hi and A_hi B_lo,
 // with D_c at TMEM column d0 + 64c, A_hi at a0 + 16c and A_lo 8 columns on. The first MMA of
-// each component accumulates only if `accumulate`; the others always do.
+// each component accumulates only if `accumulate`; the others always do. The components are
+// interleaved (the A_hi B_hi of all four, then A_lo B_hi, then A_hi B_lo), so consecutive
+// MMAs write different accumulators; each D_c still takes its three products in the same
+// order.
 __device__ __forceinline__ void mma_f16_ts_chunk_warp(uint32_t d0, uint32_t a0, uint64_t b_hi,
                                                       uint64_t b_lo, uint32_t idesc,
                                                       uint32_t accumulate) {
@@ -60,16 +63,16 @@ __device__ __forceinline__ void mma_f16_ts_chunk_warp(uint32_t d0, uint32_t a0, 
       "add.u32 l3, %1, 56;\n\t"
       "elect.sync _|e, 0xffffffff;\n\t"
       "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %4, pa;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [l0], %2, %4, pt;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %3, %4, pt;\n\t"
       "@e tcgen05.mma.cta_group::1.kind::f16 [d1], [h1], %2, %4, pa;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [d1], [l1], %2, %4, pt;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [d1], [h1], %3, %4, pt;\n\t"
       "@e tcgen05.mma.cta_group::1.kind::f16 [d2], [h2], %2, %4, pa;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [d2], [l2], %2, %4, pt;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [d2], [h2], %3, %4, pt;\n\t"
       "@e tcgen05.mma.cta_group::1.kind::f16 [d3], [h3], %2, %4, pa;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [l0], %2, %4, pt;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [d1], [l1], %2, %4, pt;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [d2], [l2], %2, %4, pt;\n\t"
       "@e tcgen05.mma.cta_group::1.kind::f16 [d3], [l3], %2, %4, pt;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %3, %4, pt;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [d1], [h1], %3, %4, pt;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f16 [d2], [h2], %3, %4, pt;\n\t"
       "@e tcgen05.mma.cta_group::1.kind::f16 [d3], [h3], %3, %4, pt;\n\t}"
       ::"r"(d0), "r"(a0), "l"(b_hi), "l"(b_lo), "r"(idesc), "r"(accumulate), "r"(1u)
       : "memory");
@@ -78,7 +81,7 @@ __device__ __forceinline__ void mma_f16_ts_chunk_warp(uint32_t d0, uint32_t a0, 
 // The 24 MMAs of one 3xTF32 chunk (two K steps of 8), issued the same way: K step kk uses
 // B descriptors b_hi[kk], b_lo[kk]; component c's A_hi block of step kk at a0 + 32c + 8kk and
 // its A_lo block 16 columns on; D_c at d0 + 64c. The first MMA of each component in K step 0
-// accumulates only if `accumulate`.
+// accumulates only if `accumulate`. Components interleaved as in the f16 chunk.
 __device__ __forceinline__ void mma_tf32_ts_chunk_warp(uint32_t d0, uint32_t a0, uint64_t bh0,
                                                        uint64_t bl0, uint64_t bh1, uint64_t bl1,
                                                        uint32_t idesc, uint32_t accumulate) {
@@ -95,28 +98,28 @@ __device__ __forceinline__ void mma_tf32_ts_chunk_warp(uint32_t d0, uint32_t a0,
       "add.u32 y4, %1, 80;\n\tadd.u32 y5, %1, 88;\n\tadd.u32 y6, %1, 112;\n\tadd.u32 y7, %1, 120;\n\t"
       "elect.sync _|e, 0xffffffff;\n\t"
       "@e tcgen05.mma.cta_group::1.kind::tf32 [%0], [x0], %2, %6, pa;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::tf32 [%0], [y0], %2, %6, pt;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::tf32 [%0], [x0], %3, %6, pt;\n\t"
       "@e tcgen05.mma.cta_group::1.kind::tf32 [d1], [x2], %2, %6, pa;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::tf32 [d1], [y2], %2, %6, pt;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::tf32 [d1], [x2], %3, %6, pt;\n\t"
       "@e tcgen05.mma.cta_group::1.kind::tf32 [d2], [x4], %2, %6, pa;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::tf32 [d2], [y4], %2, %6, pt;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::tf32 [d2], [x4], %3, %6, pt;\n\t"
       "@e tcgen05.mma.cta_group::1.kind::tf32 [d3], [x6], %2, %6, pa;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::tf32 [%0], [y0], %2, %6, pt;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::tf32 [d1], [y2], %2, %6, pt;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::tf32 [d2], [y4], %2, %6, pt;\n\t"
       "@e tcgen05.mma.cta_group::1.kind::tf32 [d3], [y6], %2, %6, pt;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::tf32 [%0], [x0], %3, %6, pt;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::tf32 [d1], [x2], %3, %6, pt;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::tf32 [d2], [x4], %3, %6, pt;\n\t"
       "@e tcgen05.mma.cta_group::1.kind::tf32 [d3], [x6], %3, %6, pt;\n\t"
       "@e tcgen05.mma.cta_group::1.kind::tf32 [%0], [x1], %4, %6, pt;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::tf32 [%0], [y1], %4, %6, pt;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::tf32 [%0], [x1], %5, %6, pt;\n\t"
       "@e tcgen05.mma.cta_group::1.kind::tf32 [d1], [x3], %4, %6, pt;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::tf32 [d1], [y3], %4, %6, pt;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::tf32 [d1], [x3], %5, %6, pt;\n\t"
       "@e tcgen05.mma.cta_group::1.kind::tf32 [d2], [x5], %4, %6, pt;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::tf32 [d2], [y5], %4, %6, pt;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::tf32 [d2], [x5], %5, %6, pt;\n\t"
       "@e tcgen05.mma.cta_group::1.kind::tf32 [d3], [x7], %4, %6, pt;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::tf32 [%0], [y1], %4, %6, pt;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::tf32 [d1], [y3], %4, %6, pt;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::tf32 [d2], [y5], %4, %6, pt;\n\t"
       "@e tcgen05.mma.cta_group::1.kind::tf32 [d3], [y7], %4, %6, pt;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::tf32 [%0], [x1], %5, %6, pt;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::tf32 [d1], [x3], %5, %6, pt;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::tf32 [d2], [x5], %5, %6, pt;\n\t"
       "@e tcgen05.mma.cta_group::1.kind::tf32 [d3], [x7], %5, %6, pt;\n\t}"
       ::"r"(d0), "r"(a0), "l"(bh0), "l"(bl0), "l"(bh1), "l"(bl1), "r"(idesc), "r"(accumulate),
         "r"(1u)
