@@ -578,6 +578,9 @@ __device__ __forceinline__ float ld_dsmem_f32(uint32_t addr) {
 __global__ void __launch_bounds__(512) prep_weights_kernel(const float* __restrict__ params,
                                                            float* __restrict__ wsplit) {
   __shared__ float wmax[16];
+  // The step kernel after this one starts its set-up now (it waits for these operands
+  // before its first weight-slot copy).
+  allow_dependents();
   const int blk = blockIdx.x, tid = threadIdx.x;
   const float* W = params + kHiddenBase + (blk % 3) * kHiddenStride;
   // The block's 2048 pairs cover every element of W_l once: their maximum is tau's input,
@@ -632,6 +635,9 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kBlockThreads
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
+  // The training step's update kernel may be scheduled onto SMs as this grid's CTAs exit
+  // (it waits for the whole grid before it reads the partial rows).
+  allow_dependents();
 
   // ---- set-up ----
   // The first tile's point, requested first: its latency overlaps the set-up below.
@@ -699,8 +705,13 @@ __global__ void __cluster_dims__(kCluster, 1, 1) __launch_bounds__(kBlockThreads
   __syncthreads();
   tc::fence_after_sync();
   cx.tmem = *tmem_base_slot;
-  if (tid == 0)
+  if (tid == 0) {
+    // This kernel may start while prep_weights_kernel still runs; everything above reads
+    // only what was complete before that kernel started. Thread 0 makes every read of the
+    // pre-split weights (these copies and the later slot reloads), so it alone waits.
+    wait_for_prerequisites();
     for (int k = 0; k < kWeightSlots; ++k) load_weight_slot(k, wsplit, weight_block(k));
+  }
 
   if (warp >= kWarps) {
     // ---- MMA warpgroup: warp 16 issues the chunks, 17-19 wait at the final barrier ----
@@ -1311,16 +1322,20 @@ cudaError_t launch_backward_tc(const PointSets& points, const float* params,
   float* partials = wsplit + kWeightBlocks * (kLayerBytes / 4);
   float* scratch = partials + static_cast<size_t>(grid) * kRowStride;
   prep_weights_kernel<<<kWeightBlocks, 512, 0, stream>>>(params, wsplit);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  // The step kernel's set-up (parameter staging, scales, the first tile's layer 0) overlaps
+  // the pre-split; its first read of the split weights waits for it.
   if (poisson) {
-    backward_tc_kernel<true><<<grid, kBlockThreads, kSmemBytes, stream>>>(
-        ps, params, wsplit, nullptr, nullptr, grad_coords, lap_out, partials, scratch, tiles,
-        dev.status);
+    e = launch_dependent(backward_tc_kernel<true>, dim3(grid), dim3(kBlockThreads), kSmemBytes,
+                         stream, ps, params, wsplit, nullptr, nullptr, grad_coords, lap_out,
+                         partials, scratch, tiles, dev.status);
   } else {
-    backward_tc_kernel<false><<<grid, kBlockThreads, kSmemBytes, stream>>>(
-        ps, params, wsplit, grad_u, grad_lap, grad_coords, nullptr, partials, scratch, tiles,
-        dev.status);
+    e = launch_dependent(backward_tc_kernel<false>, dim3(grid), dim3(kBlockThreads),
+                         kSmemBytes, stream, ps, params, wsplit, grad_u, grad_lap,
+                         grad_coords, nullptr, partials, scratch, tiles, dev.status);
   }
-  return cudaGetLastError();
+  return e;
 }
 
 float* backward_tc_partials(float* workspace) {

@@ -53,6 +53,9 @@ __global__ void __launch_bounds__(kUpdateThreads)
                        float* __restrict__ grad_out, float* __restrict__ loss_out,
                        unsigned int* status) {
   __shared__ float sums[kUpdateGroups][kUpdateCols];
+  // Launched as a dependent of the gradient kernel: its partial rows are complete and
+  // visible only after this wait.
+  wait_for_prerequisites();
   const int cx = threadIdx.x % kUpdateCols, grp = threadIdx.x / kUpdateCols;
   const int col = blockIdx.x * kUpdateCols + cx;
   const bool live = col <= kLossColumn;
@@ -120,9 +123,11 @@ cudaError_t launch_step_update(const float* partials, int rows, ExchangeState* s
                                int rank, uint64_t wait_limit_ns, const AdamArgs& adam,
                                float* grad_out, float* loss_out, unsigned int* status,
                                cudaStream_t stream) {
-  step_update_kernel<<<kUpdateBlocks, kUpdateThreads, 0, stream>>>(
-      partials, rows, state, world, rank, wait_limit_ns, adam, grad_out, loss_out, status);
-  return cudaGetLastError();
+  // A dependent launch: its CTAs take the SMs the gradient kernel's CTAs leave, without a
+  // launch gap, and wait in wait_for_prerequisites() for the whole gradient grid.
+  return launch_dependent(step_update_kernel, dim3(kUpdateBlocks), dim3(kUpdateThreads), 0,
+                          stream, partials, rows, state, world, rank, wait_limit_ns, adam,
+                          grad_out, loss_out, status);
 }
 
 }  // namespace fhb

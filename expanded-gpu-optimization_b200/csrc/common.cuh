@@ -45,6 +45,19 @@ __device__ __forceinline__ void report_status(unsigned int* status, unsigned int
   if (status != nullptr) atomicOr(status, bits);
 }
 
+// ---- programmatic dependent launch ----
+// A kernel launched with launch_dependent() may start while the kernel before it in the
+// stream still runs, as soon as every CTA of that kernel has called allow_dependents() (or
+// exited). Until it calls wait_for_prerequisites() it may read only what was complete before
+// that earlier kernel started; after the call, everything the earlier kernel wrote is
+// visible (generic and bulk-copy reads alike). Both are no-ops for an ordinary launch.
+__device__ __forceinline__ void allow_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void wait_for_prerequisites() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 // ---- mbarrier + bulk copy (non-multicast) ----
 
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {

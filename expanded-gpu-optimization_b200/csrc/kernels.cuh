@@ -4,6 +4,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "../../include/fused_hoad_b200.h"
 
 namespace fhb {
@@ -186,6 +188,26 @@ cudaError_t launch_backward_tc(const PointSets& points, const float* params,
                                const float* grad_u, const float* grad_lap, float* grad_coords,
                                float* lap_out, float* workspace, bool poisson,
                                const DeviceInfo& dev, cudaStream_t stream);
+
+// Launches `kernel` with programmatic stream serialization: it may start while the kernel
+// before it in `stream` is still running, once every CTA of that kernel has called
+// allow_dependents() (common.cuh) or exited, and it orders its reads of that kernel's
+// results with wait_for_prerequisites(). Stream capture records the same dependency.
+template <typename... Params, typename... Args>
+cudaError_t launch_dependent(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem,
+                             cudaStream_t stream, Args&&... args) {
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // ---- adam.cu ----
 cudaError_t launch_adam(float* params, const float* grad, float* exp_avg, float* exp_avg_sq,
