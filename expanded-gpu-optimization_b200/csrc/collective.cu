@@ -53,15 +53,25 @@ __global__ void __launch_bounds__(kUpdateThreads)
                        float* __restrict__ grad_out, float* __restrict__ loss_out,
                        unsigned int* status) {
   __shared__ float sums[kUpdateGroups][kUpdateCols];
-  // Launched as a dependent of the gradient kernel: its partial rows are complete and
-  // visible only after this wait.
-  wait_for_prerequisites();
   const int cx = threadIdx.x % kUpdateCols, grp = threadIdx.x / kUpdateCols;
   const int col = blockIdx.x * kUpdateCols + cx;
   const bool live = col <= kLossColumn;
   // Read before this CTA counts itself done, so before the last CTA advances them.
   const int64_t t = *adam.step + 1;
   const uint32_t e = state->epoch + 1u;
+  // The column's parameter and moments: the previous step's update kernel wrote them and
+  // finished before this step's gradient kernel started, and the gradient kernel does not
+  // write them, so they are read before the wait below.
+  const bool adam_col = grp == 0 && live && col != kLossColumn;
+  float p = 0.0f, m = 0.0f, v = 0.0f;
+  if (adam_col) {
+    p = adam.params[col];
+    m = adam.exp_avg[col];
+    v = adam.exp_avg_sq[col];
+  }
+  // Launched as a dependent of the gradient kernel: its partial rows are complete and
+  // visible only after this wait.
+  wait_for_prerequisites();
 
   sums[grp][cx] = live ? column_group_sum(partials, rows, col, grp) : 0.0f;
   __syncthreads();
@@ -97,7 +107,6 @@ __global__ void __launch_bounds__(kUpdateThreads)
         if (loss_out != nullptr) *loss_out = total;
       } else {
         const AdamScalars s = adam_scalars(t, adam.lr, adam.beta1, adam.beta2);
-        float p = adam.params[col], m = adam.exp_avg[col], v = adam.exp_avg_sq[col];
         adam_element(total, p, m, v, s, adam.beta1, adam.beta2, adam.eps);
         adam.exp_avg[col] = m;
         adam.exp_avg_sq[col] = v;
