@@ -282,6 +282,10 @@ int fhb_exchange_destroy(fhb_exchange* exchange);
  * peer wait gives up, FHB_STATUS_PEER_TIMEOUT is set, the parameters whose wait gave up are
  * left unchanged and the replicas are no longer consistent: stop or reload a checkpoint.
  * Workspace: fhb_pinn_step_workspace_bytes(n, n_boundary) bytes, 16-byte aligned.
+ * With the tensor-core kernel the step is three launches in `stream`: the weight pre-split
+ * (an ordinary launch), then the gradient kernel and the update kernel as programmatic
+ * dependent launches, each starting while the kernel before it finishes and waiting on the
+ * device for that kernel's results.
  */
 int fhb_train_step(const float* coords, int64_t n, int64_t n_total, const float* boundary,
                    int64_t n_boundary, int64_t n_boundary_total, float boundary_weight,
