@@ -61,8 +61,9 @@ def test_step_sees_state_written_right_before_it(kernel: int) -> None:
     fused, separate = _state(params), _state(params)
     ex = C.exchange_create(1, 0, 5.0, 0)
     try:
-        # 100 points is one tile (a grid of 2 CTAs: the update kernel's CTAs take the other
-        # SMs while the step kernel runs); 65,536 fills every SM for several tiles.
+        # 100 interior + 256 boundary points are 3 tiles (a grid of 4 CTAs with the
+        # tensor-core kernel: the update kernel's CTAs take the other SMs while the step
+        # kernel runs); 65,536 fills every SM for several tiles.
         for k, n in enumerate((65_536, 100, 20_000, 100, 65_536)):
             x = uniform_points(n, seed=40 + k).cuda()
             _disturb(fused, k)
